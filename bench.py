@@ -1,0 +1,550 @@
+"""Benchmark of the linear-layer hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step" = one pass of the hot path over one batch): the four
+projections of one TinyLlama-1.1B-shaped decoder layer at prefill M=512 tokens,
+fp16, fused epilogues as the engine calls them:
+    q/k/v   [512,2048] x [2560,2048]^T
+    o_proj  [512,2048] x [2048,2048]^T  + residual
+    gate/up [512,2048] x [11264,2048]^T + SwiGLU -> [512,5632]
+    down    [512,5632] x [2048,5632]^T  + residual
+45.10 GFLOP per step (2*M*N*K, epilogues not counted).  Weights ~N(0,0.02),
+activations ~N(0,1), seeded, random-init (no checkpoint).  Steps rotate over 4
+independent layer copies (352 MB of weights, > the 126 MB L2), so every step
+streams its weights from HBM.
+
+N > 1 (launched by torch.distributed.run): tensor parallel over N GPUs, the
+same total work (strong scaling): q/k/v by heads (KV heads replicated when
+N > 4), gate/up by intermediate feature, o/down by K followed by an fp32 NCCL
+all-reduce and the residual/rounding step.
+
+--impl reference: the reference has no CPU implementation of this path, so the
+reference arm times the CPU oracle's multithreaded fp32 GEMM (oracle/liborc.so)
+on the same layer, one bounded slice of the layer's rows per step.
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "tinyllama_layer_prefill_m512"
+M, H, KVD, IM = 512, 2048, 256, 5632
+N_HEADS, N_KV, HEAD_DIM = 32, 4, 64
+QKV_N = H + 2 * KVD
+GEMMS = {  # name: (N_out, K, epilogue)
+    "qkv": (QKV_N, H, "none"),
+    "o_proj": (H, H, "residual"),
+    "gate_up": (IM, H, "swiglu"),
+    "down": (H, IM, "residual"),
+}
+FLOPS = {"qkv": 2 * M * QKV_N * H, "o_proj": 2 * M * H * H, "gate_up": 2 * M * 2 * IM * H,
+         "down": 2 * M * H * IM}
+STEP_FLOPS = sum(FLOPS.values())  # 45.10e9
+N_COPIES = 4
+GRAPH_CHUNK = 500
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` on this workload, from the committed
+    ncu summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch: X')."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{WORKLOAD}.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(map(str, self.gpus)), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+                self.lines = [l for l in out.splitlines() if l.strip()]
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                s, m_ = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            mx = m_
+            sm.append(s)
+            for i, n in enumerate(names):
+                if f[5 + i].lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- our arm
+
+def make_layers(rank: int, world: int, dev):
+    """N_COPIES layer weight sets, sharded for this rank (world 1 = whole)."""
+    import orininfer_b200 as ob
+    from orininfer_b200 import tp
+    from orininfer_b200.synth import seeded
+
+    layers = []
+    for c in range(N_COPIES):
+        s = 1000 * (c + 1)
+        wq = seeded((H, H), s + 1, 0.02)
+        wk = seeded((KVD, H), s + 2, 0.02)
+        wv = seeded((KVD, H), s + 3, 0.02)
+        wo = seeded((H, H), s + 4, 0.02)
+        wg = seeded((IM, H), s + 5, 0.02)
+        wu = seeded((IM, H), s + 6, 0.02)
+        wd = seeded((H, IM), s + 7, 0.02)
+        L = {}
+        L["qkv"] = tp.shard_qkv(wq, wk, wv, N_HEADS, N_KV, HEAD_DIM, rank, world).to(dev)
+        g, u = tp.shard_gate_up_rows(wg, wu, rank, world)
+        L["gate_up"] = ob.pack_gate_up(g.to(dev), u.to(dev))
+        if world == 1:
+            L["o_proj"] = wo.to(dev)
+            L["down"] = wd.to(dev)
+        else:
+            L["o_proj"] = tp.shard_cols(wo, rank, world).to(dev)
+            L["down"] = tp.shard_cols(wd, rank, world).to(dev)
+        layers.append(L)
+    torch.cuda.synchronize()
+    return layers
+
+
+class Step:
+    """One layer pass (4 projections), on the current stream."""
+
+    def __init__(self, layers, rank, world, dev, comm=None):
+        import orininfer_b200 as ob
+        from orininfer_b200.synth import seeded
+
+        self.ob = ob
+        self.layers = layers
+        self.world = world
+        self.comm = comm
+        qd_local = H // world
+        im_local = IM // world
+        # inputs of this step: normed hidden, attention output, residual
+        # stream, post-attention normed hidden (synthetic, ~N(0,1))
+        self.h = seeded((M, H), 11, 1.0).to(dev)
+        self.attn = seeded((M, H), 12, 1.0).to(dev)[:, :qd_local].contiguous() if world > 1 \
+            else seeded((M, H), 12, 1.0).to(dev)
+        self.x = seeded((M, H), 13, 1.0).to(dev)
+        self.h2 = seeded((M, H), 14, 1.0).to(dev)
+        self.qkv = torch.empty((M, layers[0]["qkv"].shape[0]), dtype=torch.float16, device=dev)
+        self.x1 = torch.empty((M, H), dtype=torch.float16, device=dev)
+        self.act = torch.empty((M, im_local), dtype=torch.float16, device=dev)
+        self.x2 = torch.empty((M, H), dtype=torch.float16, device=dev)
+        self.partial = torch.empty((M, H), dtype=torch.float32, device=dev)
+        # our kernels per step: 4 GEMMs (+ 2 all-reduce finish kernels under TP)
+        self.launches = 4 if world == 1 else 6
+
+    def run(self, i: int, events=None):
+        L = self.layers[i % len(self.layers)]
+        ob = self.ob
+        s = torch.cuda.current_stream()
+
+        def mark(name, which):
+            if events is not None:
+                events[name][which].record(s)
+
+        mark("qkv", 0)
+        ob.linear_into(self.qkv, self.h, L["qkv"])
+        mark("qkv", 1)
+        mark("o_proj", 0)
+        if self.world == 1:
+            ob.linear_into(self.x1, self.attn, L["o_proj"], epilogue="residual", residual=self.x)
+        else:
+            self.comm.linear_row(self.attn, L["o_proj"], residual=self.x, out=self.x1,
+                                 partial=self.partial)
+        mark("o_proj", 1)
+        mark("gate_up", 0)
+        ob.linear_into(self.act, self.h2, L["gate_up"], epilogue="swiglu")
+        mark("gate_up", 1)
+        mark("down", 0)
+        if self.world == 1:
+            ob.linear_into(self.x2, self.act, L["down"], epilogue="residual", residual=self.x1)
+        else:
+            self.comm.linear_row(self.act, L["down"], residual=self.x1, out=self.x2,
+                                 partial=self.partial)
+        mark("down", 1)
+
+
+def capture(step: Step, n: int, start: int = 0, events_per_step=None):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                step.run(start + i, events_per_step[i] if events_per_step else None)
+    torch.cuda.current_stream().wait_stream(s)
+    return g
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_steps(step: Step, steps: int, warmup: int, world: int, dev_index: int):
+    """Warm up, then time exactly `steps` steps via CUDA graph chunks."""
+    chunk = min(GRAPH_CHUNK, steps)
+    g = capture(step, chunk)
+    rem = steps % chunk
+    g_rem = capture(step, rem) if rem else None
+    g_warm = capture(step, warmup) if warmup > 0 else None
+    if g_warm is not None:
+        g_warm.replay()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler([dev_index] if world == 1 else list(range(world))) as clk:
+        start.record()
+        for _ in range(steps // chunk):
+            g.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        stop.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(stop)
+    ms = max_over_ranks(ms, world)
+    del g, g_rem, g_warm
+    return ms, clk.summary()
+
+
+def kernel_breakdown(step: Step, n: int):
+    """Average device time per launch of each projection (CUDA events on the
+    launching stream, inside a captured graph of n steps)."""
+    events = [{k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for k in GEMMS} for _ in range(n)]
+    g = capture(step, n, events_per_step=events)
+    g.replay()  # warm
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    out = {}
+    for k in GEMMS:
+        ts = [e[k][0].elapsed_time(e[k][1]) for e in events]
+        out[k] = statistics.mean(ts)
+    del g
+    return out
+
+
+def e2e_through_abi(step: Step, steps: int, dev):
+    """The same metric through the public API with host buffers: every step
+    copies its inputs from pinned host memory and reads the result back."""
+    hosts = {n: getattr(step, n).cpu().pin_memory() for n in ("h", "attn", "x", "h2")}
+    out_host = torch.empty((M, H), dtype=torch.float16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in hosts.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def one(i):
+        for n, t in hosts.items():
+            getattr(step, n).copy_(t, non_blocking=True)
+        step.run(i)
+        out_host.copy_(step.x2, non_blocking=True)
+
+    for i in range(5):
+        one(i)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        one(i)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    return ms, h2d, d2h
+
+
+def cpu_baseline_layer(budget_s: float = 10.0) -> dict:
+    """The oracle's fp32 multithreaded GEMM over the same layer shapes."""
+    import numpy as np
+    from oracle import oracle as orc
+
+    threads = orc.max_threads()
+    rng = np.random.default_rng(0)
+    mats = {}
+    for k, (n_out, kk, epi) in GEMMS.items():
+        n_w = 2 * n_out if epi == "swiglu" else n_out
+        mats[k] = (rng.standard_normal((M, kk), dtype=np.float32),
+                   (rng.standard_normal((n_w, kk), dtype=np.float32) * 0.02))
+    for k, (a, w) in mats.items():  # warm (thread pool, page faults)
+        orc.gemm_f32(a[:8], w, threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for k, (a, w) in mats.items():
+            orc.gemm_f32(a, w, threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": STEP_FLOPS * reps / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{reps} full layer passes (4 fp32 GEMMs at M=512, oracle orc_gemm_f32), "
+                      f"{dt:.1f} s"}
+
+
+def run_ours(args, rank, world, local_rank):
+    import orininfer_b200  # noqa: F401  (fails loudly if the CUDA library is missing)
+    from orininfer_b200 import tp
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    comm = None
+    if world > 1:
+        uid = tp.exchange_unique_id(rank)
+        comm = tp.TPComm(rank, world, local_rank, uid, timeout_s=120.0)
+    layers = make_layers(rank, world, dev)
+    step = Step(layers, rank, world, dev, comm)
+
+    ms, clocks = time_steps(step, args.steps, args.warmup, world, local_rank)
+    ms_per_step = ms / args.steps
+    value = STEP_FLOPS * args.steps / (ms / 1e3) / 1e12
+
+    kt = kernel_breakdown(step, 64) if world == 1 else None
+    e2e_steps = min(args.steps, 300)
+    e2e_ms, h2d, d2h = e2e_through_abi(step, e2e_steps, dev)
+    e2e_ms = max_over_ranks(e2e_ms, world)
+    e2e_value = STEP_FLOPS * e2e_steps / (e2e_ms / 1e3) / 1e12
+
+    peaks, src = load_peaks()
+    line = {
+        "metric": "prefill GEMM throughput (TinyLlama layer q/k/v+o+gate/up+down, M=512)",
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
+        "config": {"workload": WORKLOAD, "M": M, "hidden": H, "intermediate": IM,
+                   "q_heads": N_HEADS, "kv_heads": N_KV, "head_dim": HEAD_DIM,
+                   "flops_per_step": STEP_FLOPS,
+                   "parallelism": "tp%d" % world if world > 1 else "single",
+                   "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies "
+                         f"({N_COPIES * 88} MB of weights)"},
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "orininfer_b200.linear_into -> orin_linear_ex (C ABI), pinned host "
+                        "inputs copied in and the layer output copied out every step"},
+        "gpu_launches": step.launches * args.steps,
+        "clocks": clocks,
+    }
+    if kt is not None:
+        dom = "gate_up"
+        avg_ms = kt[dom]
+        achieved = FLOPS[dom] / (avg_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        line["roofline"] = {
+            "kernel": "tc_linear_kernel<f16,256,SWIGLU> (gate/up + SwiGLU, 512x11264x2048)",
+            "bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "peak_source": f"{src} dense bf16 burst (MEASURED_PEAKS.json bf16_tflops)"
+            if src == "measured" else "fallback 1590 TFLOP/s",
+            "traffic": profile_traffic("gate_up"),
+            "algorithmic_flops_per_launch": FLOPS[dom],
+            "avg_launch_ms": round(avg_ms, 5),
+        }
+        line["kernels_ms"] = {k: round(v, 5) for k, v in kt.items()}
+        line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}
+        line["cpu_baseline"] = cpu_baseline_layer(args.cpu_budget)
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
+    return line
+
+
+# ---------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    """The CPU oracle (the reference has no CPU path of its own) on the same
+    layer: each step computes a bounded slice of the layer's token rows through
+    all four GEMMs in fp32 with every host thread."""
+    import numpy as np
+    from oracle import oracle as orc
+
+    threads = orc.max_threads()
+    rng = np.random.default_rng(0)
+    mats = {}
+    for k, (n_out, kk, epi) in GEMMS.items():
+        n_w = 2 * n_out if epi == "swiglu" else n_out
+        mats[k] = (rng.standard_normal((M, kk), dtype=np.float32),
+                   rng.standard_normal((n_w, kk), dtype=np.float32) * 0.02)
+    # size the row slice so warmup + steps fit in about 90 s of CPU time
+    t0 = time.perf_counter()
+    for k, (a, w) in mats.items():
+        orc.gemm_f32(a[:64], w, threads)
+    per_row = (time.perf_counter() - t0) / 64
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = int(max(4, min(M, (budget / per_row) // 4 * 4)))
+    flops_per_step = STEP_FLOPS * rows / M
+
+    def step(i):
+        r0 = (i * rows) % M
+        r1 = min(M, r0 + rows)
+        for k, (a, w) in mats.items():
+            orc.gemm_f32(a[r0:r1], w, threads)
+        return (r1 - r0)
+
+    for i in range(args.warmup):
+        step(i)
+    done_rows = 0
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        done_rows += step(i)
+    dt = time.perf_counter() - t0
+    value = STEP_FLOPS * (done_rows / M) / dt / 1e12
+    sample = (f"{rows} of the {M} token rows per step through all four projections "
+              f"(fp32, oracle orc_gemm_f32, {threads} threads)")
+    return {
+        "impl": "reference",
+        "metric": "prefill GEMM throughput (TinyLlama layer q/k/v+o+gate/up+down, M=512)",
+        "value": round(value, 4),
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": WORKLOAD, "M": M, "hidden": H, "intermediate": IM,
+                   "flops_per_step": STEP_FLOPS, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference runs this path only on a GPU (kernels/matmul.cu); its CPU "
+                "counterpart here is the oracle's restatement of the same arithmetic",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0,
+                    help="seconds of CPU work for the cpu_baseline figure")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args)), flush=True)
+        return 0
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

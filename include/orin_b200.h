@@ -1,0 +1,188 @@
+/*
+ * orin_b200.h — C ABI of the B200 (sm_100a) linear-layer hot path.
+ *
+ * Every entry point takes plain device pointers, element counts and an opaque
+ * CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream).
+ * No allocation happens on the data path except the per-device split-K
+ * workspace that orin_linear() creates lazily on its first call on a device
+ * (orin_linear_ex() lets the caller pass its own workspace instead).
+ * No C++ exception crosses this boundary: every function returns orin_status,
+ * and orin_last_error() gives a thread-local message for the last failure.
+ *
+ * Semantics shared by every GEMM entry point (the reference's, restated):
+ *   C[m, n] = round16( sum_k f32(A[m, k]) * f32(W[n, k]) )
+ * with A row-major [M, K] (activations), W row-major [N, K] (HF weight layout,
+ * "B stored transposed"), fp32 accumulation and exactly one rounding of the
+ * result to the 16-bit type.  Reference: kernels/matmul.cu:25-44 (GEMV),
+ * kernels/matmul.cu:59-68 (cublasGemmEx, CUBLAS_COMPUTE_32F),
+ * kernels/gemm_cute.cu:147,176-178 (CuTe mma.sync, fp32 accumulator).
+ */
+#ifndef ORIN_B200_H
+#define ORIN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum orin_status {
+    ORIN_OK = 0,
+    ORIN_ERR_INVALID_ARG = 1, /* null pointer, negative size, bad enum      */
+    ORIN_ERR_UNSUPPORTED = 2, /* shape/alignment this entry point can't do  */
+    ORIN_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed          */
+    ORIN_ERR_NCCL = 4,        /* an NCCL call failed                        */
+    ORIN_ERR_TIMEOUT = 5,     /* a bounded wait expired (device or host)    */
+    ORIN_ERR_NO_DEVICE = 6    /* no sm_100 device visible                   */
+} orin_status;
+
+typedef enum orin_dtype {
+    ORIN_F16 = 0,
+    ORIN_BF16 = 1
+} orin_dtype;
+
+/* What happens to the fp32 accumulator before it is stored. */
+typedef enum orin_epilogue {
+    /* C = round16(acc)                                    (kernels/matmul.cu:43) */
+    ORIN_EPI_NONE = 0,
+    /* W holds 2N rows, gate and up interleaved in 64-row groups (see
+     * orin_pack_gate_up); C[M, N] = round16(silu(round16(g)) * round16(u)).
+     * Folds kernels/fused_swiglu.cu:7-16 into the gate/up GEMM. */
+    ORIN_EPI_SWIGLU = 1,
+    /* C = round16(f32(R) + f32(round16(acc))); C may alias R.
+     * Folds kernels/softmax.cu:78-83 (add) into the O / down GEMM. */
+    ORIN_EPI_RESIDUAL = 2,
+    /* C is float: C = f32(round16(acc)).
+     * Folds kernels/softmax.cu:87-90 (bf16_to_fp32) into the LM head. */
+    ORIN_EPI_F32_OUT = 3,
+    /* C is float: C = acc, unrounded (tensor-parallel partial sums). */
+    ORIN_EPI_F32_PARTIAL = 4
+} orin_epilogue;
+
+/* Kernel selection; AUTO is what every production caller should pass. */
+typedef enum orin_algo {
+    ORIN_ALGO_AUTO = 0,
+    ORIN_ALGO_TC_WIDE = 1,   /* tcgen05, 128 tokens x 256 features per tile  */
+    ORIN_ALGO_TC_SKINNY = 2, /* tcgen05, 128 features x <=64 tokens (M<=64)  */
+    ORIN_ALGO_SIMT = 3       /* CUDA-core kernel for unaligned shapes        */
+} orin_algo;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int orin_version(void);
+
+/* Thread-local description of the last non-OK status returned on this thread. */
+const char* orin_last_error(void);
+
+/*
+ * C = epilogue(A · W^T).  Replaces kernels::matmul (include/kernels.h:51-56,
+ * kernels/matmul.cu:47-81) and, through the epilogue argument, the pairs
+ * matmul+fused_silu_mul (src/model.cu:100-104), matmul+add (src/model.cu:87-90,
+ * 107-110) and matmul+bf16_to_fp32 (src/model.cu:125-130).
+ *   C         [M, N] 16-bit, or float for F32_OUT / F32_PARTIAL
+ *   A         [M, K] 16-bit
+ *   W         [N, K] 16-bit ([2N, K] packed gate/up for SWIGLU)
+ *   residual  [M, N] 16-bit for RESIDUAL, else NULL
+ * Any M, N >= 1 and K >= 1 are accepted.  K % 8 == 0 with 16-byte aligned
+ * A, W (and C rows) takes the tcgen05 path; other shapes take the SIMT path.
+ */
+orin_status orin_linear(void* C, const void* A, const void* W,
+                        int M, int N, int K, int dtype, int epilogue,
+                        const void* residual, void* stream);
+
+/*
+ * orin_linear with an explicit kernel choice and caller-owned workspace.
+ * workspace may be NULL (then the lazily created per-device workspace is
+ * used).  A caller workspace must be at least orin_linear_workspace_size()
+ * bytes, 256-byte aligned, and zero-filled before its first use; the kernels
+ * leave it zero-filled again when they finish.  Calls that may overlap on the
+ * GPU must not share a workspace.
+ */
+orin_status orin_linear_ex(void* C, const void* A, const void* W,
+                           int M, int N, int K, int dtype, int epilogue,
+                           const void* residual, int algo,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Workspace bytes orin_linear_ex needs for this problem (0 if none). */
+size_t orin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue,
+                                  int algo);
+
+/*
+ * Build the packed gate/up weight the SWIGLU epilogue reads:
+ * rows [128g, 128g+64) = gate rows [64g, 64g+64), rows [128g+64, 128g+128) =
+ * up rows [64g, 64g+64).  w_gate, w_up [IM, K] (include/weight_store.h:17-18);
+ * w_packed [2*IM, K].  Requires IM % 64 == 0.  Runs on the device, on stream.
+ */
+orin_status orin_pack_gate_up(void* w_packed, const void* w_gate,
+                              const void* w_up, int IM, int K, int dtype,
+                              void* stream);
+
+/* out = round16(silu(f32(gate)) * f32(up)), n elements; out may alias gate.
+ * Replaces kernels::fused_silu_mul (include/kernels.h:88-94). */
+orin_status orin_silu_mul(void* out, const void* gate, const void* up,
+                          long long n, int dtype, void* stream);
+
+/* x = round16(f32(x) + f32(y)), n elements.
+ * Replaces kernels::add (include/kernels.h:97-101, kernels/softmax.cu:78-83). */
+orin_status orin_add(void* x, const void* y, long long n, int dtype,
+                     void* stream);
+
+/* out = f32(in), n elements.
+ * Replaces kernels::bf16_to_fp32 (include/kernels.h:104-108). */
+orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype,
+                           void* stream);
+
+/*
+ * Synchronise stream and report device-side failures of this library's
+ * kernels: every spin-wait inside them gives up after a bounded time and
+ * records an error code instead of hanging.  Returns ORIN_ERR_TIMEOUT (and
+ * clears the record, re-zeroing the split-K workspace) if one did.
+ */
+orin_status orin_device_check(void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Tensor parallelism over NCCL (no counterpart in the reference, which is   */
+/* single-GPU: include/kv_cache.h:7).  One process per GPU.                  */
+/* ------------------------------------------------------------------------ */
+
+#define ORIN_TP_UNIQUE_ID_BYTES 128
+
+/* Rank 0 creates the id and shares it (e.g. through a torch.distributed
+ * store); every rank then calls orin_tp_init with it. */
+orin_status orin_tp_unique_id(void* id_out /* ORIN_TP_UNIQUE_ID_BYTES */);
+
+/* Create this rank's communicator on `device`.  The NCCL communicator is
+ * non-blocking; a collective that has not finished after timeout_s seconds
+ * is aborted and reported as ORIN_ERR_TIMEOUT. */
+orin_status orin_tp_init(void** comm_out, const void* id, int rank,
+                         int world_size, int device, double timeout_s);
+
+/* In-place fp32 sum over all ranks of buf[n] on stream. */
+orin_status orin_tp_allreduce_f32(void* comm, float* buf, long long n,
+                                  void* stream);
+
+/*
+ * Row-parallel linear (o_proj / down_proj sharded along K):
+ *   partial = A_shard · W_shard^T  (fp32, unrounded, [M, N])
+ *   sum     = all-reduce(partial)  over ranks
+ *   C       = round16(f32(residual) + f32(round16(sum)))   if residual
+ *           = round16(sum)                                   otherwise
+ * partial_f32 is caller scratch of M*N floats.  C may alias residual.
+ */
+orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard,
+                               const void* W_shard, int M, int N, int K_shard,
+                               int dtype, const void* residual,
+                               float* partial_f32, void* stream);
+
+/* Block until every collective of comm issued on stream is done or the
+ * timeout passes (then the communicator is aborted). */
+orin_status orin_tp_wait(void* comm, void* stream);
+
+orin_status orin_tp_destroy(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORIN_B200_H */

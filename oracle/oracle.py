@@ -1,0 +1,179 @@
+"""Python binding of the oracle (oracle/liborc.so) and of the reference's own
+kernels compiled from its sources (oracle/_ref/*.so).
+
+TEST INFRASTRUCTURE ONLY: the tests, the smoke check and the bench's CPU
+baseline use this module as the checker; nothing in orininfer_b200 imports it.
+
+Arrays are numpy uint16 holding 16-bit float bit patterns (fp16 or bf16).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liborc.so"
+REF_CUBLAS = HERE / "_ref" / "libref_cublas.so"
+REF_CUTE = HERE / "_ref" / "libref_cute.so"
+
+F16, BF16 = 0, 1
+EPI = {"none": 0, "swiglu": 1, "residual": 2, "f32": 3, "f32_partial": 4}
+
+_vp, _i, _ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+
+
+def build() -> None:
+    """Compile liborc.so (and the reference checkers when the reference tree exists)."""
+    subprocess.run(["make", "-s", "-C", os.fspath(HERE), "orc"], check=True)
+    if Path("/root/reference/kernels/matmul.cu").exists():
+        subprocess.run(["make", "-s", "-C", os.fspath(HERE), "ref"], check=True)
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB.exists():
+        build()
+    lib = ctypes.CDLL(os.fspath(LIB))
+    lib.orc_linear.restype = _i
+    lib.orc_linear.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i]
+    lib.orc_gemm_f32.restype = None
+    lib.orc_gemm_f32.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i]
+    for n in ("orc_silu_mul",):
+        getattr(lib, n).argtypes = [_vp, _vp, _vp, _ll, _i]
+    lib.orc_add.argtypes = [_vp, _vp, _ll, _i]
+    lib.orc_widen.argtypes = [_vp, _vp, _ll, _i]
+    lib.orc_round.argtypes = [_vp, _vp, _ll, _i]
+    lib.orc_pack_gate_up.argtypes = [_vp, _vp, _vp, _i, _i]
+    lib.orc_max_threads.restype = _i
+    return lib
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def _p(a: np.ndarray | None) -> ctypes.c_void_p:
+    if a is None:
+        return ctypes.c_void_p(0)
+    assert a.flags["C_CONTIGUOUS"]
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+def linear(A: np.ndarray, W: np.ndarray, dt: int, epilogue: str = "none",
+           R: np.ndarray | None = None, threads: int = 0) -> np.ndarray:
+    """epilogue(A · W^T) with the reference's rounding points (orc.c:orc_linear)."""
+    A = np.ascontiguousarray(A, dtype=np.uint16)
+    W = np.ascontiguousarray(W, dtype=np.uint16)
+    M, K = A.shape
+    N = W.shape[0] // 2 if epilogue == "swiglu" else W.shape[0]
+    if epilogue in ("f32", "f32_partial"):
+        C = np.empty((M, N), dtype=np.float32)
+    else:
+        C = np.empty((M, N), dtype=np.uint16)
+    if R is not None:
+        R = np.ascontiguousarray(R, dtype=np.uint16)
+    rc = lib().orc_linear(_p(C), _p(A), _p(W), M, N, K, dt, EPI[epilogue], _p(R), threads)
+    if rc != 0:
+        raise MemoryError("orc_linear: allocation failed")
+    return C
+
+
+def gemm_f32(A: np.ndarray, W: np.ndarray, threads: int = 0) -> np.ndarray:
+    """Multithreaded fp32 C = A · W^T (the CPU baseline)."""
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    C = np.empty((A.shape[0], W.shape[0]), dtype=np.float32)
+    lib().orc_gemm_f32(_p(A), _p(W), _p(C), A.shape[0], W.shape[0], A.shape[1], threads)
+    return C
+
+
+def silu_mul(g: np.ndarray, u: np.ndarray, dt: int) -> np.ndarray:
+    out = np.empty_like(g, dtype=np.uint16)
+    lib().orc_silu_mul(_p(out), _p(np.ascontiguousarray(g)), _p(np.ascontiguousarray(u)),
+                       g.size, dt)
+    return out
+
+
+def add(x: np.ndarray, y: np.ndarray, dt: int) -> np.ndarray:
+    out = np.ascontiguousarray(x, dtype=np.uint16).copy()
+    lib().orc_add(_p(out), _p(np.ascontiguousarray(y)), out.size, dt)
+    return out
+
+
+def widen(x: np.ndarray, dt: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    out = np.empty(x.shape, dtype=np.float32)
+    lib().orc_widen(_p(x), _p(out), x.size, dt)
+    return out
+
+
+def round16(x: np.ndarray, dt: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().orc_round(_p(x), _p(out), x.size, dt)
+    return out
+
+
+def pack_gate_up(wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
+    wg = np.ascontiguousarray(wg, dtype=np.uint16)
+    wu = np.ascontiguousarray(wu, dtype=np.uint16)
+    IM, K = wg.shape
+    out = np.empty((2 * IM, K), dtype=np.uint16)
+    lib().orc_pack_gate_up(_p(out), _p(wg), _p(wu), IM, K)
+    return out
+
+
+class RefKernels:
+    """The reference's own bf16 kernels (built from its sources; GPU only).
+
+    Pointers are raw device addresses (ints)."""
+
+    def __init__(self, cute: bool = False):
+        path = REF_CUTE if cute else REF_CUBLAS
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        self.lib = ctypes.CDLL(os.fspath(path))
+        L = self.lib
+        L.ref_matmul.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+        L.ref_gemm_cute.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+        L.ref_fused_silu_mul.argtypes = [_vp, _vp, _vp, _i, _i]
+        L.ref_add.argtypes = [_vp, _vp, _i]
+        L.ref_bf16_to_fp32.argtypes = [_vp, _vp, _i]
+        for n in ("ref_matmul", "ref_gemm_cute", "ref_fused_silu_mul", "ref_add",
+                  "ref_bf16_to_fp32", "ref_sync"):
+            getattr(L, n).restype = _i
+
+    def _ok(self, rc: int, what: str) -> None:
+        if rc != 0:
+            raise RuntimeError(f"{what}: CUDA error {rc}")
+
+    def matmul(self, C: int, A: int, B: int, M: int, N: int, K: int) -> None:
+        self._ok(self.lib.ref_matmul(C, A, B, M, N, K), "kernels::matmul")
+
+    def gemm_cute(self, C: int, A: int, B: int, M: int, N: int, K: int) -> bool:
+        return bool(self.lib.ref_gemm_cute(C, A, B, M, N, K))
+
+    def fused_silu_mul(self, out: int, g: int, u: int, seq: int, im: int) -> None:
+        self._ok(self.lib.ref_fused_silu_mul(out, g, u, seq, im), "kernels::fused_silu_mul")
+
+    def add(self, x: int, y: int, n: int) -> None:
+        self._ok(self.lib.ref_add(x, y, n), "kernels::add")
+
+    def bf16_to_fp32(self, out: int, inp: int, n: int) -> None:
+        self._ok(self.lib.ref_bf16_to_fp32(out, inp, n), "kernels::bf16_to_fp32")
+
+    def sync(self) -> None:
+        self._ok(self.lib.ref_sync(), "cudaDeviceSynchronize")

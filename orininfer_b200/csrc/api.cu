@@ -1,0 +1,291 @@
+// api.cu — the C ABI (include/orin_b200.h): argument checks, kernel choice,
+// the per-device split-K workspace, and the elementwise entry points.
+#include "orin_b200.h"
+#include "orin_common.cuh"
+#include "orin_internal.h"
+
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+namespace orin {
+
+namespace {
+thread_local char g_err[512] = "";
+std::mutex g_ctx_mu;
+DeviceCtx g_ctx[64];
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+// Bytes of the default workspace: the largest stream-K remainder the planner
+// produces is < 2 waves of 128x256 fp32 tiles, plus one counter per tile.
+static size_t default_ws_bytes(int sm_count) {
+  const size_t tiles = 2 * static_cast<size_t>(sm_count);
+  return tiles * 128 * 256 * sizeof(float) + tiles * sizeof(int);
+}
+
+DeviceCtx* device_ctx(int device, cudaError_t* e) {
+  *e = cudaSuccess;
+  if (device < 0 || device >= 64) {
+    *e = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_ctx_mu);
+  DeviceCtx& c = g_ctx[device];
+  if (c.device == device) return &c;
+  int sms = 0;
+  if ((*e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return nullptr;
+  int major = 0;
+  if ((*e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device)) !=
+      cudaSuccess)
+    return nullptr;
+  if (major != 10) {
+    *e = cudaErrorNoKernelImageForDevice;
+    return nullptr;
+  }
+  // one allocation: the workspace, then the device error word on its own
+  // 256-byte line
+  const size_t bytes = ((default_ws_bytes(sms) + 255) / 256) * 256;
+  void* mem = nullptr;
+  if ((*e = cudaMalloc(&mem, bytes + 256)) != cudaSuccess) return nullptr;
+  if ((*e = cudaMemset(mem, 0, bytes + 256)) != cudaSuccess) {
+    cudaFree(mem);
+    return nullptr;
+  }
+  c.sm_count = sms;
+  c.ws = mem;
+  c.ws_bytes = bytes;
+  c.err = reinterpret_cast<int*>(static_cast<char*>(mem) + bytes);
+  c.device = device;
+  return &c;
+}
+
+}  // namespace orin
+
+using namespace orin;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+orin_status cuda_fail(cudaError_t e, const char* what) {
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return ORIN_ERR_CUDA;
+}
+
+orin_status check_common(int dtype, int epi) {
+  if (dtype != ORIN_F16 && dtype != ORIN_BF16) {
+    set_error("dtype %d is not ORIN_F16 or ORIN_BF16", dtype);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (epi < ORIN_EPI_NONE || epi > ORIN_EPI_F32_PARTIAL) {
+    set_error("epilogue %d is not an orin_epilogue", epi);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  return ORIN_OK;
+}
+
+// Which kernel serves this call.
+int choose_algo(int req, const void* A, const void* W, int M, int K) {
+  const bool tma_ok = (K % 8 == 0) && aligned16(A) && aligned16(W);
+  if (req == ORIN_ALGO_SIMT) return 3;
+  if (!tma_ok) return (req == ORIN_ALGO_AUTO) ? 3 : -1;
+  if (req == ORIN_ALGO_TC_WIDE) return 1;
+  if (req == ORIN_ALGO_TC_SKINNY) return (M <= 64) ? 2 : -1;
+  return (M <= 64) ? 2 : 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int orin_version(void) { return 100; }
+
+const char* orin_last_error(void) { return g_err; }
+
+size_t orin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue, int algo) {
+  if (M < 1 || N < 1 || K < 1 || check_common(dtype, epilogue) != ORIN_OK) return 0;
+  int a = algo;
+  if (a == ORIN_ALGO_AUTO) a = (M <= 64) ? 2 : 1;
+  if (a != 1 && a != 2) return 0;
+  if (a == 2 && M > 64) return 0;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();
+  Plan pl;
+  plan_tc(pl, M, N, K, epilogue, a, sms);
+  return pl.ws_bytes;
+}
+
+orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                           int epilogue, const void* residual, int algo, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  orin_status st = check_common(dtype, epilogue);
+  if (st != ORIN_OK) return st;
+  if (!C || !A || !W) {
+    set_error("orin_linear: null C, A or W");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (M < 1 || N < 1 || K < 1) {
+    set_error("orin_linear: M=%d N=%d K=%d must all be >= 1", M, N, K);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (epilogue == ORIN_EPI_RESIDUAL && !residual) {
+    set_error("orin_linear: RESIDUAL epilogue needs a residual pointer");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (epilogue == ORIN_EPI_SWIGLU && N % 64 != 0) {
+    set_error("orin_linear: SWIGLU needs the intermediate size N=%d to be a multiple of 64", N);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (algo < ORIN_ALGO_AUTO || algo > ORIN_ALGO_SIMT) {
+    set_error("orin_linear: algo %d is not an orin_algo", algo);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int a = choose_algo(algo, A, W, M, K);
+  if (a < 0) {
+    set_error("orin_linear: algo %d can't take M=%d K=%d (needs K%%8==0, 16-byte aligned "
+              "A and W%s)", algo, M, K, algo == ORIN_ALGO_TC_SKINNY ? ", M<=64" : "");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (a == 3) {
+    cudaError_t e = launch_simt(C, A, W, M, N, K, dtype, epilogue, residual, s);
+    if (e != cudaSuccess) return cuda_fail(e, "orin_linear (simt)");
+    return ORIN_OK;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = device_ctx(dev, &e);
+  if (!ctx) {
+    if (e == cudaErrorNoKernelImageForDevice) {
+      set_error("orin_linear: device %d is not an sm_100 GPU", dev);
+      return ORIN_ERR_NO_DEVICE;
+    }
+    return cuda_fail(e, "orin_linear: device set-up");
+  }
+  Plan pl;
+  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count);
+  void* ws = ctx->ws;
+  if (workspace) {
+    if (workspace_bytes < pl.ws_bytes || !aligned16(workspace)) {
+      set_error("orin_linear: workspace of %zu bytes is too small (need %zu) or unaligned",
+                workspace_bytes, pl.ws_bytes);
+      return ORIN_ERR_INVALID_ARG;
+    }
+    ws = workspace;
+  } else if (pl.ws_bytes > ctx->ws_bytes) {
+    set_error("orin_linear: internal workspace too small (%zu < %zu)", ctx->ws_bytes,
+              pl.ws_bytes);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  const size_t esz = (epilogue == ORIN_EPI_F32_OUT || epilogue == ORIN_EPI_F32_PARTIAL) ? 4 : 2;
+  pl.p.C = C;
+  pl.p.ldc = N;
+  pl.p.R = residual;
+  pl.p.ldr = N;
+  pl.p.vec_ok = aligned16(C) && ((N * esz) % 16 == 0) &&
+                (!residual || (aligned16(residual) && (N * 2) % 16 == 0));
+  const char* why = nullptr;
+  e = launch_tc(pl, dtype, epilogue, A, W, ws, ctx->err, s, &why);
+  if (e != cudaSuccess) {
+    if (why) {
+      set_error("orin_linear: %s", why);
+      return ORIN_ERR_UNSUPPORTED;
+    }
+    return cuda_fail(e, "orin_linear (tcgen05 launch)");
+  }
+  return ORIN_OK;
+}
+
+orin_status orin_linear(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epilogue, const void* residual, void* stream) {
+  return orin_linear_ex(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, nullptr, 0,
+                        stream);
+}
+
+orin_status orin_pack_gate_up(void* w_packed, const void* w_gate, const void* w_up, int IM, int K,
+                              int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (!w_packed || !w_gate || !w_up || IM < 1 || K < 1) {
+    set_error("orin_pack_gate_up: null pointer or non-positive size");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (IM % 64 != 0) {
+    set_error("orin_pack_gate_up: IM=%d must be a multiple of 64", IM);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e =
+      launch_pack_gate_up(w_packed, w_gate, w_up, IM, K, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_pack_gate_up");
+}
+
+orin_status orin_silu_mul(void* out, const void* gate, const void* up, long long n, int dtype,
+                          void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (n < 0 || (n > 0 && (!out || !gate || !up))) {
+    set_error("orin_silu_mul: null pointer or negative n");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_silu_mul(out, gate, up, n, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_silu_mul");
+}
+
+orin_status orin_add(void* x, const void* y, long long n, int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (n < 0 || (n > 0 && (!x || !y))) {
+    set_error("orin_add: null pointer or negative n");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_add(x, y, n, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_add");
+}
+
+orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (n < 0 || (n > 0 && (!out || !in))) {
+    set_error("orin_widen_f32: null pointer or negative n");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_widen(out, in, n, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_widen_f32");
+}
+
+orin_status orin_device_check(void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "orin_device_check: stream synchronize");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "orin_device_check: pending launch error");
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = device_ctx(dev, &e);
+  if (!ctx) return cuda_fail(e, "orin_device_check: device set-up");
+  int word = 0;
+  if ((e = cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(e, "orin_device_check: read error word");
+  if (word != 0) {
+    cudaMemset(ctx->ws, 0, ctx->ws_bytes);
+    cudaMemset(ctx->err, 0, sizeof(int));
+    cudaDeviceSynchronize();
+    set_error("orin_device_check: a kernel gave up waiting (device error code %d)", word);
+    return ORIN_ERR_TIMEOUT;
+  }
+  return ORIN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// orin_internal.h — host-side declarations shared by the library's .cu files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace orin {
+
+// Problem description handed to the tcgen05 kernels (by value, in the
+// kernel's parameter space).  "P" is the operand whose rows fill the 128
+// accumulator lanes of a tile, "Q" the operand whose rows fill its BN
+// accumulator columns.  Wide tiles: P = activations, Q = weights.  Skinny
+// (swap) tiles: P = weights, Q = activations.
+struct TcParams {
+  int P, Q, K;
+  int M, N;          // logical output C[M, N] (N = output columns)
+  int tiles_p, tiles_q, kb;
+  int dp_tiles;      // tiles done whole, round-robin over the grid
+  int sk_tiles;      // tiles after those, split over the grid by k-blocks
+  int group_p;       // raster: this many P tiles walk together
+  void* C;
+  long long ldc;     // elements
+  const void* R;     // residual (EPI_RESIDUAL)
+  long long ldr;
+  float* ws;         // sk_tiles x 128 x BN fp32 partial sums (zero at rest)
+  int* counters;     // sk_tiles arrival counters (zero at rest)
+  int* err;          // device error word
+  int vec_ok;        // C / R rows are 16-byte aligned for vector stores
+};
+
+struct Plan {
+  int algo;          // 1 wide, 2 skinny, 3 simt
+  int bn;            // tile columns (Q extent)
+  int grid;
+  TcParams p;
+  size_t ws_bytes;   // partial-sum bytes + counter bytes needed
+};
+
+// Per-device state: SM count, the default split-K workspace and error word.
+struct DeviceCtx {
+  int device = -1;
+  int sm_count = 0;
+  void* ws = nullptr;        // partial sums followed by counters, zeroed
+  size_t ws_bytes = 0;
+  int* err = nullptr;        // one int, zeroed
+};
+
+DeviceCtx* device_ctx(int device, cudaError_t* e);
+
+// Fill the tiling / scheduling fields of a plan for the tcgen05 kernels.
+void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count);
+
+// Launch the tcgen05 GEMM described by pl.  ws points at pl.ws_bytes of
+// zero-filled memory (partials first, then counters).
+cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const void* W,
+                      void* ws, int* err, cudaStream_t stream, const char** why);
+
+// CUDA-core GEMM for shapes the tcgen05 path can't take (K % 8 != 0,
+// unaligned rows).  Same epilogues and rounding.
+cudaError_t launch_simt(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epi, const void* R, cudaStream_t stream);
+
+// Elementwise kernels (the reference's unfused neighbours of matmul).
+cudaError_t launch_silu_mul(void* out, const void* gate, const void* up, long long n,
+                            int dtype, cudaStream_t s);
+cudaError_t launch_add(void* x, const void* y, long long n, int dtype, cudaStream_t s);
+cudaError_t launch_widen(float* out, const void* in, long long n, int dtype, cudaStream_t s);
+cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM, int K,
+                                int dtype, cudaStream_t s);
+// C = round16(f32(R) + round16(S)) (R may be null: C = round16(S)); S fp32.
+cudaError_t launch_finish_rows(void* C, const float* S, const void* R, long long n, int dtype,
+                               cudaStream_t s);
+
+// Record a failure message for orin_last_error().
+void set_error(const char* fmt, ...);
+
+}  // namespace orin

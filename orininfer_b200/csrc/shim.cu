@@ -1,0 +1,34 @@
+// shim.cu — the reference's C++ GEMM entry points (include/kernels.h:51-108,
+// kernels/gemm_cute.cu:295-324) implemented on the C ABI, so a program built
+// against the reference's headers links this library unchanged.  Everything
+// runs on the legacy default stream in bf16, as in the reference.
+#include "orin_b200.h"
+#include "orin_kernels.h"
+
+namespace kernels {
+
+void matmul(__nv_bfloat16* C, const __nv_bfloat16* A, const __nv_bfloat16* B, int M, int N,
+            int K) {
+  orin_linear(C, A, B, M, N, K, ORIN_BF16, ORIN_EPI_NONE, nullptr, nullptr);
+}
+
+void fused_silu_mul(__nv_bfloat16* out, const __nv_bfloat16* gate, const __nv_bfloat16* up,
+                    int seq_len, int intermediate_size) {
+  orin_silu_mul(out, gate, up, static_cast<long long>(seq_len) * intermediate_size, ORIN_BF16,
+                nullptr);
+}
+
+void add(__nv_bfloat16* x, const __nv_bfloat16* y, int n) {
+  orin_add(x, y, n, ORIN_BF16, nullptr);
+}
+
+void bf16_to_fp32(float* out, const __nv_bfloat16* in, int n) {
+  orin_widen_f32(out, in, n, ORIN_BF16, nullptr);
+}
+
+}  // namespace kernels
+
+bool launch_gemm_cute(__nv_bfloat16* C, const __nv_bfloat16* A, const __nv_bfloat16* B, int M,
+                      int N, int K) {
+  return orin_linear(C, A, B, M, N, K, ORIN_BF16, ORIN_EPI_NONE, nullptr, nullptr) == ORIN_OK;
+}

@@ -1,0 +1,239 @@
+// simt.cu — CUDA-core kernels around the tcgen05 GEMM:
+//   * a GEMM for the shapes TMA can't describe (K % 8 != 0, unaligned rows),
+//     with the same epilogues and rounding points as the tensor-core path;
+//   * the reference's unfused elementwise neighbours of matmul (SwiGLU, the
+//     residual add, the bf16->fp32 widen), kept so the drop-in entry points
+//     of include/kernels.h stay available;
+//   * the gate/up weight packer and the tensor-parallel finish step.
+#include "orin_common.cuh"
+#include "orin_internal.h"
+
+namespace orin {
+
+namespace {
+
+constexpr int kWarps = 8;
+
+// Dot product of one activation row and one weight row, fp32 accumulation,
+// lane-strided then reduced by shuffles.
+template <int DT>
+__device__ __forceinline__ float warp_dot(const typename Elem<DT>::T* a,
+                                          const typename Elem<DT>::T* w, int K, int lane) {
+  using E = Elem<DT>;
+  float s = 0.f;
+  for (int k = lane; k < K; k += 32) s += E::to_f(a[k]) * E::to_f(w[k]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+// One warp per output element (m, n).  grid = (ceil(N / kWarps), M).
+template <int DT, int EPI>
+__global__ void __launch_bounds__(kWarps * 32)
+    simt_linear_kernel(void* C, const void* A, const void* W, const void* R, int M, int N,
+                       int K) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int m = blockIdx.y;
+  if (n >= N || m >= M) return;
+  const T* a = static_cast<const T*>(A) + static_cast<size_t>(m) * K;
+  const T* w = static_cast<const T*>(W);
+  if constexpr (EPI == EPI_SWIGLU) {
+    const size_t gr = static_cast<size_t>(n / 64) * 128 + (n % 64);
+    const float g = warp_dot<DT>(a, w + gr * K, K, lane);
+    const float u = warp_dot<DT>(a, w + (gr + 64) * K, K, lane);
+    if (lane == 0)
+      static_cast<T*>(C)[static_cast<size_t>(m) * N + n] =
+          E::from_f(silu_f32(E::round(g)) * E::round(u));
+  } else {
+    const float acc = warp_dot<DT>(a, w + static_cast<size_t>(n) * K, K, lane);
+    if (lane == 0) {
+      const size_t i = static_cast<size_t>(m) * N + n;
+      if constexpr (EPI == EPI_NONE) {
+        static_cast<T*>(C)[i] = E::from_f(acc);
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        static_cast<T*>(C)[i] = E::from_f(E::to_f(static_cast<const T*>(R)[i]) + E::round(acc));
+      } else if constexpr (EPI == EPI_F32_OUT) {
+        static_cast<float*>(C)[i] = E::round(acc);
+      } else {
+        static_cast<float*>(C)[i] = acc;
+      }
+    }
+  }
+}
+
+template <int DT>
+__global__ void silu_mul_kernel(typename Elem<DT>::T* out, const typename Elem<DT>::T* g,
+                                const typename Elem<DT>::T* u, long long n) {
+  using E = Elem<DT>;
+  pdl_wait();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = E::from_f(silu_f32(E::to_f(g[i])) * E::to_f(u[i]));
+}
+
+template <int DT>
+__global__ void add_kernel(typename Elem<DT>::T* x, const typename Elem<DT>::T* y, long long n) {
+  using E = Elem<DT>;
+  pdl_wait();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    x[i] = E::from_f(E::to_f(x[i]) + E::to_f(y[i]));
+}
+
+template <int DT>
+__global__ void widen_kernel(float* out, const typename Elem<DT>::T* in, long long n) {
+  using E = Elem<DT>;
+  pdl_wait();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = E::to_f(in[i]);
+}
+
+template <int DT>
+__global__ void finish_kernel(typename Elem<DT>::T* C, const float* S,
+                              const typename Elem<DT>::T* R, long long n) {
+  using E = Elem<DT>;
+  pdl_wait();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float s = E::round(S[i]);
+    C[i] = E::from_f(R ? E::to_f(R[i]) + s : s);
+  }
+}
+
+// Packed row r of the gate/up weight: group r/128, gate half if r%128 < 64.
+// Copies 16 bytes per thread when every row is 16-byte aligned, else 2 bytes.
+__global__ void pack_gate_up_kernel(uint16_t* wp, const uint16_t* wg, const uint16_t* wu,
+                                    int IM, int K, int vec) {
+  pdl_wait();
+  const long long rows = 2LL * IM;
+  if (vec) {
+    const long long per_row = K / 8;
+    const long long total = rows * per_row;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const long long r = i / per_row;
+      const long long c = i - r * per_row;
+      const long long g = r / 128, h = r % 128;
+      const uint16_t* src = (h < 64 ? wg : wu) + (g * 64 + (h % 64)) * static_cast<long long>(K);
+      reinterpret_cast<uint4*>(wp + r * static_cast<long long>(K))[c] =
+          reinterpret_cast<const uint4*>(src)[c];
+    }
+  } else {
+    const long long total = rows * K;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const long long r = i / K;
+      const long long c = i - r * K;
+      const long long g = r / 128, h = r % 128;
+      const uint16_t* src = (h < 64 ? wg : wu) + (g * 64 + (h % 64)) * static_cast<long long>(K);
+      wp[i] = src[c];
+    }
+  }
+}
+
+int grid_for(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  if (b > 148LL * 16) b = 148LL * 16;
+  if (b < 1) b = 1;
+  return static_cast<int>(b);
+}
+
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <int DT>
+cudaError_t simt_dispatch(void* C, const void* A, const void* W, int M, int N, int K, int epi,
+                          const void* R, cudaStream_t s) {
+  dim3 grid((N + kWarps - 1) / kWarps, M);
+  dim3 block(kWarps * 32);
+  switch (epi) {
+    case EPI_NONE: return launch_pdl(simt_linear_kernel<DT, EPI_NONE>, grid, block, s, C, A, W, R, M, N, K);
+    case EPI_SWIGLU: return launch_pdl(simt_linear_kernel<DT, EPI_SWIGLU>, grid, block, s, C, A, W, R, M, N, K);
+    case EPI_RESIDUAL: return launch_pdl(simt_linear_kernel<DT, EPI_RESIDUAL>, grid, block, s, C, A, W, R, M, N, K);
+    case EPI_F32_OUT: return launch_pdl(simt_linear_kernel<DT, EPI_F32_OUT>, grid, block, s, C, A, W, R, M, N, K);
+    case EPI_F32_PARTIAL: return launch_pdl(simt_linear_kernel<DT, EPI_F32_PARTIAL>, grid, block, s, C, A, W, R, M, N, K);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t launch_simt(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epi, const void* R, cudaStream_t s) {
+  if (M > 65535) return cudaErrorInvalidConfiguration;
+  if (dtype == DT_F16) return simt_dispatch<DT_F16>(C, A, W, M, N, K, epi, R, s);
+  return simt_dispatch<DT_BF16>(C, A, W, M, N, K, epi, R, s);
+}
+
+cudaError_t launch_silu_mul(void* out, const void* gate, const void* up, long long n, int dtype,
+                            cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == DT_F16)
+    return launch_pdl(silu_mul_kernel<DT_F16>, dim3(grid_for(n, 256)), dim3(256), s,
+                      static_cast<__half*>(out), static_cast<const __half*>(gate),
+                      static_cast<const __half*>(up), n);
+  return launch_pdl(silu_mul_kernel<DT_BF16>, dim3(grid_for(n, 256)), dim3(256), s,
+                    static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(gate),
+                    static_cast<const __nv_bfloat16*>(up), n);
+}
+
+cudaError_t launch_add(void* x, const void* y, long long n, int dtype, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == DT_F16)
+    return launch_pdl(add_kernel<DT_F16>, dim3(grid_for(n, 256)), dim3(256), s,
+                      static_cast<__half*>(x), static_cast<const __half*>(y), n);
+  return launch_pdl(add_kernel<DT_BF16>, dim3(grid_for(n, 256)), dim3(256), s,
+                    static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), n);
+}
+
+cudaError_t launch_widen(float* out, const void* in, long long n, int dtype, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == DT_F16)
+    return launch_pdl(widen_kernel<DT_F16>, dim3(grid_for(n, 256)), dim3(256), s, out,
+                      static_cast<const __half*>(in), n);
+  return launch_pdl(widen_kernel<DT_BF16>, dim3(grid_for(n, 256)), dim3(256), s, out,
+                    static_cast<const __nv_bfloat16*>(in), n);
+}
+
+cudaError_t launch_finish_rows(void* C, const float* S, const void* R, long long n, int dtype,
+                               cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == DT_F16)
+    return launch_pdl(finish_kernel<DT_F16>, dim3(grid_for(n, 256)), dim3(256), s,
+                      static_cast<__half*>(C), S, static_cast<const __half*>(R), n);
+  return launch_pdl(finish_kernel<DT_BF16>, dim3(grid_for(n, 256)), dim3(256), s,
+                    static_cast<__nv_bfloat16*>(C), S, static_cast<const __nv_bfloat16*>(R), n);
+}
+
+cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM, int K, int dtype,
+                                cudaStream_t s) {
+  (void)dtype;
+  const int vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(wp) % 16 == 0) &&
+                  (reinterpret_cast<uintptr_t>(wg) % 16 == 0) &&
+                  (reinterpret_cast<uintptr_t>(wu) % 16 == 0);
+  const long long total = vec ? 2LL * IM * (K / 8) : 2LL * IM * K;
+  if (total <= 0) return cudaSuccess;
+  return launch_pdl(pack_gate_up_kernel, dim3(grid_for(total, 256)), dim3(256), s,
+                    static_cast<uint16_t*>(wp), static_cast<const uint16_t*>(wg),
+                    static_cast<const uint16_t*>(wu), IM, K, vec);
+}
+
+}  // namespace orin

@@ -1,0 +1,167 @@
+"""Host-side mirror of the reference's GEMM-path operator interface.
+
+The reference exposes raw-pointer functions in ``namespace kernels``
+(include/kernels.h:51-108); this module offers the same names with the same
+argument meaning over torch tensors (torch supplies device memory and
+streams), each a direct call into liborin_b200.so:
+
+    matmul(C, A, B, M, N, K)                   kernels::matmul
+    fused_silu_mul(out, gate, up, seq, im)     kernels::fused_silu_mul
+    add(x, y, n)                               kernels::add
+    bf16_to_fp32(out, inp, n)                  kernels::bf16_to_fp32
+
+plus the fused entry points that replace the reference's call pairs in
+src/model.cu (``linear`` with an epilogue) and the gate/up packer.  fp16 and
+bf16 are both accepted; the reference itself is bf16-only.
+
+Errors raise ``OrinError`` (the library's status and message).  There is no
+CPU path: tensors must live on a CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import OrinError, check
+
+_DTYPES = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+_EPILOGUES = {
+    "none": _lib.EPI_NONE,
+    "swiglu": _lib.EPI_SWIGLU,
+    "residual": _lib.EPI_RESIDUAL,
+    "f32": _lib.EPI_F32_OUT,
+    "f32_partial": _lib.EPI_F32_PARTIAL,
+}
+_ALGOS = {
+    "auto": _lib.ALGO_AUTO,
+    "wide": _lib.ALGO_TC_WIDE,
+    "skinny": _lib.ALGO_TC_SKINNY,
+    "simt": _lib.ALGO_SIMT,
+}
+
+__all__ = [
+    "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
+    "pack_gate_up", "device_check", "workspace_size",
+]
+
+
+def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def _stream(stream: Optional[torch.cuda.Stream]) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _need_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("orininfer_b200 kernels take CUDA tensors only (no CPU fallback)")
+        if not t.is_contiguous():
+            raise ValueError("orininfer_b200 kernels take contiguous tensors")
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; use float16 or bfloat16") from None
+
+
+# ----------------------------------------------------------------- reference names
+
+def matmul(C: torch.Tensor, A: torch.Tensor, B: torch.Tensor, M: int, N: int, K: int,
+           stream: Optional[torch.cuda.Stream] = None) -> None:
+    """C[M,N] = A[M,K] · B[N,K]^T (kernels/matmul.cu:47-81 semantics)."""
+    _need_cuda(C, A, B)
+    dt = _dtype_code(A)
+    check(_lib.lib.orin_linear(_ptr(C), _ptr(A), _ptr(B), M, N, K, dt, _lib.EPI_NONE, None,
+                               _stream(stream)))
+
+
+def fused_silu_mul(out: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, seq_len: int,
+                   intermediate_size: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """out = silu(gate) * up over seq_len*intermediate_size elements
+    (kernels/fused_swiglu.cu:19-26); out may alias gate."""
+    _need_cuda(out, gate, up)
+    check(_lib.lib.orin_silu_mul(_ptr(out), _ptr(gate), _ptr(up), seq_len * intermediate_size,
+                                 _dtype_code(gate), _stream(stream)))
+
+
+def add(x: torch.Tensor, y: torch.Tensor, n: int,
+        stream: Optional[torch.cuda.Stream] = None) -> None:
+    """x += y elementwise, rounded (kernels/softmax.cu:78-83)."""
+    _need_cuda(x, y)
+    check(_lib.lib.orin_add(_ptr(x), _ptr(y), n, _dtype_code(x), _stream(stream)))
+
+
+def bf16_to_fp32(out: torch.Tensor, inp: torch.Tensor, n: int,
+                 stream: Optional[torch.cuda.Stream] = None) -> None:
+    """out = float(inp) (kernels/softmax.cu:87-90); also accepts fp16 input."""
+    _need_cuda(out, inp)
+    check(_lib.lib.orin_widen_f32(_ptr(out), _ptr(inp), n, _dtype_code(inp), _stream(stream)))
+
+
+# ----------------------------------------------------------------- fused entry points
+
+def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
+                residual: Optional[torch.Tensor] = None, algo: str = "auto",
+                workspace: Optional[torch.Tensor] = None,
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """out = epilogue(x · w^T) written into `out` (see include/orin_b200.h).
+
+    x [M, K]; w [N, K] ([2N, K] packed gate/up for "swiglu"); out [M, N]
+    (float32 for "f32" / "f32_partial", else x.dtype); residual [M, N].
+    """
+    _need_cuda(out, x, w, residual, workspace)
+    dt = _dtype_code(x)
+    if w.dtype != x.dtype or (residual is not None and residual.dtype != x.dtype):
+        raise ValueError("x, w and residual must share one dtype")
+    epi = _EPILOGUES[epilogue]
+    M, K = x.shape
+    N = out.shape[-1]
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(_lib.lib.orin_linear_ex(_ptr(out), _ptr(x), _ptr(w), M, N, K, dt, epi, _ptr(residual),
+                                  _ALGOS[algo], _ptr(workspace), ws_bytes, _stream(stream)))
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
+           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+           algo: str = "auto", stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Allocating form of linear_into."""
+    M = x.shape[0]
+    N = w.shape[0] // 2 if epilogue == "swiglu" else w.shape[0]
+    if out is None:
+        odt = torch.float32 if epilogue in ("f32", "f32_partial") else x.dtype
+        out = torch.empty((M, N), dtype=odt, device=x.device)
+    return linear_into(out, x, w, epilogue=epilogue, residual=residual, algo=algo, stream=stream)
+
+
+def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Interleave gate_proj and up_proj [IM, K] into the [2*IM, K] layout the
+    fused SwiGLU epilogue reads (64-row gate/up groups)."""
+    _need_cuda(w_gate, w_up)
+    IM, K = w_gate.shape
+    out = torch.empty((2 * IM, K), dtype=w_gate.dtype, device=w_gate.device)
+    check(_lib.lib.orin_pack_gate_up(_ptr(out), _ptr(w_gate), _ptr(w_up), IM, K,
+                                     _dtype_code(w_gate), _stream(stream)))
+    return out
+
+
+def workspace_size(M: int, N: int, K: int, dtype: torch.dtype, epilogue: str = "none",
+                   algo: str = "auto") -> int:
+    return int(_lib.lib.orin_linear_workspace_size(M, N, K, _DTYPES[dtype],
+                                                   _EPILOGUES[epilogue], _ALGOS[algo]))
+
+
+def device_check(stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Synchronise and raise if a kernel of this library gave up a bounded wait."""
+    check(_lib.lib.orin_device_check(_stream(stream)))

@@ -1,0 +1,110 @@
+"""The C ABI library: loads, exports every declared entry point, rejects bad
+arguments on the host before any device work (CPU only)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from orininfer_b200 import _lib
+from orininfer_b200 import kernels as K
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_c_symbols():
+    src = open(os.path.join(ROOT, "include", "orin_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(orin_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_c_symbols()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(_lib.lib, n), f"{n} declared in include/orin_b200.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_library_exports_reference_cxx_entry_points():
+    hdr = open(os.path.join(ROOT, "include", "orin_kernels.h")).read()
+    for name in ("matmul", "fused_silu_mul", "add", "bf16_to_fp32", "launch_gemm_cute"):
+        assert re.search(rf"\b{name}\s*\(", hdr)
+    for name, sym in _lib.SHIM_SYMBOLS.items():
+        assert hasattr(_lib.lib, sym), f"{name} ({sym}) not exported"
+
+
+def test_version():
+    assert _lib.lib.orin_version() >= 100
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(dtype=7), _lib.ERR_INVALID_ARG),
+    (dict(epi=9), _lib.ERR_INVALID_ARG),
+    (dict(M=0), _lib.ERR_INVALID_ARG),
+    (dict(N=-1), _lib.ERR_INVALID_ARG),
+    (dict(K=0), _lib.ERR_INVALID_ARG),
+    (dict(C=0), _lib.ERR_INVALID_ARG),
+    (dict(epi=_lib.EPI_RESIDUAL, R=0), _lib.ERR_INVALID_ARG),
+    (dict(epi=_lib.EPI_SWIGLU, N=100), _lib.ERR_UNSUPPORTED),
+    (dict(algo=9), _lib.ERR_INVALID_ARG),
+])
+def test_linear_rejects_bad_arguments_on_host(kw, code):
+    a = dict(C=16, A=32, W=48, M=4, N=128, K=64, dtype=_lib.F16, epi=_lib.EPI_NONE, R=0, algo=0)
+    a.update(kw)
+    st = _lib.lib.orin_linear_ex(a["C"], a["A"], a["W"], a["M"], a["N"], a["K"], a["dtype"],
+                                 a["epi"], a["R"], a["algo"], None, 0, None)
+    assert st == code
+    assert _lib.lib.orin_last_error()
+
+
+def test_skinny_algo_rejects_wide_m():
+    st = _lib.lib.orin_linear_ex(16, 32, 48, 65, 128, 64, _lib.F16, 0, 0, _lib.ALGO_TC_SKINNY,
+                                 None, 0, None)
+    assert st == _lib.ERR_UNSUPPORTED
+
+
+def test_tc_algo_rejects_unaligned_k():
+    st = _lib.lib.orin_linear_ex(16, 32, 48, 4, 128, 12, _lib.F16, 0, 0, _lib.ALGO_TC_WIDE,
+                                 None, 0, None)
+    assert st == _lib.ERR_UNSUPPORTED
+
+
+def test_elementwise_and_pack_reject_bad_arguments():
+    L = _lib.lib
+    assert L.orin_silu_mul(None, None, None, -1, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_add(None, 16, 10, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_widen_f32(16, 16, 10, 5, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_pack_gate_up(16, 16, 16, 100, 64, 0, None) == _lib.ERR_UNSUPPORTED
+    assert L.orin_pack_gate_up(None, 16, 16, 128, 64, 0, None) == _lib.ERR_INVALID_ARG
+    # zero-length elementwise calls are no-ops
+    assert L.orin_add(None, None, 0, 0, None) == _lib.OK
+
+
+def test_tp_rejects_bad_arguments():
+    L = _lib.lib
+    h = ctypes.c_void_p()
+    assert L.orin_tp_init(ctypes.byref(h), None, 0, 1, 0, 1.0) == _lib.ERR_INVALID_ARG
+    buf = ctypes.create_string_buffer(128)
+    assert L.orin_tp_init(ctypes.byref(h), buf, 2, 2, 0, 1.0) == _lib.ERR_INVALID_ARG
+    assert L.orin_tp_allreduce_f32(None, 16, 4, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_tp_linear_row(None, 16, 16, 16, 1, 1, 1, 0, None, None, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_tp_destroy(None) == _lib.OK
+
+
+def test_workspace_size_matches_plan():
+    # M=512 QKV projection: 4 x 10 tiles of 128x256, all split over the grid
+    sz = _lib.lib.orin_linear_workspace_size(512, 2560, 2048, _lib.F16, 0, 0)
+    assert sz == 40 * 128 * 256 * 4 + 40 * 4
+    # enough tiles for whole waves and an exact multiple of the grid: no workspace
+    assert _lib.lib.orin_linear_workspace_size(128 * 148, 256, 64, _lib.F16, 0, 1) == 0
+
+
+def test_python_mirror_rejects_cpu_tensors():
+    x = torch.zeros(4, 64, dtype=torch.float16)
+    w = torch.zeros(128, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        K.linear(x, w)
+    with pytest.raises(ValueError):
+        K.matmul(torch.zeros(4, 128, dtype=torch.float16), x, w, 4, 128, 64)

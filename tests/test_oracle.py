@@ -1,0 +1,140 @@
+"""The CPU oracle against independent references (CPU only).
+
+* a float64 torch restatement of each epilogue with the reference's rounding
+  points (kernels/matmul.cu:32-43, kernels/fused_swiglu.cu:11-15,
+  kernels/softmax.cu:81,89, src/model.cu:98-130);
+* the golden fixtures in tests/golden/, produced by running the reference's
+  own kernels (compiled from its sources) on a B200.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from tests._util import TORCH_DT, assert_close, bits, from_bits, seeded
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def torch_ref(x, w, dt, epi, res=None):
+    """float64 accumulation, then the reference's rounding points."""
+    tdt = TORCH_DT[dt]
+    acc = x.double() @ w.double().T
+    r16 = lambda t: t.to(tdt).double()
+    if epi == "none":
+        return acc.to(tdt)
+    if epi == "residual":
+        return (res.double() + r16(acc)).to(tdt)
+    if epi == "f32":
+        return r16(acc).float()
+    if epi == "f32_partial":
+        return acc.float()
+    if epi == "swiglu":
+        N = w.shape[0] // 2
+        idx = torch.arange(N)
+        gr = (idx // 64) * 128 + idx % 64
+        g = r16(acc[:, gr]).float()
+        u = r16(acc[:, gr + 64]).float()
+        return (g / (1.0 + torch.exp(-g)) * u).to(tdt)
+    raise ValueError(epi)
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("epi", ["none", "residual", "f32", "f32_partial", "swiglu"])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (5, 192, 200), (33, 128, 1000), (64, 256, 2048)])
+def test_oracle_matches_float64(dt, epi, M, N, K):
+    tdt = TORCH_DT[dt]
+    x = seeded((M, K), 1, 1.0, tdt)
+    wrows = 2 * N if epi == "swiglu" else N
+    w = seeded((wrows, K), 2, 0.02, tdt)
+    res = seeded((M, N), 3, 1.0, tdt) if epi == "residual" else None
+    got = orc.linear(bits(x), bits(w), dt, epi, bits(res) if res is not None else None)
+    ref = torch_ref(x, w, dt, epi, res)
+    if epi in ("f32", "f32_partial"):
+        got_t = torch.from_numpy(got)
+    else:
+        got_t = from_bits(got, tdt)
+    assert_close(got_t.float(), ref.float(), f"oracle {epi} dt={dt} {M}x{N}x{K}")
+
+
+def test_rounding_is_round_to_nearest_even():
+    g = torch.Generator().manual_seed(7)
+    f = torch.cat([torch.randn(20000, generator=g) * s for s in (1e-6, 1e-3, 1.0, 1e3, 6e4)])
+    f = torch.cat([f, torch.tensor([0.0, -0.0, float("inf"), -float("inf"), 65504.0, 65520.0])])
+    for dt in (0, 1):
+        ours = orc.round16(f.numpy(), dt)
+        theirs = bits(f.to(TORCH_DT[dt]))
+        assert np.array_equal(ours, theirs)
+        back = orc.widen(ours, dt)
+        assert np.array_equal(back, f.to(TORCH_DT[dt]).float().numpy())
+
+
+def test_pack_gate_up_layout():
+    IM, K = 192, 16
+    wg = np.arange(IM * K, dtype=np.uint16).reshape(IM, K)
+    wu = (np.arange(IM * K, dtype=np.uint16) + 30000).reshape(IM, K)
+    wp = orc.pack_gate_up(wg, wu)
+    for g in range(IM // 64):
+        assert np.array_equal(wp[128 * g:128 * g + 64], wg[64 * g:64 * g + 64])
+        assert np.array_equal(wp[128 * g + 64:128 * g + 128], wu[64 * g:64 * g + 64])
+
+
+def test_elementwise_match_torch():
+    for dt in (0, 1):
+        tdt = TORCH_DT[dt]
+        g = seeded((4096,), 11, 3.0, tdt)
+        u = seeded((4096,), 12, 1.0, tdt)
+        got = from_bits(orc.silu_mul(bits(g), bits(u), dt), tdt)
+        gf = g.float()
+        ref = (gf / (1.0 + torch.exp(-gf)) * u.float()).to(tdt)
+        assert_close(got.float(), ref.float(), "silu_mul")
+        got = from_bits(orc.add(bits(g), bits(u), dt), tdt)
+        assert torch.equal(got, (g.float() + u.float()).to(tdt))
+
+
+def test_gemm_f32_baseline_is_exact_enough():
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((37, 301), dtype=np.float32)
+    W = rng.standard_normal((53, 301), dtype=np.float32)
+    C = orc.gemm_f32(A, W)
+    np.testing.assert_allclose(C, A.astype(np.float64) @ W.T.astype(np.float64), rtol=1e-4, atol=1e-4)
+
+
+def _golden_files():
+    return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+@pytest.mark.parametrize("path", _golden_files(), ids=lambda p: os.path.basename(p))
+def test_oracle_matches_reference_golden(path):
+    """Outputs of the reference's own kernels (see tests/golden/make_golden.py)."""
+    z = np.load(path)
+    kind = str(z["kind"])
+    dt = 1  # the reference is bf16-only
+    if kind == "matmul":
+        got = orc.linear(z["A"], z["B"], dt, "none")
+        ref = z["C"]
+        # same arithmetic up to fp32 summation order: nearly all bit-identical
+        assert (got == ref).mean() >= 0.97
+        assert_close(from_bits(got, torch.bfloat16).float(), from_bits(ref, torch.bfloat16).float(),
+                     f"golden {os.path.basename(path)}")
+    elif kind == "silu_mul":
+        got = orc.silu_mul(z["gate"], z["up"], dt)
+        assert (got == z["out"]).mean() >= 0.999
+    elif kind == "add":
+        got = orc.add(z["x"], z["y"], dt)
+        assert np.array_equal(got, z["out"])
+    elif kind == "bf16_to_fp32":
+        assert np.array_equal(orc.widen(z["x"], dt), z["out"])
+    else:
+        pytest.fail(f"unknown golden kind {kind}")
+
+
+def test_golden_fixtures_present():
+    files = _golden_files()
+    kinds = {str(np.load(p)["kind"]) for p in files}
+    assert {"matmul", "silu_mul", "add", "bf16_to_fp32"} <= kinds, (
+        "tests/golden is missing reference fixtures; regenerate with "
+        "tests/golden/make_golden.py on a GPU")

@@ -1,0 +1,120 @@
+"""Tensor-parallel sharding and reduction logic on the CPU (gloo, 2 ranks).
+
+Each rank shards seeded weights exactly as bench.py / the engine would, runs
+its shard in float64 (standing in for the kernel), and the partials of the
+row-parallel projections are summed with a gloo all-reduce; the assembled
+outputs must equal the unsharded layer."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from orininfer_b200 import tp
+from orininfer_b200.synth import seeded
+
+H, KVD, IM, NH, NKV, HD = 256, 64, 384, 8, 2, 32
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _weights():
+    return dict(wq=seeded((H, H), 1, 0.02), wk=seeded((KVD, H), 2, 0.02),
+                wv=seeded((KVD, H), 3, 0.02), wo=seeded((H, H), 4, 0.02),
+                wg=seeded((IM, H), 5, 0.02), wu=seeded((IM, H), 6, 0.02),
+                wd=seeded((H, IM), 7, 0.02))
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = _weights()
+        x = seeded((5, H), 9, 1.0).double()
+        attn = seeded((5, H), 10, 1.0).double()
+        act = seeded((5, IM), 11, 1.0).double()
+        # column-parallel q/k/v: this rank's heads
+        qkv = x @ tp.shard_qkv(w["wq"], w["wk"], w["wv"], NH, NKV, HD, rank, world).double().T
+        # row-parallel o/down: partial sums, then all-reduce
+        qd = H // world
+        po = attn[:, rank * qd:(rank + 1) * qd] @ tp.shard_cols(w["wo"], rank, world).double().T
+        dist.all_reduce(po)
+        imr = IM // world
+        pd = act[:, rank * imr:(rank + 1) * imr] @ tp.shard_cols(w["wd"], rank, world).double().T
+        dist.all_reduce(pd)
+        g, u = tp.shard_gate_up_rows(w["wg"], w["wu"], rank, world)
+        gu = x @ g.double().T, x @ u.double().T
+        q.put((rank, qkv, po, pd, gu))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_sharding_reassembles_the_layer():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict()
+    for _ in range(world):
+        r, *vals = q.get(timeout=120)
+        res[r] = vals
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    w = _weights()
+    x = seeded((5, H), 9, 1.0).double()
+    attn = seeded((5, H), 10, 1.0).double()
+    act = seeded((5, IM), 11, 1.0).double()
+    # row-parallel results identical on every rank and equal to the full GEMM
+    for r in range(world):
+        torch.testing.assert_close(res[r][1], attn @ w["wo"].double().T)
+        torch.testing.assert_close(res[r][2], act @ w["wd"].double().T)
+    # column-parallel q heads reassemble; KV heads split between the 2 ranks
+    q_full = x @ w["wq"].double().T
+    qd = H // world
+    kv_per = KVD // world
+    for r in range(world):
+        got = res[r][0]
+        torch.testing.assert_close(got[:, :qd], q_full[:, r * qd:(r + 1) * qd])
+        k_full = x @ w["wk"].double().T
+        torch.testing.assert_close(got[:, qd:qd + kv_per], k_full[:, r * kv_per:(r + 1) * kv_per])
+    g_full = torch.cat([res[r][3][0] for r in range(world)], dim=1)
+    torch.testing.assert_close(g_full, x @ w["wg"].double().T)
+
+
+def test_kv_head_replication_when_ranks_exceed_kv_heads():
+    assert tp.kv_heads_of(0, 8, 4) == [0] and tp.kv_heads_of(1, 8, 4) == [0]
+    assert tp.kv_heads_of(7, 8, 4) == [3]
+    assert tp.kv_heads_of(1, 2, 4) == [2, 3]
+    with pytest.raises(ValueError):
+        tp.kv_heads_of(0, 3, 4)
+
+
+def test_shard_shapes_tinyllama_tp8():
+    w = dict(wq=torch.zeros(2048, 2048, dtype=torch.float16), wk=torch.zeros(256, 2048, dtype=torch.float16),
+             wv=torch.zeros(256, 2048, dtype=torch.float16))
+    s = tp.shard_qkv(w["wq"], w["wk"], w["wv"], 32, 4, 64, 3, 8)
+    assert s.shape == (256 + 64 + 64, 2048)
+    g, u = tp.shard_gate_up_rows(torch.zeros(5632, 8), torch.zeros(5632, 8), 7, 8)
+    assert g.shape == (704, 8)
+    assert tp.shard_cols(torch.zeros(2048, 5632), 2, 8).shape == (2048, 704)
+
+
+def test_ragged_vocab_split():
+    parts = tp.ragged_split(128256, 8)
+    assert parts[0] == (0, 16032) and parts[-1][1] == 128256
+    parts = tp.ragged_split(32000, 3)
+    assert sum(e - s for s, e in parts) == 32000 and max(e - s for s, e in parts) - min(e - s for s, e in parts) <= 1
+    with pytest.raises(ValueError):
+        tp.shard_rows(torch.zeros(10, 4), 0, 3)
