@@ -263,6 +263,8 @@ def max_over_ranks(v: float, world: int) -> float:
 
 def time_steps(step: Step, steps: int, warmup: int, world: int, dev_index: int):
     """Warm up, then time exactly `steps` steps via CUDA graph chunks."""
+    step.run(0)  # uncaptured first call: per-device set-up happens outside capture
+    torch.cuda.synchronize()
     chunk = min(GRAPH_CHUNK, steps)
     g = capture(step, chunk)
     rem = steps % chunk
@@ -381,8 +383,8 @@ def run_ours(args, rank, world, local_rank):
     ms_per_step = ms / args.steps
     value = STEP_FLOPS * args.steps / (ms / 1e3) / 1e12
 
-    kt = kernel_breakdown(step, 64) if world == 1 else None
-    e2e_steps = min(args.steps, 300)
+    kt = kernel_breakdown(step, args.breakdown_steps) if world == 1 else None
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
     e2e_ms, h2d, d2h = e2e_through_abi(step, e2e_steps, dev)
     e2e_ms = max_over_ranks(e2e_ms, world)
     e2e_value = STEP_FLOPS * e2e_steps / (e2e_ms / 1e3) / 1e12
@@ -431,11 +433,50 @@ def run_ours(args, rank, world, local_rank):
         }
         line["kernels_ms"] = {k: round(v, 5) for k, v in kt.items()}
         line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}
-        line["cpu_baseline"] = cpu_baseline_layer(args.cpu_budget)
+        line["cpu_baseline"] = cpu_baseline_layer(args.cpu_budget) if args.cpu_budget > 0 \
+            else None
     if comm is not None:
         torch.cuda.synchronize()
         comm.close()
     return line
+
+
+def run_one_kernel(args):
+    """One projection of the layer, eagerly: a bounded case for profilers."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers = make_layers(0, 1, dev)
+    step = Step(layers, 0, 1, dev)
+    name = args.kernel
+    ob = step.ob
+
+    def launch(i):
+        L = layers[i % len(layers)]
+        if name == "qkv":
+            ob.linear_into(step.qkv, step.h, L["qkv"])
+        elif name == "o_proj":
+            ob.linear_into(step.x1, step.attn, L["o_proj"], epilogue="residual", residual=step.x)
+        elif name == "gate_up":
+            ob.linear_into(step.act, step.h2, L["gate_up"], epilogue="swiglu")
+        else:
+            ob.linear_into(step.x2, step.act, L["down"], epilogue="residual", residual=step.x1)
+
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    ts = []
+    for i in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch(args.warmup + i)
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    ob.device_check()
+    avg = statistics.mean(ts)
+    return {"kernel": name, "workload": WORKLOAD, "launches": args.steps,
+            "avg_ms": round(avg, 5), "tflops": round(FLOPS[name] / (avg / 1e3) / 1e12, 2)}
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -512,7 +553,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0,
-                    help="seconds of CPU work for the cpu_baseline figure")
+                    help="seconds of CPU work for the cpu_baseline figure (0: skip)")
+    ap.add_argument("--e2e-steps", type=int, default=300,
+                    help="steps of the end-to-end (host buffers, C ABI) measurement")
+    ap.add_argument("--breakdown-steps", type=int, default=64,
+                    help="steps of the per-projection CUDA-event breakdown")
+    ap.add_argument("--kernel", choices=list(GEMMS), default=None,
+                    help="run only this projection, eagerly, warmup+steps times, and print "
+                         "its event-timed average (a small case for profilers)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -520,6 +568,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.kernel is not None:
+        print(json.dumps(run_one_kernel(args)), flush=True)
+        return 0
 
     if args.impl == "reference":
         if rank != 0:

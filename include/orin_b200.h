@@ -5,7 +5,9 @@
  * CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream).
  * No allocation happens on the data path except the per-device split-K
  * workspace that orin_linear() creates lazily on its first call on a device
- * (orin_linear_ex() lets the caller pass its own workspace instead).
+ * (orin_linear_ex() lets the caller pass its own workspace instead).  That
+ * first call must not be inside CUDA stream capture; later calls may be
+ * captured into graphs.
  * No C++ exception crosses this boundary: every function returns orin_status,
  * and orin_last_error() gives a thread-local message for the last failure.
  *

@@ -48,6 +48,7 @@ def _load() -> ctypes.CDLL:
     lib.orc_round.argtypes = [_vp, _vp, _ll, _i]
     lib.orc_pack_gate_up.argtypes = [_vp, _vp, _vp, _i, _i]
     lib.orc_max_threads.restype = _i
+    lib.orc_gemv_reference_order.argtypes = [_vp, _vp, _vp, _i, _i, _i]
     return lib
 
 
@@ -88,6 +89,16 @@ def linear(A: np.ndarray, W: np.ndarray, dt: int, epilogue: str = "none",
     rc = lib().orc_linear(_p(C), _p(A), _p(W), M, N, K, dt, EPI[epilogue], _p(R), threads)
     if rc != 0:
         raise MemoryError("orc_linear: allocation failed")
+    return C
+
+
+def gemv_reference_order(A: np.ndarray, B: np.ndarray, dt: int) -> np.ndarray:
+    """The reference GEMV's own summation order (orc.c:orc_gemv_reference_order)."""
+    A = np.ascontiguousarray(A, dtype=np.uint16).reshape(-1)
+    B = np.ascontiguousarray(B, dtype=np.uint16)
+    N, K = B.shape
+    C = np.empty((1, N), dtype=np.uint16)
+    lib().orc_gemv_reference_order(_p(C), _p(A), _p(B), N, K, dt)
     return C
 
 

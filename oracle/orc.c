@@ -193,6 +193,35 @@ int orc_linear(void* C, const uint16_t* A, const uint16_t* W, int M, int N, int 
     return 0;
 }
 
+/*
+ * The reference's decode GEMV in its exact summation order
+ * (kernels/matmul.cu:25-44, launched at :49-51 with T = min(K, 256) threads):
+ * thread t accumulates k = t, t+T, ... with fused multiply-adds, then
+ * for (s = T/2; s > 0; s >>= 1) sdata[t] += sdata[t+s] for t < s.
+ * When T is not a power of two that tree never adds some partial sums
+ * (e.g. T = 200 loses sdata[24] at s = 12); this restatement keeps that
+ * behaviour so it can be compared bit-for-bit with the reference's output.
+ * The product kernels compute the full sum instead.
+ */
+void orc_gemv_reference_order(uint16_t* C, const uint16_t* A, const uint16_t* B, int N, int K,
+                              int dt) {
+    const int T = K < 256 ? K : 256;
+    float* sd = (float*)malloc(sizeof(float) * (size_t)T);
+    if (!sd) return;
+    for (int n = 0; n < N; ++n) {
+        const uint16_t* b = B + (size_t)n * K;
+        for (int t = 0; t < T; ++t) {
+            float sum = 0.0f;
+            for (int k = t; k < K; k += T) sum = fmaf(to_f(A[k], dt), to_f(b[k], dt), sum);
+            sd[t] = sum;
+        }
+        for (int st = T / 2; st > 0; st >>= 1)
+            for (int t = 0; t < st; ++t) sd[t] += sd[t + st];
+        C[n] = from_f(sd[0], dt);
+    }
+    free(sd);
+}
+
 /* kernels/fused_swiglu.cu:11-15 */
 void orc_silu_mul(uint16_t* out, const uint16_t* g, const uint16_t* u, long long n, int dt) {
     for (long long i = 0; i < n; ++i) out[i] = from_f(silu(to_f(g[i], dt)) * to_f(u[i], dt), dt);

@@ -31,6 +31,12 @@ static size_t default_ws_bytes(int sm_count) {
   return tiles * 128 * 256 * sizeof(float) + tiles * sizeof(int);
 }
 
+bool device_ctx_ready(int device) {
+  if (device < 0 || device >= 64) return false;
+  std::lock_guard<std::mutex> lock(g_ctx_mu);
+  return g_ctx[device].device == device;
+}
+
 DeviceCtx* device_ctx(int device, cudaError_t* e) {
   *e = cudaSuccess;
   if (device < 0 || device >= 64) {
@@ -166,6 +172,16 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (!device_ctx_ready(dev)) {
+    // The first call on a device allocates the split-K workspace; that can't
+    // happen inside stream capture.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) {
+      set_error("orin_linear: the first call on device %d allocates its workspace and must "
+                "not be stream-captured; make one uncaptured call first", dev);
+      return ORIN_ERR_INVALID_ARG;
+    }
+  }
   DeviceCtx* ctx = device_ctx(dev, &e);
   if (!ctx) {
     if (e == cudaErrorNoKernelImageForDevice) {

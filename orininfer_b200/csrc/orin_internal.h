@@ -48,6 +48,7 @@ struct DeviceCtx {
 };
 
 DeviceCtx* device_ctx(int device, cudaError_t* e);
+bool device_ctx_ready(int device);
 
 // Fill the tiling / scheduling fields of a plan for the tcgen05 kernels.
 void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count);

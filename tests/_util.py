@@ -4,13 +4,20 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-# Parity bar for the 16-bit GEMM outputs against the oracle:
-#   max relative error  max_i |y_i - r_i| / max(|r_i|, 0.01 * rms(r))  <= 1e-2
-#   mean absolute error mean_i |y_i - r_i|                              <= 1e-3
-# The floor keeps outputs that cancel to ~0 from dominating; one 16-bit ulp
-# of a normal value is <= 2**-7 relative (bf16), below the 1e-2 bar.
+# Parity bar for the GEMM outputs against the oracle (same 16-bit inputs):
+#   max relative error  max_i |y_i - r_i| / max_i |r_i|   <= 1e-2
+#   mean absolute error mean_i |y_i - r_i|                <= 1e-3
+#   and, for 16-bit outputs of one GEMM, at least 95% of them bit-identical
+#   (both sides accumulate in fp32; only the summation order differs, which
+#   flips a final rounding for well under 1% of outputs).
+# The relative error is taken against the largest output: the reference
+# rounds the accumulator before the residual add (round16(x + round16(acc))),
+# so where x and acc cancel a one-ulp flip of round16(acc) is an absolute
+# error of ulp(acc) on an output near zero, and an elementwise ratio there
+# says nothing about the kernel.
 MAX_REL = 1e-2
 MAE = 1e-3
+EXACT_MIN = 0.95
 
 TORCH_DT = {0: torch.float16, 1: torch.bfloat16}
 DT_CODE = {torch.float16: 0, torch.bfloat16: 1}
@@ -28,19 +35,25 @@ def from_bits(a: np.ndarray, dtype) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(dtype)
 
 
-def errors(y, r) -> tuple[float, float]:
+def errors(y, r) -> tuple[float, float, float]:
+    """(max relative error, mean absolute error, fraction exactly equal)."""
     y = torch.as_tensor(y).double().flatten()
     r = torch.as_tensor(r).double().flatten()
+    if r.numel() == 0:
+        return 0.0, 0.0, 1.0
     d = (y - r).abs()
-    rms = r.pow(2).mean().sqrt().item() if r.numel() else 0.0
-    floor = max(0.01 * rms, 1e-30)
-    max_rel = (d / r.abs().clamp_min(floor)).max().item() if r.numel() else 0.0
-    return max_rel, d.mean().item() if r.numel() else 0.0
+    scale = max(r.abs().max().item(), 1e-30)
+    return d.max().item() / scale, d.mean().item(), (d == 0).double().mean().item()
 
 
-def assert_close(y, r, what: str = "", max_rel: float = MAX_REL, mae: float = MAE) -> None:
+def assert_close(y, r, what: str = "", max_rel: float = MAX_REL, mae: float = MAE,
+                 exact_min: float | None = None) -> tuple[float, float, float]:
     y = torch.as_tensor(y)
     r = torch.as_tensor(r)
     assert torch.isfinite(y.double()).all(), f"{what}: non-finite output"
-    mr, ma = errors(y, r)
-    assert mr <= max_rel and ma <= mae, f"{what}: max_rel={mr:.3e} (<= {max_rel}), mae={ma:.3e} (<= {mae})"
+    mr, ma, ex = errors(y, r)
+    assert mr <= max_rel and ma <= mae, (
+        f"{what}: max_rel={mr:.3e} (<= {max_rel}), mae={ma:.3e} (<= {mae}), exact={ex:.4f}")
+    if exact_min is not None:
+        assert ex >= exact_min, f"{what}: only {ex:.4f} of outputs bit-identical (>= {exact_min})"
+    return mr, ma, ex

@@ -8,8 +8,14 @@ oracle/_ref/ from the reference sources:
 Each fixture holds seeded bf16 inputs (as uint16 bit patterns) and the
 reference kernel's output for them:
   matmul      kernels::matmul — M==1 runs gemv_kernel (kernels/matmul.cu:25-44),
-              M>1 runs cublasGemmEx (kernels/matmul.cu:59-68); "cute" fixtures
-              run the CuTe sm80 kernel (kernels/gemm_cute.cu) of the non-cuBLAS build
+              M>1 runs cublasGemmEx (kernels/matmul.cu:59-68); the "rowgemv"
+              fixture is the non-cuBLAS build with an unaligned M, which takes
+              the per-row GEMV fallback (kernels/matmul.cu:71-77) without
+              launching the CuTe kernel (its alignment check, gemm_cute.cu:302,
+              returns first).  The CuTe kernel itself is not run: built for
+              sm_100a it raised an illegal-address error on a B200 (its
+              128-thread copy layouts under a 256-thread MMA index past the
+              tile).
   silu_mul    kernels::fused_silu_mul (kernels/fused_swiglu.cu)
   add         kernels::add (kernels/softmax.cu:78-83)
   bf16_to_fp32 kernels::bf16_to_fp32 (kernels/softmax.cu:87-90)
@@ -45,19 +51,17 @@ def main(out_dir: str) -> None:
     ref = RefKernels(cute=False)
     cute = RefKernels(cute=True)
     seed = 100
-    # (name, M, N, K, which library)
+    # (name, M, N, K, which library, which reference code path runs)
     cases = [
-        ("gemv_1x256x512", 1, 256, 512, ref),
-        ("gemv_1x2048x2048", 1, 2048, 2048, ref),
-        ("gemv_1x96x200", 1, 96, 200, ref),
-        ("cublas_16x384x256", 16, 384, 256, ref),
-        ("cublas_128x256x1024", 128, 256, 1024, ref),
-        ("cublas_33x100x72", 33, 100, 72, ref),
-        ("cute_128x256x512", 128, 256, 512, cute),
-        ("cute_256x128x2048", 256, 128, 2048, cute),
-        ("rowgemv_3x64x96", 3, 64, 96, cute),
+        ("gemv_1x256x512", 1, 256, 512, ref, "gemv"),
+        ("gemv_1x2048x2048", 1, 2048, 2048, ref, "gemv"),
+        ("gemv_1x96x200", 1, 96, 200, ref, "gemv"),
+        ("cublas_16x384x256", 16, 384, 256, ref, "cublas"),
+        ("cublas_128x256x1024", 128, 256, 1024, ref, "cublas"),
+        ("cublas_33x100x72", 33, 100, 72, ref, "cublas"),
+        ("rowgemv_3x64x96", 3, 64, 96, cute, "rowgemv"),
     ]
-    for name, M, N, K, lib in cases:
+    for name, M, N, K, lib, path in cases:
         seed += 1
         A = seeded((M, K), seed, 1.0)
         B = seeded((N, K), seed + 1000, 0.02)
@@ -65,26 +69,29 @@ def main(out_dir: str) -> None:
         dC = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         lib.matmul(dC.data_ptr(), dA.data_ptr(), dB.data_ptr(), M, N, K)
         lib.sync()
-        np.savez_compressed(os.path.join(out_dir, f"matmul_{name}.npz"), kind="matmul",
+        np.savez_compressed(os.path.join(out_dir, f"matmul_{name}.npz"), kind="matmul", path=path,
                             A=u16(A), B=u16(B), C=u16(dC), M=M, N=N, K=K)
         print("wrote", name, flush=True)
+    # every device buffer is held in a variable for as long as a kernel uses it
     n = 3 * 4096 + 17
     g = seeded((n,), 501, 3.0)
     u = seeded((n,), 502, 1.0)
+    dg, du = g.to(dev), u.to(dev)
     dout = torch.empty(n, dtype=torch.bfloat16, device=dev)
-    ref.fused_silu_mul(dout.data_ptr(), g.to(dev).data_ptr(), u.to(dev).data_ptr(), 1, n)
+    ref.fused_silu_mul(dout.data_ptr(), dg.data_ptr(), du.data_ptr(), 1, n)
     ref.sync()
     np.savez_compressed(os.path.join(out_dir, "silu_mul.npz"), kind="silu_mul", gate=u16(g),
                         up=u16(u), out=u16(dout))
     x = seeded((n,), 503, 1.0)
     y = seeded((n,), 504, 1.0)
-    dx = x.to(dev)
-    ref.add(dx.data_ptr(), y.to(dev).data_ptr(), n)
+    dx, dy = x.to(dev), y.to(dev)
+    ref.add(dx.data_ptr(), dy.data_ptr(), n)
     ref.sync()
     np.savez_compressed(os.path.join(out_dir, "add.npz"), kind="add", x=u16(x), y=u16(y),
                         out=u16(dx))
+    dx2 = x.to(dev)
     df = torch.empty(n, dtype=torch.float32, device=dev)
-    ref.bf16_to_fp32(df.data_ptr(), x.to(dev).data_ptr(), n)
+    ref.bf16_to_fp32(df.data_ptr(), dx2.data_ptr(), n)
     ref.sync()
     np.savez_compressed(os.path.join(out_dir, "bf16_to_fp32.npz"), kind="bf16_to_fp32",
                         x=u16(x), out=df.cpu().numpy())

@@ -11,7 +11,7 @@ import torch
 import orininfer_b200 as ob
 from orininfer_b200 import _lib
 from oracle import oracle as orc
-from tests._util import TORCH_DT, assert_close, bits, from_bits, seeded
+from tests._util import EXACT_MIN, TORCH_DT, assert_close, bits, from_bits, seeded
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -35,7 +35,8 @@ def run_case(M, N, K, dt, epi, algo="auto", seed=0, check_rows=None):
         ref_t = torch.from_numpy(ref)
     else:
         ref_t = from_bits(ref, tdt).float()
-    assert_close(y[rows].float(), ref_t.float(), f"{algo} {epi} dt={dt} M={M} N={N} K={K}")
+    assert_close(y[rows].float(), ref_t.float(), f"{algo} {epi} dt={dt} M={M} N={N} K={K}",
+                 exact_min=None if epi == "f32_partial" else EXACT_MIN)
     return y
 
 
@@ -131,8 +132,7 @@ def test_dependent_chain_with_programmatic_launch():
         r = bits(x)
         for w in ws:
             r = orc.linear(r, bits(w), 0, "none")
-        assert_close(h.cpu().float(), from_bits(r, torch.float16).float(), f"chain {algo} M={M}",
-                     max_rel=2e-2)
+        assert_close(h.cpu().float(), from_bits(r, torch.float16).float(), f"chain {algo} M={M}")
 
 
 def test_tinyllama_layer_prefill_m512():
@@ -166,28 +166,32 @@ def test_reference_entry_points_drop_in():
     for M, N, K in ((1, 256, 512), (64, 384, 256), (128, 256, 1024)):
         x = seeded((M, K), 1, 1.0, tdt)
         w = seeded((N, K), 2, 0.02, tdt)
+        dx, dw = x.to(DEV), w.to(DEV)  # keep the device copies alive across the calls
         c = torch.empty((M, N), dtype=tdt, device=DEV)
-        _lib.shim("kernels::matmul")(c.data_ptr(), x.to(DEV).data_ptr(), w.to(DEV).data_ptr(), M, N, K)
+        _lib.shim("kernels::matmul")(c.data_ptr(), dx.data_ptr(), dw.data_ptr(), M, N, K)
         torch.cuda.synchronize()
         ref = orc.linear(bits(x), bits(w), dt, "none")
-        assert_close(c.cpu().float(), from_bits(ref, tdt).float(), "kernels::matmul")
+        assert_close(c.cpu().float(), from_bits(ref, tdt).float(), "kernels::matmul",
+                     exact_min=EXACT_MIN)
         c.zero_()
-        assert _lib.shim("launch_gemm_cute")(c.data_ptr(), x.to(DEV).data_ptr(), w.to(DEV).data_ptr(), M, N, K)
+        assert _lib.shim("launch_gemm_cute")(c.data_ptr(), dx.data_ptr(), dw.data_ptr(), M, N, K)
         torch.cuda.synchronize()
-        assert_close(c.cpu().float(), from_bits(ref, tdt).float(), "launch_gemm_cute")
+        assert_close(c.cpu().float(), from_bits(ref, tdt).float(), "launch_gemm_cute",
+                     exact_min=EXACT_MIN)
     n = 5000
     g = seeded((n,), 3, 3.0, tdt)
     u = seeded((n,), 4, 1.0, tdt)
+    dg, du = g.to(DEV), u.to(DEV)
     out = torch.empty(n, dtype=tdt, device=DEV)
-    _lib.shim("kernels::fused_silu_mul")(out.data_ptr(), g.to(DEV).data_ptr(), u.to(DEV).data_ptr(), 1, n)
+    _lib.shim("kernels::fused_silu_mul")(out.data_ptr(), dg.data_ptr(), du.data_ptr(), 1, n)
     torch.cuda.synchronize()
     assert (bits(out.cpu()) == orc.silu_mul(bits(g), bits(u), dt)).mean() > 0.999
     xx = g.to(DEV)
-    _lib.shim("kernels::add")(xx.data_ptr(), u.to(DEV).data_ptr(), n)
+    _lib.shim("kernels::add")(xx.data_ptr(), du.data_ptr(), n)
     torch.cuda.synchronize()
     assert np.array_equal(bits(xx.cpu()), orc.add(bits(g), bits(u), dt))
     f = torch.empty(n, dtype=torch.float32, device=DEV)
-    _lib.shim("kernels::bf16_to_fp32")(f.data_ptr(), g.to(DEV).data_ptr(), n)
+    _lib.shim("kernels::bf16_to_fp32")(f.data_ptr(), dg.data_ptr(), n)
     torch.cuda.synchronize()
     assert np.array_equal(f.cpu().numpy(), orc.widen(bits(g), dt))
 

@@ -52,7 +52,9 @@ def _worker(rank, world, port, q):
         dist.all_reduce(pd)
         g, u = tp.shard_gate_up_rows(w["wg"], w["wu"], rank, world)
         gu = x @ g.double().T, x @ u.double().T
-        q.put((rank, qkv, po, pd, gu))
+        # numpy arrays travel by value (torch tensors would be shared through
+        # file descriptors that vanish when this process exits)
+        q.put((rank, qkv.numpy(), po.numpy(), pd.numpy(), (gu[0].numpy(), gu[1].numpy())))
     finally:
         dist.destroy_process_group()
 
@@ -67,8 +69,9 @@ def test_two_rank_sharding_reassembles_the_layer():
         p.start()
     res = dict()
     for _ in range(world):
-        r, *vals = q.get(timeout=120)
-        res[r] = vals
+        r, qkv, po, pd, gu = q.get(timeout=120)
+        res[r] = [torch.from_numpy(qkv), torch.from_numpy(po), torch.from_numpy(pd),
+                  (torch.from_numpy(gu[0]), torch.from_numpy(gu[1]))]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
