@@ -295,7 +295,8 @@ def time_steps(step: Step, steps: int, warmup: int, world: int, dev_index: int):
 def kernel_breakdown(step: Step, n: int):
     """Average device time per launch of each projection (CUDA events on the
     launching stream, inside a captured graph of n steps)."""
-    events = [{k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    events = [{k: (torch.cuda.Event(enable_timing=True, external=True),
+                   torch.cuda.Event(enable_timing=True, external=True))
                for k in GEMMS} for _ in range(n)]
     g = capture(step, n, events_per_step=events)
     g.replay()  # warm

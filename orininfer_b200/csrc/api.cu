@@ -24,8 +24,9 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
-// Bytes of the default workspace: the largest stream-K remainder the planner
-// produces is < 2 waves of 128x256 fp32 tiles, plus one counter per tile.
+// Bytes of the default workspace: the planner splits fewer than one wave of
+// tiles (< sm_count 128x256 fp32 tiles), plus one counter per tile; sized for
+// two waves to leave room.
 static size_t default_ws_bytes(int sm_count) {
   const size_t tiles = 2 * static_cast<size_t>(sm_count);
   return tiles * 128 * 256 * sizeof(float) + tiles * sizeof(int);

@@ -46,6 +46,7 @@ constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
 constexpr int kThreads = 192;  // 6 warps
 constexpr int kEpiThreads = 128;
 constexpr int kGroupP = 8;     // P tiles per raster group
+constexpr int kMinSplitIters = 4;  // least k-blocks a CTA takes of a split tile
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
 __host__ __device__ constexpr int tc_stages(int bn) {
@@ -92,10 +93,15 @@ struct SegIter {
     dp_waves = p.dp_tiles / G;
     w = 0;
     const long long total = static_cast<long long>(p.sk_tiles) * kb;
-    base = total / G;
-    rem = total % G;
-    pos = c * base + (c < rem ? c : rem);
-    end = pos + base + (c < rem ? 1 : 0);
+    const int g = p.sk_ctas;  // CTAs that take part in the split phase
+    base = g > 0 ? total / g : 0;
+    rem = g > 0 ? total % g : 0;
+    if (c < g) {
+      pos = c * base + (c < rem ? c : rem);
+      end = pos + base + (c < rem ? 1 : 0);
+    } else {
+      pos = end = 0;
+    }
   }
 
   __device__ __forceinline__ bool next(Seg& s) {
@@ -159,7 +165,10 @@ __device__ __forceinline__ void store16_row(typename Elem<DT>::T* dst, const flo
       }
     }
   } else {
-    for (int i = 0; i < cnt && i < valid; ++i) dst[i] = E::from_f(v[i]);
+    // fully unrolled so v stays in registers
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < cnt && i < valid) dst[i] = E::from_f(v[i]);
   }
 }
 
@@ -180,7 +189,9 @@ __device__ __forceinline__ void load16_row(const typename Elem<DT>::T* src, floa
       }
     }
   } else {
-    for (int i = 0; i < cnt; ++i) v[i] = (i < valid) ? E::to_f(src[i]) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < cnt) v[i] = (i < valid) ? E::to_f(src[i]) : 0.0f;
   }
 }
 
@@ -192,7 +203,9 @@ __device__ __forceinline__ void store32f_row(float* dst, const float* v, int cnt
       if (i < cnt) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     }
   } else {
-    for (int i = 0; i < cnt && i < valid; ++i) dst[i] = v[i];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < cnt && i < valid) dst[i] = v[i];
   }
 }
 
@@ -294,6 +307,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
         }
         named_bar_sync(1, kEpiThreads);
         if (lr < 64 && n < p.N) {
+#pragma unroll
           for (int j = 0; j < CW; ++j) {
             const int m = tq * BN + c + j;
             if (m < p.M) {
@@ -630,18 +644,17 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   p.group_p = kGroupP;
   const int tiles = p.tiles_p * p.tiles_q;
   const int G = sm_count;
-  if (tiles >= G) {
-    const int waves = tiles / G;
-    p.dp_tiles = (tiles % G == 0) ? tiles : (waves - 1) * G;
-  } else {
-    p.dp_tiles = 0;
-  }
+  // Whole waves: one tile per CTA, full K.  The tiles left over (fewer than
+  // a wave) are split by k-blocks so every CTA gets a share, but no CTA gets
+  // less than kMinSplitIters k-blocks (fewer partial sums to combine).
+  p.dp_tiles = (tiles / G) * G;
   p.sk_tiles = tiles - p.dp_tiles;
-  pl.grid = G;
-  if (p.dp_tiles == 0) {
-    const long long iters = static_cast<long long>(p.sk_tiles) * p.kb;
-    if (iters < G) pl.grid = static_cast<int>(iters);
-  }
+  const long long sk_iters = static_cast<long long>(p.sk_tiles) * p.kb;
+  long long sk_ctas = sk_iters / kMinSplitIters;
+  if (sk_ctas < p.sk_tiles) sk_ctas = p.sk_tiles;
+  if (sk_ctas > G) sk_ctas = G;
+  p.sk_ctas = p.sk_tiles > 0 ? static_cast<int>(sk_ctas) : 0;
+  pl.grid = p.dp_tiles > 0 ? G : p.sk_ctas;
   const size_t part = static_cast<size_t>(p.sk_tiles) * kBM * pl.bn * sizeof(float);
   pl.ws_bytes = (p.sk_tiles > 0) ? part + static_cast<size_t>(p.sk_tiles) * sizeof(int) : 0;
 }

@@ -18,7 +18,8 @@ struct TcParams {
   int M, N;          // logical output C[M, N] (N = output columns)
   int tiles_p, tiles_q, kb;
   int dp_tiles;      // tiles done whole, round-robin over the grid
-  int sk_tiles;      // tiles after those, split over the grid by k-blocks
+  int sk_tiles;      // tiles after those, split by k-blocks over the first
+  int sk_ctas;       //   sk_ctas CTAs of the grid
   int group_p;       // raster: this many P tiles walk together
   void* C;
   long long ldc;     // elements

@@ -113,7 +113,7 @@ def test_oracle_matches_reference_golden(path):
     z = np.load(path)
     kind = str(z["kind"])
     dt = 1  # the reference is bf16-only
-    path_kind = str(z["path"]) if "path" in z else ("gemv" if int(z["M"]) == 1 else "cublas")
+    path_kind = str(z["path"]) if kind == "matmul" else None
     if kind == "matmul" and path_kind in ("gemv", "rowgemv"):
         # the reference's GEMV (one launch per row in the non-cuBLAS build's
         # fallback): the oracle's restatement of its summation order
@@ -135,6 +135,8 @@ def test_oracle_matches_reference_golden(path):
                      f"golden {os.path.basename(path)}")
     elif kind == "silu_mul":
         got = orc.silu_mul(z["gate"], z["up"], dt)
+        # expf on the GPU and in libm may differ in the last fp32 ulp, which
+        # can flip a bf16 rounding now and then
         assert (got == z["out"]).mean() >= 0.999
     elif kind == "add":
         got = orc.add(z["x"], z["y"], dt)
