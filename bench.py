@@ -311,6 +311,54 @@ def kernel_breakdown(step: Step, n: int):
     return out
 
 
+def cublas_bar(step: Step, steps: int) -> dict:
+    """The reference's M>1 path on this workload: cublasGemmEx-equivalent
+    fp16 GEMMs (torch.nn.functional.linear -> cuBLAS), unfused, with the
+    reference's separate SwiGLU and residual-add passes, graph-timed like
+    our arm.  A comparison bar only; nothing here is our kernel."""
+    import torch.nn.functional as F
+
+    L0 = step.layers
+    gate_w = [L["gate_up"] for L in L0]  # packed rows: the same FLOPs
+
+    def run(i):
+        L = L0[i % len(L0)]
+        q = F.linear(step.h, L["qkv"])
+        o = F.linear(step.attn, L["o_proj"])
+        x1 = step.x + o
+        gu = F.linear(step.h2, gate_w[i % len(L0)])
+        a = F.silu(gu[:, :IM]) * gu[:, IM:]
+        d = F.linear(a, L["down"])
+        x2 = x1 + d
+        return q, x2
+
+    run(0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    n = min(steps, 200)
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                run(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (5 * n)
+    del g
+    return {"ms_per_step": round(ms, 5), "tflops": round(STEP_FLOPS / (ms / 1e3) / 1e12, 2),
+            "what": "torch.nn.functional.linear (cuBLAS) x4 + unfused SiLU*up and residual adds, "
+                    "CUDA graph, same weights"}
+
+
 def e2e_through_abi(step: Step, steps: int, dev):
     """The same metric through the public API with host buffers: every step
     copies its inputs from pinned host memory and reads the result back."""
@@ -385,6 +433,7 @@ def run_ours(args, rank, world, local_rank):
     value = STEP_FLOPS * args.steps / (ms / 1e3) / 1e12
 
     kt = kernel_breakdown(step, args.breakdown_steps) if world == 1 else None
+    bar = cublas_bar(step, args.steps) if world == 1 and args.cublas_bar else None
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     e2e_ms, h2d, d2h = e2e_through_abi(step, e2e_steps, dev)
     e2e_ms = max_over_ranks(e2e_ms, world)
@@ -433,6 +482,8 @@ def run_ours(args, rank, world, local_rank):
             "avg_launch_ms": round(avg_ms, 5),
         }
         line["kernels_ms"] = {k: round(v, 5) for k, v in kt.items()}
+        if bar is not None:
+            line["cublas_bar"] = bar
         line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}
         line["cpu_baseline"] = cpu_baseline_layer(args.cpu_budget) if args.cpu_budget > 0 \
             else None
@@ -559,6 +610,8 @@ def main():
                     help="steps of the end-to-end (host buffers, C ABI) measurement")
     ap.add_argument("--breakdown-steps", type=int, default=64,
                     help="steps of the per-projection CUDA-event breakdown")
+    ap.add_argument("--no-cublas-bar", dest="cublas_bar", action="store_false",
+                    help="skip timing the cuBLAS comparison bar")
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,
                     help="run only this projection, eagerly, warmup+steps times, and print "
                          "its event-timed average (a small case for profilers)")

@@ -3,10 +3,10 @@
  *
  * Every entry point takes plain device pointers, element counts and an opaque
  * CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream).
- * No allocation happens on the data path except the per-device split-K
- * workspace that orin_linear() creates lazily on its first call on a device
- * (orin_linear_ex() lets the caller pass its own workspace instead).  That
- * first call must not be inside CUDA stream capture; later calls may be
+ * Nothing is allocated: split-K partial sums stay on chip (thread-block
+ * clusters combine them through distributed shared memory).  The first GEMM
+ * call on a device does a one-time set-up (device attributes, the device
+ * error word); it must not be inside CUDA stream capture, later calls may be
  * captured into graphs.
  * No C++ exception crosses this boundary: every function returns orin_status,
  * and orin_last_error() gives a thread-local message for the last failure.
@@ -93,22 +93,13 @@ orin_status orin_linear(void* C, const void* A, const void* W,
                         const void* residual, void* stream);
 
 /*
- * orin_linear with an explicit kernel choice and caller-owned workspace.
- * workspace may be NULL (then the lazily created per-device workspace is
- * used).  A caller workspace must be at least orin_linear_workspace_size()
- * bytes, 256-byte aligned, and zero-filled before its first use; the kernels
- * leave it zero-filled again when they finish.  Calls that may overlap on the
- * GPU must not share a workspace.
+ * orin_linear with an explicit kernel choice (orin_algo).  ORIN_ALGO_AUTO is
+ * what orin_linear passes; the others exist for tests and tuning and return
+ * ORIN_ERR_UNSUPPORTED for shapes they can't take.
  */
 orin_status orin_linear_ex(void* C, const void* A, const void* W,
                            int M, int N, int K, int dtype, int epilogue,
-                           const void* residual, int algo,
-                           void* workspace, size_t workspace_bytes,
-                           void* stream);
-
-/* Workspace bytes orin_linear_ex needs for this problem (0 if none). */
-size_t orin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue,
-                                  int algo);
+                           const void* residual, int algo, void* stream);
 
 /*
  * Build the packed gate/up weight the SWIGLU epilogue reads:
@@ -139,7 +130,7 @@ orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype,
  * Synchronise stream and report device-side failures of this library's
  * kernels: every spin-wait inside them gives up after a bounded time and
  * records an error code instead of hanging.  Returns ORIN_ERR_TIMEOUT (and
- * clears the record, re-zeroing the split-K workspace) if one did.
+ * clears the record) if one did.
  */
 orin_status orin_device_check(void* stream);
 

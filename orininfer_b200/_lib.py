@@ -55,8 +55,7 @@ SIGNATURES = {
     "orin_version": (_i, []),
     "orin_last_error": (ctypes.c_char_p, []),
     "orin_linear": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
-    "orin_linear_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _sz, _vp]),
-    "orin_linear_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "orin_linear_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "orin_pack_gate_up": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "orin_silu_mul": (_i, [_vp, _vp, _vp, _ll, _i, _vp]),
     "orin_add": (_i, [_vp, _vp, _ll, _i, _vp]),

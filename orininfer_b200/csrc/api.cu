@@ -1,5 +1,5 @@
 // api.cu — the C ABI (include/orin_b200.h): argument checks, kernel choice,
-// the per-device split-K workspace, and the elementwise entry points.
+// per-device set-up and the elementwise entry points.
 #include "orin_b200.h"
 #include "orin_common.cuh"
 #include "orin_internal.h"
@@ -24,13 +24,9 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
-// Bytes of the default workspace: the planner splits fewer than one wave of
-// tiles (< sm_count 128x256 fp32 tiles), plus one counter per tile; sized for
-// two waves to leave room.
-static size_t default_ws_bytes(int sm_count) {
-  const size_t tiles = 2 * static_cast<size_t>(sm_count);
-  return tiles * 128 * 256 * sizeof(float) + tiles * sizeof(int);
-}
+// The device error word: kernels that give up a bounded wait record a code
+// here (one copy per device; host code reaches it through its address).
+__device__ int g_device_error_word;
 
 bool device_ctx_ready(int device) {
   if (device < 0 || device >= 64) return false;
@@ -58,19 +54,10 @@ DeviceCtx* device_ctx(int device, cudaError_t* e) {
     *e = cudaErrorNoKernelImageForDevice;
     return nullptr;
   }
-  // one allocation: the workspace, then the device error word on its own
-  // 256-byte line
-  const size_t bytes = ((default_ws_bytes(sms) + 255) / 256) * 256;
-  void* mem = nullptr;
-  if ((*e = cudaMalloc(&mem, bytes + 256)) != cudaSuccess) return nullptr;
-  if ((*e = cudaMemset(mem, 0, bytes + 256)) != cudaSuccess) {
-    cudaFree(mem);
-    return nullptr;
-  }
+  void* addr = nullptr;
+  if ((*e = cudaGetSymbolAddress(&addr, g_device_error_word)) != cudaSuccess) return nullptr;
   c.sm_count = sms;
-  c.ws = mem;
-  c.ws_bytes = bytes;
-  c.err = reinterpret_cast<int*>(static_cast<char*>(mem) + bytes);
+  c.err = static_cast<int*>(addr);
   c.device = device;
   return &c;
 }
@@ -118,24 +105,8 @@ int orin_version(void) { return 100; }
 
 const char* orin_last_error(void) { return g_err; }
 
-size_t orin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue, int algo) {
-  if (M < 1 || N < 1 || K < 1 || check_common(dtype, epilogue) != ORIN_OK) return 0;
-  int a = algo;
-  if (a == ORIN_ALGO_AUTO) a = (M <= 64) ? 2 : 1;
-  if (a != 1 && a != 2) return 0;
-  if (a == 2 && M > 64) return 0;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaGetLastError();
-  Plan pl;
-  plan_tc(pl, M, N, K, epilogue, a, sms);
-  return pl.ws_bytes;
-}
-
 orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
-                           int epilogue, const void* residual, int algo, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+                           int epilogue, const void* residual, int algo, void* stream) {
   orin_status st = check_common(dtype, epilogue);
   if (st != ORIN_OK) return st;
   if (!C || !A || !W) {
@@ -174,12 +145,11 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (!device_ctx_ready(dev)) {
-    // The first call on a device allocates the split-K workspace; that can't
-    // happen inside stream capture.
+    // The first call on a device loads its set-up; keep it out of capture.
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) {
-      set_error("orin_linear: the first call on device %d allocates its workspace and must "
-                "not be stream-captured; make one uncaptured call first", dev);
+      set_error("orin_linear: the first call on device %d sets the device up and must not be "
+                "stream-captured; make one uncaptured call first", dev);
       return ORIN_ERR_INVALID_ARG;
     }
   }
@@ -193,19 +163,6 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   }
   Plan pl;
   plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count);
-  void* ws = ctx->ws;
-  if (workspace) {
-    if (workspace_bytes < pl.ws_bytes || !aligned16(workspace)) {
-      set_error("orin_linear: workspace of %zu bytes is too small (need %zu) or unaligned",
-                workspace_bytes, pl.ws_bytes);
-      return ORIN_ERR_INVALID_ARG;
-    }
-    ws = workspace;
-  } else if (pl.ws_bytes > ctx->ws_bytes) {
-    set_error("orin_linear: internal workspace too small (%zu < %zu)", ctx->ws_bytes,
-              pl.ws_bytes);
-    return ORIN_ERR_UNSUPPORTED;
-  }
   const size_t esz = (epilogue == ORIN_EPI_F32_OUT || epilogue == ORIN_EPI_F32_PARTIAL) ? 4 : 2;
   pl.p.C = C;
   pl.p.ldc = N;
@@ -214,7 +171,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   pl.p.vec_ok = aligned16(C) && ((N * esz) % 16 == 0) &&
                 (!residual || (aligned16(residual) && (N * 2) % 16 == 0));
   const char* why = nullptr;
-  e = launch_tc(pl, dtype, epilogue, A, W, ws, ctx->err, s, &why);
+  e = launch_tc(pl, dtype, epilogue, A, W, ctx->err, s, &why);
   if (e != cudaSuccess) {
     if (why) {
       set_error("orin_linear: %s", why);
@@ -227,8 +184,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
 
 orin_status orin_linear(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epilogue, const void* residual, void* stream) {
-  return orin_linear_ex(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, nullptr, 0,
-                        stream);
+  return orin_linear_ex(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, stream);
 }
 
 orin_status orin_pack_gate_up(void* w_packed, const void* w_gate, const void* w_up, int IM, int K,
@@ -296,7 +252,6 @@ orin_status orin_device_check(void* stream) {
   if ((e = cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
     return cuda_fail(e, "orin_device_check: read error word");
   if (word != 0) {
-    cudaMemset(ctx->ws, 0, ctx->ws_bytes);
     cudaMemset(ctx->err, 0, sizeof(int));
     cudaDeviceSynchronize();
     set_error("orin_device_check: a kernel gave up waiting (device error code %d)", word);

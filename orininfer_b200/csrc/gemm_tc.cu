@@ -1,9 +1,9 @@
 // gemm_tc.cu — the sm_100a linear-layer kernel: C = epilogue(A · W^T).
 //
-// One persistent kernel template covers both shapes of the hot path:
-//   * wide tiles (prefill, M > 64): 128 tokens x 256 weight rows per tile;
-//   * skinny tiles (decode, M <= 64): 128 weight rows x {16,32,64} tokens per
-//     tile ("swap AB": the weight matrix feeds the 128-lane side of the MMA,
+// One kernel template covers both shapes of the hot path:
+//   * wide tiles (prefill, M > 64): 128 tokens x {128,256} weight rows;
+//   * skinny tiles (decode, M <= 64): 128 weight rows x {16,32,64} tokens
+//     ("swap AB": the weight matrix feeds the 128-lane side of the MMA,
 //     so a one-token GEMV still streams weights through the tensor core at
 //     full HBM speed, with no CUDA-core fp16->fp32 conversions).
 //
@@ -19,14 +19,17 @@
 //   warps 2-5 epilogue: tcgen05.ld (32 lanes x 32 columns per warp), the
 //             fused epilogue (SwiGLU / residual / fp32 widen), global stores.
 //
-// Scheduling: tiles are rastered in groups of P tiles so concurrently running
-// CTAs share operand panels in L2.  Whole waves of tiles are done
-// round-robin; the tiles left over (fewer than two waves) are split over all
-// CTAs by k-block ranges ("stream-K").  A CTA that holds only part of a tile's
-// k-range adds its fp32 partial into a workspace tile (vector atomics, done in
-// L2) and bumps the tile's counter; the last arriver reads the sum, applies
-// the epilogue, and zeroes the workspace tile and counter again.  No CTA ever
-// waits on another CTA.
+// Scheduling (chosen on the host per problem):
+//   * split 1 — persistent: CTA c takes tiles c, c+grid, ... over the full K;
+//     the next tile's mainloop overlaps this tile's epilogue.  Tiles are
+//     rastered in groups of P tiles so concurrent CTAs share panels in L2.
+//   * split S (2..8) — for problems with fewer tiles than SMs: each tile's
+//     K range is split over a thread-block cluster of S CTAs.  Each CTA
+//     stages its fp32 partial tile in its own shared memory (the operand ring,
+//     idle by then); after a cluster barrier every CTA sums a slice of rows
+//     over all S partials through distributed shared memory, in rank order
+//     (deterministic), applies the epilogue and stores with coalesced writes.
+//     No global workspace, no atomics.
 //
 // Every mbarrier wait is bounded (orin_common.cuh): after 2 s the CTA records
 // an error code in the device error word and unwinds instead of hanging.
@@ -37,6 +40,7 @@
 #include "orin_internal.h"
 
 #include <stdio.h>
+#include <stdlib.h>
 
 namespace orin {
 
@@ -46,7 +50,6 @@ constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
 constexpr int kThreads = 192;  // 6 warps
 constexpr int kEpiThreads = 128;
 constexpr int kGroupP = 8;     // P tiles per raster group
-constexpr int kMinSplitIters = 4;  // least k-blocks a CTA takes of a split tile
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
 __host__ __device__ constexpr int tc_stages(int bn) {
@@ -66,70 +69,48 @@ __host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap) {
 }
 
 // ---------------------------------------------------------------------------
-// Work decomposition, computed identically by every role of every CTA.
+// Work decomposition, computed identically by every role of a CTA.
+//   split == 1: persistent; CTA c takes tiles c, c + grid, c + 2*grid, ...
+//               over the full K range.
+//   split == S: one cluster of S CTAs per tile; cluster rank r takes k-blocks
+//               [r*kb/S, (r+1)*kb/S).
 // ---------------------------------------------------------------------------
 
-struct Seg {
+struct Unit {
   int tile;
-  int k0, k1;     // k-block range [k0, k1)
-  int sk;         // -1: this CTA owns the whole tile; else stream-K tile index
-  int ncontrib;   // CTAs that contribute to stream-K tile sk
+  int k0, k1;  // k-block range [k0, k1)
 };
 
-struct SegIter {
-  int G, c, kb, dp_waves, w, dp_tiles;
-  long long pos, end, base, rem;
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
 
-  __device__ __forceinline__ long long owner(long long i) const {
-    const long long big = rem * (base + 1);
-    return (i < big) ? i / (base + 1) : rem + (i - big) / base;
-  }
-
+struct UnitIter {
+  int tile, stride, tiles, k0, k1, kb;
   __device__ __forceinline__ void init(const TcParams& p) {
-    G = gridDim.x;
-    c = blockIdx.x;
     kb = p.kb;
-    dp_tiles = p.dp_tiles;
-    dp_waves = p.dp_tiles / G;
-    w = 0;
-    const long long total = static_cast<long long>(p.sk_tiles) * kb;
-    const int g = p.sk_ctas;  // CTAs that take part in the split phase
-    base = g > 0 ? total / g : 0;
-    rem = g > 0 ? total % g : 0;
-    if (c < g) {
-      pos = c * base + (c < rem ? c : rem);
-      end = pos + base + (c < rem ? 1 : 0);
+    tiles = p.tiles_p * p.tiles_q;
+    if (p.split == 1) {
+      tile = blockIdx.x;
+      stride = gridDim.x;
+      k0 = 0;
+      k1 = kb;
     } else {
-      pos = end = 0;
+      const int r = static_cast<int>(cluster_rank());
+      tile = blockIdx.x / p.split;
+      stride = tiles;  // one unit only
+      k0 = static_cast<int>((static_cast<long long>(r) * kb) / p.split);
+      k1 = static_cast<int>((static_cast<long long>(r + 1) * kb) / p.split);
     }
   }
-
-  __device__ __forceinline__ bool next(Seg& s) {
-    if (w < dp_waves) {
-      s.tile = w * G + c;
-      s.k0 = 0;
-      s.k1 = kb;
-      s.sk = -1;
-      s.ncontrib = 1;
-      ++w;
-      return true;
-    }
-    if (pos >= end) return false;
-    const long long t = pos / kb;
-    const int k0 = static_cast<int>(pos - t * kb);
-    const long long left = end - pos;
-    const int k1 = static_cast<int>((k0 + left < kb) ? (k0 + left) : kb);
-    s.tile = dp_tiles + static_cast<int>(t);
-    s.k0 = k0;
-    s.k1 = k1;
-    if (k0 == 0 && k1 == kb) {
-      s.sk = -1;
-      s.ncontrib = 1;
-    } else {
-      s.sk = static_cast<int>(t);
-      s.ncontrib = static_cast<int>(owner(t * kb + kb - 1) - owner(t * kb) + 1);
-    }
-    pos += k1 - k0;
+  __device__ __forceinline__ bool next(Unit& u) {
+    if (tile >= tiles) return false;
+    u.tile = tile;
+    u.k0 = k0;
+    u.k1 = k1;
+    tile += stride;
     return true;
   }
 };
@@ -209,29 +190,13 @@ __device__ __forceinline__ void store32f_row(float* dst, const float* v, int cnt
   }
 }
 
-// Source of accumulator chunks for the epilogue: tensor memory (the CTA owns
-// the whole tile) or the stream-K workspace tile (the last arriver), which is
-// zeroed as it is read.
+// Accumulator chunks for the direct epilogue come from tensor memory.
 template <int CW>
 struct TmemChunks {
   uint32_t taddr;  // lane base + accumulator buffer column
   __device__ __forceinline__ void get(int col, float* v) const {
     if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + col, v);
     else tmem_ld_32x32b_x16(taddr + col, v);
-  }
-};
-
-template <int CW>
-struct WsChunks {
-  float* row;  // this thread's row of the workspace tile
-  __device__ __forceinline__ void get(int col, float* v) const {
-    float4* p = reinterpret_cast<float4*>(row + col);
-#pragma unroll
-    for (int i = 0; i < CW / 4; ++i) {
-      const float4 f = __ldcg(p + i);
-      v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-      __stcg(p + i, make_float4(0.f, 0.f, 0.f, 0.f));
-    }
   }
 };
 
@@ -347,6 +312,186 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 }
 
 // ---------------------------------------------------------------------------
+// Cluster split-K: shared-memory staging and the DSMEM reduction
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_smem_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// All threads of all CTAs of the cluster; release/acquire orders the shared
+// memory writes before it with the remote reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Row pitch (floats) of the fp32 staging tile: +4 keeps the per-row float4
+// writes of a warp (32 rows) on distinct banks.
+template <int BN>
+__host__ __device__ constexpr int stage_pitch() { return BN + 4; }
+
+// Sum the S partial tiles of this cluster over rows [r0, r1) of the tile in
+// a fixed order (rank 0 .. S-1), apply the epilogue and store.  Threads map to
+// consecutive 4-column groups so global stores and residual loads coalesce.
+template <int DT, int BN, int EPI, bool SWAP>
+__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int tp,
+                                            int tq, int r0, int r1, int et) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int PITCH = stage_pitch<BN>();
+  const bool vec = p.vec_ok != 0;
+  auto sum4 = [&](int row, int col) {
+    const uint32_t off = stage + static_cast<uint32_t>((row * PITCH + col) * 4);
+    float4 a = ld_dsmem_f4(mapa_shared(off, 0));
+    for (int r = 1; r < S; ++r) {
+      const float4 b = ld_dsmem_f4(mapa_shared(off, static_cast<uint32_t>(r)));
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    return a;
+  };
+  if constexpr (!SWAP) {
+    if constexpr (EPI == EPI_SWIGLU) {
+      // gate 4-column groups: 16 per 128-column block
+      constexpr int G = BN / 8;
+      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
+        const int row = r0 + e / G;
+        const int gg = e % G;
+        const int gc = (gg / 16) * 128 + (gg % 16) * 4;
+        const float4 g = sum4(row, gc);
+        const float4 u = sum4(row, gc + 64);
+        const int m = tp * kBM + row;
+        const int n = (tq * BN) / 2 + (gg / 16) * 64 + (gg % 16) * 4;
+        if (m < p.M && n < p.N) {
+          float o[4] = {silu_f32(E::round(g.x)) * E::round(u.x), silu_f32(E::round(g.y)) * E::round(u.y),
+                        silu_f32(E::round(g.z)) * E::round(u.z), silu_f32(E::round(g.w)) * E::round(u.w)};
+          T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
+          if (vec && n + 4 <= p.N) {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
+          } else {
+            for (int j = 0; j < 4; ++j)
+              if (n + j < p.N) dst[j] = E::from_f(o[j]);
+          }
+        }
+      }
+    } else {
+      constexpr int G = BN / 4;
+      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
+        const int row = r0 + e / G;
+        const int g = e % G;
+        const float4 a = sum4(row, 4 * g);
+        const int m = tp * kBM + row;
+        const int n = tq * BN + 4 * g;
+        if (m >= p.M || n >= p.N) continue;
+        float o[4] = {a.x, a.y, a.z, a.w};
+        const bool full = vec && n + 4 <= p.N;
+        if constexpr (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL) {
+          if constexpr (EPI == EPI_F32_OUT) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = E::round(o[j]);
+          }
+          float* dst = static_cast<float*>(p.C) + m * p.ldc + n;
+          if (full) {
+            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+          } else {
+            for (int j = 0; j < 4; ++j)
+              if (n + j < p.N) dst[j] = o[j];
+          }
+        } else {
+          if constexpr (EPI == EPI_RESIDUAL) {
+            const T* rs = static_cast<const T*>(p.R) + m * p.ldr + n;
+            if (full) {
+              const uint2 rv = *reinterpret_cast<const uint2*>(rs);
+              const float2 r01 = E::unpack2(rv.x), r23 = E::unpack2(rv.y);
+              o[0] = r01.x + E::round(o[0]);
+              o[1] = r01.y + E::round(o[1]);
+              o[2] = r23.x + E::round(o[2]);
+              o[3] = r23.y + E::round(o[3]);
+            } else {
+              for (int j = 0; j < 4; ++j)
+                if (n + j < p.N) o[j] = E::to_f(rs[j]) + E::round(o[j]);
+            }
+          }
+          T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
+          if (full) {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
+          } else {
+            for (int j = 0; j < 4; ++j)
+              if (n + j < p.N) dst[j] = E::from_f(o[j]);
+          }
+        }
+      }
+    }
+  } else {
+    // Skinny: rows are weight rows (features), columns tokens.
+    constexpr int G = BN / 4;
+    if constexpr (EPI == EPI_SWIGLU) {
+      // rows [0,64) gate, [64,128) up of features tp*64 + row; r0/r1 index
+      // gate rows here
+      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
+        const int row = r0 + e / G;
+        const int g = e % G;
+        const float4 gv = sum4(row, 4 * g);
+        const float4 uv = sum4(row + 64, 4 * g);
+        const int n = tp * 64 + row;
+        if (n >= p.N) continue;
+        const float go[4] = {gv.x, gv.y, gv.z, gv.w};
+        const float uo[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int m = tq * BN + 4 * g + j;
+          if (m < p.M)
+            static_cast<T*>(p.C)[m * p.ldc + n] =
+                E::from_f(silu_f32(E::round(go[j])) * E::round(uo[j]));
+        }
+      }
+    } else {
+      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
+        // consecutive threads take consecutive rows (features) so the
+        // stores of one token row coalesce
+        const int row = r0 + e % (r1 - r0);
+        const int g = e / (r1 - r0);
+        const float4 a = sum4(row, 4 * g);
+        const int n = tp * kBM + row;
+        if (n >= p.N) continue;
+        const float o[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int m = tq * BN + 4 * g + j;
+          if (m >= p.M) continue;
+          if constexpr (EPI == EPI_NONE) {
+            static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o[j]);
+          } else if constexpr (EPI == EPI_RESIDUAL) {
+            const float r = E::to_f(static_cast<const T*>(p.R)[m * p.ldr + n]);
+            static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(r + E::round(o[j]));
+          } else if constexpr (EPI == EPI_F32_OUT) {
+            static_cast<float*>(p.C)[m * p.ldc + n] = E::round(o[j]);
+          } else {
+            static_cast<float*>(p.C)[m * p.ldc + n] = o[j];
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 
@@ -360,6 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t TMEM_COLS = tc_tmem_cols(BN);
   constexpr uint32_t IDESC = instr_desc_f16(DT, kBM, BN);
   constexpr int CW = (BN >= 32) ? 32 : 16;
+  static_assert(kBM * stage_pitch<BN>() * 4 <= STAGES * STAGE_BYTES,
+                "split-K staging tile must fit in the operand ring");
 
   extern __shared__ uint8_t dsmem[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -369,12 +516,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
-  __shared__ int arrival;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t ring = (smem_u32(dsmem) + 1023u) & ~1023u;
   float* xch = reinterpret_cast<float*>(dsmem + (ring - smem_u32(dsmem)) + STAGES * STAGE_BYTES);
+  const int S = p.split;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -403,13 +550,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = tmem_slot;
   pdl_launch_dependents();
 
+  // split mode: this CTA's one tile (for the reduction after the roles)
+  int split_tp = 0, split_tq = 0;
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();  // weights: streamed once
       const uint64_t pol_x = l2_policy_evict_last();   // activations: re-read
-      // Which of the two operands is the weight matrix (independent of the
-      // previous kernel in the stream)?
+      // The weight operand does not depend on the previous kernel in the
+      // stream, so its loads may start before griddepcontrol.wait.
       const void* tm_w = SWAP ? static_cast<const void*>(&tm_p) : static_cast<const void*>(&tm_q);
       const void* tm_x = SWAP ? static_cast<const void*>(&tm_q) : static_cast<const void*>(&tm_p);
       const uint32_t off_w = SWAP ? 0u : A_BYTES;
@@ -420,16 +570,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool waited = false;
       int stage = 0;
       uint32_t phase = 0;
-      SegIter it;
+      UnitIter it;
       it.init(p);
-      Seg s;
+      Unit u;
       bool ok = true;
-      while (ok && it.next(s)) {
+      while (ok && it.next(u)) {
         int tp, tq;
-        tile_coords(s.tile, p, tp, tq);
+        tile_coords(u.tile, p, tp, tq);
         const int row_w = SWAP ? tp * kBM : tq * BN;
         const int row_x = SWAP ? tq * BN : tp * kBM;
-        for (int k = s.k0; k < s.k1; ++k) {
+        for (int k = u.k0; k < u.k1; ++k) {
           if (n_issued >= STAGES) {
             if (!waited) {
               pdl_wait();
@@ -490,11 +640,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      SegIter it;
+      UnitIter it;
       it.init(p);
-      Seg s;
+      Unit u;
       bool ok = true;
-      while (ok && it.next(s)) {
+      while (ok && it.next(u)) {
         if (!mbar_wait_bounded(smem_u32(&tempty_bar[acc]), acc_phase ^ 1u, &abort_flag, p.err,
                                DEVERR_TIMEOUT_MMA)) {
           ok = false;
@@ -502,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int k = s.k0; k < s.k1; ++k) {
+        for (int k = u.k0; k < u.k1; ++k) {
           if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase, &abort_flag, p.err,
                                  DEVERR_TIMEOUT_MMA)) {
             ok = false;
@@ -515,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
             const uint64_t ad = smem_desc_kmajor_sw128(a_addr + kk * kUmmaK * 2);
             const uint64_t bd = smem_desc_kmajor_sw128(b_addr + kk * kUmmaK * 2);
-            tc_mma_f16(d, ad, bd, IDESC, (k > s.k0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(smem_u32(&empty_bar[stage]));
           if (++stage == STAGES) {
@@ -547,13 +697,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     const int quad = warp & 3;  // tcgen05.ld: warp w reaches lanes 32*(w%4)..+31
     const int lr = quad * 32 + lane;
-    const int et = threadIdx.x - 64;  // 0..127 within the epilogue group
     int acc = 0;
     uint32_t acc_phase = 0;
-    SegIter it;
+    UnitIter it;
     it.init(p);
-    Seg s;
-    while (it.next(s)) {
+    Unit u;
+    while (it.next(u)) {
       const bool failed = !mbar_wait_bounded(smem_u32(&tfull_bar[acc]), acc_phase, &abort_flag,
                                              p.err, DEVERR_TIMEOUT_EPILOGUE);
       // all 128 epilogue threads leave together (the epilogue uses named
@@ -561,51 +710,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (named_bar_or(1, kEpiThreads, failed)) break;
       tc_fence_after();
       int tp, tq;
-      tile_coords(s.tile, p, tp, tq);
+      tile_coords(u.tile, p, tp, tq);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if (s.sk < 0) {
+      if (S == 1) {
         TmemChunks<CW> src{taddr};
         emit_tile<DT, BN, EPI, SWAP, CW>(p, src, tp, tq, lr, xch);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
       } else {
-        // Partial tile: add into the workspace tile, then count arrivals.
-        float* wrow = p.ws + (static_cast<size_t>(s.sk) * kBM + lr) * BN;
-        const int prow = tp * kBM + lr;
-        const bool rval = prow < p.P;
+        // Stage this CTA's fp32 partial tile in its own shared memory (the
+        // operand ring is idle: every load was consumed by the finished MMAs).
+        split_tp = tp;
+        split_tq = tq;
+        fence_proxy_async_smem();
+        const uint32_t row_addr = ring + static_cast<uint32_t>(lr * stage_pitch<BN>() * 4);
         float v[32];
 #pragma unroll 1
         for (int c = 0; c < BN; c += CW) {
           if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + c, v);
           else tmem_ld_32x32b_x16(taddr + c, v);
-          if (rval) {
 #pragma unroll
-            for (int i = 0; i < CW / 4; ++i)
-              atomicAdd(reinterpret_cast<float4*>(wrow + c) + i,
-                        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-        __threadfence();
-        named_bar_sync(1, kEpiThreads);
-        if (et == 0) arrival = atomicAdd(p.counters + s.sk, 1);
-        named_bar_sync(1, kEpiThreads);
-        if (arrival == s.ncontrib - 1) {
-          __threadfence();
-          WsChunks<CW> src{wrow};
-          emit_tile<DT, BN, EPI, SWAP, CW>(p, src, tp, tq, lr, xch);
-          if (et == 0) p.counters[s.sk] = 0;
+          for (int i = 0; i < CW; i += 4)
+            st_smem_f4(row_addr + (c + i) * 4, v[i], v[i + 1], v[i + 2], v[i + 3]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+  }
+
+  if (S > 1) {
+    // Every thread of every CTA of the cluster reaches both barriers exactly
+    // once, on the normal and on the unwinding path.
+    cluster_sync_all();
+    if (warp >= 2) {
+      // this rank reduces rows [r0, r1) of the tile (gate rows only for the
+      // skinny SwiGLU, whose up rows sit 64 below)
+      const int r = static_cast<int>(cluster_rank());
+      const int rows = (SWAP && EPI == EPI_SWIGLU) ? 64 : kBM;
+      const int r0 = (r * rows) / S;
+      const int r1 = ((r + 1) * rows) / S;
+      if (!abort_flag)
+        reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_tp, split_tq, r0, r1,
+                                       static_cast<int>(threadIdx.x) - 64);
+    }
+    cluster_sync_all();
   }
 
   tc_fence_before();
@@ -620,44 +773,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side: planning, tensor maps, launch
 // ---------------------------------------------------------------------------
-
-void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
-  const int wrows = (epi == EPI_SWIGLU) ? 2 * N : N;  // rows of W
-  TcParams& p = pl.p;
-  p = TcParams{};
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  pl.algo = algo;
-  if (algo == 2) {
-    pl.bn = (M <= 16) ? 16 : (M <= 32) ? 32 : 64;
-    p.P = wrows;
-    p.Q = M;
-  } else {
-    pl.bn = 256;
-    p.P = M;
-    p.Q = wrows;
-  }
-  p.tiles_p = (p.P + kBM - 1) / kBM;
-  p.tiles_q = (p.Q + pl.bn - 1) / pl.bn;
-  p.kb = (K + kBK - 1) / kBK;
-  p.group_p = kGroupP;
-  const int tiles = p.tiles_p * p.tiles_q;
-  const int G = sm_count;
-  // Whole waves: one tile per CTA, full K.  The tiles left over (fewer than
-  // a wave) are split by k-blocks so every CTA gets a share, but no CTA gets
-  // less than kMinSplitIters k-blocks (fewer partial sums to combine).
-  p.dp_tiles = (tiles / G) * G;
-  p.sk_tiles = tiles - p.dp_tiles;
-  const long long sk_iters = static_cast<long long>(p.sk_tiles) * p.kb;
-  long long sk_ctas = sk_iters / kMinSplitIters;
-  if (sk_ctas < p.sk_tiles) sk_ctas = p.sk_tiles;
-  if (sk_ctas > G) sk_ctas = G;
-  p.sk_ctas = p.sk_tiles > 0 ? static_cast<int>(sk_ctas) : 0;
-  pl.grid = p.dp_tiles > 0 ? G : p.sk_ctas;
-  const size_t part = static_cast<size_t>(p.sk_tiles) * kBM * pl.bn * sizeof(float);
-  pl.ws_bytes = (p.sk_tiles > 0) ? part + static_cast<size_t>(p.sk_tiles) * sizeof(int) : 0;
-}
 
 namespace {
 
@@ -749,12 +864,46 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (pl.p.split > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = pl.p.split;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, tp, tq, pl.p);
+}
+
+// How many clusters of `split` CTAs of this tile shape can be resident at
+// once (all epilogues of one shape use the same shared memory).
+template <int BN, bool SWAP>
+int max_active_clusters(int split) {
+  constexpr int smem = tc_smem_bytes(BN, EPI_NONE, SWAP);
+  auto kern = tc_linear_kernel<DT_F16, BN, EPI_NONE, SWAP>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(split * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tp, tq, pl.p);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 template <int DT, bool SWAP, int BN>
@@ -773,7 +922,10 @@ cudaError_t dispatch_epi(const Plan& pl, int epi, const CUtensorMap& a, const CU
 template <int DT>
 cudaError_t dispatch_shape(const Plan& pl, int epi, const CUtensorMap& a, const CUtensorMap& b,
                            cudaStream_t s) {
-  if (pl.algo == 1) return dispatch_epi<DT, false, 256>(pl, epi, a, b, s);
+  if (pl.algo == 1) {
+    if (pl.bn == 128) return dispatch_epi<DT, false, 128>(pl, epi, a, b, s);
+    return dispatch_epi<DT, false, 256>(pl, epi, a, b, s);
+  }
   switch (pl.bn) {
     case 16: return dispatch_epi<DT, true, 16>(pl, epi, a, b, s);
     case 32: return dispatch_epi<DT, true, 32>(pl, epi, a, b, s);
@@ -782,10 +934,140 @@ cudaError_t dispatch_shape(const Plan& pl, int epi, const CUtensorMap& a, const 
   return cudaErrorInvalidValue;
 }
 
+// Per-device cache of resident-cluster counts: [shape][split].
+struct ClusterCaps {
+  int dev = -1;
+  int caps[5][9];  // shapes: wide 256, wide 128, skinny 16, 32, 64
+};
+
+int shape_index(int algo, int bn) {
+  if (algo == 1) return bn == 256 ? 0 : 1;
+  return bn == 16 ? 2 : bn == 32 ? 3 : 4;
+}
+
+int cluster_cap(int algo, int bn, int split) {
+  thread_local ClusterCaps cache[8];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  ClusterCaps& c = cache[dev & 7];
+  if (c.dev != dev) {
+    c.dev = dev;
+    for (auto& row : c.caps)
+      for (int& v : row) v = -1;
+  }
+  int& v = c.caps[shape_index(algo, bn)][split];
+  if (v < 0) {
+    if (algo == 1)
+      v = (bn == 256) ? max_active_clusters<256, false>(split)
+                      : max_active_clusters<128, false>(split);
+    else
+      v = (bn == 16) ? max_active_clusters<16, true>(split)
+                     : (bn == 32) ? max_active_clusters<32, true>(split)
+                                  : max_active_clusters<64, true>(split);
+  }
+  return v;
+}
+
+// Optional tuning override "BN,SPLIT" for wide tiles (ORIN_TC_PLAN).
+bool plan_override(int& bn, int& split) {
+  static int o_bn = -1, o_split = -1;
+  static bool read = false;
+  if (!read) {
+    read = true;
+    const char* e = getenv("ORIN_TC_PLAN");
+    if (e && sscanf(e, "%d,%d", &o_bn, &o_split) != 2) o_bn = o_split = -1;
+    if (o_bn != 128 && o_bn != 256) o_bn = -1;
+    if (o_split < 1 || o_split > 8) o_bn = -1;
+  }
+  if (o_bn < 0) return false;
+  bn = o_bn;
+  split = o_split;
+  return true;
+}
+
 }  // namespace
 
+void fill_tiles(Plan& pl, int M, int wrows, int K, int bn, int split, int sm_count) {
+  TcParams& p = pl.p;
+  pl.bn = bn;
+  p.tiles_p = (p.P + kBM - 1) / kBM;
+  p.tiles_q = (p.Q + bn - 1) / bn;
+  p.kb = (K + kBK - 1) / kBK;
+  p.group_p = kGroupP;
+  p.split = split;
+  const int tiles = p.tiles_p * p.tiles_q;
+  pl.grid = (split == 1) ? (tiles < sm_count ? tiles : sm_count) : tiles * split;
+  (void)M;
+  (void)wrows;
+}
+
+// Choose the tile width and the split-K factor.  Cost unit: one 64-deep
+// k-block of a 128x256 tile on one SM.  A split of S runs as clusters of S
+// CTAs; its partial tiles are combined through distributed shared memory.
+void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
+  const int wrows = (epi == EPI_SWIGLU) ? 2 * N : N;  // rows of W
+  TcParams& p = pl.p;
+  p = TcParams{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  pl.algo = algo;
+  const int kb = (K + kBK - 1) / kBK;
+  const int G = sm_count;
+  if (algo == 2) {
+    // skinny: HBM-bound; split K until (almost) every SM streams weights
+    const int bn = (M <= 16) ? 16 : (M <= 32) ? 32 : 64;
+    p.P = wrows;
+    p.Q = M;
+    const int tiles = (wrows + kBM - 1) / kBM;
+    int split = 1;
+    if (tiles < G) {
+      split = G / tiles;
+      if (split > 8) split = 8;
+      if (split > kb / 2) split = kb / 2 > 0 ? kb / 2 : 1;
+      while (split > 1 && cluster_cap(2, bn, split) <= 0) --split;
+    }
+    fill_tiles(pl, M, wrows, K, bn, split, G);
+    return;
+  }
+  p.P = M;
+  p.Q = wrows;
+  int obn = 0, osplit = 0;
+  if (plan_override(obn, osplit) && !(epi == EPI_SWIGLU && obn % 128)) {
+    fill_tiles(pl, M, wrows, K, obn, osplit > kb ? kb : osplit, G);
+    return;
+  }
+  const double kFill = 2.5, kReduce = 4.0;
+  double best = 1e30;
+  int best_bn = 256, best_split = 1;
+  for (int bn : {256, 128}) {
+    const double kc = (bn == 256) ? 1.0 : 0.55;
+    const long long tiles = static_cast<long long>((M + kBM - 1) / kBM) * ((wrows + bn - 1) / bn);
+    // persistent, whole K per tile
+    const long long waves1 = (tiles + G - 1) / G;
+    double cost = waves1 * (kb * kc + kFill);
+    if (cost < best) {
+      best = cost;
+      best_bn = bn;
+      best_split = 1;
+    }
+    for (int s = 2; s <= 8 && s <= kb / 2; ++s) {
+      const int cap_clusters = cluster_cap(1, bn, s);
+      if (cap_clusters <= 0) continue;
+      const long long waves = (tiles + cap_clusters - 1) / cap_clusters;
+      cost = waves * (((kb + s - 1) / s) * kc + kFill) + kReduce * bn / 256.0;
+      if (cost < best) {
+        best = cost;
+        best_bn = bn;
+        best_split = s;
+      }
+    }
+  }
+  fill_tiles(pl, M, wrows, K, best_bn, best_split, G);
+}
+
 cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const void* W,
-                      void* ws, int* err, cudaStream_t stream, const char** why) {
+                      int* err, cudaStream_t stream, const char** why) {
   Plan pl = pl0;
   const TcParams& p = pl.p;
   const bool swap = pl.algo == 2;
@@ -800,11 +1082,6 @@ cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const 
     return cudaErrorInvalidValue;
   }
   pl.p.err = err;
-  if (p.sk_tiles > 0) {
-    pl.p.ws = static_cast<float*>(ws);
-    pl.p.counters = reinterpret_cast<int*>(static_cast<char*>(ws) +
-                                           static_cast<size_t>(p.sk_tiles) * kBM * pl.bn * sizeof(float));
-  }
   if (dtype == DT_F16) return dispatch_shape<DT_F16>(pl, epi, tmp, tmq, stream);
   return dispatch_shape<DT_BF16>(pl, epi, tmp, tmq, stream);
 }

@@ -17,16 +17,13 @@ struct TcParams {
   int P, Q, K;
   int M, N;          // logical output C[M, N] (N = output columns)
   int tiles_p, tiles_q, kb;
-  int dp_tiles;      // tiles done whole, round-robin over the grid
-  int sk_tiles;      // tiles after those, split by k-blocks over the first
-  int sk_ctas;       //   sk_ctas CTAs of the grid
+  int split;         // 1: persistent over tiles; S > 1: clusters of S CTAs
+                     //    split each tile's K range
   int group_p;       // raster: this many P tiles walk together
   void* C;
   long long ldc;     // elements
   const void* R;     // residual (EPI_RESIDUAL)
   long long ldr;
-  float* ws;         // sk_tiles x 128 x BN fp32 partial sums (zero at rest)
-  int* counters;     // sk_tiles arrival counters (zero at rest)
   int* err;          // device error word
   int vec_ok;        // C / R rows are 16-byte aligned for vector stores
 };
@@ -36,16 +33,13 @@ struct Plan {
   int bn;            // tile columns (Q extent)
   int grid;
   TcParams p;
-  size_t ws_bytes;   // partial-sum bytes + counter bytes needed
 };
 
-// Per-device state: SM count, the default split-K workspace and error word.
+// Per-device state: SM count and the device error word.
 struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
-  void* ws = nullptr;        // partial sums followed by counters, zeroed
-  size_t ws_bytes = 0;
-  int* err = nullptr;        // one int, zeroed
+  int* err = nullptr;        // device address of the error word
 };
 
 DeviceCtx* device_ctx(int device, cudaError_t* e);
@@ -54,10 +48,9 @@ bool device_ctx_ready(int device);
 // Fill the tiling / scheduling fields of a plan for the tcgen05 kernels.
 void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count);
 
-// Launch the tcgen05 GEMM described by pl.  ws points at pl.ws_bytes of
-// zero-filled memory (partials first, then counters).
+// Launch the tcgen05 GEMM described by pl.
 cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const void* W,
-                      void* ws, int* err, cudaStream_t stream, const char** why);
+                      int* err, cudaStream_t stream, const char** why);
 
 // CUDA-core GEMM for shapes the tcgen05 path can't take (K % 8 != 0,
 // unaligned rows).  Same epilogues and rounding.

@@ -44,7 +44,7 @@ _ALGOS = {
 
 __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
-    "pack_gate_up", "device_check", "workspace_size",
+    "pack_gate_up", "device_check",
 ]
 
 
@@ -112,23 +112,21 @@ def bf16_to_fp32(out: torch.Tensor, inp: torch.Tensor, n: int,
 
 def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
                 residual: Optional[torch.Tensor] = None, algo: str = "auto",
-                workspace: Optional[torch.Tensor] = None,
                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """out = epilogue(x · w^T) written into `out` (see include/orin_b200.h).
 
     x [M, K]; w [N, K] ([2N, K] packed gate/up for "swiglu"); out [M, N]
     (float32 for "f32" / "f32_partial", else x.dtype); residual [M, N].
     """
-    _need_cuda(out, x, w, residual, workspace)
+    _need_cuda(out, x, w, residual)
     dt = _dtype_code(x)
     if w.dtype != x.dtype or (residual is not None and residual.dtype != x.dtype):
         raise ValueError("x, w and residual must share one dtype")
     epi = _EPILOGUES[epilogue]
     M, K = x.shape
     N = out.shape[-1]
-    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(_lib.lib.orin_linear_ex(_ptr(out), _ptr(x), _ptr(w), M, N, K, dt, epi, _ptr(residual),
-                                  _ALGOS[algo], _ptr(workspace), ws_bytes, _stream(stream)))
+                                  _ALGOS[algo], _stream(stream)))
     return out
 
 
@@ -154,12 +152,6 @@ def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,
     check(_lib.lib.orin_pack_gate_up(_ptr(out), _ptr(w_gate), _ptr(w_up), IM, K,
                                      _dtype_code(w_gate), _stream(stream)))
     return out
-
-
-def workspace_size(M: int, N: int, K: int, dtype: torch.dtype, epilogue: str = "none",
-                   algo: str = "auto") -> int:
-    return int(_lib.lib.orin_linear_workspace_size(M, N, K, _DTYPES[dtype],
-                                                   _EPILOGUES[epilogue], _ALGOS[algo]))
 
 
 def device_check(stream: Optional[torch.cuda.Stream] = None) -> None:

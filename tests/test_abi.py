@@ -54,20 +54,20 @@ def test_linear_rejects_bad_arguments_on_host(kw, code):
     a = dict(C=16, A=32, W=48, M=4, N=128, K=64, dtype=_lib.F16, epi=_lib.EPI_NONE, R=0, algo=0)
     a.update(kw)
     st = _lib.lib.orin_linear_ex(a["C"], a["A"], a["W"], a["M"], a["N"], a["K"], a["dtype"],
-                                 a["epi"], a["R"], a["algo"], None, 0, None)
+                                 a["epi"], a["R"], a["algo"], None)
     assert st == code
     assert _lib.lib.orin_last_error()
 
 
 def test_skinny_algo_rejects_wide_m():
     st = _lib.lib.orin_linear_ex(16, 32, 48, 65, 128, 64, _lib.F16, 0, 0, _lib.ALGO_TC_SKINNY,
-                                 None, 0, None)
+                                 None)
     assert st == _lib.ERR_UNSUPPORTED
 
 
 def test_tc_algo_rejects_unaligned_k():
     st = _lib.lib.orin_linear_ex(16, 32, 48, 4, 128, 12, _lib.F16, 0, 0, _lib.ALGO_TC_WIDE,
-                                 None, 0, None)
+                                 None)
     assert st == _lib.ERR_UNSUPPORTED
 
 
@@ -91,14 +91,6 @@ def test_tp_rejects_bad_arguments():
     assert L.orin_tp_allreduce_f32(None, 16, 4, None) == _lib.ERR_INVALID_ARG
     assert L.orin_tp_linear_row(None, 16, 16, 16, 1, 1, 1, 0, None, None, None) == _lib.ERR_INVALID_ARG
     assert L.orin_tp_destroy(None) == _lib.OK
-
-
-def test_workspace_size_matches_plan():
-    # M=512 QKV projection: 4 x 10 tiles of 128x256, all split over the grid
-    sz = _lib.lib.orin_linear_workspace_size(512, 2560, 2048, _lib.F16, 0, 0)
-    assert sz == 40 * 128 * 256 * 4 + 40 * 4
-    # enough tiles for whole waves and an exact multiple of the grid: no workspace
-    assert _lib.lib.orin_linear_workspace_size(128 * 148, 256, 64, _lib.F16, 0, 1) == 0
 
 
 def test_python_mirror_rejects_cpu_tensors():

@@ -100,24 +100,6 @@ def test_output_guard_regions_untouched():
         assert (buf[:guard] == 1234.0).all() and (buf[guard + M * N:] == 1234.0).all()
 
 
-def test_caller_workspace_left_zeroed():
-    M, N, K = 512, 2560, 2048
-    need = ob.workspace_size(M, N, K, torch.float16)
-    assert need > 0
-    ws = torch.zeros(need // 4 + 64, dtype=torch.float32, device=DEV)
-    x = seeded((M, K), 1, 1.0)
-    w = seeded((N, K), 2, 0.02)
-    out = torch.empty((M, N), dtype=torch.float16, device=DEV)
-    for _ in range(2):
-        ob.linear_into(out, x.to(DEV), w.to(DEV), workspace=ws)
-        ob.device_check()
-        assert int(ws.count_nonzero()) == 0
-    ref = orc.linear(bits(x), bits(w), 0, "none")
-    assert_close(out.cpu().float(), from_bits(ref, torch.float16).float(), "caller workspace")
-    with pytest.raises(ob.OrinError):
-        ob.linear_into(out, x.to(DEV), w.to(DEV), workspace=ws[:16])
-
-
 def test_dependent_chain_with_programmatic_launch():
     """A chain of dependent GEMMs back to back (each kernel starts its weight
     loads before the previous one finishes) matches the oracle chain."""

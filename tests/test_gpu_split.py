@@ -1,0 +1,54 @@
+"""Every wide-tile plan — tile width 128/256, split-K 1..8 through thread-block
+clusters — against the oracle (B200 only).
+
+The plan is forced with the ORIN_TC_PLAN tuning override, which the library
+reads once per process, so each plan runs in its own subprocess."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,5", "128,8"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("plan", PLANS)
+def test_forced_plan_matches_oracle(plan):
+    env = dict(os.environ, ORIN_TC_PLAN=plan, PYTHONPATH=ROOT)
+    r = subprocess.run([sys.executable, os.path.abspath(__file__)], env=env, cwd=ROOT,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, f"plan {plan}:\n{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
+
+
+def _main() -> None:
+    import torch
+
+    import orininfer_b200 as ob
+    from oracle import oracle as orc
+    from tests._util import EXACT_MIN, assert_close, bits, from_bits, seeded
+
+    dev = torch.device("cuda:0")
+    cases = [(512, 2560, 2048, "none"), (200, 300, 520, "none"), (256, 640, 1024, "residual"),
+             (130, 704, 512, "swiglu"), (512, 1000, 2048, "f32"), (96, 512, 4096, "f32_partial")]
+    for dt in (0, 1):
+        tdt = torch.float16 if dt == 0 else torch.bfloat16
+        for i, (M, N, K, epi) in enumerate(cases):
+            wrows = 2 * N if epi == "swiglu" else N
+            x = seeded((M, K), 10 + i, 1.0, tdt)
+            w = seeded((wrows, K), 20 + i, 0.02, tdt)
+            r = seeded((M, N), 30 + i, 1.0, tdt) if epi == "residual" else None
+            y = ob.linear(x.to(dev), w.to(dev), epilogue=epi, algo="wide",
+                          residual=r.to(dev) if r is not None else None)
+            ob.device_check()
+            ref = orc.linear(bits(x), bits(w), dt, epi, bits(r) if r is not None else None)
+            ref_t = torch.from_numpy(ref) if epi in ("f32", "f32_partial") else from_bits(ref, tdt)
+            assert_close(y.cpu().float(), ref_t.float(),
+                         f"plan {os.environ.get('ORIN_TC_PLAN')} {epi} dt={dt} {M}x{N}x{K}",
+                         exact_min=None if epi == "f32_partial" else EXACT_MIN)
+    print("ok")
+
+
+if __name__ == "__main__":
+    _main()
