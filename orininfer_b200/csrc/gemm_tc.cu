@@ -347,147 +347,203 @@ __device__ __forceinline__ void cluster_sync_all() {
 template <int BN>
 __host__ __device__ constexpr int stage_pitch() { return BN + 4; }
 
-// Sum the S partial tiles of this cluster over rows [r0, r1) of the tile in
-// a fixed order (rank 0 .. S-1), apply the epilogue and store.  Threads map to
-// consecutive 4-column groups so global stores and residual loads coalesce.
+__device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Output one reduced 4-column group (row, col .. col+3) of the tile.
 template <int DT, int BN, int EPI, bool SWAP>
-__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int tp,
-                                            int tq, int r0, int r1, int et) {
+__device__ __forceinline__ void out_group(const TcParams& p, int tp, int tq, int row, int col,
+                                          const float4& a, const float4* up) {
   using E = Elem<DT>;
   using T = typename E::T;
-  constexpr int PITCH = stage_pitch<BN>();
   const bool vec = p.vec_ok != 0;
-  auto sum4 = [&](int row, int col) {
-    const uint32_t off = stage + static_cast<uint32_t>((row * PITCH + col) * 4);
-    float4 a = ld_dsmem_f4(mapa_shared(off, 0));
-    for (int r = 1; r < S; ++r) {
-      const float4 b = ld_dsmem_f4(mapa_shared(off, static_cast<uint32_t>(r)));
-      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-    }
-    return a;
-  };
   if constexpr (!SWAP) {
+    const int m = tp * kBM + row;
     if constexpr (EPI == EPI_SWIGLU) {
-      // gate 4-column groups: 16 per 128-column block
-      constexpr int G = BN / 8;
-      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
-        const int row = r0 + e / G;
-        const int gg = e % G;
-        const int gc = (gg / 16) * 128 + (gg % 16) * 4;
-        const float4 g = sum4(row, gc);
-        const float4 u = sum4(row, gc + 64);
-        const int m = tp * kBM + row;
-        const int n = (tq * BN) / 2 + (gg / 16) * 64 + (gg % 16) * 4;
-        if (m < p.M && n < p.N) {
-          float o[4] = {silu_f32(E::round(g.x)) * E::round(u.x), silu_f32(E::round(g.y)) * E::round(u.y),
-                        silu_f32(E::round(g.z)) * E::round(u.z), silu_f32(E::round(g.w)) * E::round(u.w)};
-          T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
-          if (vec && n + 4 <= p.N) {
-            *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
-          } else {
-            for (int j = 0; j < 4; ++j)
-              if (n + j < p.N) dst[j] = E::from_f(o[j]);
-          }
-        }
+      const int n = (tq * BN) / 2 + (col / 128) * 64 + (col % 128);
+      if (m >= p.M || n >= p.N) return;
+      const float4 u = *up;
+      float o[4] = {silu_f32(E::round(a.x)) * E::round(u.x), silu_f32(E::round(a.y)) * E::round(u.y),
+                    silu_f32(E::round(a.z)) * E::round(u.z), silu_f32(E::round(a.w)) * E::round(u.w)};
+      T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
+      if (vec && n + 4 <= p.N) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
+      } else {
+        for (int j = 0; j < 4; ++j)
+          if (n + j < p.N) dst[j] = E::from_f(o[j]);
       }
     } else {
-      constexpr int G = BN / 4;
-      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
-        const int row = r0 + e / G;
-        const int g = e % G;
-        const float4 a = sum4(row, 4 * g);
-        const int m = tp * kBM + row;
-        const int n = tq * BN + 4 * g;
-        if (m >= p.M || n >= p.N) continue;
-        float o[4] = {a.x, a.y, a.z, a.w};
-        const bool full = vec && n + 4 <= p.N;
-        if constexpr (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL) {
-          if constexpr (EPI == EPI_F32_OUT) {
+      const int n = tq * BN + col;
+      if (m >= p.M || n >= p.N) return;
+      float o[4] = {a.x, a.y, a.z, a.w};
+      const bool full = vec && n + 4 <= p.N;
+      if constexpr (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL) {
+        if constexpr (EPI == EPI_F32_OUT) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) o[j] = E::round(o[j]);
-          }
-          float* dst = static_cast<float*>(p.C) + m * p.ldc + n;
-          if (full) {
-            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-          } else {
-            for (int j = 0; j < 4; ++j)
-              if (n + j < p.N) dst[j] = o[j];
-          }
+          for (int j = 0; j < 4; ++j) o[j] = E::round(o[j]);
+        }
+        float* dst = static_cast<float*>(p.C) + m * p.ldc + n;
+        if (full) {
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
         } else {
-          if constexpr (EPI == EPI_RESIDUAL) {
-            const T* rs = static_cast<const T*>(p.R) + m * p.ldr + n;
-            if (full) {
-              const uint2 rv = *reinterpret_cast<const uint2*>(rs);
-              const float2 r01 = E::unpack2(rv.x), r23 = E::unpack2(rv.y);
-              o[0] = r01.x + E::round(o[0]);
-              o[1] = r01.y + E::round(o[1]);
-              o[2] = r23.x + E::round(o[2]);
-              o[3] = r23.y + E::round(o[3]);
-            } else {
-              for (int j = 0; j < 4; ++j)
-                if (n + j < p.N) o[j] = E::to_f(rs[j]) + E::round(o[j]);
-            }
-          }
-          T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
+          for (int j = 0; j < 4; ++j)
+            if (n + j < p.N) dst[j] = o[j];
+        }
+      } else {
+        if constexpr (EPI == EPI_RESIDUAL) {
+          const T* rs = static_cast<const T*>(p.R) + m * p.ldr + n;
           if (full) {
-            *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
+            const uint2 rv = *reinterpret_cast<const uint2*>(rs);
+            const float2 r01 = E::unpack2(rv.x), r23 = E::unpack2(rv.y);
+            o[0] = r01.x + E::round(o[0]);
+            o[1] = r01.y + E::round(o[1]);
+            o[2] = r23.x + E::round(o[2]);
+            o[3] = r23.y + E::round(o[3]);
           } else {
             for (int j = 0; j < 4; ++j)
-              if (n + j < p.N) dst[j] = E::from_f(o[j]);
+              if (n + j < p.N) o[j] = E::to_f(rs[j]) + E::round(o[j]);
           }
+        }
+        T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
+        if (full) {
+          *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
+        } else {
+          for (int j = 0; j < 4; ++j)
+            if (n + j < p.N) dst[j] = E::from_f(o[j]);
         }
       }
     }
   } else {
-    // Skinny: rows are weight rows (features), columns tokens.
-    constexpr int G = BN / 4;
+    // skinny: rows are weight rows (features), columns tokens
+    const float o[4] = {a.x, a.y, a.z, a.w};
     if constexpr (EPI == EPI_SWIGLU) {
-      // rows [0,64) gate, [64,128) up of features tp*64 + row; r0/r1 index
-      // gate rows here
-      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
-        const int row = r0 + e / G;
-        const int g = e % G;
-        const float4 gv = sum4(row, 4 * g);
-        const float4 uv = sum4(row + 64, 4 * g);
-        const int n = tp * 64 + row;
-        if (n >= p.N) continue;
-        const float go[4] = {gv.x, gv.y, gv.z, gv.w};
-        const float uo[4] = {uv.x, uv.y, uv.z, uv.w};
+      const int n = tp * 64 + row;
+      if (n >= p.N) return;
+      const float uo[4] = {up->x, up->y, up->z, up->w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = tq * BN + 4 * g + j;
-          if (m < p.M)
-            static_cast<T*>(p.C)[m * p.ldc + n] =
-                E::from_f(silu_f32(E::round(go[j])) * E::round(uo[j]));
-        }
+      for (int j = 0; j < 4; ++j) {
+        const int m = tq * BN + col + j;
+        if (m < p.M)
+          static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(silu_f32(E::round(o[j])) * E::round(uo[j]));
       }
     } else {
-      for (int e = et; e < (r1 - r0) * G; e += kEpiThreads) {
-        // consecutive threads take consecutive rows (features) so the
-        // stores of one token row coalesce
-        const int row = r0 + e % (r1 - r0);
-        const int g = e / (r1 - r0);
-        const float4 a = sum4(row, 4 * g);
-        const int n = tp * kBM + row;
-        if (n >= p.N) continue;
-        const float o[4] = {a.x, a.y, a.z, a.w};
+      const int n = tp * kBM + row;
+      if (n >= p.N) return;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = tq * BN + 4 * g + j;
-          if (m >= p.M) continue;
-          if constexpr (EPI == EPI_NONE) {
-            static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o[j]);
-          } else if constexpr (EPI == EPI_RESIDUAL) {
-            const float r = E::to_f(static_cast<const T*>(p.R)[m * p.ldr + n]);
-            static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(r + E::round(o[j]));
-          } else if constexpr (EPI == EPI_F32_OUT) {
-            static_cast<float*>(p.C)[m * p.ldc + n] = E::round(o[j]);
-          } else {
-            static_cast<float*>(p.C)[m * p.ldc + n] = o[j];
+      for (int j = 0; j < 4; ++j) {
+        const int m = tq * BN + col + j;
+        if (m >= p.M) continue;
+        if constexpr (EPI == EPI_NONE) {
+          static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o[j]);
+        } else if constexpr (EPI == EPI_RESIDUAL) {
+          const float r = E::to_f(static_cast<const T*>(p.R)[m * p.ldr + n]);
+          static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(r + E::round(o[j]));
+        } else if constexpr (EPI == EPI_F32_OUT) {
+          static_cast<float*>(p.C)[m * p.ldc + n] = E::round(o[j]);
+        } else {
+          static_cast<float*>(p.C)[m * p.ldc + n] = o[j];
+        }
+      }
+    }
+  }
+}
+
+// Sum the S partial tiles of this cluster over rows [r0, r1) of the tile, in
+// rank order 0..S-1 (deterministic), apply the epilogue and store.  Work item
+// = one 4-column group of one row (for SwiGLU: a gate group and its up group);
+// each thread issues the loads of U items from all S ranks before summing, so
+// up to 16 shared-memory loads (local or distributed) are in flight per thread.
+template <int DT, int BN, int EPI, bool SWAP, int S>
+__device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage, int tp, int tq,
+                                              int r0, int r1, int tid, int nthreads) {
+  constexpr int PITCH = stage_pitch<BN>();
+  constexpr bool PAIRS = (EPI == EPI_SWIGLU);
+  constexpr int LOADS = PAIRS ? 2 * S : S;
+  constexpr int U = (16 / LOADS) > 0 ? (16 / LOADS) : 1;
+  // items per row: 4-column groups (gate groups only for the wide SwiGLU)
+  constexpr int G = (PAIRS && !SWAP) ? BN / 8 : BN / 4;
+  const int rows = r1 - r0;
+  const int items = rows * G;
+  const uint32_t me = cluster_rank();
+  uint32_t base[S];
+#pragma unroll
+  for (int r = 0; r < S; ++r)
+    base[r] = (static_cast<uint32_t>(r) == me) ? stage : mapa_shared(stage, static_cast<uint32_t>(r));
+  for (int i0 = tid; i0 < items; i0 += nthreads * U) {
+    float4 v[U][LOADS];
+    int rowv[U], colv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = i0 + u * nthreads;
+      int row, col;
+      if constexpr (SWAP) {
+        // consecutive threads take consecutive rows (features): the stores
+        // of one token row then coalesce
+        row = r0 + e % rows;
+        col = 4 * (e / rows);
+      } else if constexpr (PAIRS) {
+        const int gg = e % G;
+        row = r0 + e / G;
+        col = (gg / 16) * 128 + (gg % 16) * 4;
+      } else {
+        row = r0 + e / G;
+        col = 4 * (e % G);
+      }
+      rowv[u] = row;
+      colv[u] = col;
+      if (e < items) {
+        const uint32_t off = static_cast<uint32_t>((row * PITCH + col) * 4);
+        // the up half: 64 columns right (wide) or 64 rows down (skinny)
+        const uint32_t off2 = SWAP ? off + static_cast<uint32_t>(64 * PITCH * 4) : off + 256u;
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+          const uint32_t a = base[r] + off;
+          v[u][r] = (static_cast<uint32_t>(r) == me) ? ld_smem_f4(a) : ld_dsmem_f4(a);
+          if constexpr (PAIRS) {
+            const uint32_t a2 = base[r] + off2;
+            v[u][S + r] = (static_cast<uint32_t>(r) == me) ? ld_smem_f4(a2) : ld_dsmem_f4(a2);
           }
         }
       }
     }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (i0 + u * nthreads >= items) continue;
+      float4 a = v[u][0];
+#pragma unroll
+      for (int r = 1; r < S; ++r) {
+        a.x += v[u][r].x; a.y += v[u][r].y; a.z += v[u][r].z; a.w += v[u][r].w;
+      }
+      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (PAIRS) {
+        b = v[u][S];
+#pragma unroll
+        for (int r = 1; r < S; ++r) {
+          b.x += v[u][S + r].x; b.y += v[u][S + r].y; b.z += v[u][S + r].z; b.w += v[u][S + r].w;
+        }
+      }
+      out_group<DT, BN, EPI, SWAP>(p, tp, tq, rowv[u], colv[u], a, &b);
+    }
+  }
+}
+
+template <int DT, int BN, int EPI, bool SWAP>
+__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int tp,
+                                            int tq, int r0, int r1, int tid, int nthreads) {
+  switch (S) {
+    case 2: reduce_rows_s<DT, BN, EPI, SWAP, 2>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    case 3: reduce_rows_s<DT, BN, EPI, SWAP, 3>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    case 4: reduce_rows_s<DT, BN, EPI, SWAP, 4>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    case 5: reduce_rows_s<DT, BN, EPI, SWAP, 5>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    case 6: reduce_rows_s<DT, BN, EPI, SWAP, 6>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    case 7: reduce_rows_s<DT, BN, EPI, SWAP, 7>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    default: reduce_rows_s<DT, BN, EPI, SWAP, 8>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
   }
 }
 
@@ -516,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ int split_coords[2];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -746,18 +803,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (S > 1) {
     // Every thread of every CTA of the cluster reaches both barriers exactly
     // once, on the normal and on the unwinding path.
-    cluster_sync_all();
-    if (warp >= 2) {
-      // this rank reduces rows [r0, r1) of the tile (gate rows only for the
-      // skinny SwiGLU, whose up rows sit 64 below)
-      const int r = static_cast<int>(cluster_rank());
-      const int rows = (SWAP && EPI == EPI_SWIGLU) ? 64 : kBM;
-      const int r0 = (r * rows) / S;
-      const int r1 = ((r + 1) * rows) / S;
-      if (!abort_flag)
-        reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_tp, split_tq, r0, r1,
-                                       static_cast<int>(threadIdx.x) - 64);
+    if (threadIdx.x == 64) {
+      split_coords[0] = split_tp;
+      split_coords[1] = split_tq;
     }
+    cluster_sync_all();
+    // this rank reduces rows [r0, r1) of the tile (gate rows only for the
+    // skinny SwiGLU, whose up rows sit 64 below), with all 192 threads
+    const int r = static_cast<int>(cluster_rank());
+    const int rows = (SWAP && EPI == EPI_SWIGLU) ? 64 : kBM;
+    const int r0 = (r * rows) / S;
+    const int r1 = ((r + 1) * rows) / S;
+    if (!abort_flag)
+      reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_coords[0], split_coords[1], r0, r1,
+                                     static_cast<int>(threadIdx.x), kThreads);
     cluster_sync_all();
   }
 
@@ -1052,10 +1111,11 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
       best_split = 1;
     }
     for (int s = 2; s <= 8 && s <= kb / 2; ++s) {
+      // split plans run as a single wave of clusters (a second wave would
+      // pay the per-CTA set-up and the reduction again)
       const int cap_clusters = cluster_cap(1, bn, s);
-      if (cap_clusters <= 0) continue;
-      const long long waves = (tiles + cap_clusters - 1) / cap_clusters;
-      cost = waves * (((kb + s - 1) / s) * kc + kFill) + kReduce * bn / 256.0;
+      if (cap_clusters <= 0 || tiles > cap_clusters) continue;
+      cost = (((kb + s - 1) / s) * kc + kFill) + kReduce * bn / 256.0;
       if (cost < best) {
         best = cost;
         best_bn = bn;
