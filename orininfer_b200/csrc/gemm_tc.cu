@@ -51,9 +51,14 @@ constexpr int kThreads = 192;  // 6 warps
 constexpr int kEpiThreads = 128;
 constexpr int kGroupP = 8;     // P tiles per raster group
 
-__host__ __device__ constexpr int tc_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
-__host__ __device__ constexpr int tc_stages(int bn) {
-  return (196608 / tc_stage_bytes(bn)) > 12 ? 12 : (196608 / tc_stage_bytes(bn));
+// Weight/token rows (Q operand) one CTA loads per stage: a CTA pair splits
+// them between its two CTAs.
+__host__ __device__ constexpr int tc_qrows(int bn, bool pair) { return pair ? bn / 2 : bn; }
+__host__ __device__ constexpr int tc_stage_bytes(int bn, bool pair) {
+  return kBM * kBK * 2 + tc_qrows(bn, pair) * kBK * 2;
+}
+__host__ __device__ constexpr int tc_stages(int bn, bool pair) {
+  return (196608 / tc_stage_bytes(bn, pair)) > 12 ? 12 : (196608 / tc_stage_bytes(bn, pair));
 }
 __host__ __device__ constexpr uint32_t tc_tmem_cols(int bn) {
   // two accumulator buffers of bn fp32 columns, rounded to a power of two >= 32
@@ -64,16 +69,17 @@ __host__ __device__ constexpr int tc_xch_bytes(int bn, int epi, bool swap) {
   // skinny SwiGLU: up-half rows hand their rounded values to gate-half rows
   return (swap && epi == EPI_SWIGLU) ? 64 * 32 * 4 : 0;
 }
-__host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap) {
-  return tc_stages(bn) * tc_stage_bytes(bn) + tc_xch_bytes(bn, epi, swap) + 1024;
+__host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap, bool pair) {
+  return tc_stages(bn, pair) * tc_stage_bytes(bn, pair) + tc_xch_bytes(bn, epi, swap) + 1024;
 }
 
 // ---------------------------------------------------------------------------
-// Work decomposition, computed identically by every role of a CTA.
-//   split == 1: persistent; CTA c takes tiles c, c + grid, c + 2*grid, ...
-//               over the full K range.
-//   split == S: one cluster of S CTAs per tile; cluster rank r takes k-blocks
-//               [r*kb/S, (r+1)*kb/S).
+// Work decomposition, computed identically by every role of a CTA.  A tile is
+// 128 (one CTA) or 256 (a CTA pair, tcgen05 cta_group::2) P rows by BN Q rows.
+//   split == 1: persistent; CTA group g takes tiles g, g + groups, ... over
+//               the full K range.
+//   split == S: one cluster of S groups per tile; group j takes k-blocks
+//               [j*kb/S, (j+1)*kb/S).
 // ---------------------------------------------------------------------------
 
 struct Unit {
@@ -88,21 +94,22 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 }
 
 struct UnitIter {
-  int tile, stride, tiles, k0, k1, kb;
-  __device__ __forceinline__ void init(const TcParams& p) {
-    kb = p.kb;
+  int tile, stride, tiles, k0, k1;
+  // group: CTAs that share one tile's accumulator (2 for a CTA pair)
+  __device__ __forceinline__ void init(const TcParams& p, int group) {
+    const int kb = p.kb;
     tiles = p.tiles_p * p.tiles_q;
     if (p.split == 1) {
-      tile = blockIdx.x;
-      stride = gridDim.x;
+      tile = blockIdx.x / group;
+      stride = gridDim.x / group;
       k0 = 0;
       k1 = kb;
     } else {
-      const int r = static_cast<int>(cluster_rank());
-      tile = blockIdx.x / p.split;
+      const int j = static_cast<int>(cluster_rank()) / group;
+      tile = blockIdx.x / (group * p.split);
       stride = tiles;  // one unit only
-      k0 = static_cast<int>((static_cast<long long>(r) * kb) / p.split);
-      k1 = static_cast<int>((static_cast<long long>(r + 1) * kb) / p.split);
+      k0 = static_cast<int>((static_cast<long long>(j) * kb) / p.split);
+      k1 = static_cast<int>((static_cast<long long>(j + 1) * kb) / p.split);
     }
   }
   __device__ __forceinline__ bool next(Unit& u) {
@@ -203,18 +210,18 @@ struct TmemChunks {
 // Apply the epilogue to one tile row held by this thread (row `lr` of the
 // tile) and store it.  Chunks come from `src` CW columns at a time.
 template <int DT, int BN, int EPI, bool SWAP, int CW, class Src>
-__device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int tp, int tq,
-                                          int lr, float* xch) {
+__device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int prow0,
+                                          int qcol0, int lr, float* xch) {
   using E = Elem<DT>;
   using T = typename E::T;
   const bool vec = p.vec_ok != 0;
   float v[32];
   if constexpr (!SWAP) {
-    const int m = tp * kBM + lr;
+    const int m = prow0 + lr;
     const bool mval = m < p.M;
     if constexpr (EPI == EPI_SWIGLU) {
       // Q columns are packed [gate 64 | up 64] groups; output column of the
-      // first gate column of group g is (tq*BN + 128g) / 2.
+      // first gate column of group g is (qcol0 + 128g) / 2.
       float u[32];
 #pragma unroll 1
       for (int g = 0; g < BN / 128; ++g) {
@@ -222,7 +229,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
         for (int h = 0; h < 64; h += 32) {
           src.get(128 * g + h, v);
           src.get(128 * g + 64 + h, u);
-          const int n = (tq * BN + 128 * g) / 2 + h;
+          const int n = (qcol0 + 128 * g) / 2 + h;
           if (mval && n < p.N) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -235,7 +242,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 #pragma unroll 1
       for (int c = 0; c < BN; c += CW) {
         src.get(c, v);
-        const int n = tq * BN + c;
+        const int n = qcol0 + c;
         if (mval && n < p.N) {
           const int valid = p.N - n;
           if constexpr (EPI == EPI_NONE) {
@@ -257,12 +264,12 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
       }
     }
   } else {
-    // Skinny: this thread's row is weight row (feature) tp*128 + lr; its
-    // columns are tokens tq*BN + c.
+    // Skinny: this thread's row is weight row (feature) prow0 + lr; its
+    // columns are tokens qcol0 + c.
     if constexpr (EPI == EPI_SWIGLU) {
       // Packed rows: lanes 0-63 gate, 64-127 up, of output features
-      // tp*64 + (lr % 64).
-      const int n = tp * 64 + (lr & 63);
+      // prow0/2 + (lr % 64).
+      const int n = prow0 / 2 + (lr & 63);
 #pragma unroll 1
       for (int c = 0; c < BN; c += CW) {
         src.get(c, v);
@@ -274,7 +281,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
         if (lr < 64 && n < p.N) {
 #pragma unroll
           for (int j = 0; j < CW; ++j) {
-            const int m = tq * BN + c + j;
+            const int m = qcol0 + c + j;
             if (m < p.M) {
               const float o = silu_f32(E::round(v[j])) * xch[lr * 32 + j];
               static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o);
@@ -284,7 +291,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
         named_bar_sync(1, kEpiThreads);
       }
     } else {
-      const int n = tp * kBM + lr;
+      const int n = prow0 + lr;
       const bool nval = n < p.N;
 #pragma unroll 1
       for (int c = 0; c < BN; c += CW) {
@@ -292,7 +299,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
         if (!nval) continue;
 #pragma unroll
         for (int j = 0; j < CW; ++j) {
-          const int m = tq * BN + c + j;
+          const int m = qcol0 + c + j;
           if (m < p.M) {
             if constexpr (EPI == EPI_NONE) {
               static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(v[j]);
@@ -314,12 +321,6 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 // ---------------------------------------------------------------------------
 // Cluster split-K: shared-memory staging and the DSMEM reduction
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
 
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
@@ -358,15 +359,15 @@ __device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
 
 // Output one reduced 4-column group (row, col .. col+3) of the tile.
 template <int DT, int BN, int EPI, bool SWAP>
-__device__ __forceinline__ void out_group(const TcParams& p, int tp, int tq, int row, int col,
+__device__ __forceinline__ void out_group(const TcParams& p, int prow0, int qcol0, int row, int col,
                                           const float4& a, const float4* up) {
   using E = Elem<DT>;
   using T = typename E::T;
   const bool vec = p.vec_ok != 0;
   if constexpr (!SWAP) {
-    const int m = tp * kBM + row;
+    const int m = prow0 + row;
     if constexpr (EPI == EPI_SWIGLU) {
-      const int n = (tq * BN) / 2 + (col / 128) * 64 + (col % 128);
+      const int n = qcol0 / 2 + (col / 128) * 64 + (col % 128);
       if (m >= p.M || n >= p.N) return;
       const float4 u = *up;
       float o[4] = {silu_f32(E::round(a.x)) * E::round(u.x), silu_f32(E::round(a.y)) * E::round(u.y),
@@ -379,7 +380,7 @@ __device__ __forceinline__ void out_group(const TcParams& p, int tp, int tq, int
           if (n + j < p.N) dst[j] = E::from_f(o[j]);
       }
     } else {
-      const int n = tq * BN + col;
+      const int n = qcol0 + col;
       if (m >= p.M || n >= p.N) return;
       float o[4] = {a.x, a.y, a.z, a.w};
       const bool full = vec && n + 4 <= p.N;
@@ -423,21 +424,21 @@ __device__ __forceinline__ void out_group(const TcParams& p, int tp, int tq, int
     // skinny: rows are weight rows (features), columns tokens
     const float o[4] = {a.x, a.y, a.z, a.w};
     if constexpr (EPI == EPI_SWIGLU) {
-      const int n = tp * 64 + row;
+      const int n = prow0 / 2 + row;
       if (n >= p.N) return;
       const float uo[4] = {up->x, up->y, up->z, up->w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int m = tq * BN + col + j;
+        const int m = qcol0 + col + j;
         if (m < p.M)
           static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(silu_f32(E::round(o[j])) * E::round(uo[j]));
       }
     } else {
-      const int n = tp * kBM + row;
+      const int n = prow0 + row;
       if (n >= p.N) return;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int m = tq * BN + col + j;
+        const int m = qcol0 + col + j;
         if (m >= p.M) continue;
         if constexpr (EPI == EPI_NONE) {
           static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o[j]);
@@ -460,8 +461,9 @@ __device__ __forceinline__ void out_group(const TcParams& p, int tp, int tq, int
 // each thread issues the loads of U items from all S ranks before summing, so
 // up to 16 shared-memory loads (local or distributed) are in flight per thread.
 template <int DT, int BN, int EPI, bool SWAP, int S>
-__device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage, int tp, int tq,
-                                              int r0, int r1, int tid, int nthreads) {
+__device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage, int prow0,
+                                              int qcol0, int r0, int r1, int tid, int nthreads,
+                                              uint32_t src0, uint32_t src_step) {
   constexpr int PITCH = stage_pitch<BN>();
   constexpr bool PAIRS = (EPI == EPI_SWIGLU);
   constexpr int LOADS = PAIRS ? 2 * S : S;
@@ -471,10 +473,15 @@ __device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage,
   const int rows = r1 - r0;
   const int items = rows * G;
   const uint32_t me = cluster_rank();
+  // the S partials of this CTA's rows live in cluster ranks src0 + r*src_step
   uint32_t base[S];
+  bool local[S];
 #pragma unroll
-  for (int r = 0; r < S; ++r)
-    base[r] = (static_cast<uint32_t>(r) == me) ? stage : mapa_shared(stage, static_cast<uint32_t>(r));
+  for (int r = 0; r < S; ++r) {
+    const uint32_t src = src0 + static_cast<uint32_t>(r) * src_step;
+    local[r] = (src == me);
+    base[r] = local[r] ? stage : mapa_shared(stage, src);
+  }
   for (int i0 = tid; i0 < items; i0 += nthreads * U) {
     float4 v[U][LOADS];
     int rowv[U], colv[U];
@@ -504,10 +511,10 @@ __device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage,
 #pragma unroll
         for (int r = 0; r < S; ++r) {
           const uint32_t a = base[r] + off;
-          v[u][r] = (static_cast<uint32_t>(r) == me) ? ld_smem_f4(a) : ld_dsmem_f4(a);
+          v[u][r] = local[r] ? ld_smem_f4(a) : ld_dsmem_f4(a);
           if constexpr (PAIRS) {
             const uint32_t a2 = base[r] + off2;
-            v[u][S + r] = (static_cast<uint32_t>(r) == me) ? ld_smem_f4(a2) : ld_dsmem_f4(a2);
+            v[u][S + r] = local[r] ? ld_smem_f4(a2) : ld_dsmem_f4(a2);
           }
         }
       }
@@ -528,38 +535,60 @@ __device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage,
           b.x += v[u][S + r].x; b.y += v[u][S + r].y; b.z += v[u][S + r].z; b.w += v[u][S + r].w;
         }
       }
-      out_group<DT, BN, EPI, SWAP>(p, tp, tq, rowv[u], colv[u], a, &b);
+      out_group<DT, BN, EPI, SWAP>(p, prow0, qcol0, rowv[u], colv[u], a, &b);
     }
   }
 }
 
 template <int DT, int BN, int EPI, bool SWAP>
-__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int tp,
-                                            int tq, int r0, int r1, int tid, int nthreads) {
+__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int prow0,
+                                            int qcol0, int r0, int r1, int tid, int nthreads,
+                                            uint32_t src0, uint32_t src_step) {
+#define ORIN_REDUCE_CASE(n)                                                                    \
+  case n:                                                                                      \
+    reduce_rows_s<DT, BN, EPI, SWAP, n>(p, stage, prow0, qcol0, r0, r1, tid, nthreads, src0,   \
+                                        src_step);                                             \
+    break;
   switch (S) {
-    case 2: reduce_rows_s<DT, BN, EPI, SWAP, 2>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    case 3: reduce_rows_s<DT, BN, EPI, SWAP, 3>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    case 4: reduce_rows_s<DT, BN, EPI, SWAP, 4>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    case 5: reduce_rows_s<DT, BN, EPI, SWAP, 5>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    case 6: reduce_rows_s<DT, BN, EPI, SWAP, 6>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    case 7: reduce_rows_s<DT, BN, EPI, SWAP, 7>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
-    default: reduce_rows_s<DT, BN, EPI, SWAP, 8>(p, stage, tp, tq, r0, r1, tid, nthreads); break;
+    ORIN_REDUCE_CASE(2)
+    ORIN_REDUCE_CASE(3)
+    ORIN_REDUCE_CASE(4)
+    ORIN_REDUCE_CASE(5)
+    ORIN_REDUCE_CASE(6)
+    ORIN_REDUCE_CASE(7)
+    default:
+      reduce_rows_s<DT, BN, EPI, SWAP, 8>(p, stage, prow0, qcol0, r0, r1, tid, nthreads, src0,
+                                          src_step);
+      break;
   }
+#undef ORIN_REDUCE_CASE
 }
 
 // ---------------------------------------------------------------------------
 // The kernel
+//
+// PAIR (wide tiles only): the CTAs of cluster ranks 2i and 2i+1 form a
+// tcgen05 CTA pair.  Each loads its own 128 A rows and half of the tile's B
+// rows; both signal the leader's (even rank) full barrier.  The leader's MMA
+// warp issues M=256 cta_group::2 MMAs, and its commits arrive on the empty
+// and accumulator-full barriers of both CTAs (one commit per barrier).  Each
+// CTA's epilogue reads its own 128 accumulator rows and releases the buffer on
+// the leader's accumulator-empty barrier.
 // ---------------------------------------------------------------------------
 
-template <int DT, int BN, int EPI, bool SWAP>
+template <int DT, int BN, int EPI, bool SWAP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tm_p,
                      const __grid_constant__ CUtensorMap tm_q, const TcParams p) {
-  constexpr int STAGES = tc_stages(BN);
+  static_assert(!(PAIR && SWAP), "CTA pairs are used for wide tiles only");
+  constexpr int GROUP = PAIR ? 2 : 1;         // CTAs per tile accumulator
+  constexpr int TILE_P = GROUP * kBM;         // P rows per tile
+  constexpr int QR = tc_qrows(BN, PAIR);      // Q rows this CTA loads per stage
+  constexpr int STAGES = tc_stages(BN, PAIR);
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
-  constexpr uint32_t STAGE_BYTES = tc_stage_bytes(BN);
+  constexpr uint32_t STAGE_BYTES = tc_stage_bytes(BN, PAIR);
   constexpr uint32_t TMEM_COLS = tc_tmem_cols(BN);
-  constexpr uint32_t IDESC = instr_desc_f16(DT, kBM, BN);
+  constexpr uint32_t IDESC = instr_desc_f16(DT, TILE_P, BN);
   constexpr int CW = (BN >= 32) ? 32 : 16;
   static_assert(kBM * stage_pitch<BN>() * 4 <= STAGES * STAGE_BYTES,
                 "split-K staging tile must fit in the operand ring");
@@ -579,6 +608,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t ring = (smem_u32(dsmem) + 1023u) & ~1023u;
   float* xch = reinterpret_cast<float*>(dsmem + (ring - smem_u32(dsmem)) + STAGES * STAGE_BYTES);
   const int S = p.split;
+  const bool clustered = PAIR || S > 1;
+  const uint32_t crank = clustered ? cluster_rank() : 0u;
+  const int half = PAIR ? static_cast<int>(crank & 1u) : 0;  // which 128 rows of the tile
+  const bool leader = (half == 0);
+  const uint32_t lead_rank = crank & ~1u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -587,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull_bar[b]), 1);
-      mbar_init(smem_u32(&tempty_bar[b]), kEpiThreads / 32);
+      mbar_init(smem_u32(&tempty_bar[b]), GROUP * (kEpiThreads / 32));
     }
     mbar_init(smem_u32(&drain_bar), 1);
     abort_flag = 0;
@@ -598,17 +632,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_q);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&tmem_slot), TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(&tmem_slot), TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(&tmem_slot), TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // the pair signals each other's barriers: both must be initialised first
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   pdl_launch_dependents();
 
   // split mode: this CTA's one tile (for the reduction after the roles)
-  int split_tp = 0, split_tq = 0;
+  int split_prow = 0, split_qcol = 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -621,6 +662,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const void* tm_x = SWAP ? static_cast<const void*>(&tm_q) : static_cast<const void*>(&tm_p);
       const uint32_t off_w = SWAP ? 0u : A_BYTES;
       const uint32_t off_x = SWAP ? A_BYTES : 0u;
+      auto full_addr = [&](int st) -> uint32_t {
+        const uint32_t a = smem_u32(&full_bar[st]);
+        return PAIR ? mapa_shared(a, lead_rank) : a;
+      };
+      auto load = [&](uint32_t dst, const void* tm, uint32_t bar, int c0, int c1, uint64_t pol) {
+        if constexpr (PAIR) tma_load_2d_pair(dst, tm, bar, c0, c1, pol);
+        else tma_load_2d(dst, tm, bar, c0, c1, pol);
+      };
       int pend_k[STAGES], pend_row[STAGES];
       uint32_t arm_par[STAGES];
       int n_issued = 0;
@@ -628,21 +677,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       UnitIter it;
-      it.init(p);
+      it.init(p, GROUP);
       Unit u;
       bool ok = true;
       while (ok && it.next(u)) {
         int tp, tq;
         tile_coords(u.tile, p, tp, tq);
-        const int row_w = SWAP ? tp * kBM : tq * BN;
-        const int row_x = SWAP ? tq * BN : tp * kBM;
+        const int row_w = SWAP ? tp * kBM : tq * BN + half * QR;
+        const int row_x = SWAP ? tq * BN : tp * TILE_P + half * kBM;
         for (int k = u.k0; k < u.k1; ++k) {
           if (n_issued >= STAGES) {
             if (!waited) {
               pdl_wait();
               for (int i = 0; i < STAGES; ++i)
-                tma_load_2d(ring + i * STAGE_BYTES + off_x, tm_x, smem_u32(&full_bar[i]),
-                            pend_k[i] * kBK, pend_row[i], pol_x);
+                load(ring + i * STAGE_BYTES + off_x, tm_x, full_addr(i), pend_k[i] * kBK,
+                     pend_row[i], pol_x);
               waited = true;
             }
             if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag, p.err,
@@ -652,12 +701,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const uint32_t sbase = ring + stage * STAGE_BYTES;
-          const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t fb = full_addr(stage);
+          // the pair leader expects both CTAs' bytes on its own barrier
+          if (leader) mbar_arrive_expect_tx(smem_u32(&full_bar[stage]), GROUP * STAGE_BYTES);
           arm_par[stage] = phase;
-          tma_load_2d(sbase + off_w, tm_w, fb, k * kBK, row_w, pol_w);
+          load(sbase + off_w, tm_w, fb, k * kBK, row_w, pol_w);
           if (waited) {
-            tma_load_2d(sbase + off_x, tm_x, fb, k * kBK, row_x, pol_x);
+            load(sbase + off_x, tm_x, fb, k * kBK, row_x, pol_x);
           } else {
             pend_k[stage] = k;
             pend_row[stage] = row_x;
@@ -673,32 +723,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();
         const int n = n_issued < STAGES ? n_issued : STAGES;
         for (int i = 0; i < n; ++i)
-          tma_load_2d(ring + i * STAGE_BYTES + off_x, tm_x, smem_u32(&full_bar[i]),
-                      pend_k[i] * kBK, pend_row[i], pol_x);
+          load(ring + i * STAGE_BYTES + off_x, tm_x, full_addr(i), pend_k[i] * kBK, pend_row[i],
+               pol_x);
       }
       if (!ok) {
         // Unwinding: let copies already in flight land before the CTA exits.
-        const int n = n_issued < STAGES ? n_issued : STAGES;
-        for (int i = 0; i < n; ++i) {
-          const unsigned long long t0 = global_timer_ns();
-          while (!mbar_try_wait(smem_u32(&full_bar[i]), arm_par[i])) {
-            if (global_timer_ns() - t0 > 100000000ull) {
-              atomicCAS(p.err, 0, DEVERR_TIMEOUT_DRAIN);
-              break;
+        if (leader) {
+          const int n = n_issued < STAGES ? n_issued : STAGES;
+          for (int i = 0; i < n; ++i) {
+            const unsigned long long t0 = global_timer_ns();
+            while (!mbar_try_wait(smem_u32(&full_bar[i]), arm_par[i])) {
+              if (global_timer_ns() - t0 > 100000000ull) {
+                atomicCAS(p.err, 0, DEVERR_TIMEOUT_DRAIN);
+                break;
+              }
             }
+          }
+        } else {
+          // the peer's copies complete on the leader's barriers: give them
+          // time to land
+          const unsigned long long t0 = global_timer_ns();
+          while (global_timer_ns() - t0 < 2000000ull) {
           }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
+      const uint32_t peer = crank ^ 1u;
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          tc_commit_pair(smem_u32(bar));
+          tc_commit_pair(mapa_shared(smem_u32(bar), peer));
+        } else {
+          tc_commit(smem_u32(bar));
+        }
+      };
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       UnitIter it;
-      it.init(p);
+      it.init(p, GROUP);
       Unit u;
       bool ok = true;
       while (ok && it.next(u)) {
@@ -722,16 +789,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
             const uint64_t ad = smem_desc_kmajor_sw128(a_addr + kk * kUmmaK * 2);
             const uint64_t bd = smem_desc_kmajor_sw128(b_addr + kk * kUmmaK * 2);
-            tc_mma_f16(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR) tc_mma_f16_pair(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
+            else tc_mma_f16(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(smem_u32(&empty_bar[stage]));
+          commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(smem_u32(&tfull_bar[acc]));
+        commit(&tfull_bar[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -739,7 +807,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         // Make sure no MMA is still writing tensor memory before teardown.
-        tc_commit(smem_u32(&drain_bar));
+        if constexpr (PAIR) tc_commit_pair(smem_u32(&drain_bar));
+        else tc_commit(smem_u32(&drain_bar));
         const unsigned long long t0 = global_timer_ns();
         while (!mbar_try_wait(smem_u32(&drain_bar), 0)) {
           if (global_timer_ns() - t0 > 100000000ull) {
@@ -754,10 +823,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     const int quad = warp & 3;  // tcgen05.ld: warp w reaches lanes 32*(w%4)..+31
     const int lr = quad * 32 + lane;
+    const uint32_t lead_tempty0 =
+        PAIR ? mapa_shared(smem_u32(&tempty_bar[0]), lead_rank) : smem_u32(&tempty_bar[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
     UnitIter it;
-    it.init(p);
+    it.init(p, GROUP);
     Unit u;
     while (it.next(u)) {
       const bool failed = !mbar_wait_bounded(smem_u32(&tfull_bar[acc]), acc_phase, &abort_flag,
@@ -768,16 +839,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int tp, tq;
       tile_coords(u.tile, p, tp, tq);
+      const int prow0 = SWAP ? tp * kBM : tp * TILE_P + half * kBM;
+      const int qcol0 = tq * BN;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       if (S == 1) {
         TmemChunks<CW> src{taddr};
-        emit_tile<DT, BN, EPI, SWAP, CW>(p, src, tp, tq, lr, xch);
+        emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
       } else {
         // Stage this CTA's fp32 partial tile in its own shared memory (the
         // operand ring is idle: every load was consumed by the finished MMAs).
-        split_tp = tp;
-        split_tq = tq;
+        split_prow = prow0;
+        split_qcol = qcol0;
         fence_proxy_async_smem();
         const uint32_t row_addr = ring + static_cast<uint32_t>(lr * stage_pitch<BN>() * 4);
         float v[32];
@@ -792,7 +865,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+      if (lane == 0) {
+        const uint32_t te = lead_tempty0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
+        if (PAIR && !leader) mbar_arrive_cluster(te);
+        else mbar_arrive(te);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -804,19 +881,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every thread of every CTA of the cluster reaches both barriers exactly
     // once, on the normal and on the unwinding path.
     if (threadIdx.x == 64) {
-      split_coords[0] = split_tp;
-      split_coords[1] = split_tq;
+      split_coords[0] = split_prow;
+      split_coords[1] = split_qcol;
     }
     cluster_sync_all();
-    // this rank reduces rows [r0, r1) of the tile (gate rows only for the
-    // skinny SwiGLU, whose up rows sit 64 below), with all 192 threads
-    const int r = static_cast<int>(cluster_rank());
+    // this CTA reduces rows [r0, r1) of its 128 (gate rows only for the
+    // skinny SwiGLU, whose up rows sit 64 below), with all 192 threads; the
+    // partials of these rows are in the CTAs with the same pair half
+    const int j = static_cast<int>(crank) / GROUP;
     const int rows = (SWAP && EPI == EPI_SWIGLU) ? 64 : kBM;
-    const int r0 = (r * rows) / S;
-    const int r1 = ((r + 1) * rows) / S;
+    const int r0 = (j * rows) / S;
+    const int r1 = ((j + 1) * rows) / S;
     if (!abort_flag)
       reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_coords[0], split_coords[1], r0, r1,
-                                     static_cast<int>(threadIdx.x), kThreads);
+                                     static_cast<int>(threadIdx.x), kThreads,
+                                     static_cast<uint32_t>(half), static_cast<uint32_t>(GROUP));
+    cluster_sync_all();
+  } else if constexpr (PAIR) {
+    // neither CTA of the pair may leave while the other can still signal it
     cluster_sync_all();
   }
 
@@ -825,7 +907,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -905,11 +988,11 @@ bool make_tmap(CUtensorMap* out, const void* ptr, int dt, unsigned long long row
   return true;
 }
 
-template <int DT, int BN, int EPI, bool SWAP>
+template <int DT, int BN, int EPI, bool SWAP, bool PAIR>
 cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap& tq,
                        cudaStream_t stream) {
-  constexpr int smem = tc_smem_bytes(BN, EPI, SWAP);
-  auto kern = tc_linear_kernel<DT, BN, EPI, SWAP>;
+  constexpr int smem = tc_smem_bytes(BN, EPI, SWAP, PAIR);
+  auto kern = tc_linear_kernel<DT, BN, EPI, SWAP, PAIR>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -918,6 +1001,7 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
+  const int cluster = (PAIR ? 2 : 1) * pl.p.split;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(kThreads);
@@ -927,9 +1011,9 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   int na = 1;
-  if (pl.p.split > 1) {
+  if (cluster > 1) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = pl.p.split;
+    attr[1].val.clusterDim.x = cluster;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     na = 2;
@@ -939,20 +1023,20 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   return cudaLaunchKernelEx(&cfg, kern, tp, tq, pl.p);
 }
 
-// How many clusters of `split` CTAs of this tile shape can be resident at
+// How many clusters of `cluster` CTAs of this tile shape can be resident at
 // once (all epilogues of one shape use the same shared memory).
-template <int BN, bool SWAP>
-int max_active_clusters(int split) {
-  constexpr int smem = tc_smem_bytes(BN, EPI_NONE, SWAP);
-  auto kern = tc_linear_kernel<DT_F16, BN, EPI_NONE, SWAP>;
+template <int BN, bool SWAP, bool PAIR>
+int max_active_clusters(int cluster) {
+  constexpr int smem = tc_smem_bytes(BN, EPI_NONE, SWAP, PAIR);
+  auto kern = tc_linear_kernel<DT_F16, BN, EPI_NONE, SWAP, PAIR>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(split * 64);
+  cfg.gridDim = dim3(cluster * 64);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.x = cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
@@ -965,15 +1049,15 @@ int max_active_clusters(int split) {
   return n;
 }
 
-template <int DT, bool SWAP, int BN>
+template <int DT, bool SWAP, int BN, bool PAIR>
 cudaError_t dispatch_epi(const Plan& pl, int epi, const CUtensorMap& a, const CUtensorMap& b,
                          cudaStream_t s) {
   switch (epi) {
-    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP>(pl, a, b, s);
-    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP>(pl, a, b, s);
-    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP>(pl, a, b, s);
-    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP>(pl, a, b, s);
-    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP>(pl, a, b, s);
+    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP, PAIR>(pl, a, b, s);
+    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP, PAIR>(pl, a, b, s);
+    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP, PAIR>(pl, a, b, s);
+    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP, PAIR>(pl, a, b, s);
+    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP, PAIR>(pl, a, b, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -982,29 +1066,31 @@ template <int DT>
 cudaError_t dispatch_shape(const Plan& pl, int epi, const CUtensorMap& a, const CUtensorMap& b,
                            cudaStream_t s) {
   if (pl.algo == 1) {
-    if (pl.bn == 128) return dispatch_epi<DT, false, 128>(pl, epi, a, b, s);
-    return dispatch_epi<DT, false, 256>(pl, epi, a, b, s);
+    if (pl.pair) return dispatch_epi<DT, false, 256, true>(pl, epi, a, b, s);
+    if (pl.bn == 128) return dispatch_epi<DT, false, 128, false>(pl, epi, a, b, s);
+    return dispatch_epi<DT, false, 256, false>(pl, epi, a, b, s);
   }
   switch (pl.bn) {
-    case 16: return dispatch_epi<DT, true, 16>(pl, epi, a, b, s);
-    case 32: return dispatch_epi<DT, true, 32>(pl, epi, a, b, s);
-    case 64: return dispatch_epi<DT, true, 64>(pl, epi, a, b, s);
+    case 16: return dispatch_epi<DT, true, 16, false>(pl, epi, a, b, s);
+    case 32: return dispatch_epi<DT, true, 32, false>(pl, epi, a, b, s);
+    case 64: return dispatch_epi<DT, true, 64, false>(pl, epi, a, b, s);
   }
   return cudaErrorInvalidValue;
 }
 
-// Per-device cache of resident-cluster counts: [shape][split].
+// Per-device cache of resident-cluster counts: [shape][cluster size].
 struct ClusterCaps {
   int dev = -1;
-  int caps[5][9];  // shapes: wide 256, wide 128, skinny 16, 32, 64
+  int caps[6][9];  // shapes: wide 256, wide 128, skinny 16, 32, 64, wide 256 pair
 };
 
-int shape_index(int algo, int bn) {
-  if (algo == 1) return bn == 256 ? 0 : 1;
+int shape_index(int algo, int bn, int pair) {
+  if (algo == 1) return pair ? 5 : (bn == 256 ? 0 : 1);
   return bn == 16 ? 2 : bn == 32 ? 3 : 4;
 }
 
-int cluster_cap(int algo, int bn, int split) {
+int cluster_cap(int algo, int bn, int pair, int cluster) {
+  if (cluster < 1 || cluster > 8) return 0;
   thread_local ClusterCaps cache[8];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1014,55 +1100,71 @@ int cluster_cap(int algo, int bn, int split) {
     for (auto& row : c.caps)
       for (int& v : row) v = -1;
   }
-  int& v = c.caps[shape_index(algo, bn)][split];
+  int& v = c.caps[shape_index(algo, bn, pair)][cluster];
   if (v < 0) {
     if (algo == 1)
-      v = (bn == 256) ? max_active_clusters<256, false>(split)
-                      : max_active_clusters<128, false>(split);
+      v = pair ? max_active_clusters<256, false, true>(cluster)
+               : (bn == 256) ? max_active_clusters<256, false, false>(cluster)
+                             : max_active_clusters<128, false, false>(cluster);
     else
-      v = (bn == 16) ? max_active_clusters<16, true>(split)
-                     : (bn == 32) ? max_active_clusters<32, true>(split)
-                                  : max_active_clusters<64, true>(split);
+      v = (bn == 16) ? max_active_clusters<16, true, false>(cluster)
+                     : (bn == 32) ? max_active_clusters<32, true, false>(cluster)
+                                  : max_active_clusters<64, true, false>(cluster);
   }
   return v;
 }
 
-// Optional tuning override "BN,SPLIT" for wide tiles (ORIN_TC_PLAN).
-bool plan_override(int& bn, int& split) {
-  static int o_bn = -1, o_split = -1;
+// Optional tuning override "BN,SPLIT[,PAIR]" for wide tiles (ORIN_TC_PLAN).
+bool plan_override(int& bn, int& split, int& pair) {
+  static int o_bn = -1, o_split = -1, o_pair = 0;
   static bool read = false;
   if (!read) {
     read = true;
     const char* e = getenv("ORIN_TC_PLAN");
-    if (e && sscanf(e, "%d,%d", &o_bn, &o_split) != 2) o_bn = o_split = -1;
+    if (e) {
+      const int n = sscanf(e, "%d,%d,%d", &o_bn, &o_split, &o_pair);
+      if (n < 2) o_bn = -1;
+      if (n < 3) o_pair = 0;
+    }
     if (o_bn != 128 && o_bn != 256) o_bn = -1;
     if (o_split < 1 || o_split > 8) o_bn = -1;
+    if (o_pair && (o_bn != 256 || o_split > 4)) o_bn = -1;
   }
   if (o_bn < 0) return false;
   bn = o_bn;
   split = o_split;
+  pair = o_pair;
   return true;
 }
 
 }  // namespace
 
-void fill_tiles(Plan& pl, int M, int wrows, int K, int bn, int split, int sm_count) {
+void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
   TcParams& p = pl.p;
+  const int tile_p = pair ? 2 * kBM : kBM;
+  const int group = pair ? 2 : 1;
   pl.bn = bn;
-  p.tiles_p = (p.P + kBM - 1) / kBM;
+  pl.pair = pair;
+  p.tiles_p = (p.P + tile_p - 1) / tile_p;
   p.tiles_q = (p.Q + bn - 1) / bn;
   p.kb = (K + kBK - 1) / kBK;
   p.group_p = kGroupP;
   p.split = split;
   const int tiles = p.tiles_p * p.tiles_q;
-  pl.grid = (split == 1) ? (tiles < sm_count ? tiles : sm_count) : tiles * split;
-  (void)M;
-  (void)wrows;
+  if (split == 1) {
+    const int groups = sm_count / group;
+    pl.grid = group * (tiles < groups ? tiles : groups);
+  } else {
+    pl.grid = tiles * split * group;
+  }
 }
 
-// Choose the tile width and the split-K factor.  Cost unit: one 64-deep
-// k-block of a 128x256 tile on one SM.  A split of S runs as clusters of S
-// CTAs; its partial tiles are combined through distributed shared memory.
+// Choose the tile shape and the split-K factor.  Cost unit: the time one SM
+// needs for a 64-deep k-block of a 128x256 tile at full tensor rate; the
+// per-k-block factors below reflect how close each shape gets to that rate
+// (one CTA with 256-wide tiles is bounded by its L2->shared bandwidth; a CTA
+// pair loads a third less per SM).  A split of S runs as clusters whose
+// partial tiles are combined through distributed shared memory.
 void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   const int wrows = (epi == EPI_SWIGLU) ? 2 * N : N;  // rows of W
   TcParams& p = pl.p;
@@ -1084,46 +1186,53 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
       split = G / tiles;
       if (split > 8) split = 8;
       if (split > kb / 2) split = kb / 2 > 0 ? kb / 2 : 1;
-      while (split > 1 && cluster_cap(2, bn, split) <= 0) --split;
+      while (split > 1 && cluster_cap(2, bn, 0, split) <= 0) --split;
     }
-    fill_tiles(pl, M, wrows, K, bn, split, G);
+    fill_tiles(pl, K, bn, split, 0, G);
     return;
   }
   p.P = M;
   p.Q = wrows;
-  int obn = 0, osplit = 0;
-  if (plan_override(obn, osplit) && !(epi == EPI_SWIGLU && obn % 128)) {
-    fill_tiles(pl, M, wrows, K, obn, osplit > kb ? kb : osplit, G);
+  int obn = 0, osplit = 0, opair = 0;
+  if (plan_override(obn, osplit, opair) && !(epi == EPI_SWIGLU && obn % 128)) {
+    fill_tiles(pl, K, obn, osplit > kb ? kb : osplit, opair, G);
     return;
   }
   const double kFill = 2.5, kReduce = 4.0;
+  struct Shape { int bn, pair; double kc; };
+  const Shape shapes[3] = {{256, 1, 1.1}, {256, 0, 1.35}, {128, 0, 0.75}};
   double best = 1e30;
-  int best_bn = 256, best_split = 1;
-  for (int bn : {256, 128}) {
-    const double kc = (bn == 256) ? 1.0 : 0.55;
-    const long long tiles = static_cast<long long>((M + kBM - 1) / kBM) * ((wrows + bn - 1) / bn);
+  int best_bn = 256, best_split = 1, best_pair = 0;
+  for (const Shape& sh : shapes) {
+    const int tile_p = sh.pair ? 2 * kBM : kBM;
+    const int group = sh.pair ? 2 : 1;
+    const long long tiles =
+        static_cast<long long>((M + tile_p - 1) / tile_p) * ((wrows + sh.bn - 1) / sh.bn);
     // persistent, whole K per tile
-    const long long waves1 = (tiles + G - 1) / G;
-    double cost = waves1 * (kb * kc + kFill);
+    const int groups = G / group;
+    const long long waves1 = (tiles + groups - 1) / groups;
+    double cost = waves1 * (kb * sh.kc + kFill);
     if (cost < best) {
       best = cost;
-      best_bn = bn;
+      best_bn = sh.bn;
       best_split = 1;
+      best_pair = sh.pair;
     }
-    for (int s = 2; s <= 8 && s <= kb / 2; ++s) {
+    for (int s = 2; s * group <= 8 && s <= kb / 2; ++s) {
       // split plans run as a single wave of clusters (a second wave would
       // pay the per-CTA set-up and the reduction again)
-      const int cap_clusters = cluster_cap(1, bn, s);
+      const int cap_clusters = cluster_cap(1, sh.bn, sh.pair, s * group);
       if (cap_clusters <= 0 || tiles > cap_clusters) continue;
-      cost = (((kb + s - 1) / s) * kc + kFill) + kReduce * bn / 256.0;
+      cost = (((kb + s - 1) / s) * sh.kc + kFill) + kReduce * sh.bn / 256.0;
       if (cost < best) {
         best = cost;
-        best_bn = bn;
+        best_bn = sh.bn;
         best_split = s;
+        best_pair = sh.pair;
       }
     }
   }
-  fill_tiles(pl, M, wrows, K, best_bn, best_split, G);
+  fill_tiles(pl, K, best_bn, best_split, best_pair, G);
 }
 
 cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const void* W,
@@ -1137,7 +1246,7 @@ cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const 
   if (!make_tmap(&tmp, pptr, dtype, static_cast<unsigned long long>(p.P),
                  static_cast<unsigned long long>(p.K), kBM) ||
       !make_tmap(&tmq, qptr, dtype, static_cast<unsigned long long>(p.Q),
-                 static_cast<unsigned long long>(p.K), pl.bn)) {
+                 static_cast<unsigned long long>(p.K), tc_qrows(pl.bn, pl.pair != 0))) {
     if (why) *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }

@@ -31,6 +31,7 @@ struct TcParams {
 struct Plan {
   int algo;          // 1 wide, 2 skinny, 3 simt
   int bn;            // tile columns (Q extent)
+  int pair;          // 1: tiles of 256 P rows on tcgen05 CTA pairs
   int grid;
   TcParams p;
 };

@@ -1,5 +1,6 @@
-"""Every wide-tile plan — tile width 128/256, split-K 1..8 through thread-block
-clusters — against the oracle (B200 only).
+"""Every wide-tile plan — tile width 128/256, one CTA or a tcgen05 CTA pair
+per tile, split-K 1..8 through thread-block clusters — against the oracle
+(B200 only).
 
 The plan is forced with the ORIN_TC_PLAN tuning override, which the library
 reads once per process, so each plan runs in its own subprocess."""
@@ -10,7 +11,10 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,5", "128,8"]
+# "BN,SPLIT" = one CTA per 128-row tile; "BN,SPLIT,1" = tcgen05 CTA pairs
+# (256-row tiles); SPLIT > 1 = k-split over a thread-block cluster
+PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,5", "128,8",
+         "256,1,1", "256,2,1", "256,3,1", "256,4,1"]
 
 
 @pytest.mark.gpu
