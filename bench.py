@@ -415,6 +415,12 @@ def cpu_baseline_layer(budget_s: float = 10.0) -> dict:
                       f"{dt:.1f} s"}
 
 
+def ob_plan(M_, N_, K_, epi):
+    import orininfer_b200 as ob
+    p = ob.kernels.plan_info(M_, N_, K_, torch.float16, epi)
+    return f"{p['kernel']} {'pair ' if p['cta_pair'] else ''}{p['tile_cols']}-wide split{p['split_k']} grid{p['grid']}"
+
+
 def run_ours(args, rank, world, local_rank):
     import orininfer_b200  # noqa: F401  (fails loudly if the CUDA library is missing)
     from orininfer_b200 import tp
@@ -482,6 +488,8 @@ def run_ours(args, rank, world, local_rank):
             "avg_launch_ms": round(avg_ms, 5),
         }
         line["kernels_ms"] = {k: round(v, 5) for k, v in kt.items()}
+        line["kernels_plan"] = {
+            k: ob_plan(M, n, kk, epi) for k, (n, kk, epi) in GEMMS.items()}
         if bar is not None:
             line["cublas_bar"] = bar
         line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}

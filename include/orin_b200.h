@@ -102,6 +102,16 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W,
                            const void* residual, int algo, void* stream);
 
 /*
+ * Diagnostics: the launch orin_linear_ex would make for this problem on the
+ * current device.  info[0] kernel (1 tcgen05 wide tiles, 2 tcgen05 skinny
+ * tiles, 3 CUDA cores), info[1] tile columns, info[2] 1 if tiles run on
+ * tcgen05 CTA pairs, info[3] split-K factor (cluster split), info[4] grid
+ * size (CTAs), info[5] number of tiles.  Assumes 16-byte aligned operands.
+ */
+orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int algo,
+                           int info[6]);
+
+/*
  * Build the packed gate/up weight the SWIGLU epilogue reads:
  * rows [128g, 128g+64) = gate rows [64g, 64g+64), rows [128g+64, 128g+128) =
  * up rows [64g, 64g+64).  w_gate, w_up [IM, K] (include/weight_store.h:17-18);

@@ -182,6 +182,37 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   return ORIN_OK;
 }
 
+orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int algo, int info[6]) {
+  orin_status st = check_common(dtype, epilogue);
+  if (st != ORIN_OK) return st;
+  if (!info || M < 1 || N < 1 || K < 1) {
+    set_error("orin_plan_info: bad arguments");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  static const char probe[16] __attribute__((aligned(16))) = {0};
+  const int a = choose_algo(algo, probe, probe, M, K);
+  if (a < 0) {
+    set_error("orin_plan_info: algo %d can't take M=%d K=%d", algo, M, K);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  for (int i = 0; i < 6; ++i) info[i] = 0;
+  info[0] = a;
+  if (a == 3) return ORIN_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = device_ctx(dev, &e);
+  if (!ctx) return cuda_fail(e, "orin_plan_info: device set-up");
+  Plan pl;
+  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count);
+  info[1] = pl.bn;
+  info[2] = pl.pair;
+  info[3] = pl.p.split;
+  info[4] = pl.grid;
+  info[5] = pl.p.tiles_p * pl.p.tiles_q;
+  return ORIN_OK;
+}
+
 orin_status orin_linear(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epilogue, const void* residual, void* stream) {
   return orin_linear_ex(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, stream);

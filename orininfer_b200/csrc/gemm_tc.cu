@@ -57,8 +57,11 @@ __host__ __device__ constexpr int tc_qrows(int bn, bool pair) { return pair ? bn
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool pair) {
   return kBM * kBK * 2 + tc_qrows(bn, pair) * kBK * 2;
 }
+// Stages come in pairs: the MMA issuer waits once per pair of stages (one
+// barrier wait costs about as much as issuing a stage's MMAs).
 __host__ __device__ constexpr int tc_stages(int bn, bool pair) {
-  return (196608 / tc_stage_bytes(bn, pair)) > 12 ? 12 : (196608 / tc_stage_bytes(bn, pair));
+  return ((196608 / tc_stage_bytes(bn, pair)) > 12 ? 12 : (196608 / tc_stage_bytes(bn, pair))) &
+         ~1;
 }
 __host__ __device__ constexpr uint32_t tc_tmem_cols(int bn) {
   // two accumulator buffers of bn fp32 columns, rounded to a power of two >= 32
@@ -69,8 +72,13 @@ __host__ __device__ constexpr int tc_xch_bytes(int bn, int epi, bool swap) {
   // skinny SwiGLU: up-half rows hand their rounded values to gate-half rows
   return (swap && epi == EPI_SWIGLU) ? 64 * 32 * 4 : 0;
 }
+// Wide tiles stage their output in two 16 KB buffers (128 rows x 128 bytes,
+// 128-byte swizzle) for TMA stores.
+constexpr int kOutBuf = 128 * 128;
+__host__ __device__ constexpr int tc_out_bytes(bool swap) { return swap ? 0 : 2 * kOutBuf; }
 __host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap, bool pair) {
-  return tc_stages(bn, pair) * tc_stage_bytes(bn, pair) + tc_xch_bytes(bn, epi, swap) + 1024;
+  return tc_stages(bn, pair) * tc_stage_bytes(bn, pair) + tc_xch_bytes(bn, epi, swap) +
+         tc_out_bytes(swap) + 1024;
 }
 
 // ---------------------------------------------------------------------------
@@ -78,8 +86,10 @@ __host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap, bool
 // 128 (one CTA) or 256 (a CTA pair, tcgen05 cta_group::2) P rows by BN Q rows.
 //   split == 1: persistent; CTA group g takes tiles g, g + groups, ... over
 //               the full K range.
-//   split == S: one cluster of S groups per tile; group j takes k-blocks
-//               [j*kb/S, (j+1)*kb/S).
+//   split == S: one cluster of S groups per tile; group j takes a range of
+//               whole k-block pairs.
+// The k-block count kb is rounded up to even (a trailing block past K is
+// zero-filled by TMA), so stage pairs never straddle two tiles.
 // ---------------------------------------------------------------------------
 
 struct Unit {
@@ -105,11 +115,13 @@ struct UnitIter {
       k0 = 0;
       k1 = kb;
     } else {
+      // k ranges are whole pairs of k-blocks (kb is even)
       const int j = static_cast<int>(cluster_rank()) / group;
+      const int kp = kb / 2;
       tile = blockIdx.x / (group * p.split);
       stride = tiles;  // one unit only
-      k0 = static_cast<int>((static_cast<long long>(j) * kb) / p.split);
-      k1 = static_cast<int>((static_cast<long long>(j + 1) * kb) / p.split);
+      k0 = 2 * static_cast<int>((static_cast<long long>(j) * kp) / p.split);
+      k1 = 2 * static_cast<int>((static_cast<long long>(j + 1) * kp) / p.split);
     }
   }
   __device__ __forceinline__ bool next(Unit& u) {
@@ -319,12 +331,12 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 }
 
 // ---------------------------------------------------------------------------
-// Cluster split-K: shared-memory staging and the DSMEM reduction
+// Epilogue through TMA stores (wide tiles)
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+__device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
   float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(addr)
                : "memory");
@@ -337,6 +349,296 @@ __device__ __forceinline__ void st_smem_f4(uint32_t addr, float a, float b, floa
                : "memory");
 }
 
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled buffer
+// (the layout TMA reads and writes with CU_TENSOR_MAP_SWIZZLE_128B).
+__device__ __forceinline__ uint32_t sw128(int r, int j) {
+  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// One thread of the 128 epilogue threads waits (bounded) on `bar`; the rest
+// park on a named barrier instead of polling.  Returns false on timeout, in
+// every thread.
+__device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, int et,
+                                         volatile int* abort_flag, int* err, volatile int* flag) {
+  if (et == 0) *flag = mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE) ? 1 : 0;
+  named_bar_sync(1, kEpiThreads);
+  return *flag != 0;
+}
+
+// Store one tile held in tensor memory: for each 128-byte-wide chunk of
+// output columns, every thread writes its row into a swizzled staging buffer
+// and one thread issues the TMA store.  The residual chunk, if any, is first
+// TMA-loaded into the same buffer.  Rows and columns outside C are clipped by
+// the TMA unit.
+template <int DT, int BN, int EPI>
+__device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr, int prow0,
+                                              int qcol0, int lr, int et, uint32_t outbuf,
+                                              int& obuf, const void* tm_c, const void* tm_r,
+                                              uint32_t res_bar, uint32_t& res_phase,
+                                              volatile int* abort_flag, volatile int* flag) {
+  using E = Elem<DT>;
+  constexpr bool F32 = (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL);
+  constexpr int CH = F32 ? 32 : 64;  // output columns per 128-byte chunk
+  constexpr int OUT_COLS = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  constexpr int NCH = OUT_COLS / CH;
+  const int ocol0 = (EPI == EPI_SWIGLU) ? qcol0 / 2 : qcol0;
+#pragma unroll 1
+  for (int oc = 0; oc < NCH; ++oc) {
+    const uint32_t buf = outbuf + static_cast<uint32_t>(obuf * kOutBuf);
+    const int ocol = ocol0 + oc * CH;
+    // the store that last used this buffer must have read it
+    if (et == 0) bulk_wait_group_read<1>();
+    if constexpr (EPI == EPI_RESIDUAL) {
+      if (et == 0) {
+        mbar_arrive_expect_tx(res_bar, kOutBuf);
+        tma_load_2d_plain(buf, tm_r, res_bar, ocol, prow0);
+      }
+    }
+    named_bar_sync(1, kEpiThreads);
+    if constexpr (EPI == EPI_RESIDUAL) {
+      if (!epi_wait(res_bar, res_phase, et, abort_flag, p.err, flag)) return false;
+      res_phase ^= 1u;
+    }
+    if constexpr (F32) {
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + oc * 32, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) o[t] = (EPI == EPI_F32_OUT) ? E::round(v[4 * j + t]) : v[4 * j + t];
+        st_smem_f4(buf + sw128(lr, j), o[0], o[1], o[2], o[3]);
+      }
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+        if constexpr (EPI == EPI_SWIGLU) {
+          // output chunk oc <- packed group oc: gate cols [128oc, 128oc+64), up +64
+          float u[32];
+          tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
+          tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = silu_f32(E::round(v[j])) * E::round(u[j]);
+        } else {
+          tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t a = buf + sw128(lr, 4 * h + j);
+          if constexpr (EPI == EPI_RESIDUAL) {
+            uint4 r;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                         : "r"(a));
+            float2 f;
+            f = E::unpack2(r.x); v[8 * j + 0] = f.x + E::round(v[8 * j + 0]); v[8 * j + 1] = f.y + E::round(v[8 * j + 1]);
+            f = E::unpack2(r.y); v[8 * j + 2] = f.x + E::round(v[8 * j + 2]); v[8 * j + 3] = f.y + E::round(v[8 * j + 3]);
+            f = E::unpack2(r.z); v[8 * j + 4] = f.x + E::round(v[8 * j + 4]); v[8 * j + 5] = f.y + E::round(v[8 * j + 5]);
+            f = E::unpack2(r.w); v[8 * j + 6] = f.x + E::round(v[8 * j + 6]); v[8 * j + 7] = f.y + E::round(v[8 * j + 7]);
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                       "r"(E::pack2(v[8 * j + 0], v[8 * j + 1])), "r"(E::pack2(v[8 * j + 2], v[8 * j + 3])),
+                       "r"(E::pack2(v[8 * j + 4], v[8 * j + 5])), "r"(E::pack2(v[8 * j + 6], v[8 * j + 7]))
+                       : "memory");
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1, kEpiThreads);
+    if (et == 0) {
+      tma_store_2d(tm_c, buf, ocol, prow0);
+      bulk_commit_group();
+    }
+    obuf ^= 1;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Cluster split-K for wide tiles.  The S CTAs of a tile own consecutive blocks
+// of column units (unit = 32 accumulator columns; SwiGLU: a 32-column gate
+// chunk with its up chunk 64 columns to the right).  Each CTA
+//   1. stages the units it does not own, grouped by owner, in its own shared
+//      memory (rows of 128-byte segments, 16-byte chunks XOR-swizzled by row);
+//   2. after a cluster barrier, sends each owner its block with one bulk copy
+//      into the owner's receive slot (DMA engine, completion counted on the
+//      owner's mbarrier, armed with the expected bytes beforehand);
+//   3. sums, for the units it owns, its own part (re-read from tensor memory)
+//      and then the S-1 received parts in rank order (a fixed order:
+//      deterministic), applies the epilogue, stores.
+// Shared memory (the idle operand ring): the staging blocks first, then the
+// S-1 receive slots.
+// ---------------------------------------------------------------------------
+
+template <int BN, int EPI>
+__host__ __device__ constexpr int split_units() { return EPI == EPI_SWIGLU ? BN / 64 : BN / 32; }
+template <int EPI>
+__host__ __device__ constexpr int unit_cols() { return EPI == EPI_SWIGLU ? 64 : 32; }
+// accumulator column of unit u's first half (its second half is +64 for SwiGLU)
+template <int EPI>
+__device__ __forceinline__ int unit_col(int u) {
+  return EPI == EPI_SWIGLU ? (u / 2) * 128 + (u % 2) * 32 : u * 32;
+}
+__host__ __device__ constexpr int owner_first_unit(int j, int units, int S) {
+  // owner of unit u is (u*S)/units; this is the first u with owner j
+  return (j * units + S - 1) / S;
+}
+__host__ __device__ constexpr int owner_units(int j, int units, int S) {
+  return owner_first_unit(j + 1, units, S) - owner_first_unit(j, units, S);
+}
+// Shared memory a split of S needs (bytes): staging of the units a CTA does
+// not own plus S-1 receive slots, maximised over the cluster ranks.
+__host__ __device__ constexpr int split_smem_bytes(int units, int ucols, int S) {
+  int worst = 0;
+  for (int j = 0; j < S; ++j) {
+    const int own = owner_units(j, units, S);
+    const int b = ((units - own) + (S - 1) * own) * 128 * ucols * 4;
+    worst = b > worst ? b : worst;
+  }
+  return worst;
+}
+
+// 16-byte chunk c of row r in a block whose rows are `segs` 128-byte segments
+__device__ __forceinline__ uint32_t blk_off(int r, int c, int segs) {
+  return static_cast<uint32_t>(r * segs * 128 + ((c & ~7) << 4) + (((c & 7) ^ (r & 7)) << 4));
+}
+
+template <int DT, int BN, int EPI>
+__device__ __forceinline__ void stage_unowned(uint32_t ring, uint32_t taddr, int lr, int S, int j) {
+  constexpr int U = split_units<BN, EPI>();
+  constexpr int UC = unit_cols<EPI>();
+  uint32_t base = ring;
+#pragma unroll 1
+  for (int o = 0; o < S; ++o) {
+    const int n_o = owner_units(o, U, S);
+    if (o == j) continue;
+    const int u0 = owner_first_unit(o, U, S);
+    const int segs = n_o * UC / 32;  // 128-byte segments per row
+#pragma unroll 1
+    for (int ui = 0; ui < n_o; ++ui) {
+      const int c = unit_col<EPI>(u0 + ui);
+#pragma unroll
+      for (int part = 0; part < UC / 32; ++part) {
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + c + part * 64, v);
+        const int chunk0 = (ui * UC + part * 32) / 4;  // first 16-byte chunk in the row
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          st_smem_f4(base + blk_off(lr, chunk0 + i, segs), v[4 * i], v[4 * i + 1], v[4 * i + 2],
+                     v[4 * i + 3]);
+      }
+    }
+    base += static_cast<uint32_t>(128 * n_o * UC * 4);
+  }
+}
+
+// Byte offset of the receive slots in the ring of owner j.
+template <int BN, int EPI>
+__device__ __forceinline__ uint32_t recv_base(int S, int j) {
+  constexpr int U = split_units<BN, EPI>();
+  constexpr int UC = unit_cols<EPI>();
+  return static_cast<uint32_t>((U - owner_units(j, U, S)) * 128 * UC * 4);
+}
+
+// One thread: send every other owner its staged block.
+template <int BN, int EPI>
+__device__ __forceinline__ void send_blocks(uint32_t ring, uint32_t recv_bar_local, int S, int j,
+                                            int half, int group) {
+  constexpr int U = split_units<BN, EPI>();
+  constexpr int UC = unit_cols<EPI>();
+  uint32_t src = ring;
+#pragma unroll 1
+  for (int o = 0; o < S; ++o) {
+    const int n_o = owner_units(o, U, S);
+    if (o == j) continue;
+    const uint32_t bytes = static_cast<uint32_t>(128 * n_o * UC * 4);
+    const int slot = (j < o) ? j : j - 1;  // my slot at owner o
+    const uint32_t rank = static_cast<uint32_t>(half + o * group);
+    const uint32_t dst = mapa_shared(ring + recv_base<BN, EPI>(S, o) + slot * bytes, rank);
+    bulk_copy_s2cluster(dst, src, bytes, mapa_shared(recv_bar_local, rank));
+    src += bytes;
+  }
+}
+
+template <int DT, int BN, int EPI>
+__device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring, uint32_t taddr,
+                                                int lr, int S, int j, int prow0, int qcol0) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int U = split_units<BN, EPI>();
+  constexpr int UC = unit_cols<EPI>();
+  const int u0 = owner_first_unit(j, U, S);
+  const int n_j = owner_units(j, U, S);
+  const int segs = n_j * UC / 32;
+  const uint32_t slots = ring + recv_base<BN, EPI>(S, j);
+  const uint32_t slot_bytes = static_cast<uint32_t>(128 * n_j * UC * 4);
+  const int m = prow0 + lr;
+  const bool vec = p.vec_ok != 0;
+#pragma unroll 1
+  for (int ui = 0; ui < n_j; ++ui) {
+    const int u = u0 + ui;
+    const int c = unit_col<EPI>(u);
+    float v[32], w[32];
+    tmem_ld_32x32b_x32(taddr + c, v);
+    if constexpr (EPI == EPI_SWIGLU) tmem_ld_32x32b_x32(taddr + c + 64, w);
+#pragma unroll 1
+    for (int sl = 0; sl < S - 1; ++sl) {
+      const uint32_t sb = slots + sl * slot_bytes;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 a = ld_smem_f4(sb + blk_off(lr, (ui * UC) / 4 + i, segs));
+        v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
+        if constexpr (EPI == EPI_SWIGLU) {
+          const float4 b = ld_smem_f4(sb + blk_off(lr, (ui * UC + 32) / 4 + i, segs));
+          w[4 * i] += b.x; w[4 * i + 1] += b.y; w[4 * i + 2] += b.z; w[4 * i + 3] += b.w;
+        }
+      }
+    }
+    if (m >= p.M) continue;
+    if constexpr (EPI == EPI_SWIGLU) {
+      const int n = qcol0 / 2 + (u / 2) * 64 + (u % 2) * 32;
+      if (n >= p.N) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = silu_f32(E::round(v[i])) * E::round(w[i]);
+      store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, p.N - n, vec);
+    } else {
+      const int n = qcol0 + c;
+      if (n >= p.N) continue;
+      const int valid = p.N - n;
+      if constexpr (EPI == EPI_NONE) {
+        store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        float r[32];
+        load16_row<DT>(static_cast<const T*>(p.R) + m * p.ldr + n, r, 32, valid, vec);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = r[i] + E::round(v[i]);
+        store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
+      } else if constexpr (EPI == EPI_F32_OUT) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = E::round(v[i]);
+        store32f_row(static_cast<float*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
+      } else {
+        store32f_row(static_cast<float*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Cluster split-K: shared-memory staging and the DSMEM reduction
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+
 // All threads of all CTAs of the cluster; release/acquire orders the shared
 // memory writes before it with the remote reads after it.
 __device__ __forceinline__ void cluster_sync_all() {
@@ -347,15 +649,6 @@ __device__ __forceinline__ void cluster_sync_all() {
 // writes of a warp (32 rows) on distinct banks.
 template <int BN>
 __host__ __device__ constexpr int stage_pitch() { return BN + 4; }
-
-__device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 
 // Output one reduced 4-column group (row, col .. col+3) of the tile.
 template <int DT, int BN, int EPI, bool SWAP>
@@ -579,7 +872,9 @@ __device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, i
 template <int DT, int BN, int EPI, bool SWAP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tm_p,
-                     const __grid_constant__ CUtensorMap tm_q, const TcParams p) {
+                     const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_c,
+                     const __grid_constant__ CUtensorMap tm_r, const TcParams p) {
   static_assert(!(PAIR && SWAP), "CTA pairs are used for wide tiles only");
   constexpr int GROUP = PAIR ? 2 : 1;         // CTAs per tile accumulator
   constexpr int TILE_P = GROUP * kBM;         // P rows per tile
@@ -594,19 +889,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 "split-K staging tile must fit in the operand ring");
 
   extern __shared__ uint8_t dsmem[];
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  constexpr int PAIRS = STAGES / 2;
+  static_assert(STAGES % 2 == 0, "stages come in pairs");
+  __shared__ __align__(8) uint64_t full_bar[PAIRS];  // one per pair of stages
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
   __shared__ __align__(8) uint64_t tfull_bar[2];
   __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(8) uint64_t res_bar;
+  __shared__ __align__(8) uint64_t recv_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ volatile int epi_flag;
   __shared__ int split_coords[2];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t ring = (smem_u32(dsmem) + 1023u) & ~1023u;
   float* xch = reinterpret_cast<float*>(dsmem + (ring - smem_u32(dsmem)) + STAGES * STAGE_BYTES);
+  // output staging (wide tiles): 1024-aligned, after the ring
+  const uint32_t outbuf = ring + STAGES * STAGE_BYTES;
   const int S = p.split;
   const bool clustered = PAIR || S > 1;
   const uint32_t crank = clustered ? cluster_rank() : 0u;
@@ -615,21 +917,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t lead_rank = crank & ~1u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), 1);
-      mbar_init(smem_u32(&empty_bar[s]), 1);
-    }
+    for (int s = 0; s < PAIRS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&empty_bar[s]), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull_bar[b]), 1);
       mbar_init(smem_u32(&tempty_bar[b]), GROUP * (kEpiThreads / 32));
     }
     mbar_init(smem_u32(&drain_bar), 1);
+    mbar_init(smem_u32(&res_bar), 1);
+    mbar_init(smem_u32(&recv_bar), 1);
     abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_p);
     tma_prefetch_desc(&tm_q);
+    if (!SWAP && p.out_tma) {
+      tma_prefetch_desc(&tm_c);
+      if (EPI == EPI_RESIDUAL) tma_prefetch_desc(&tm_r);
+    }
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -662,8 +968,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const void* tm_x = SWAP ? static_cast<const void*>(&tm_q) : static_cast<const void*>(&tm_p);
       const uint32_t off_w = SWAP ? 0u : A_BYTES;
       const uint32_t off_x = SWAP ? A_BYTES : 0u;
+      // stage st completes on the barrier of its stage pair
       auto full_addr = [&](int st) -> uint32_t {
-        const uint32_t a = smem_u32(&full_bar[st]);
+        const uint32_t a = smem_u32(&full_bar[st >> 1]);
         return PAIR ? mapa_shared(a, lead_rank) : a;
       };
       auto load = [&](uint32_t dst, const void* tm, uint32_t bar, int c0, int c1, uint64_t pol) {
@@ -671,7 +978,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else tma_load_2d(dst, tm, bar, c0, c1, pol);
       };
       int pend_k[STAGES], pend_row[STAGES];
-      uint32_t arm_par[STAGES];
+      uint32_t arm_par[PAIRS];
       int n_issued = 0;
       bool waited = false;
       int stage = 0;
@@ -702,9 +1009,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t sbase = ring + stage * STAGE_BYTES;
           const uint32_t fb = full_addr(stage);
-          // the pair leader expects both CTAs' bytes on its own barrier
-          if (leader) mbar_arrive_expect_tx(smem_u32(&full_bar[stage]), GROUP * STAGE_BYTES);
-          arm_par[stage] = phase;
+          // the first stage of a pair arms the pair's barrier with the bytes
+          // of both stages (of both CTAs of a CTA pair, on the leader's)
+          if ((stage & 1) == 0) {
+            if (leader) mbar_arrive_expect_tx(smem_u32(&full_bar[stage >> 1]), 2 * GROUP * STAGE_BYTES);
+            arm_par[stage >> 1] = phase;
+          }
           load(sbase + off_w, tm_w, fb, k * kBK, row_w, pol_w);
           if (waited) {
             load(sbase + off_x, tm_x, fb, k * kBK, row_x, pol_x);
@@ -729,7 +1039,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         // Unwinding: let copies already in flight land before the CTA exits.
         if (leader) {
-          const int n = n_issued < STAGES ? n_issued : STAGES;
+          const int n = (n_issued < STAGES ? n_issued : STAGES) / 2;
           for (int i = 0; i < n; ++i) {
             const unsigned long long t0 = global_timer_ns();
             while (!mbar_try_wait(smem_u32(&full_bar[i]), arm_par[i])) {
@@ -764,6 +1074,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      const uint64_t desc0 = smem_desc_kmajor_sw128(ring);
       UnitIter it;
       it.init(p, GROUP);
       Unit u;
@@ -776,24 +1087,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int k = u.k0; k < u.k1; ++k) {
-          if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase, &abort_flag, p.err,
+        for (int k = u.k0; k < u.k1; k += 2) {
+          // one wait covers two stages (stage is even here)
+          if (!mbar_wait_bounded(smem_u32(&full_bar[stage >> 1]), phase, &abort_flag, p.err,
                                  DEVERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = ring + stage * STAGE_BYTES;
-          const uint32_t b_addr = a_addr + A_BYTES;
+          // descriptors differ from the ring's first one only in the start
+          // address field (bits 0-13, address >> 4), which never carries
+          const uint64_t sd = desc0 + static_cast<uint64_t>((stage * STAGE_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-            const uint64_t ad = smem_desc_kmajor_sw128(a_addr + kk * kUmmaK * 2);
-            const uint64_t bd = smem_desc_kmajor_sw128(b_addr + kk * kUmmaK * 2);
-            if constexpr (PAIR) tc_mma_f16_pair(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
-            else tc_mma_f16(d, ad, bd, IDESC, (k > u.k0 || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+              const uint64_t ad = sd + static_cast<uint64_t>((h * STAGE_BYTES + kk * kUmmaK * 2) >> 4);
+              const uint64_t bd = ad + static_cast<uint64_t>(A_BYTES >> 4);
+              const uint32_t accum = (k + h > u.k0 || kk > 0) ? 1u : 0u;
+              if constexpr (PAIR) tc_mma_f16_pair(d, ad, bd, IDESC, accum);
+              else tc_mma_f16(d, ad, bd, IDESC, accum);
+            }
+            commit(&empty_bar[stage + h]);
           }
-          commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
+          stage += 2;
+          if (stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -823,19 +1141,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     const int quad = warp & 3;  // tcgen05.ld: warp w reaches lanes 32*(w%4)..+31
     const int lr = quad * 32 + lane;
+    const int et = static_cast<int>(threadIdx.x) - 64;  // 0..127
     const uint32_t lead_tempty0 =
         PAIR ? mapa_shared(smem_u32(&tempty_bar[0]), lead_rank) : smem_u32(&tempty_bar[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
+    int obuf = 0;
+    uint32_t res_phase = 0;
     UnitIter it;
     it.init(p, GROUP);
     Unit u;
     while (it.next(u)) {
-      const bool failed = !mbar_wait_bounded(smem_u32(&tfull_bar[acc]), acc_phase, &abort_flag,
-                                             p.err, DEVERR_TIMEOUT_EPILOGUE);
-      // all 128 epilogue threads leave together (the epilogue uses named
-      // barriers, which a thread that left early would never reach)
-      if (named_bar_or(1, kEpiThreads, failed)) break;
+      // one thread waits for the accumulator, the others sleep on a named
+      // barrier (no polling next to the MMA issuer)
+      if (!epi_wait(smem_u32(&tfull_bar[acc]), acc_phase, et, &abort_flag, p.err, &epi_flag)) break;
       tc_fence_after();
       int tp, tq;
       tile_coords(u.tile, p, tp, tq);
@@ -843,60 +1162,115 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qcol0 = tq * BN;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      bool ok = true;
       if (S == 1) {
-        TmemChunks<CW> src{taddr};
-        emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
+        if constexpr (!SWAP) {
+          if (p.out_tma) {
+            ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, obuf, &tm_c,
+                                            &tm_r, smem_u32(&res_bar), res_phase, &abort_flag,
+                                            &epi_flag);
+          } else {
+            TmemChunks<CW> src{taddr};
+            emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
+          }
+        } else {
+          TmemChunks<CW> src{taddr};
+          emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
+        }
       } else {
-        // Stage this CTA's fp32 partial tile in its own shared memory (the
-        // operand ring is idle: every load was consumed by the finished MMAs).
         split_prow = prow0;
         split_qcol = qcol0;
-        fence_proxy_async_smem();
-        const uint32_t row_addr = ring + static_cast<uint32_t>(lr * stage_pitch<BN>() * 4);
-        float v[32];
+        if constexpr (SWAP) {
+          // Stage this CTA's fp32 partial tile in its own shared memory (the
+          // operand ring is idle: every load was consumed by the finished MMAs).
+          fence_proxy_async_smem();
+          const uint32_t row_addr = ring + static_cast<uint32_t>(lr * stage_pitch<BN>() * 4);
+          float v[32];
 #pragma unroll 1
-        for (int c = 0; c < BN; c += CW) {
-          if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + c, v);
-          else tmem_ld_32x32b_x16(taddr + c, v);
+          for (int c = 0; c < BN; c += CW) {
+            if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + c, v);
+            else tmem_ld_32x32b_x16(taddr + c, v);
 #pragma unroll
-          for (int i = 0; i < CW; i += 4)
-            st_smem_f4(row_addr + (c + i) * 4, v[i], v[i + 1], v[i + 2], v[i + 3]);
+            for (int i = 0; i < CW; i += 4)
+              st_smem_f4(row_addr + (c + i) * 4, v[i], v[i + 1], v[i + 2], v[i + 3]);
+          }
+        }
+        if constexpr (!SWAP) {
+          // wide tiles: stage the column units other CTAs own (this CTA's
+          // ring is idle: its MMAs are done)
+          fence_proxy_async_smem();
+          stage_unowned<DT, BN, EPI>(ring, taddr, lr, S, static_cast<int>(crank) / GROUP);
+          fence_proxy_async_smem();
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        const uint32_t te = lead_tempty0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
-        if (PAIR && !leader) mbar_arrive_cluster(te);
-        else mbar_arrive(te);
+      if (!ok) break;
+      if (S == 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t te = lead_tempty0 + static_cast<uint32_t>(acc * sizeof(uint64_t));
+          if (PAIR && !leader) mbar_arrive_cluster(te);
+          else mbar_arrive(te);
+        }
       }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    // every TMA store of this CTA has finished before it exits
+    if (et == 0) bulk_wait_group<0>();
   }
 
   if (S > 1) {
-    // Every thread of every CTA of the cluster reaches both barriers exactly
-    // once, on the normal and on the unwinding path.
+    // Every thread of every CTA of the cluster reaches each cluster barrier
+    // exactly once, on the normal and on the unwinding path.
     if (threadIdx.x == 64) {
       split_coords[0] = split_prow;
       split_coords[1] = split_qcol;
     }
-    cluster_sync_all();
-    // this CTA reduces rows [r0, r1) of its 128 (gate rows only for the
-    // skinny SwiGLU, whose up rows sit 64 below), with all 192 threads; the
-    // partials of these rows are in the CTAs with the same pair half
-    const int j = static_cast<int>(crank) / GROUP;
-    const int rows = (SWAP && EPI == EPI_SWIGLU) ? 64 : kBM;
-    const int r0 = (j * rows) / S;
-    const int r1 = ((j + 1) * rows) / S;
-    if (!abort_flag)
-      reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_coords[0], split_coords[1], r0, r1,
-                                     static_cast<int>(threadIdx.x), kThreads,
-                                     static_cast<uint32_t>(half), static_cast<uint32_t>(GROUP));
-    cluster_sync_all();
+    const int j = static_cast<int>(crank) / GROUP;  // this CTA's k-split index
+    if constexpr (!SWAP) {
+      constexpr int U = split_units<BN, EPI>();
+      constexpr int UC = unit_cols<EPI>();
+      // arm the receive barrier before anyone can send
+      if (threadIdx.x == 0)
+        mbar_arrive_expect_tx(smem_u32(&recv_bar),
+                              static_cast<uint32_t>((S - 1) * owner_units(j, U, S) * 128 * UC * 4));
+      // (1) every CTA has staged its blocks, its ring is free to receive,
+      // and every receive barrier is armed
+      cluster_sync_all();
+      if (threadIdx.x == 64 && !abort_flag)
+        send_blocks<BN, EPI>(ring, smem_u32(&recv_bar), S, j, half, GROUP);
+      if (warp >= 2) {
+        const int et = static_cast<int>(threadIdx.x) - 64;
+        const bool got = epi_wait(smem_u32(&recv_bar), 0, et, &abort_flag, p.err, &epi_flag);
+        const int quad = warp & 3;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+        if (got && !abort_flag) {
+          tc_fence_after();
+          reduce_received<DT, BN, EPI>(p, ring, taddr, quad * 32 + lane, S, j, split_coords[0],
+                                       split_coords[1]);
+        }
+      }
+      // (2) every copy has landed (each owner waited for its bytes): no CTA
+      // leaves while a copy still reads its shared memory
+      cluster_sync_all();
+    } else {
+      // (1) every CTA has staged its partial tile
+      cluster_sync_all();
+      // skinny tiles (small partials): each CTA sums a slice of rows over all
+      // the staged partials through distributed shared memory
+      const int rows = (EPI == EPI_SWIGLU) ? 64 : kBM;
+      const int r0 = (j * rows) / S;
+      const int r1 = ((j + 1) * rows) / S;
+      if (!abort_flag)
+        reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_coords[0], split_coords[1], r0, r1,
+                                       static_cast<int>(threadIdx.x), kThreads,
+                                       static_cast<uint32_t>(half), static_cast<uint32_t>(GROUP));
+      // (2) nobody reads a peer's shared memory any more
+      cluster_sync_all();
+    }
   } else if constexpr (PAIR) {
     // neither CTA of the pair may leave while the other can still signal it
     cluster_sync_all();
@@ -941,10 +1315,10 @@ EncodeTiledFn get_encode() {
 struct TmapKey {
   const void* ptr;
   unsigned long long rows, cols;
-  int box_rows, dt;
+  int box_cols, box_rows, type;
   bool operator==(const TmapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
-           dt == o.dt;
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_cols == o.box_cols &&
+           box_rows == o.box_rows && type == o.type;
   }
 };
 
@@ -954,15 +1328,17 @@ struct TmapEntry {
   bool used;
 };
 
-// Row-major [rows, cols] 16-bit matrix (leading dimension = cols), boxes of
-// 64 columns x box_rows rows, 128-byte swizzle, zero fill outside.  Encoded
-// maps are cached per host thread (encoding costs microseconds).
-bool make_tmap(CUtensorMap* out, const void* ptr, int dt, unsigned long long rows,
-               unsigned long long cols, int box_rows) {
+// Row-major [rows, cols] matrix (leading dimension = cols), boxes of
+// box_cols x box_rows with 128-byte swizzle (box_cols * element size is 128
+// bytes for every map made here), zero fill outside.  type: 0 f16, 1 bf16,
+// 2 f32.  Encoded maps are cached per host thread (encoding costs
+// microseconds).
+bool make_tmap(CUtensorMap* out, const void* ptr, int type, unsigned long long rows,
+               unsigned long long cols, int box_cols, int box_rows) {
   constexpr int kCache = 64;
   thread_local TmapEntry cache[kCache];
   thread_local int victim = 0;
-  const TmapKey key{ptr, rows, cols, box_rows, dt};
+  const TmapKey key{ptr, rows, cols, box_cols, box_rows, type};
   for (int i = 0; i < kCache; ++i) {
     if (cache[i].used && cache[i].key == key) {
       *out = cache[i].map;
@@ -971,12 +1347,15 @@ bool make_tmap(CUtensorMap* out, const void* ptr, int dt, unsigned long long row
   }
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
+  const int esz = (type == 2) ? 4 : 2;
+  const CUtensorMapDataType dt = (type == 0)   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : (type == 1) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {cols * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(out, dt == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                   2, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = enc(out, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
@@ -990,7 +1369,7 @@ bool make_tmap(CUtensorMap* out, const void* ptr, int dt, unsigned long long row
 
 template <int DT, int BN, int EPI, bool SWAP, bool PAIR>
 cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap& tq,
-                       cudaStream_t stream) {
+                       const CUtensorMap& tc, const CUtensorMap& tr, cudaStream_t stream) {
   constexpr int smem = tc_smem_bytes(BN, EPI, SWAP, PAIR);
   auto kern = tc_linear_kernel<DT, BN, EPI, SWAP, PAIR>;
   static int configured[64] = {0};
@@ -1020,7 +1399,7 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, tp, tq, pl.p);
+  return cudaLaunchKernelEx(&cfg, kern, tp, tq, tc, tr, pl.p);
 }
 
 // How many clusters of `cluster` CTAs of this tile shape can be resident at
@@ -1049,31 +1428,36 @@ int max_active_clusters(int cluster) {
   return n;
 }
 
+struct Maps {
+  CUtensorMap p, q, c, r;
+};
+
 template <int DT, bool SWAP, int BN, bool PAIR>
-cudaError_t dispatch_epi(const Plan& pl, int epi, const CUtensorMap& a, const CUtensorMap& b,
-                         cudaStream_t s) {
+cudaError_t dispatch_epi(const Plan& pl, int epi, const Maps& m, cudaStream_t s) {
   switch (epi) {
-    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP, PAIR>(pl, a, b, s);
-    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP, PAIR>(pl, a, b, s);
-    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP, PAIR>(pl, a, b, s);
-    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP, PAIR>(pl, a, b, s);
-    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP, PAIR>(pl, a, b, s);
+    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
+    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
+    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
+    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
+    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
   }
   return cudaErrorInvalidValue;
 }
 
 template <int DT>
-cudaError_t dispatch_shape(const Plan& pl, int epi, const CUtensorMap& a, const CUtensorMap& b,
-                           cudaStream_t s) {
+cudaError_t dispatch_shape(const Plan& pl, int epi, const Maps& m, cudaStream_t s) {
   if (pl.algo == 1) {
-    if (pl.pair) return dispatch_epi<DT, false, 256, true>(pl, epi, a, b, s);
-    if (pl.bn == 128) return dispatch_epi<DT, false, 128, false>(pl, epi, a, b, s);
-    return dispatch_epi<DT, false, 256, false>(pl, epi, a, b, s);
+    if (pl.pair) {
+      if (pl.bn == 128) return dispatch_epi<DT, false, 128, true>(pl, epi, m, s);
+      return dispatch_epi<DT, false, 256, true>(pl, epi, m, s);
+    }
+    if (pl.bn == 128) return dispatch_epi<DT, false, 128, false>(pl, epi, m, s);
+    return dispatch_epi<DT, false, 256, false>(pl, epi, m, s);
   }
   switch (pl.bn) {
-    case 16: return dispatch_epi<DT, true, 16, false>(pl, epi, a, b, s);
-    case 32: return dispatch_epi<DT, true, 32, false>(pl, epi, a, b, s);
-    case 64: return dispatch_epi<DT, true, 64, false>(pl, epi, a, b, s);
+    case 16: return dispatch_epi<DT, true, 16, false>(pl, epi, m, s);
+    case 32: return dispatch_epi<DT, true, 32, false>(pl, epi, m, s);
+    case 64: return dispatch_epi<DT, true, 64, false>(pl, epi, m, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -1081,11 +1465,11 @@ cudaError_t dispatch_shape(const Plan& pl, int epi, const CUtensorMap& a, const 
 // Per-device cache of resident-cluster counts: [shape][cluster size].
 struct ClusterCaps {
   int dev = -1;
-  int caps[6][9];  // shapes: wide 256, wide 128, skinny 16, 32, 64, wide 256 pair
+  int caps[7][9];  // shapes: wide 256, wide 128, skinny 16, 32, 64, pair 256, pair 128
 };
 
 int shape_index(int algo, int bn, int pair) {
-  if (algo == 1) return pair ? 5 : (bn == 256 ? 0 : 1);
+  if (algo == 1) return pair ? (bn == 256 ? 5 : 6) : (bn == 256 ? 0 : 1);
   return bn == 16 ? 2 : bn == 32 ? 3 : 4;
 }
 
@@ -1103,7 +1487,8 @@ int cluster_cap(int algo, int bn, int pair, int cluster) {
   int& v = c.caps[shape_index(algo, bn, pair)][cluster];
   if (v < 0) {
     if (algo == 1)
-      v = pair ? max_active_clusters<256, false, true>(cluster)
+      v = pair ? ((bn == 256) ? max_active_clusters<256, false, true>(cluster)
+                              : max_active_clusters<128, false, true>(cluster))
                : (bn == 256) ? max_active_clusters<256, false, false>(cluster)
                              : max_active_clusters<128, false, false>(cluster);
     else
@@ -1128,7 +1513,7 @@ bool plan_override(int& bn, int& split, int& pair) {
     }
     if (o_bn != 128 && o_bn != 256) o_bn = -1;
     if (o_split < 1 || o_split > 8) o_bn = -1;
-    if (o_pair && (o_bn != 256 || o_split > 4)) o_bn = -1;
+    if (o_pair && o_split > 4) o_bn = -1;
   }
   if (o_bn < 0) return false;
   bn = o_bn;
@@ -1148,6 +1533,7 @@ void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
   p.tiles_p = (p.P + tile_p - 1) / tile_p;
   p.tiles_q = (p.Q + bn - 1) / bn;
   p.kb = (K + kBK - 1) / kBK;
+  p.kb += p.kb & 1;  // whole stage pairs; the extra block is zero-filled
   p.group_p = kGroupP;
   p.split = split;
   const int tiles = p.tiles_p * p.tiles_q;
@@ -1159,12 +1545,14 @@ void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
   }
 }
 
-// Choose the tile shape and the split-K factor.  Cost unit: the time one SM
-// needs for a 64-deep k-block of a 128x256 tile at full tensor rate; the
-// per-k-block factors below reflect how close each shape gets to that rate
-// (one CTA with 256-wide tiles is bounded by its L2->shared bandwidth; a CTA
-// pair loads a third less per SM).  A split of S runs as clusters whose
-// partial tiles are combined through distributed shared memory.
+// Choose the tile shape and the split-K factor with a cost model fitted to
+// measurements on B200 (microseconds):
+//   launch   fixed cost of one launch (set-up, first loads, last epilogue);
+//   t_kb     time one CTA needs per 64-deep k-block, growing with the number
+//            of CTAs running at once (they share L2 bandwidth);
+//   exchange split-K: staging, the cluster barriers and the bulk copies.
+// Tiles are dealt in waves of at most `groups` tiles; every wave pays its
+// k-blocks at the rate of its own CTA count.
 void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   const int wrows = (epi == EPI_SWIGLU) ? 2 * N : N;  // rows of W
   TcParams& p = pl.p;
@@ -1173,7 +1561,8 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   p.N = N;
   p.K = K;
   pl.algo = algo;
-  const int kb = (K + kBK - 1) / kBK;
+  int kb = (K + kBK - 1) / kBK;
+  kb += kb & 1;
   const int G = sm_count;
   if (algo == 2) {
     // skinny: HBM-bound; split K until (almost) every SM streams weights
@@ -1195,35 +1584,57 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   p.Q = wrows;
   int obn = 0, osplit = 0, opair = 0;
   if (plan_override(obn, osplit, opair) && !(epi == EPI_SWIGLU && obn % 128)) {
-    fill_tiles(pl, K, obn, osplit > kb ? kb : osplit, opair, G);
+    const int units = (epi == EPI_SWIGLU) ? obn / 64 : obn / 32;
+    int sp = osplit > kb / 2 ? kb / 2 : osplit;
+    if (sp > units) sp = units;
+    const int ring_bytes = tc_stages(obn, opair != 0) * tc_stage_bytes(obn, opair != 0);
+    while (sp > 1 && split_smem_bytes(units, epi == EPI_SWIGLU ? 64 : 32, sp) > ring_bytes) --sp;
+    fill_tiles(pl, K, obn, sp, opair, G);
     return;
   }
-  const double kFill = 2.5, kReduce = 4.0;
-  struct Shape { int bn, pair; double kc; };
-  const Shape shapes[3] = {{256, 1, 1.1}, {256, 0, 1.35}, {128, 0, 0.75}};
+  struct Shape {
+    int bn, pair;
+    double launch, t0, t_slope;  // t_kb = t0 + t_slope * ctas / sm_count
+  };
+  const Shape shapes[4] = {{256, 1, 4.0, 0.28, 0.16},
+                           {128, 1, 4.0, 0.25, 0.07},
+                           {256, 0, 3.5, 0.29, 0.17},
+                           {128, 0, 3.5, 0.23, 0.05}};
+  auto t_kb = [&](const Shape& sh, long long ctas) {
+    return sh.t0 + sh.t_slope * static_cast<double>(ctas) / G;
+  };
   double best = 1e30;
   int best_bn = 256, best_split = 1, best_pair = 0;
   for (const Shape& sh : shapes) {
+    if (epi == EPI_SWIGLU && sh.bn % 128) continue;
     const int tile_p = sh.pair ? 2 * kBM : kBM;
     const int group = sh.pair ? 2 : 1;
     const long long tiles =
         static_cast<long long>((M + tile_p - 1) / tile_p) * ((wrows + sh.bn - 1) / sh.bn);
     // persistent, whole K per tile
-    const int groups = G / group;
-    const long long waves1 = (tiles + groups - 1) / groups;
-    double cost = waves1 * (kb * sh.kc + kFill);
+    const long long groups = G / group;
+    double cost = sh.launch;
+    for (long long done = 0; done < tiles; done += groups) {
+      const long long in_wave = (tiles - done < groups) ? tiles - done : groups;
+      cost += kb * t_kb(sh, in_wave * group);
+    }
     if (cost < best) {
       best = cost;
       best_bn = sh.bn;
       best_split = 1;
       best_pair = sh.pair;
     }
-    for (int s = 2; s * group <= 8 && s <= kb / 2; ++s) {
-      // split plans run as a single wave of clusters (a second wave would
-      // pay the per-CTA set-up and the reduction again)
+    // split columns are handed out in units (32 accumulator columns, 64 for
+    // SwiGLU pairs): at most one owner per unit
+    const int units = (epi == EPI_SWIGLU) ? sh.bn / 64 : sh.bn / 32;
+    const int ring_bytes = tc_stages(sh.bn, sh.pair) * tc_stage_bytes(sh.bn, sh.pair);
+    for (int s = 2; s * group <= 8 && s <= kb / 2 && s <= units; ++s) {
+      if (split_smem_bytes(units, epi == EPI_SWIGLU ? 64 : 32, s) > ring_bytes) continue;
+      // split plans run as a single wave of clusters
       const int cap_clusters = cluster_cap(1, sh.bn, sh.pair, s * group);
       if (cap_clusters <= 0 || tiles > cap_clusters) continue;
-      cost = (((kb + s - 1) / s) * sh.kc + kFill) + kReduce * sh.bn / 256.0;
+      const int kbc = 2 * (((kb / 2) + s - 1) / s);
+      cost = sh.launch + kbc * t_kb(sh, tiles * s * group) + 2.0 + 2.0 * s;
       if (cost < best) {
         best = cost;
         best_bn = sh.bn;
@@ -1242,17 +1653,35 @@ cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const 
   const bool swap = pl.algo == 2;
   const void* pptr = swap ? W : A;
   const void* qptr = swap ? A : W;
-  CUtensorMap tmp, tmq;
-  if (!make_tmap(&tmp, pptr, dtype, static_cast<unsigned long long>(p.P),
-                 static_cast<unsigned long long>(p.K), kBM) ||
-      !make_tmap(&tmq, qptr, dtype, static_cast<unsigned long long>(p.Q),
-                 static_cast<unsigned long long>(p.K), tc_qrows(pl.bn, pl.pair != 0))) {
+  Maps m;
+  if (!make_tmap(&m.p, pptr, dtype, static_cast<unsigned long long>(p.P),
+                 static_cast<unsigned long long>(p.K), kBK, kBM) ||
+      !make_tmap(&m.q, qptr, dtype, static_cast<unsigned long long>(p.Q),
+                 static_cast<unsigned long long>(p.K), kBK, tc_qrows(pl.bn, pl.pair != 0))) {
     if (why) *why = "cuTensorMapEncodeTiled failed";
     return cudaErrorInvalidValue;
   }
+  m.c = m.p;
+  m.r = m.p;
+  pl.p.out_tma = 0;
+  if (!swap && pl.p.split == 1) {
+    // wide tiles store through TMA when C (and the residual) rows allow it
+    const bool f32 = (epi == EPI_F32_OUT || epi == EPI_F32_PARTIAL);
+    const int esz = f32 ? 4 : 2;
+    const bool c_ok = (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && ((p.ldc * esz) % 16 == 0);
+    const bool r_ok = (epi != EPI_RESIDUAL) ||
+                      ((reinterpret_cast<uintptr_t>(p.R) % 16 == 0) && ((p.ldr * 2) % 16 == 0));
+    if (c_ok && r_ok &&
+        make_tmap(&m.c, p.C, f32 ? 2 : dtype, static_cast<unsigned long long>(p.M),
+                  static_cast<unsigned long long>(p.N), f32 ? 32 : 64, kBM) &&
+        (epi != EPI_RESIDUAL ||
+         make_tmap(&m.r, p.R, dtype, static_cast<unsigned long long>(p.M),
+                   static_cast<unsigned long long>(p.N), 64, kBM)))
+      pl.p.out_tma = 1;
+  }
   pl.p.err = err;
-  if (dtype == DT_F16) return dispatch_shape<DT_F16>(pl, epi, tmp, tmq, stream);
-  return dispatch_shape<DT_BF16>(pl, epi, tmp, tmq, stream);
+  if (dtype == DT_F16) return dispatch_shape<DT_F16>(pl, epi, m, stream);
+  return dispatch_shape<DT_BF16>(pl, epi, m, stream);
 }
 
 }  // namespace orin

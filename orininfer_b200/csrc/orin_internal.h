@@ -26,6 +26,7 @@ struct TcParams {
   long long ldr;
   int* err;          // device error word
   int vec_ok;        // C / R rows are 16-byte aligned for vector stores
+  int out_tma;       // wide tiles: stores (and the residual) go through TMA
 };
 
 struct Plan {

@@ -44,7 +44,7 @@ _ALGOS = {
 
 __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
-    "pack_gate_up", "device_check",
+    "pack_gate_up", "device_check", "plan_info",
 ]
 
 
@@ -152,6 +152,17 @@ def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,
     check(_lib.lib.orin_pack_gate_up(_ptr(out), _ptr(w_gate), _ptr(w_up), IM, K,
                                      _dtype_code(w_gate), _stream(stream)))
     return out
+
+
+def plan_info(M: int, N: int, K: int, dtype: torch.dtype = torch.float16,
+              epilogue: str = "none", algo: str = "auto") -> dict:
+    """The launch orin_linear would make for this problem on the current GPU."""
+    info = (ctypes.c_int * 6)()
+    check(_lib.lib.orin_plan_info(M, N, K, _DTYPES[dtype], _EPILOGUES[epilogue], _ALGOS[algo],
+                                  info))
+    kind = {1: "tcgen05-wide", 2: "tcgen05-skinny", 3: "cuda-core"}[info[0]]
+    return {"kernel": kind, "tile_cols": info[1], "cta_pair": bool(info[2]), "split_k": info[3],
+            "grid": info[4], "tiles": info[5]}
 
 
 def device_check(stream: Optional[torch.cuda.Stream] = None) -> None:

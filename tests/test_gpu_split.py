@@ -13,8 +13,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 # "BN,SPLIT" = one CTA per 128-row tile; "BN,SPLIT,1" = tcgen05 CTA pairs
 # (256-row tiles); SPLIT > 1 = k-split over a thread-block cluster
-PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,5", "128,8",
-         "256,1,1", "256,2,1", "256,3,1", "256,4,1"]
+PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,4", "128,3",
+         "256,1,1", "256,2,1", "256,3,1", "256,4,1", "128,1,1", "128,2,1", "128,4,1"]
 
 
 @pytest.mark.gpu

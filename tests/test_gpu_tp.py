@@ -1,0 +1,96 @@
+"""Tensor-parallel row linear over NCCL on 2 GPUs (one process per GPU).
+
+Each rank holds a K-shard of the o_proj / down_proj weight; orin_tp_linear_row
+computes its fp32 partial, all-reduces it over NCCL and applies the residual
+and the single rounding.  The result must match the unsharded oracle on every
+rank.  Column-parallel shards (q/k/v by head, packed gate/up) are plain
+orin_linear calls on the shard and are checked the same way."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+H, IM, M = 1024, 2048, 96
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import orininfer_b200 as ob
+    from oracle import oracle as orc
+    from orininfer_b200 import tp
+    from orininfer_b200.synth import seeded
+    from tests._util import EXACT_MIN, assert_close, bits, from_bits
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        comm = tp.TPComm(rank, world, rank, tp.exchange_unique_id(rank), timeout_s=60.0)
+        act = seeded((M, IM), 1, 1.0)
+        wd = seeded((H, IM), 2, 0.02)
+        res = seeded((M, H), 3, 1.0)
+        # row-parallel down_proj with the residual folded in
+        ks = IM // world
+        out = comm.linear_row(act[:, rank * ks:(rank + 1) * ks].contiguous().to(dev),
+                              tp.shard_cols(wd, rank, world).to(dev), residual=res.to(dev))
+        comm.wait()
+        ob.device_check()
+        ref = orc.linear(bits(act), bits(wd), 0, "residual", bits(res))
+        # the fp32 sum over ranks differs from one GPU's only in summation order
+        assert_close(out.cpu().float(), from_bits(ref, torch.float16).float(),
+                     f"row-parallel rank {rank}", exact_min=EXACT_MIN)
+        # column-parallel gate/up with SwiGLU on this rank's packed shard
+        wg = seeded((IM, H), 4, 0.02)
+        wu = seeded((IM, H), 5, 0.02)
+        x = seeded((M, H), 6, 1.0)
+        y = ob.linear(x.to(dev), tp.shard_gate_up(wg.to(dev), wu.to(dev), rank, world),
+                      epilogue="swiglu")
+        ob.device_check()
+        ims = IM // world
+        g, u = tp.shard_gate_up_rows(wg, wu, rank, world)
+        ref2 = orc.linear(bits(x), orc.pack_gate_up(bits(g), bits(u)), 0, "swiglu")
+        assert_close(y.cpu().float(), from_bits(ref2, torch.float16).float(),
+                     f"column-parallel rank {rank}", exact_min=EXACT_MIN)
+        assert y.shape == (M, ims)
+        torch.cuda.synchronize()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+def test_two_gpu_row_and_column_parallel():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=300)
+        results[r] = msg
+    for p in procs:
+        p.join(timeout=120)
+    assert all(m == "ok" for m in results.values()), results
