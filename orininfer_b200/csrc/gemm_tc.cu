@@ -57,8 +57,9 @@ __host__ __device__ constexpr int tc_qrows(int bn, bool pair) { return pair ? bn
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool pair) {
   return kBM * kBK * 2 + tc_qrows(bn, pair) * kBK * 2;
 }
-// Stages come in pairs: the MMA issuer waits once per pair of stages (one
-// barrier wait costs about as much as issuing a stage's MMAs).
+// Stages come in pairs: the MMA issuer waits once per pair of stages and the
+// producer refills a pair per wait (one barrier wait costs about as much as
+// issuing a stage's MMAs or its loads).
 __host__ __device__ constexpr int tc_stages(int bn, bool pair) {
   return ((196608 / tc_stage_bytes(bn, pair)) > 12 ? 12 : (196608 / tc_stage_bytes(bn, pair))) &
          ~1;
@@ -891,8 +892,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t dsmem[];
   constexpr int PAIRS = STAGES / 2;
   static_assert(STAGES % 2 == 0, "stages come in pairs");
-  __shared__ __align__(8) uint64_t full_bar[PAIRS];  // one per pair of stages
-  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t full_bar[PAIRS];   // one per pair of stages
+  __shared__ __align__(8) uint64_t empty_bar[PAIRS];  // one per pair of stages
   __shared__ __align__(8) uint64_t tfull_bar[2];
   __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ __align__(8) uint64_t drain_bar;
@@ -917,8 +918,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t lead_rank = crank & ~1u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PAIRS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
-    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&empty_bar[s]), 1);
+    for (int s = 0; s < PAIRS; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull_bar[b]), 1);
       mbar_init(smem_u32(&tempty_bar[b]), GROUP * (kEpiThreads / 32));
@@ -1001,8 +1004,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                      pend_row[i], pol_x);
               waited = true;
             }
-            if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag, p.err,
-                                   DEVERR_TIMEOUT_PRODUCER)) {
+            // one wait frees a whole pair of stages
+            if ((stage & 1) == 0 &&
+                !mbar_wait_bounded(smem_u32(&empty_bar[stage >> 1]), phase ^ 1u, &abort_flag,
+                                   p.err, DEVERR_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
             }
@@ -1108,8 +1113,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               if constexpr (PAIR) tc_mma_f16_pair(d, ad, bd, IDESC, accum);
               else tc_mma_f16(d, ad, bd, IDESC, accum);
             }
-            commit(&empty_bar[stage + h]);
           }
+          // both stages of the pair are free once these MMAs complete
+          commit(&empty_bar[stage >> 1]);
           stage += 2;
           if (stage == STAGES) {
             stage = 0;
