@@ -387,6 +387,107 @@ def e2e_through_abi(step: Step, steps: int, dev):
     return ms, h2d, d2h
 
 
+VOCAB, N_LAYERS = 32000, 22
+DECODE_TOKENS = (1, 8, 32, 64)
+
+
+def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
+    """The decode-time GEMM path of a whole TinyLlama-shaped model: 22 layers x
+    (q/k/v, o_proj + residual, gate/up + SwiGLU, down + residual) and the LM
+    head (fp32 logits), at M in {1, 8, 32, 64} tokens, one CUDA graph per M.
+    Attention and the norms are not part of the path: the o_proj input and the
+    normed hidden are fixed synthetic buffers.  1.55 GB of random-init fp16
+    weights (> L2), so every step streams them from HBM; GB/s counts the
+    algorithmic bytes (weights once, activations in, outputs out)."""
+    import torch.nn.functional as F
+
+    import orininfer_b200 as ob
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2024)
+
+    def weight(rows, cols):
+        return (torch.randn((rows, cols), generator=gen, device=dev) * 0.02).half()
+
+    layers = [{"qkv": weight(QKV_N, H), "o_proj": weight(H, H), "gate_up": weight(2 * IM, H),
+               "down": weight(H, IM)} for _ in range(N_LAYERS)]
+    lm_head = weight(VOCAB, H)
+    w_bytes = 2 * (N_LAYERS * (QKV_N * H + H * H + 2 * IM * H + H * IM) + VOCAB * H)
+    out = {"what": "22 layers x (q/k/v, o_proj+residual, gate/up+SwiGLU, down+residual) + "
+                   "LM head (fp32 logits), CUDA graph per M, weights > L2",
+           "weight_bytes": w_bytes, "launches_per_step": 4 * N_LAYERS + 1, "by_tokens": {}}
+    peaks, _ = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+
+    def graph_ms(fn):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) / reps
+
+    for m in DECODE_TOKENS:
+        x = (torch.randn((m, H), generator=gen, device=dev)).half()      # normed hidden
+        attn = (torch.randn((m, H), generator=gen, device=dev)).half()   # attention output
+        h = (torch.randn((m, H), generator=gen, device=dev)).half()      # residual stream
+        h0 = h.clone()
+        qkv = torch.empty((m, QKV_N), dtype=torch.float16, device=dev)
+        act = torch.empty((m, IM), dtype=torch.float16, device=dev)
+        logits = torch.empty((m, VOCAB), dtype=torch.float32, device=dev)
+
+        def ours():
+            h.copy_(h0)
+            for L in layers:
+                ob.linear_into(qkv, x, L["qkv"])
+                ob.linear_into(h, attn, L["o_proj"], epilogue="residual", residual=h)
+                ob.linear_into(act, x, L["gate_up"], epilogue="swiglu")
+                ob.linear_into(h, act, L["down"], epilogue="residual", residual=h)
+            ob.linear_into(logits, h, lm_head, epilogue="f32")
+
+        ms = graph_ms(ours)
+        ob.device_check()
+        a_bytes = 2 * m * (N_LAYERS * (H + QKV_N + 3 * H + H + IM + IM + 2 * H) + H) + 4 * m * VOCAB
+        gbs = (w_bytes + a_bytes) / (ms / 1e3) / 1e9
+        rec = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1),
+               "hbm_frac": round(gbs / hbm, 4)}
+        if with_cublas:
+            def ref():
+                hh = h0.clone()
+                for L in layers:
+                    F.linear(x, L["qkv"], out=qkv)
+                    hh = hh + F.linear(attn, L["o_proj"])
+                    gu = F.linear(x, L["gate_up"]).view(m, IM // 64, 2, 64)
+                    a_ = (F.silu(gu[:, :, 0].float()) * gu[:, :, 1].float()).half()
+                    hh = hh + F.linear(a_.reshape(m, IM), L["down"])
+                F.linear(hh, lm_head).float()
+
+            cms = graph_ms(ref)
+            rec["cublas_ms_per_step"] = round(cms, 4)
+            rec["cublas_gbs"] = round((w_bytes + a_bytes) / (cms / 1e3) / 1e9, 1)
+        out["by_tokens"][str(m)] = rec
+        del x, attn, h, h0, qkv, act, logits
+    out["peak_hbm_gbs"] = hbm
+    del layers, lm_head
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline_layer(budget_s: float = 10.0) -> dict:
     """The oracle's fp32 multithreaded GEMM over the same layer shapes."""
     import numpy as np
@@ -495,6 +596,8 @@ def run_ours(args, rank, world, local_rank):
         line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}
         line["cpu_baseline"] = cpu_baseline_layer(args.cpu_budget) if args.cpu_budget > 0 \
             else None
+        if args.decode_reps > 0:
+            line["decode"] = decode_path(dev, args.decode_reps, args.cublas_bar)
     if comm is not None:
         torch.cuda.synchronize()
         comm.close()
@@ -509,17 +612,25 @@ def run_one_kernel(args):
     step = Step(layers, 0, 1, dev)
     name = args.kernel
     ob = step.ob
+    m = args.tokens if args.tokens is not None else M
+    if not 1 <= m <= M:
+        raise SystemExit(f"--tokens must be in [1, {M}]")
+
+    def rows(t):
+        return t[:m]  # leading rows of a row-major buffer: still contiguous
 
     def launch(i):
         L = layers[i % len(layers)]
         if name == "qkv":
-            ob.linear_into(step.qkv, step.h, L["qkv"])
+            ob.linear_into(rows(step.qkv), rows(step.h), L["qkv"])
         elif name == "o_proj":
-            ob.linear_into(step.x1, step.attn, L["o_proj"], epilogue="residual", residual=step.x)
+            ob.linear_into(rows(step.x1), rows(step.attn), L["o_proj"], epilogue="residual",
+                           residual=rows(step.x))
         elif name == "gate_up":
-            ob.linear_into(step.act, step.h2, L["gate_up"], epilogue="swiglu")
+            ob.linear_into(rows(step.act), rows(step.h2), L["gate_up"], epilogue="swiglu")
         else:
-            ob.linear_into(step.x2, step.act, L["down"], epilogue="residual", residual=step.x1)
+            ob.linear_into(rows(step.x2), rows(step.act), L["down"], epilogue="residual",
+                           residual=rows(step.x1))
 
     for i in range(args.warmup):
         launch(i)
@@ -535,8 +646,15 @@ def run_one_kernel(args):
         ts.append(a.elapsed_time(b))
     ob.device_check()
     avg = statistics.mean(ts)
-    return {"kernel": name, "workload": WORKLOAD, "launches": args.steps,
-            "avg_ms": round(avg, 5), "tflops": round(FLOPS[name] / (avg / 1e3) / 1e12, 2)}
+    n_out, kk, epi = GEMMS[name]
+    n_w = 2 * n_out if epi == "swiglu" else n_out
+    flops = FLOPS[name] * m // M
+    # algorithmic bytes: weight + activation read, output written (+ residual read)
+    nbytes = 2 * (n_w * kk + m * kk + m * n_out * (2 if epi == "residual" else 1))
+    return {"kernel": name, "workload": WORKLOAD, "tokens": m, "launches": args.steps,
+            "avg_ms": round(avg, 5), "tflops": round(flops / (avg / 1e3) / 1e12, 2),
+            "gbs": round(nbytes / (avg / 1e3) / 1e9, 1), "algorithmic_bytes": nbytes,
+            "plan": ob_plan(m, n_out, kk, epi)}
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -618,11 +736,17 @@ def main():
                     help="steps of the end-to-end (host buffers, C ABI) measurement")
     ap.add_argument("--breakdown-steps", type=int, default=64,
                     help="steps of the per-projection CUDA-event breakdown")
+    ap.add_argument("--decode-reps", type=int, default=20,
+                    help="graph replays of the whole-model decode GEMM path per token count "
+                         "(0: skip)")
     ap.add_argument("--no-cublas-bar", dest="cublas_bar", action="store_false",
                     help="skip timing the cuBLAS comparison bar")
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,
                     help="run only this projection, eagerly, warmup+steps times, and print "
                          "its event-timed average (a small case for profilers)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="with --kernel: token rows M of that projection (default: the "
+                         "workload's 512; 1..64 is the decode GEMV / skinny path)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

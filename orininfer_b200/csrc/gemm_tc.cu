@@ -57,13 +57,6 @@ __host__ __device__ constexpr int tc_qrows(int bn, bool pair) { return pair ? bn
 __host__ __device__ constexpr int tc_stage_bytes(int bn, bool pair) {
   return kBM * kBK * 2 + tc_qrows(bn, pair) * kBK * 2;
 }
-// Stages come in pairs: the MMA issuer waits once per pair of stages and the
-// producer refills a pair per wait (one barrier wait costs about as much as
-// issuing a stage's MMAs or its loads).
-__host__ __device__ constexpr int tc_stages(int bn, bool pair) {
-  return ((196608 / tc_stage_bytes(bn, pair)) > 12 ? 12 : (196608 / tc_stage_bytes(bn, pair))) &
-         ~1;
-}
 __host__ __device__ constexpr uint32_t tc_tmem_cols(int bn) {
   // two accumulator buffers of bn fp32 columns, rounded to a power of two >= 32
   return (2 * bn <= 32) ? 32u : (2 * bn <= 64) ? 64u : (2 * bn <= 128) ? 128u
@@ -73,14 +66,50 @@ __host__ __device__ constexpr int tc_xch_bytes(int bn, int epi, bool swap) {
   // skinny SwiGLU: up-half rows hand their rounded values to gate-half rows
   return (swap && epi == EPI_SWIGLU) ? 64 * 32 * 4 : 0;
 }
+// Skinny split-K: every CTA of a cluster pushes each fp32 partial row of its
+// tile into the shared memory of the CTA that owns (reduces) that row.  Owners
+// hold contiguous slices of the tile's output features (64 for SwiGLU, whose
+// gate and up rows travel together, else 128); a slot row is [gate | up] or
+// one partial row, +4 floats of padding.
+__host__ __device__ constexpr int tc_push_features(int epi) { return epi == EPI_SWIGLU ? 64 : 128; }
+__host__ __device__ constexpr int tc_push_pitch(int bn, int epi) {
+  return (epi == EPI_SWIGLU ? 2 * bn : bn) + 4;
+}
+__host__ __device__ constexpr int tc_push_bytes(int bn, int epi, bool swap) {
+  // S senders x ceil(F / S) rows <= F + 7 rows for S <= 8
+  return swap ? (tc_push_features(epi) + 8) * tc_push_pitch(bn, epi) * 4 : 0;
+}
+// Shared memory a skinny CTA may use: up to 64 token columns, two CTAs per SM,
+// so that the next kernel's CTAs (programmatic dependent launch) are resident
+// and streaming their weights while this kernel's CTAs finish.
+__host__ __device__ constexpr int tc_skinny_budget(int bn) {
+  return bn <= 32 ? 113 * 1024 : 227 * 1024;
+}
+// Stages come in pairs: the MMA issuer waits once per pair of stages and the
+// producer refills a pair per wait (one barrier wait costs about as much as
+// issuing a stage's MMAs or its loads).
+__host__ __device__ constexpr int tc_stages_fit(int bytes, int stage) {
+  return ((bytes / stage) > 12 ? 12 : (bytes / stage)) & ~1;
+}
+__host__ __device__ constexpr int tc_stages(int bn, bool pair, bool swap = false, int epi = 0) {
+  return swap ? tc_stages_fit(tc_skinny_budget(bn) - tc_xch_bytes(bn, epi, true) -
+                                  tc_push_bytes(bn, epi, true) - 2048,
+                              tc_stage_bytes(bn, false))
+              : tc_stages_fit(196608, tc_stage_bytes(bn, pair));
+}
 // Wide tiles stage their output in two 16 KB buffers (128 rows x 128 bytes,
 // 128-byte swizzle) for TMA stores.
 constexpr int kOutBuf = 128 * 128;
 __host__ __device__ constexpr int tc_out_bytes(bool swap) { return swap ? 0 : 2 * kOutBuf; }
 __host__ __device__ constexpr int tc_smem_bytes(int bn, int epi, bool swap, bool pair) {
-  return tc_stages(bn, pair) * tc_stage_bytes(bn, pair) + tc_xch_bytes(bn, epi, swap) +
-         tc_out_bytes(swap) + 1024;
+  return tc_stages(bn, pair, swap, epi) * tc_stage_bytes(bn, pair) + tc_xch_bytes(bn, epi, swap) +
+         tc_push_bytes(bn, epi, swap) + tc_out_bytes(swap) + 1024;
 }
+static_assert(tc_smem_bytes(16, EPI_SWIGLU, true, false) + 1024 <= 114 * 1024, "two per SM");
+static_assert(tc_smem_bytes(32, EPI_SWIGLU, true, false) + 1024 <= 114 * 1024, "two per SM");
+static_assert(tc_smem_bytes(32, EPI_NONE, true, false) + 1024 <= 114 * 1024, "two per SM");
+static_assert(tc_stages(16, false, true, EPI_SWIGLU) >= 4 && tc_stages(64, false, true, 0) >= 4,
+              "skinny rings keep at least two stage pairs");
 
 // ---------------------------------------------------------------------------
 // Work decomposition, computed identically by every role of a CTA.  A tile is
@@ -630,14 +659,6 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
 // Cluster split-K: shared-memory staging and the DSMEM reduction
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 
 
 // All threads of all CTAs of the cluster; release/acquire orders the shared
@@ -749,99 +770,48 @@ __device__ __forceinline__ void out_group(const TcParams& p, int prow0, int qcol
   }
 }
 
-// Sum the S partial tiles of this cluster over rows [r0, r1) of the tile, in
-// rank order 0..S-1 (deterministic), apply the epilogue and store.  Work item
-// = one 4-column group of one row (for SwiGLU: a gate group and its up group);
-// each thread issues the loads of U items from all S ranks before summing, so
-// up to 16 shared-memory loads (local or distributed) are in flight per thread.
-template <int DT, int BN, int EPI, bool SWAP, int S>
-__device__ __forceinline__ void reduce_rows_s(const TcParams& p, uint32_t stage, int prow0,
-                                              int qcol0, int r0, int r1, int tid, int nthreads,
-                                              uint32_t src0, uint32_t src_step) {
-  constexpr int PITCH = stage_pitch<BN>();
-  constexpr bool PAIRS = (EPI == EPI_SWIGLU);
-  constexpr int LOADS = PAIRS ? 2 * S : S;
-  constexpr int U = (16 / LOADS) > 0 ? (16 / LOADS) : 1;
-  // items per row: 4-column groups (gate groups only for the wide SwiGLU)
-  constexpr int G = (PAIRS && !SWAP) ? BN / 8 : BN / 4;
-  const int rows = r1 - r0;
-  const int items = rows * G;
-  const uint32_t me = cluster_rank();
-  // the S partials of this CTA's rows live in cluster ranks src0 + r*src_step
-  uint32_t base[S];
-  bool local[S];
+// Skinny split-K, owner side: sum the S partial rows pushed for each owned
+// feature [f0, f1) of the tile in sender order 0..S-1 (deterministic), apply
+// the epilogue and store.  Work item = one feature x one 4-token group;
+// consecutive threads take consecutive features, so the stores of one token
+// row coalesce.  rm = slot rows per sender.
+template <int DT, int BN, int EPI, int S>
+__device__ __forceinline__ void reduce_pushed_s(const TcParams& p, uint32_t pbuf, int prow0,
+                                                int qcol0, int f0, int f1, int rm, int tid,
+                                                int nthreads) {
+  constexpr int PITCH = tc_push_pitch(BN, EPI);
+  const int rows = f1 - f0;
+  const int items = rows * (BN / 4);
+  for (int e = tid; e < items; e += nthreads) {
+    const int i = e % rows;
+    const int col = 4 * (e / rows);
+    float4 x[S], y[S];
 #pragma unroll
-  for (int r = 0; r < S; ++r) {
-    const uint32_t src = src0 + static_cast<uint32_t>(r) * src_step;
-    local[r] = (src == me);
-    base[r] = local[r] ? stage : mapa_shared(stage, src);
-  }
-  for (int i0 = tid; i0 < items; i0 += nthreads * U) {
-    float4 v[U][LOADS];
-    int rowv[U], colv[U];
+    for (int r = 0; r < S; ++r) {
+      const uint32_t a = pbuf + static_cast<uint32_t>(((r * rm + i) * PITCH + col) * 4);
+      x[r] = ld_smem_f4(a);
+      if constexpr (EPI == EPI_SWIGLU) y[r] = ld_smem_f4(a + BN * 4);
+    }
+    float4 a = x[0], b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (EPI == EPI_SWIGLU) b = y[0];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int e = i0 + u * nthreads;
-      int row, col;
-      if constexpr (SWAP) {
-        // consecutive threads take consecutive rows (features): the stores
-        // of one token row then coalesce
-        row = r0 + e % rows;
-        col = 4 * (e / rows);
-      } else if constexpr (PAIRS) {
-        const int gg = e % G;
-        row = r0 + e / G;
-        col = (gg / 16) * 128 + (gg % 16) * 4;
-      } else {
-        row = r0 + e / G;
-        col = 4 * (e % G);
-      }
-      rowv[u] = row;
-      colv[u] = col;
-      if (e < items) {
-        const uint32_t off = static_cast<uint32_t>((row * PITCH + col) * 4);
-        // the up half: 64 columns right (wide) or 64 rows down (skinny)
-        const uint32_t off2 = SWAP ? off + static_cast<uint32_t>(64 * PITCH * 4) : off + 256u;
-#pragma unroll
-        for (int r = 0; r < S; ++r) {
-          const uint32_t a = base[r] + off;
-          v[u][r] = local[r] ? ld_smem_f4(a) : ld_dsmem_f4(a);
-          if constexpr (PAIRS) {
-            const uint32_t a2 = base[r] + off2;
-            v[u][S + r] = local[r] ? ld_smem_f4(a2) : ld_dsmem_f4(a2);
-          }
-        }
+    for (int r = 1; r < S; ++r) {
+      a.x += x[r].x; a.y += x[r].y; a.z += x[r].z; a.w += x[r].w;
+      if constexpr (EPI == EPI_SWIGLU) {
+        b.x += y[r].x; b.y += y[r].y; b.z += y[r].z; b.w += y[r].w;
       }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (i0 + u * nthreads >= items) continue;
-      float4 a = v[u][0];
-#pragma unroll
-      for (int r = 1; r < S; ++r) {
-        a.x += v[u][r].x; a.y += v[u][r].y; a.z += v[u][r].z; a.w += v[u][r].w;
-      }
-      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-      if constexpr (PAIRS) {
-        b = v[u][S];
-#pragma unroll
-        for (int r = 1; r < S; ++r) {
-          b.x += v[u][S + r].x; b.y += v[u][S + r].y; b.z += v[u][S + r].z; b.w += v[u][S + r].w;
-        }
-      }
-      out_group<DT, BN, EPI, SWAP>(p, prow0, qcol0, rowv[u], colv[u], a, &b);
-    }
+    out_group<DT, BN, EPI, true>(p, prow0, qcol0, f0 + i, col, a, &b);
   }
 }
 
-template <int DT, int BN, int EPI, bool SWAP>
-__device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, int S, int prow0,
-                                            int qcol0, int r0, int r1, int tid, int nthreads,
-                                            uint32_t src0, uint32_t src_step) {
-#define ORIN_REDUCE_CASE(n)                                                                    \
-  case n:                                                                                      \
-    reduce_rows_s<DT, BN, EPI, SWAP, n>(p, stage, prow0, qcol0, r0, r1, tid, nthreads, src0,   \
-                                        src_step);                                             \
+template <int DT, int BN, int EPI>
+__device__ __forceinline__ void reduce_pushed(const TcParams& p, uint32_t pbuf, int S, int prow0,
+                                              int qcol0, int f0, int f1, int rm, int tid,
+                                              int nthreads) {
+#define ORIN_REDUCE_CASE(n)                                                                   \
+  case n:                                                                                     \
+    reduce_pushed_s<DT, BN, EPI, n>(p, pbuf, prow0, qcol0, f0, f1, rm, tid, nthreads);        \
     break;
   switch (S) {
     ORIN_REDUCE_CASE(2)
@@ -851,8 +821,7 @@ __device__ __forceinline__ void reduce_rows(const TcParams& p, uint32_t stage, i
     ORIN_REDUCE_CASE(6)
     ORIN_REDUCE_CASE(7)
     default:
-      reduce_rows_s<DT, BN, EPI, SWAP, 8>(p, stage, prow0, qcol0, r0, r1, tid, nthreads, src0,
-                                          src_step);
+      reduce_pushed_s<DT, BN, EPI, 8>(p, pbuf, prow0, qcol0, f0, f1, rm, tid, nthreads);
       break;
   }
 #undef ORIN_REDUCE_CASE
@@ -880,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int GROUP = PAIR ? 2 : 1;         // CTAs per tile accumulator
   constexpr int TILE_P = GROUP * kBM;         // P rows per tile
   constexpr int QR = tc_qrows(BN, PAIR);      // Q rows this CTA loads per stage
-  constexpr int STAGES = tc_stages(BN, PAIR);
+  constexpr int STAGES = tc_stages(BN, PAIR, SWAP, EPI);
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t STAGE_BYTES = tc_stage_bytes(BN, PAIR);
   constexpr uint32_t TMEM_COLS = tc_tmem_cols(BN);
@@ -910,6 +879,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* xch = reinterpret_cast<float*>(dsmem + (ring - smem_u32(dsmem)) + STAGES * STAGE_BYTES);
   // output staging (wide tiles): 1024-aligned, after the ring
   const uint32_t outbuf = ring + STAGES * STAGE_BYTES;
+  // skinny split-K receive slots, after the SwiGLU exchange rows
+  const uint32_t pbuf = ring + STAGES * STAGE_BYTES + tc_xch_bytes(BN, EPI, SWAP);
   const int S = p.split;
   const bool clustered = PAIR || S > 1;
   const uint32_t crank = clustered ? cluster_rank() : 0u;
@@ -955,6 +926,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  // Skinny split: the CTAs of a cluster push partial rows into each other's
+  // shared memory.  A first cluster-barrier phase, arrived at here and waited
+  // on just before the first push, makes sure every CTA has started.
+  bool push_waited = false;
+  if (SWAP && S > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
 
   // split mode: this CTA's one tile (for the reduction after the roles)
@@ -982,6 +958,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int pend_k[STAGES], pend_row[STAGES];
       uint32_t arm_par[PAIRS];
+      // Skinny tiles: the first unit's weight boxes beyond the ring are
+      // prefetched into L2 before griddepcontrol.wait, so that streaming them
+      // overlaps the previous kernel (weights do not depend on it).
+      int pf_row = -1, pf_k0 = 0, pf_k1 = 0;
+      auto prefetch_weights = [&]() {
+        if constexpr (SWAP) {
+          const int kb_real = (p.K + kBK - 1) / kBK;
+          const int end = pf_k1 < kb_real ? pf_k1 : kb_real;
+          for (int k = pf_k0; k < end; ++k) tma_prefetch_l2_2d(tm_w, k * kBK, pf_row);
+        }
+      };
       int n_issued = 0;
       bool waited = false;
       int stage = 0;
@@ -995,9 +982,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords(u.tile, p, tp, tq);
         const int row_w = SWAP ? tp * kBM : tq * BN + half * QR;
         const int row_x = SWAP ? tq * BN : tp * TILE_P + half * kBM;
+        if (pf_row < 0) {
+          pf_row = row_w;
+          pf_k0 = u.k0 + STAGES;
+          pf_k1 = u.k1;
+        }
         for (int k = u.k0; k < u.k1; ++k) {
           if (n_issued >= STAGES) {
             if (!waited) {
+              prefetch_weights();
               pdl_wait();
               for (int i = 0; i < STAGES; ++i)
                 load(ring + i * STAGE_BYTES + off_x, tm_x, full_addr(i), pend_k[i] * kBK,
@@ -1187,10 +1180,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         split_prow = prow0;
         split_qcol = qcol0;
         if constexpr (SWAP) {
-          // Stage this CTA's fp32 partial tile in its own shared memory (the
-          // operand ring is idle: every load was consumed by the finished MMAs).
-          fence_proxy_async_smem();
-          const uint32_t row_addr = ring + static_cast<uint32_t>(lr * stage_pitch<BN>() * 4);
+          // Push this thread's partial row to the CTA that owns its feature
+          // (local rows go to this CTA's own slots through the same path).
+          if (!push_waited) {
+            cluster_wait();
+            push_waited = true;
+          }
+          constexpr int F = tc_push_features(EPI);
+          constexpr int PITCH = tc_push_pitch(BN, EPI);
+          const int f = (EPI == EPI_SWIGLU) ? (lr & 63) : lr;
+          const int owner = (f * S) / F;
+          const int f0 = (owner * F + S - 1) / S;
+          const int rm = (F + S - 1) / S;
+          const int col0 = (EPI == EPI_SWIGLU && lr >= 64) ? BN : 0;
+          const uint32_t dst = mapa_shared(
+              pbuf + static_cast<uint32_t>(((static_cast<int>(crank) * rm + (f - f0)) * PITCH + col0) * 4),
+              static_cast<uint32_t>(owner));
           float v[32];
 #pragma unroll 1
           for (int c = 0; c < BN; c += CW) {
@@ -1198,7 +1203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             else tmem_ld_32x32b_x16(taddr + c, v);
 #pragma unroll
             for (int i = 0; i < CW; i += 4)
-              st_smem_f4(row_addr + (c + i) * 4, v[i], v[i + 1], v[i + 2], v[i + 3]);
+              st_cluster_f4(dst + (c + i) * 4, v[i], v[i + 1], v[i + 2], v[i + 3]);
           }
         }
         if constexpr (!SWAP) {
@@ -1263,19 +1268,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // leaves while a copy still reads its shared memory
       cluster_sync_all();
     } else {
-      // (1) every CTA has staged its partial tile
+      // Skinny tiles: each CTA pushed its partial rows before arriving here;
+      // after this barrier every CTA reads only its own shared memory, so no
+      // CTA's memory is accessed by a peer once it passes it.
+      if (!push_waited) cluster_wait();
       cluster_sync_all();
-      // skinny tiles (small partials): each CTA sums a slice of rows over all
-      // the staged partials through distributed shared memory
-      const int rows = (EPI == EPI_SWIGLU) ? 64 : kBM;
-      const int r0 = (j * rows) / S;
-      const int r1 = ((j + 1) * rows) / S;
+      constexpr int F = tc_push_features(EPI);
+      const int f0 = (j * F + S - 1) / S;
+      const int f1 = ((j + 1) * F + S - 1) / S;
       if (!abort_flag)
-        reduce_rows<DT, BN, EPI, SWAP>(p, ring, S, split_coords[0], split_coords[1], r0, r1,
-                                       static_cast<int>(threadIdx.x), kThreads,
-                                       static_cast<uint32_t>(half), static_cast<uint32_t>(GROUP));
-      // (2) nobody reads a peer's shared memory any more
-      cluster_sync_all();
+        reduce_pushed<DT, BN, EPI>(p, pbuf, S, split_coords[0], split_coords[1], f0, f1,
+                                   (F + S - 1) / S, static_cast<int>(threadIdx.x), kThreads);
     }
   } else if constexpr (PAIR) {
     // neither CTA of the pair may leave while the other can still signal it
@@ -1384,6 +1387,11 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
+    // every kernel of this library asks for the largest shared-memory
+    // carveout, so consecutive kernels can share an SM without reconfiguring it
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
   const int cluster = (PAIR ? 2 : 1) * pl.p.split;
@@ -1409,12 +1417,15 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
 }
 
 // How many clusters of `cluster` CTAs of this tile shape can be resident at
-// once (all epilogues of one shape use the same shared memory).
+// once (skinny tiles: measured with the SwiGLU epilogue, the largest).
 template <int BN, bool SWAP, bool PAIR>
 int max_active_clusters(int cluster) {
-  constexpr int smem = tc_smem_bytes(BN, EPI_NONE, SWAP, PAIR);
-  auto kern = tc_linear_kernel<DT_F16, BN, EPI_NONE, SWAP, PAIR>;
+  constexpr int EPI = SWAP ? EPI_SWIGLU : EPI_NONE;
+  constexpr int smem = tc_smem_bytes(BN, EPI, SWAP, PAIR);
+  auto kern = tc_linear_kernel<DT_F16, BN, EPI, SWAP, PAIR>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster * 64);
   cfg.blockDim = dim3(kThreads);
@@ -1581,7 +1592,10 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
       split = G / tiles;
       if (split > 8) split = 8;
       if (split > kb / 2) split = kb / 2 > 0 ? kb / 2 : 1;
-      while (split > 1 && cluster_cap(2, bn, 0, split) <= 0) --split;
+      // every cluster resident in one wave, next to one co-resident kernel
+      // where two skinny CTAs fit on an SM
+      const int share = (tc_skinny_budget(bn) < 114 * 1024) ? 2 : 1;
+      while (split > 1 && cluster_cap(2, bn, 0, split) / share < tiles) --split;
     }
     fill_tiles(pl, K, bn, split, 0, G);
     return;

@@ -249,6 +249,23 @@ __device__ __forceinline__ void st_cluster_f4(uint32_t addr, float a, float b, f
                : "memory");
 }
 
+// The two halves of a cluster barrier, for a phase whose arrival and wait
+// are far apart.  Every thread of every CTA of the cluster arrives once and
+// waits once per phase, in that order.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait;" ::: "memory");
+}
+
+// Bring one tensor-map box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

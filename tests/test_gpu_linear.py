@@ -69,6 +69,19 @@ def test_epilogues(epi, dt, algo, M, N, K):
 
 
 @pytest.mark.parametrize("epi", ["none", "residual", "swiglu", "f32"])
+@pytest.mark.parametrize("M", [1, 24, 64])
+@pytest.mark.parametrize("K", [256, 384, 512, 640, 768, 896])
+def test_skinny_split_factors(epi, M, K):
+    # two 128-row weight tiles and K/128 pairs of 64-wide k-blocks: the
+    # planner splits K over K/128 CTAs of a cluster (2..7), each pushing its
+    # partial rows to the CTAs that own them
+    N = 128 if epi == "swiglu" else 256
+    plan = ob.plan_info(M, N, K, torch.float16, epi, "skinny")
+    assert plan["split_k"] == K // 128, plan
+    run_case(M, N, K, 0, epi, "skinny", seed=K + M)
+
+
+@pytest.mark.parametrize("epi", ["none", "residual", "swiglu", "f32"])
 def test_simt_path_unaligned_k(epi):
     # K % 8 != 0: TMA can't describe the rows; the CUDA-core kernel serves it
     run_case(7, 128, 12, 0, epi, "auto")
