@@ -171,7 +171,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 
 // ---------------------------------------------------------------------------
 // TMA (tensor copies global -> shared, completion counted on an mbarrier).
-// No multicast form is used anywhere in this library.
+// Every copy lands in exactly one CTA's shared memory.
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
@@ -189,7 +189,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
 
 // CTA-pair form (tcgen05 cta_group::2): the destination is this CTA's shared
 // memory, the completion is counted on the mbarrier at `bar`, a shared::cluster
-// address that may be the pair leader's.  Not a multicast copy.
+// address that may be the pair leader's.  The data lands in this CTA only.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar,
                                                  int c0, int c1, uint64_t policy) {
   asm volatile(
