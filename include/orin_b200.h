@@ -178,6 +178,23 @@ orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard,
                                int dtype, const void* residual,
                                float* partial_f32, void* stream);
 
+/*
+ * orin_tp_linear_row without the caller's partial buffer (no counterpart in
+ * the reference): the fp32 partial sums live in a file-scope device array of
+ * orin_tp_static_partial_capacity() floats (64 MiB), one per device; the
+ * entry point allocates nothing.  M*N above that capacity returns
+ * ORIN_ERR_UNSUPPORTED.  The array is shared by every call on a device: calls
+ * on one device must be ordered (one stream), or they corrupt each other's
+ * sums.  The first call on a device looks the array up and must not be
+ * inside stream capture.
+ */
+orin_status orin_tp_linear_row_static(void* comm, void* C, const void* A_shard,
+                                      const void* W_shard, int M, int N, int K_shard,
+                                      int dtype, const void* residual, void* stream);
+
+/* Floats of the static partial-sum array behind orin_tp_linear_row_static. */
+long long orin_tp_static_partial_capacity(void);
+
 /* Block until every collective of comm issued on stream is done or the
  * timeout passes (then the communicator is aborted). */
 orin_status orin_tp_wait(void* comm, void* stream);

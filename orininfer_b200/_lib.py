@@ -66,6 +66,8 @@ SIGNATURES = {
     "orin_tp_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i, _i, ctypes.c_double]),
     "orin_tp_allreduce_f32": (_i, [_vp, _vp, _ll, _vp]),
     "orin_tp_linear_row": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "orin_tp_linear_row_static": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "orin_tp_static_partial_capacity": (_ll, []),
     "orin_tp_wait": (_i, [_vp, _vp]),
     "orin_tp_destroy": (_i, [_vp]),
 }
