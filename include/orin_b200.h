@@ -67,7 +67,8 @@ typedef enum orin_algo {
     ORIN_ALGO_AUTO = 0,
     ORIN_ALGO_TC_WIDE = 1,   /* tcgen05, 128 tokens x 256 features per tile  */
     ORIN_ALGO_TC_SKINNY = 2, /* tcgen05, 128 features x <=64 tokens (M<=64)  */
-    ORIN_ALGO_SIMT = 3       /* CUDA-core kernel for unaligned shapes        */
+    ORIN_ALGO_SIMT = 3,      /* CUDA-core kernel for unaligned shapes        */
+    ORIN_ALGO_GEMV = 4       /* decode weight stream, M <= 16 tokens         */
 } orin_algo;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -86,7 +87,8 @@ const char* orin_last_error(void);
  *   W         [N, K] 16-bit ([2N, K] packed gate/up for SWIGLU)
  *   residual  [M, N] 16-bit for RESIDUAL, else NULL
  * Any M, N >= 1 and K >= 1 are accepted.  K % 8 == 0 with 16-byte aligned
- * A, W (and C rows) takes the tcgen05 path; other shapes take the SIMT path.
+ * A, W (and C rows) takes the decode weight stream for M <= 16 and the
+ * tcgen05 path above; other shapes take the SIMT path.
  */
 orin_status orin_linear(void* C, const void* A, const void* W,
                         int M, int N, int K, int dtype, int epilogue,
@@ -104,7 +106,8 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W,
 /*
  * Diagnostics: the launch orin_linear_ex would make for this problem on the
  * current device.  info[0] kernel (1 tcgen05 wide tiles, 2 tcgen05 skinny
- * tiles, 3 CUDA cores), info[1] tile columns, info[2] 1 if tiles run on
+ * tiles, 3 CUDA cores, 4 decode weight stream), info[1] tile columns
+ * (tokens per tile for 4), info[2] 1 if tiles run on
  * tcgen05 CTA pairs, info[3] split-K factor (cluster split), info[4] grid
  * size (CTAs), info[5] number of tiles.  Assumes 16-byte aligned operands.
  */

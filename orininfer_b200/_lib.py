@@ -42,6 +42,7 @@ ALGO_AUTO = 0
 ALGO_TC_WIDE = 1
 ALGO_TC_SKINNY = 2
 ALGO_SIMT = 3
+ALGO_GEMV = 4
 
 TP_UNIQUE_ID_BYTES = 128
 

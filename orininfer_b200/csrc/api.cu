@@ -88,12 +88,17 @@ orin_status check_common(int dtype, int epi) {
 }
 
 // Which kernel serves this call.
+// Tokens up to which AUTO takes the decode weight stream (csrc/gemv.cu).
+constexpr int kGemvAutoTokens = 16;
+
 int choose_algo(int req, const void* A, const void* W, int M, int K) {
   const bool tma_ok = (K % 8 == 0) && aligned16(A) && aligned16(W);
   if (req == ORIN_ALGO_SIMT) return 3;
   if (!tma_ok) return (req == ORIN_ALGO_AUTO) ? 3 : -1;
   if (req == ORIN_ALGO_TC_WIDE) return 1;
   if (req == ORIN_ALGO_TC_SKINNY) return (M <= 64) ? 2 : -1;
+  if (req == ORIN_ALGO_GEMV) return (M <= kGemvMaxTokens) ? 4 : -1;
+  if (M <= kGemvAutoTokens) return 4;
   return (M <= 64) ? 2 : 1;
 }
 
@@ -125,7 +130,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
     set_error("orin_linear: SWIGLU needs the intermediate size N=%d to be a multiple of 64", N);
     return ORIN_ERR_UNSUPPORTED;
   }
-  if (algo < ORIN_ALGO_AUTO || algo > ORIN_ALGO_SIMT) {
+  if (algo < ORIN_ALGO_AUTO || algo > ORIN_ALGO_GEMV) {
     set_error("orin_linear: algo %d is not an orin_algo", algo);
     return ORIN_ERR_INVALID_ARG;
   }
@@ -133,12 +138,18 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   const int a = choose_algo(algo, A, W, M, K);
   if (a < 0) {
     set_error("orin_linear: algo %d can't take M=%d K=%d (needs K%%8==0, 16-byte aligned "
-              "A and W%s)", algo, M, K, algo == ORIN_ALGO_TC_SKINNY ? ", M<=64" : "");
+              "A and W%s)", algo, M, K,
+              algo == ORIN_ALGO_TC_SKINNY ? ", M<=64" : algo == ORIN_ALGO_GEMV ? ", M<=16" : "");
     return ORIN_ERR_UNSUPPORTED;
   }
   if (a == 3) {
     cudaError_t e = launch_simt(C, A, W, M, N, K, dtype, epilogue, residual, s);
     if (e != cudaSuccess) return cuda_fail(e, "orin_linear (simt)");
+    return ORIN_OK;
+  }
+  if (a == 4) {
+    cudaError_t e = launch_gemv(C, A, W, M, N, K, dtype, epilogue, residual, s);
+    if (e != cudaSuccess) return cuda_fail(e, "orin_linear (gemv)");
     return ORIN_OK;
   }
   int dev = 0;
@@ -198,6 +209,13 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
   for (int i = 0; i < 6; ++i) info[i] = 0;
   info[0] = a;
   if (a == 3) return ORIN_OK;
+  if (a == 4) {
+    info[1] = (M <= 8) ? 8 : 16;
+    info[3] = 1;
+    info[4] = gemv_grid(N);
+    info[5] = info[4];
+    return ORIN_OK;
+  }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");

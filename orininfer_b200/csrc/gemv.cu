@@ -1,0 +1,302 @@
+// gemv.cu — decode-time linear layers (M <= 16 tokens) as a weight stream.
+//
+// At decode the weight matrix is read once per step and the token count is
+// tiny, so the kernel is bound by how early and how deeply it can keep HBM
+// busy.  Design:
+//
+// * One CTA (8 warps) per group of 16 output features: its 16 weight rows
+//   (32 for SwiGLU: 16 gate rows and the 16 matching up rows of the packed
+//   layout), over the whole of K, split evenly across the 8 warps.
+// * Every lane streams two weight rows (g and g + 8, g = lane / 4) with
+//   128-bit non-caching loads: lanes 4g .. 4g+3 cover 64 contiguous bytes of a
+//   row per 32-element k-block.  The loads of a batch of k-blocks are all in
+//   flight at once (registers, not shared memory, hold them).
+// * The products run on mma.sync.m16n8k16 (fp32 accumulate): weight rows are
+//   the MMA's M, tokens its N (8 per tile).  Within a 32-element k-block the
+//   two MMAs use a fixed permutation of k, the same for weights and tokens:
+//   lane (g, q) holds k = 8q .. 8q+7 of its rows and of token g, words 0-1 for
+//   the first MMA and 2-3 for the second.  A permutation of the k-sum leaves
+//   the dot product unchanged, and every 16-byte load is already a fragment.
+// * The first batch of weight loads and an L2 prefetch of the rest of the
+//   warp's weights are issued before griddepcontrol.wait: weights do not
+//   depend on the previous kernel, so under programmatic dependent launch
+//   they stream while it finishes.  Tokens and the residual are read after
+//   the wait, through L2 (ld.global.cg).
+// * The 8 warps' partial fragments are summed in shared memory in warp order
+//   (deterministic), and warp 0 applies the epilogue with the rounding points
+//   of the other kernels.
+//
+// The reference's decode path is kernels/matmul.cu:25-44 (one CTA per output
+// row, 2-byte loads, shared-memory tree reduction); this replaces it for
+// M = 1 and the skinny cuBLAS calls for M <= 16.  No spin-waits, no mbarriers.
+#include "orin_common.cuh"
+#include "orin_internal.h"
+
+namespace orin {
+namespace {
+
+constexpr int kGvWarps = 8;
+constexpr int kGvThreads = kGvWarps * 32;
+constexpr int kGvRows = 16;    // output features per CTA (MMA M)
+constexpr int kGvBlockK = 32;  // k elements per block: two m16n8k16 MMAs
+
+struct GvParams {
+  const void* W;
+  const void* X;
+  void* C;
+  const void* R;
+  int M, N, K;
+  int w_rows;  // rows of W: N, or 2N for the packed gate/up weight
+};
+
+__device__ __forceinline__ uint4 ld_weights(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Written by the previous kernel: read through L2 only.
+__device__ __forceinline__ uint4 ld_l2_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ unsigned short ld_l2_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void prefetch_l2_bytes(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (DT == DT_F16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float bits_to_f(unsigned short b) {
+  if constexpr (DT == DT_F16) return __half2float(__ushort_as_half(b));
+  else return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// NT token tiles of 8 (M <= 8 * NT).
+template <int DT, int EPI, int NT>
+__global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  constexpr int H = (EPI == EPI_SWIGLU) ? 2 : 1;  // row sets per group: gate, up
+  constexpr int U = (H == 2 || NT == 2) ? 4 : 8;  // k-blocks per load batch
+  constexpr int V = H * NT * 4;                   // fragment values per lane
+  __shared__ float red[kGvWarps][V][32];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int q = lane & 3;
+  const int f0 = blockIdx.x * kGvRows;  // first output feature of this CTA
+
+  // first weight row of each row set (packed gate/up: 64-row gate and up groups)
+  int wrow[H];
+  if constexpr (EPI == EPI_SWIGLU) {
+    wrow[0] = (f0 / 64) * 128 + (f0 % 64);
+    wrow[1] = wrow[0] + 64;
+  } else {
+    wrow[0] = f0;
+  }
+  const int nkb = (p.K + kGvBlockK - 1) / kGvBlockK;
+  const int kb0 = (warp * nkb) / kGvWarps;
+  const int kb1 = ((warp + 1) * nkb) / kGvWarps;
+  const T* W = static_cast<const T*>(p.W);
+  const T* X = static_cast<const T*>(p.X);
+
+  const T* wp[H][2];
+  bool wv[H][2];
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = wrow[h] + g + 8 * r;
+      wv[h][r] = row < p.w_rows;
+      wp[h][r] = W + static_cast<long long>(wv[h][r] ? row : 0) * p.K + 8 * q;
+    }
+  }
+
+  float acc[H][NT][4];
+#pragma unroll
+  for (int h = 0; h < H; ++h)
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[h][t][i] = 0.f;
+
+  bool waited = false;
+  for (int kb = kb0; kb < kb1; kb += U) {
+    uint4 w[U][H][2];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = (kb + u) * kGvBlockK + 8 * q;
+      const bool kin = (kb + u < kb1) && (k < p.K);
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          w[u][h][r] = (kin && wv[h][r]) ? ld_weights(wp[h][r] + (kb + u) * kGvBlockK)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (!waited) {
+      // the rest of this warp's k-range of every row of the group, into L2
+      const int rest = kb + U;
+      if (rest < kb1 && lane < kGvRows * H) {
+        const int row = wrow[lane / kGvRows] + lane % kGvRows;
+        const int k_end = (kb1 * kGvBlockK < p.K) ? kb1 * kGvBlockK : p.K;
+        if (row < p.w_rows)
+          prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + rest * kGvBlockK,
+                            static_cast<uint32_t>((k_end - rest * kGvBlockK) * 2));
+      }
+      pdl_launch_dependents();
+      pdl_wait();
+      waited = true;
+    }
+    uint4 x[U][NT];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = (kb + u) * kGvBlockK + 8 * q;
+      const bool kin = (kb + u < kb1) && (k < p.K);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int tok = 8 * t + g;
+        x[u][t] = (kin && tok < p.M) ? ld_l2_v4(X + static_cast<long long>(tok) * p.K + k)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          mma_16816<DT>(acc[h][t], w[u][h][0].x, w[u][h][1].x, w[u][h][0].y, w[u][h][1].y,
+                        x[u][t].x, x[u][t].y);
+          mma_16816<DT>(acc[h][t], w[u][h][0].z, w[u][h][1].z, w[u][h][0].w, w[u][h][1].w,
+                        x[u][t].z, x[u][t].w);
+        }
+  }
+  if (!waited) {
+    // a warp without k-blocks (K shorter than 8 blocks) still orders its
+    // reads of the residual after the previous kernel
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+
+#pragma unroll
+  for (int h = 0; h < H; ++h)
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[warp][(h * NT + t) * 4 + i][lane] = acc[h][t][i];
+  __syncthreads();
+  if (warp != 0) return;
+
+  float s[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    float a = red[0][v][lane];
+#pragma unroll
+    for (int ww = 1; ww < kGvWarps; ++ww) a += red[ww][v][lane];
+    s[v] = a;
+  }
+  // fragment value i of tile t: row g + 8*(i/2), token 8t + 2q + (i%2)
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = f0 + g + 8 * (i >> 1);
+      const int m = 8 * t + 2 * q + (i & 1);
+      if (n >= p.N || m >= p.M) continue;
+      const long long o = static_cast<long long>(m) * p.N + n;
+      const float a = s[t * 4 + i];
+      if constexpr (EPI == EPI_NONE) {
+        static_cast<T*>(p.C)[o] = E::from_f(a);
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        const float r = bits_to_f<DT>(ld_l2_u16(static_cast<const T*>(p.R) + o));
+        static_cast<T*>(p.C)[o] = E::from_f(r + E::round(a));
+      } else if constexpr (EPI == EPI_F32_OUT) {
+        static_cast<float*>(p.C)[o] = E::round(a);
+      } else if constexpr (EPI == EPI_F32_PARTIAL) {
+        static_cast<float*>(p.C)[o] = a;
+      } else {
+        const float u = s[(NT + t) * 4 + i];
+        static_cast<T*>(p.C)[o] = E::from_f(silu_f32(E::round(a)) * E::round(u));
+      }
+    }
+  }
+}
+
+template <int DT, int EPI, int NT>
+cudaError_t gemv_launch(const GvParams& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + kGvRows - 1) / kGvRows);
+  cfg.blockDim = dim3(kGvThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<DT, EPI, NT>, p);
+}
+
+template <int DT, int NT>
+cudaError_t gemv_dispatch(const GvParams& p, int epi, cudaStream_t s) {
+  switch (epi) {
+    case EPI_NONE: return gemv_launch<DT, EPI_NONE, NT>(p, s);
+    case EPI_SWIGLU: return gemv_launch<DT, EPI_SWIGLU, NT>(p, s);
+    case EPI_RESIDUAL: return gemv_launch<DT, EPI_RESIDUAL, NT>(p, s);
+    case EPI_F32_OUT: return gemv_launch<DT, EPI_F32_OUT, NT>(p, s);
+    case EPI_F32_PARTIAL: return gemv_launch<DT, EPI_F32_PARTIAL, NT>(p, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int gemv_grid(int N) { return (N + kGvRows - 1) / kGvRows; }
+
+cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epi, const void* R, cudaStream_t s) {
+  if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
+  GvParams p;
+  p.W = W;
+  p.X = A;
+  p.C = C;
+  p.R = R;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.w_rows = (epi == EPI_SWIGLU) ? 2 * N : N;
+  if (dtype == DT_F16)
+    return (M <= 8) ? gemv_dispatch<DT_F16, 1>(p, epi, s) : gemv_dispatch<DT_F16, 2>(p, epi, s);
+  return (M <= 8) ? gemv_dispatch<DT_BF16, 1>(p, epi, s) : gemv_dispatch<DT_BF16, 2>(p, epi, s);
+}
+
+}  // namespace orin

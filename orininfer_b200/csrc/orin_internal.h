@@ -30,7 +30,7 @@ struct TcParams {
 };
 
 struct Plan {
-  int algo;          // 1 wide, 2 skinny, 3 simt
+  int algo;          // 1 wide, 2 skinny, 3 simt, 4 gemv
   int bn;            // tile columns (Q extent)
   int pair;          // 1: tiles of 256 P rows on tcgen05 CTA pairs
   int grid;
@@ -53,6 +53,13 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count);
 // Launch the tcgen05 GEMM described by pl.
 cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const void* W,
                       int* err, cudaStream_t stream, const char** why);
+
+// Decode-time weight-streaming kernel (csrc/gemv.cu) for M <= kGemvMaxTokens,
+// K % 8 == 0 and 16-byte aligned A and W.  Same epilogues and rounding.
+constexpr int kGemvMaxTokens = 16;
+cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epi, const void* R, cudaStream_t stream);
+int gemv_grid(int N);
 
 // CUDA-core GEMM for shapes the tcgen05 path can't take (K % 8 != 0,
 // unaligned rows).  Same epilogues and rounding.

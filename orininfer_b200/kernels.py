@@ -40,6 +40,7 @@ _ALGOS = {
     "wide": _lib.ALGO_TC_WIDE,
     "skinny": _lib.ALGO_TC_SKINNY,
     "simt": _lib.ALGO_SIMT,
+    "gemv": _lib.ALGO_GEMV,
 }
 
 __all__ = [
@@ -160,7 +161,7 @@ def plan_info(M: int, N: int, K: int, dtype: torch.dtype = torch.float16,
     info = (ctypes.c_int * 6)()
     check(_lib.lib.orin_plan_info(M, N, K, _DTYPES[dtype], _EPILOGUES[epilogue], _ALGOS[algo],
                                   info))
-    kind = {1: "tcgen05-wide", 2: "tcgen05-skinny", 3: "cuda-core"}[info[0]]
+    kind = {1: "tcgen05-wide", 2: "tcgen05-skinny", 3: "cuda-core", 4: "gemv"}[info[0]]
     return {"kernel": kind, "tile_cols": info[1], "cta_pair": bool(info[2]), "split_k": info[3],
             "grid": info[4], "tiles": info[5]}
 

@@ -68,6 +68,30 @@ def test_epilogues(epi, dt, algo, M, N, K):
     run_case(M, N, K, dt, epi, algo)
 
 
+GEMV = [(1, 2048, 2048), (1, 200, 520), (3, 384, 72), (8, 2560, 2048), (9, 1024, 5632),
+        (16, 256, 8), (5, 4100, 136)]
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("M,N,K", GEMV)
+def test_gemv_none(dt, M, N, K):
+    # decode weight stream: ragged feature groups (N % 16), K not a multiple of
+    # the 32-element k-block, K = 8 (one block: seven warps without work)
+    run_case(M, N, K, dt, "none", "gemv")
+
+
+@pytest.mark.parametrize("epi", ["residual", "f32", "f32_partial", "swiglu"])
+@pytest.mark.parametrize("M", [1, 7, 16])
+def test_gemv_epilogues(epi, M):
+    run_case(M, 384, 1000, 1 if M == 7 else 0, epi, "gemv", seed=M)
+
+
+def test_gemv_is_the_decode_default():
+    for M in (1, 8, 16):
+        assert ob.plan_info(M, 2048, 2048)["kernel"] == "gemv"
+    assert ob.plan_info(17, 2048, 2048)["kernel"] == "tcgen05-skinny"
+
+
 @pytest.mark.parametrize("epi", ["none", "residual", "swiglu", "f32"])
 @pytest.mark.parametrize("M", [1, 24, 64])
 @pytest.mark.parametrize("K", [256, 384, 512, 640, 768, 896])
@@ -102,7 +126,8 @@ def test_residual_in_place():
 
 
 def test_output_guard_regions_untouched():
-    for algo, (M, N, K) in (("wide", (200, 300, 136)), ("skinny", (5, 200, 64))):
+    for algo, (M, N, K) in (("wide", (200, 300, 136)), ("skinny", (5, 200, 64)),
+                            ("gemv", (5, 200, 64))):
         guard = 4096
         buf = torch.full((guard + M * N + guard,), 1234.0, dtype=torch.float16, device=DEV)
         out = buf[guard:guard + M * N].view(M, N)
@@ -117,7 +142,7 @@ def test_dependent_chain_with_programmatic_launch():
     """A chain of dependent GEMMs back to back (each kernel starts its weight
     loads before the previous one finishes) matches the oracle chain."""
     dims = [512, 1024, 256, 768, 512]
-    for M, algo in ((1, "skinny"), (48, "skinny"), (256, "wide")):
+    for M, algo in ((1, "skinny"), (48, "skinny"), (256, "wide"), (1, "gemv"), (12, "gemv")):
         x = seeded((M, dims[0]), 10, 1.0)
         ws = [seeded((dims[i + 1], dims[i]), 20 + i, 0.05) for i in range(len(dims) - 1)]
         h = x.to(DEV)
