@@ -16,8 +16,9 @@ streams its weights from HBM.
 
 N > 1 (launched by torch.distributed.run): tensor parallel over N GPUs, the
 same total work (strong scaling): q/k/v by heads (KV heads replicated when
-N > 4), gate/up by intermediate feature, o/down by K followed by an fp32 NCCL
-all-reduce and the residual/rounding step.
+N > 4), gate/up by intermediate feature, o/down by K followed by the fp32
+reduction of the partial sums over NVLink peer memory (or ncclAllReduce with
+--nccl-reduce) and the residual/rounding step.
 
 --impl reference: the reference has no CPU implementation of this path, so the
 reference arm times the CPU oracle's multithreaded fp32 GEMM (oracle/liborc.so)
@@ -580,6 +581,10 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         uid = tp.exchange_unique_id(rank)
         comm = tp.TPComm(rank, world, local_rank, uid, timeout_s=120.0)
+        if not args.nccl_reduce:
+            # o/down partial sums reduced over NVLink peer memory (falls back
+            # to ncclAllReduce only where a call does not fit)
+            comm.enable_p2p(M * H)
     layers = make_layers(rank, world, dev)
     step = Step(layers, rank, world, dev, comm)
 
@@ -612,6 +617,8 @@ def run_ours(args, rank, world, local_rank):
                    "q_heads": N_HEADS, "kv_heads": N_KV, "head_dim": HEAD_DIM,
                    "flops_per_step": STEP_FLOPS,
                    "parallelism": "tp%d" % world if world > 1 else "single",
+                   "tp_reduce": ("nccl" if args.nccl_reduce else "nvlink-p2p") if world > 1
+                   else None,
                    "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies "
                          f"({N_COPIES * 88} MB of weights)"},
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
@@ -788,6 +795,9 @@ def main():
     ap.add_argument("--decode-reps", type=int, default=20,
                     help="graph replays of the whole-model decode GEMM path per token count "
                          "(0: skip)")
+    ap.add_argument("--nccl-reduce", action="store_true",
+                    help="N>1: reduce the row-parallel partial sums with ncclAllReduce instead "
+                         "of the peer-memory kernels")
     ap.add_argument("--no-cublas-bar", dest="cublas_bar", action="store_false",
                     help="skip timing the cuBLAS comparison bar")
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,

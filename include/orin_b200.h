@@ -174,7 +174,8 @@ orin_status orin_tp_allreduce_f32(void* comm, float* buf, long long n,
  *   sum     = all-reduce(partial)  over ranks
  *   C       = round16(f32(residual) + f32(round16(sum)))   if residual
  *           = round16(sum)                                   otherwise
- * partial_f32 is caller scratch of M*N floats.  C may alias residual.
+ * partial_f32 is caller scratch of M*N floats (may be NULL when the call
+ * takes the peer-memory reduction below).  C may alias residual.
  */
 orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard,
                                const void* W_shard, int M, int N, int K_shard,
@@ -197,6 +198,23 @@ orin_status orin_tp_linear_row_static(void* comm, void* C, const void* A_shard,
 
 /* Floats of the static partial-sum array behind orin_tp_linear_row_static. */
 long long orin_tp_static_partial_capacity(void);
+
+/*
+ * Give the communicator a peer-memory reduction for row-parallel calls
+ * (no counterpart in the reference).  Collective: every rank calls it with
+ * the same max_elems.  Each rank allocates one region (fp32 partials and
+ * 16-bit results of max_elems elements, plus flags) and maps every peer's
+ * (CUDA IPC over NVLink; the handles travel over the communicator).  From
+ * then on orin_tp_linear_row with M*N <= max_elems, N % 8 == 0 and 16-byte
+ * aligned C and residual reduces with one kernel of plain peer loads and
+ * stores instead of ncclAllReduce: each rank sums the rows it owns over all
+ * ranks in rank order (deterministic), applies residual and rounding, and
+ * copies the other ranks' finished rows (blocks synchronise only with the
+ * same block of each peer).  Every cross-GPU wait gives up after
+ * 2 s (orin_device_check reports ORIN_ERR_TIMEOUT; destroy the communicator).
+ * ORIN_ERR_UNSUPPORTED if the GPUs can't map each other's memory.
+ */
+orin_status orin_tp_enable_p2p(void* comm, long long max_elems, void* stream);
 
 /* Block until every collective of comm issued on stream is done or the
  * timeout passes (then the communicator is aborted). */

@@ -26,7 +26,8 @@ enum : int {
   DEVERR_TIMEOUT_PRODUCER = 1,
   DEVERR_TIMEOUT_MMA = 2,
   DEVERR_TIMEOUT_EPILOGUE = 3,
-  DEVERR_TIMEOUT_DRAIN = 4
+  DEVERR_TIMEOUT_DRAIN = 4,
+  DEVERR_TIMEOUT_PEER = 5
 };
 
 // A spin-wait that has not completed after this long gives up.

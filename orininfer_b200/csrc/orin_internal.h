@@ -77,6 +77,30 @@ cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM
 cudaError_t launch_finish_rows(void* C, const float* S, const void* R, long long n, int dtype,
                                cudaStream_t s);
 
+// Row-parallel reduction over peer memory (csrc/tp_p2p.cu).  Each rank's
+// shared region starts with a flag block of ints written by the peers, one
+// per (block, rank): "partial ready" at kP2PArrive + b * kP2PMaxRanks + rank,
+// "rows done" at kP2PDone + b * kP2PMaxRanks + rank.
+constexpr int kP2PMaxRanks = 8;
+constexpr int kP2PMaxBlocks = 1024;
+constexpr int kP2PArrive = 0;
+constexpr int kP2PDone = kP2PMaxBlocks * kP2PMaxRanks;
+constexpr int kP2PFlagBytes = 2 * kP2PMaxBlocks * kP2PMaxRanks * 4;
+struct P2PView {
+  int rank, world, N;
+  long long row0[kP2PMaxRanks + 1];  // rank r owns rows [row0[r], row0[r+1])
+  const float* partial[kP2PMaxRanks];
+  const void* result[kP2PMaxRanks];
+  int* flags[kP2PMaxRanks];
+  int* local_flags;
+  void* result_local;
+  void* C;
+  const void* R;
+  int* epoch;  // kP2PMaxBlocks per-block epochs (this rank's memory)
+  int* err;
+};
+cudaError_t launch_p2p_reduce(const P2PView& v, int dtype, cudaStream_t s);
+
 // Record a failure message for orin_last_error().
 void set_error(const char* fmt, ...);
 

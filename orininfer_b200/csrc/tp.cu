@@ -11,6 +11,11 @@
 // Communicators are created non-blocking; every wait on NCCL or on the stream
 // is bounded by the communicator's timeout, after which it is aborted and the
 // call returns ORIN_ERR_TIMEOUT.
+//
+// orin_tp_enable_p2p gives a communicator a peer-memory region (one
+// cudaMalloc per rank, mapped by every peer through CUDA IPC; the handles
+// travel over the communicator itself): row-parallel calls that fit then
+// reduce with the kernel of tp_p2p.cu instead of ncclAllReduce.
 #include "orin_b200.h"
 #include "orin_internal.h"
 
@@ -28,7 +33,17 @@ struct TpComm {
   int rank = 0, world = 1, device = 0;
   double timeout_s = 30.0;
   bool aborted = false;
+  // peer-memory reduction (orin_tp_enable_p2p)
+  bool p2p = false;
+  long long p2p_cap = 0;               // partial-sum elements the region holds
+  char* region = nullptr;              // flags | fp32 partial | 16-bit result
+  char* peer_region[kP2PMaxRanks] = {};
+  int* state = nullptr;                // per-block epochs (kP2PMaxBlocks ints)
 };
+
+constexpr long long align256(long long b) { return (b + 255) & ~255LL; }
+long long p2p_partial_off() { return kP2PFlagBytes; }
+long long p2p_result_off(long long cap) { return kP2PFlagBytes + align256(cap * 4); }
 
 static_assert(sizeof(ncclUniqueId) == ORIN_TP_UNIQUE_ID_BYTES, "NCCL unique id size changed");
 
@@ -143,8 +158,51 @@ orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard, const v
                                int M, int N, int K_shard, int dtype, const void* residual,
                                float* partial_f32, void* stream) {
   TpComm* c = static_cast<TpComm*>(comm);
-  if (!c || !C || !partial_f32) {
-    set_error("orin_tp_linear_row: null communicator, output or partial buffer");
+  if (!c || !C || M < 1 || N < 1) {
+    set_error("orin_tp_linear_row: null communicator or output, or non-positive size");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  const bool aligned = (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(residual) % 16 == 0);
+  if (c->p2p && static_cast<long long>(M) * N <= c->p2p_cap && N % 8 == 0 && aligned) {
+    float* part = reinterpret_cast<float*>(c->region + p2p_partial_off());
+    orin_status st = orin_linear(part, A_shard, W_shard, M, N, K_shard, dtype,
+                                 ORIN_EPI_F32_PARTIAL, nullptr, stream);
+    if (st != ORIN_OK) return st;
+    cudaError_t e = cudaSuccess;
+    DeviceCtx* ctx = device_ctx(c->device, &e);
+    if (!ctx) {
+      set_error("orin_tp_linear_row: device set-up: %s", cudaGetErrorString(e));
+      return ORIN_ERR_CUDA;
+    }
+    P2PView v = {};
+    v.rank = c->rank;
+    v.world = c->world;
+    v.N = N;
+    for (int r = 0; r <= c->world; ++r)
+      v.row0[r] = static_cast<long long>(r) * M / c->world;
+    for (int r = 0; r < c->world; ++r) {
+      char* base = (r == c->rank) ? c->region : c->peer_region[r];
+      v.partial[r] = reinterpret_cast<const float*>(base + p2p_partial_off());
+      v.result[r] = base + p2p_result_off(c->p2p_cap);
+      v.flags[r] = reinterpret_cast<int*>(base);
+    }
+    v.local_flags = reinterpret_cast<int*>(c->region);
+    v.result_local = c->region + p2p_result_off(c->p2p_cap);
+    v.C = C;
+    v.R = residual;
+    v.epoch = c->state;
+    v.err = ctx->err;
+    e = launch_p2p_reduce(v, dtype, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+      set_error("orin_tp_linear_row: peer-memory reduction: %s", cudaGetErrorString(e));
+      return ORIN_ERR_CUDA;
+    }
+    return ORIN_OK;
+  }
+  if (!partial_f32) {
+    set_error("orin_tp_linear_row: null partial buffer (needed unless the peer-memory "
+              "reduction is enabled and the problem fits it)");
     return ORIN_ERR_INVALID_ARG;
   }
   orin_status st = orin_linear(partial_f32, A_shard, W_shard, M, N, K_shard, dtype,
@@ -158,6 +216,89 @@ orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard, const v
     set_error("orin_tp_linear_row: finish kernel: %s", cudaGetErrorString(e));
     return ORIN_ERR_CUDA;
   }
+  return ORIN_OK;
+}
+
+orin_status orin_tp_enable_p2p(void* comm, long long max_elems, void* stream) {
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (!c || max_elems < 8) {
+    set_error("orin_tp_enable_p2p: null communicator or max_elems < 8");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (c->aborted) {
+    set_error("orin_tp_enable_p2p: communicator was aborted");
+    return ORIN_ERR_NCCL;
+  }
+  if (c->p2p) {
+    if (max_elems <= c->p2p_cap) return ORIN_OK;
+    set_error("orin_tp_enable_p2p: already enabled for %lld elements", c->p2p_cap);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (c->world > kP2PMaxRanks) {
+    set_error("orin_tp_enable_p2p: %d ranks; at most %d", c->world, kP2PMaxRanks);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = cudaSetDevice(c->device);
+  const long long bytes = p2p_result_off(max_elems) + align256(max_elems * 2);
+  char* region = nullptr;
+  int* state = nullptr;
+  char* dbuf = nullptr;
+  cudaIpcMemHandle_t handles[kP2PMaxRanks];
+  orin_status st = ORIN_OK;
+  auto fail = [&](orin_status code, const char* what) {
+    set_error("orin_tp_enable_p2p: %s: %s", what, cudaGetErrorString(e));
+    st = code;
+  };
+  if (e != cudaSuccess) fail(ORIN_ERR_CUDA, "cudaSetDevice");
+  if (st == ORIN_OK && (e = cudaMalloc(&region, bytes)) != cudaSuccess) fail(ORIN_ERR_CUDA, "cudaMalloc");
+  if (st == ORIN_OK && (e = cudaMalloc(&state, kP2PMaxBlocks * sizeof(int))) != cudaSuccess)
+    fail(ORIN_ERR_CUDA, "cudaMalloc");
+  if (st == ORIN_OK) {
+    // flags and counters are zero before any peer can learn where they are
+    cudaMemset(region, 0, kP2PFlagBytes);
+    cudaMemset(state, 0, kP2PMaxBlocks * sizeof(int));
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) fail(ORIN_ERR_CUDA, "zeroing the flags");
+  }
+  if (st == ORIN_OK && (e = cudaIpcGetMemHandle(&handles[c->rank], region)) != cudaSuccess)
+    fail(ORIN_ERR_UNSUPPORTED, "cudaIpcGetMemHandle");
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  if (st == ORIN_OK && (e = cudaMalloc(&dbuf, hb * c->world)) != cudaSuccess)
+    fail(ORIN_ERR_CUDA, "cudaMalloc");
+  if (st == ORIN_OK &&
+      (e = cudaMemcpy(dbuf + hb * c->rank, &handles[c->rank], hb, cudaMemcpyHostToDevice)) !=
+          cudaSuccess)
+    fail(ORIN_ERR_CUDA, "cudaMemcpy");
+  if (st == ORIN_OK) {
+    ncclResult_t r = ncclAllGather(dbuf + hb * c->rank, dbuf, hb, ncclUint8, c->comm,
+                                   static_cast<cudaStream_t>(stream));
+    st = settle(c, r, "orin_tp_enable_p2p: handle exchange");
+    if (st == ORIN_OK) st = orin_tp_wait(c, stream);
+  }
+  if (st == ORIN_OK &&
+      (e = cudaMemcpy(handles, dbuf, hb * c->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
+    fail(ORIN_ERR_CUDA, "cudaMemcpy");
+  for (int p = 0; st == ORIN_OK && p < c->world; ++p) {
+    if (p == c->rank) continue;
+    void* ptr = nullptr;
+    e = cudaIpcOpenMemHandle(&ptr, handles[p], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      fail(ORIN_ERR_UNSUPPORTED, "cudaIpcOpenMemHandle (no peer access between these GPUs?)");
+      break;
+    }
+    c->peer_region[p] = static_cast<char*>(ptr);
+  }
+  if (dbuf) cudaFree(dbuf);
+  if (st != ORIN_OK) {
+    for (int p = 0; p < c->world; ++p)
+      if (c->peer_region[p]) cudaIpcCloseMemHandle(c->peer_region[p]), c->peer_region[p] = nullptr;
+    if (region) cudaFree(region);
+    if (state) cudaFree(state);
+    return st;
+  }
+  c->region = region;
+  c->state = state;
+  c->p2p_cap = max_elems;
+  c->p2p = true;
   return ORIN_OK;
 }
 
@@ -193,6 +334,25 @@ orin_status orin_tp_destroy(void* comm) {
   TpComm* c = static_cast<TpComm*>(comm);
   if (!c) return ORIN_OK;
   orin_status st = ORIN_OK;
+  if (c->p2p) {
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    // no peer may still read this rank's region: one collective step first
+    if (!c->aborted) {
+      int* one = nullptr;
+      if (cudaMalloc(&one, sizeof(int)) == cudaSuccess) {
+        cudaMemset(one, 0, sizeof(int));
+        ncclResult_t r = ncclAllReduce(one, one, 1, ncclInt32, ncclSum, c->comm, nullptr);
+        if (settle(c, r, "orin_tp_destroy barrier") == ORIN_OK) orin_tp_wait(c, nullptr);
+        cudaFree(one);
+      }
+    }
+    for (int p = 0; p < c->world; ++p)
+      if (c->peer_region[p]) cudaIpcCloseMemHandle(c->peer_region[p]);
+    cudaFree(c->region);
+    cudaFree(c->state);
+    c->p2p = false;
+  }
   if (c->comm && !c->aborted) {
     ncclResult_t r = ncclCommFinalize(c->comm);
     st = settle(c, r, "ncclCommFinalize");

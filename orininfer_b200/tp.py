@@ -150,6 +150,11 @@ class TPComm:
                                           _ptr(partial), _stream(stream)))
         return out
 
+    def enable_p2p(self, max_elems: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Collective: reduce row-parallel calls of up to max_elems outputs over
+        NVLink peer memory instead of NCCL (orin_tp_enable_p2p)."""
+        check(_lib.lib.orin_tp_enable_p2p(self._h, int(max_elems), _stream(stream)))
+
     def wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         check(_lib.lib.orin_tp_wait(self._h, _stream(stream)))
 

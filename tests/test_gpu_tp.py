@@ -1,4 +1,5 @@
-"""Tensor-parallel row linear over NCCL on 2 GPUs (one process per GPU).
+"""Tensor-parallel row linear on 2 GPUs (one process per GPU), reduced by
+NCCL and by the peer-memory kernels.
 
 Each rank holds a K-shard of the o_proj / down_proj weight; orin_tp_linear_row
 computes its fp32 partial, all-reduces it over NCCL and applies the residual
@@ -48,14 +49,51 @@ def _worker(rank, world, port, q):
         res = seeded((M, H), 3, 1.0)
         # row-parallel down_proj with the residual folded in
         ks = IM // world
-        out = comm.linear_row(act[:, rank * ks:(rank + 1) * ks].contiguous().to(dev),
-                              tp.shard_cols(wd, rank, world).to(dev), residual=res.to(dev))
+        a_dev = act[:, rank * ks:(rank + 1) * ks].contiguous().to(dev)
+        w_dev = tp.shard_cols(wd, rank, world).to(dev)
+        r_dev = res.to(dev)
+        out = comm.linear_row(a_dev, w_dev, residual=r_dev)
         comm.wait()
         ob.device_check()
         ref = orc.linear(bits(act), bits(wd), 0, "residual", bits(res))
         # the fp32 sum over ranks differs from one GPU's only in summation order
         assert_close(out.cpu().float(), from_bits(ref, torch.float16).float(),
                      f"row-parallel rank {rank}", exact_min=EXACT_MIN)
+
+        # The same calls reduced over NVLink peer memory: two ranks sum p0 + p1
+        # either way, so the bits equal the NCCL path's.
+        comm.enable_p2p(M * H)
+        outs = [comm.linear_row(a_dev, w_dev, residual=r_dev) for _ in range(3)]
+        comm.wait()
+        ob.device_check()
+        for i, o in enumerate(outs):
+            assert torch.equal(o.view(torch.int16), out.view(torch.int16)), f"p2p call {i}"
+        # captured once, replayed: the epoch lives in device memory
+        static_out = torch.empty_like(out)
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                comm.linear_row(a_dev, w_dev, residual=r_dev, out=static_out, stream=cs)
+        torch.cuda.current_stream().wait_stream(cs)
+        for rep in range(3):
+            static_out.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            ob.device_check()
+            assert torch.equal(static_out.view(torch.int16), out.view(torch.int16)), \
+                f"graph replay {rep}"
+        del g
+        # no residual, and rows that do not split evenly over the ranks
+        m7 = 7
+        a7 = seeded((m7, IM), 8, 1.0)
+        o7 = comm.linear_row(a7[:, rank * ks:(rank + 1) * ks].contiguous().to(dev), w_dev)
+        comm.wait()
+        ob.device_check()
+        ref7 = orc.linear(bits(a7), bits(wd), 0, "none")
+        assert_close(o7.cpu().float(), from_bits(ref7, torch.float16).float(),
+                     f"p2p no residual M=7 rank {rank}", exact_min=EXACT_MIN)
         # column-parallel gate/up with SwiGLU on this rank's packed shard
         wg = seeded((IM, H), 4, 0.02)
         wu = seeded((IM, H), 5, 0.02)
