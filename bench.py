@@ -537,6 +537,92 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
     return out
 
 
+L3_M, L3_H, L3_IM, L3_HEADS, L3_KV, L3_HD = 4096, 4096, 14336, 32, 8, 128
+L3_FLOPS = 2 * L3_M * ((L3_HEADS + 2 * L3_KV) * L3_HD * L3_H + L3_H * L3_H + 2 * L3_IM * L3_H
+                       + L3_H * L3_IM)  # 1786.7 GFLOP
+
+
+def llama3_tp_layer(rank: int, world: int, dev, comm, reps: int) -> dict:
+    """Llama-3-8B-shaped decoder layer projections at prefill M=4096, tensor
+    parallel over the job's GPUs: q/k/v column-parallel by heads (32/N query,
+    8/N KV heads per rank), gate/up by intermediate feature, o_proj and
+    down_proj row-parallel with the cross-GPU reduction, residual and SwiGLU
+    fused as in the TinyLlama step.  Each rank draws its own random-init shard
+    (the shapes are what a sharded checkpoint would give), rotated over enough
+    copies to exceed L2.  1786.7 GFLOP per step for the whole job."""
+    import math
+
+    import orininfer_b200 as ob
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77 + rank)
+
+    def w(r, c):
+        return (torch.randn((r, c), generator=gen, device=dev) * 0.02).half()
+
+    qkv_rows = (L3_HEADS // world + 2 * max(1, L3_KV // world)) * L3_HD
+    im_l = L3_IM // world
+    per_rank = 2 * (qkv_rows * L3_H + L3_H * (L3_H // world) + 2 * im_l * L3_H + L3_H * im_l)
+    copies = max(1, min(4, math.ceil(300e6 / per_rank)))
+    layers = [dict(qkv=w(qkv_rows, L3_H), o=w(L3_H, L3_H // world), gu=w(2 * im_l, L3_H),
+                   d=w(L3_H, im_l)) for _ in range(copies)]
+    x = w(L3_M, L3_H) * 50          # ~N(0,1) activations
+    attn = w(L3_M, L3_H // world) * 50
+    res = w(L3_M, L3_H) * 50
+    qkv = torch.empty((L3_M, qkv_rows), dtype=torch.float16, device=dev)
+    x1 = torch.empty((L3_M, L3_H), dtype=torch.float16, device=dev)
+    act = torch.empty((L3_M, im_l), dtype=torch.float16, device=dev)
+    x2 = torch.empty((L3_M, L3_H), dtype=torch.float16, device=dev)
+    part = torch.empty((L3_M, L3_H), dtype=torch.float32, device=dev) if world > 1 else None
+
+    def run(i):
+        L = layers[i % copies]
+        ob.linear_into(qkv, x, L["qkv"])
+        if world == 1:
+            ob.linear_into(x1, attn, L["o"], epilogue="residual", residual=res)
+        else:
+            comm.linear_row(attn, L["o"], residual=res, out=x1, partial=part)
+        ob.linear_into(act, x, L["gu"], epilogue="swiglu")
+        if world == 1:
+            ob.linear_into(x2, act, L["d"], epilogue="residual", residual=x1)
+        else:
+            comm.linear_row(act, L["d"], residual=x1, out=x2, partial=part)
+
+    run(0)
+    torch.cuda.synchronize()
+    n = 20
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(g, stream=cs):
+            for i in range(n):
+                run(i)
+    torch.cuda.current_stream().wait_stream(cs)
+    g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / (reps * n), world)
+    del g
+    ob.device_check()
+    peaks, src = load_peaks()
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    job = L3_FLOPS / (ms / 1e3) / 1e12
+    return {"workload": "llama3_8b_layer_prefill_m4096", "tp": world, "ms_per_step": round(ms, 4),
+            "tflops": round(job, 1), "tflops_per_gpu": round(job / world, 1),
+            "frac_of_peak_per_gpu": round(job / world / peak, 4),
+            "peak": f"{peak} TFLOP/s dense bf16 burst ({src})", "flops_per_step": L3_FLOPS,
+            "steps": reps * n, "weight_copies": copies}
+
+
 def cpu_baseline_layer(budget_s: float = 10.0) -> dict:
     """The oracle's fp32 multithreaded GEMM over the same layer shapes."""
     import numpy as np
@@ -584,7 +670,7 @@ def run_ours(args, rank, world, local_rank):
         if not args.nccl_reduce:
             # o/down partial sums reduced over NVLink peer memory (falls back
             # to ncclAllReduce only where a call does not fit)
-            comm.enable_p2p(M * H)
+            comm.enable_p2p(max(M * H, L3_M * L3_H))
     layers = make_layers(rank, world, dev)
     step = Step(layers, rank, world, dev, comm)
 
@@ -654,6 +740,8 @@ def run_ours(args, rank, world, local_rank):
             else None
         if args.decode_reps > 0:
             line["decode"] = decode_path(dev, args.decode_reps, args.cublas_bar)
+    if args.llama3_reps > 0:
+        line["llama3_tp"] = llama3_tp_layer(rank, world, dev, comm, args.llama3_reps)
     if comm is not None:
         torch.cuda.synchronize()
         comm.close()
@@ -794,6 +882,9 @@ def main():
                     help="steps of the per-projection CUDA-event breakdown")
     ap.add_argument("--decode-reps", type=int, default=20,
                     help="graph replays of the whole-model decode GEMM path per token count "
+                         "(0: skip)")
+    ap.add_argument("--llama3-reps", type=int, default=3,
+                    help="graph replays (20 steps each) of the Llama-3-8B TP layer measurement "
                          "(0: skip)")
     ap.add_argument("--nccl-reduce", action="store_true",
                     help="N>1: reduce the row-parallel partial sums with ncclAllReduce instead "
