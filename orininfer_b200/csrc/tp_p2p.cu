@@ -136,14 +136,24 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(const P2PVie
   long long lo, hi;
   chunk_of(v, v.rank, lo, hi);
   for (long long i = lo + 8 * threadIdx.x; i < hi; i += 8 * kP2PThreads) {
-    const float4 a0 = ld_peer_f4(v.partial[0] + i);
-    const float4 b0 = ld_peer_f4(v.partial[0] + i + 4);
-    float s[8] = {a0.x, a0.y, a0.z, a0.w, b0.x, b0.y, b0.z, b0.w};
-    for (int p = 1; p < v.world; ++p) {
-      const float4 a = ld_peer_f4(v.partial[p] + i);
-      const float4 b = ld_peer_f4(v.partial[p] + i + 4);
-      s[0] += a.x; s[1] += a.y; s[2] += a.z; s[3] += a.w;
-      s[4] += b.x; s[5] += b.y; s[6] += b.z; s[7] += b.w;
+    // every rank's loads are issued before the first add (peer loads take
+    // 1-2 us; issued one rank at a time they would serialise), then summed in
+    // rank order
+    float4 a[kP2PMaxRanks], b[kP2PMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kP2PMaxRanks; ++p) {
+      if (p < v.world) {
+        a[p] = ld_peer_f4(v.partial[p] + i);
+        b[p] = ld_peer_f4(v.partial[p] + i + 4);
+      }
+    }
+    float s[8] = {a[0].x, a[0].y, a[0].z, a[0].w, b[0].x, b[0].y, b[0].z, b[0].w};
+#pragma unroll
+    for (int p = 1; p < kP2PMaxRanks; ++p) {
+      if (p < v.world) {
+        s[0] += a[p].x; s[1] += a[p].y; s[2] += a[p].z; s[3] += a[p].w;
+        s[4] += b[p].x; s[5] += b[p].y; s[6] += b[p].z; s[7] += b[p].w;
+      }
     }
     float o[8];
     if (R) {
@@ -172,8 +182,21 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_allreduce_kernel(const P2PVie
       if (q == v.rank) continue;
       chunk_of(v, q, lo, hi);
       const T* src = static_cast<const T*>(v.result[q]);
-      for (long long i = lo + 8 * threadIdx.x; i < hi; i += 8 * kP2PThreads)
-        *reinterpret_cast<uint4*>(C + i) = ld_peer_u4(src + i);
+      // four chunks in flight per thread before their stores
+      constexpr int kU = 4;
+      for (long long i0 = lo + 8 * threadIdx.x; i0 < hi; i0 += 8LL * kP2PThreads * kU) {
+        uint4 t[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const long long i = i0 + 8LL * kP2PThreads * u;
+          if (i < hi) t[u] = ld_peer_u4(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const long long i = i0 + 8LL * kP2PThreads * u;
+          if (i < hi) *reinterpret_cast<uint4*>(C + i) = t[u];
+        }
+      }
     }
   }
   if (threadIdx.x == 0) v.epoch[blockIdx.x] = e;
