@@ -68,7 +68,7 @@ typedef enum orin_algo {
     ORIN_ALGO_TC_WIDE = 1,   /* tcgen05, 128 tokens x 256 features per tile  */
     ORIN_ALGO_TC_SKINNY = 2, /* tcgen05, 128 features x <=64 tokens (M<=64)  */
     ORIN_ALGO_SIMT = 3,      /* CUDA-core kernel for unaligned shapes        */
-    ORIN_ALGO_GEMV = 4       /* decode weight stream, M <= 16 tokens         */
+    ORIN_ALGO_GEMV = 4       /* decode weight stream, M <= 32 tokens         */
 } orin_algo;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -87,8 +87,8 @@ const char* orin_last_error(void);
  *   W         [N, K] 16-bit ([2N, K] packed gate/up for SWIGLU)
  *   residual  [M, N] 16-bit for RESIDUAL, else NULL
  * Any M, N >= 1 and K >= 1 are accepted.  K % 8 == 0 with 16-byte aligned
- * A, W (and C rows) takes the decode weight stream for M <= 16 and the
- * tcgen05 path above; other shapes take the SIMT path.
+ * A, W (and C rows) takes the decode weight stream for M <= 16 (up to 32
+ * on request) and the tcgen05 path above; other shapes take the SIMT path.
  */
 orin_status orin_linear(void* C, const void* A, const void* W,
                         int M, int N, int K, int dtype, int epilogue,

@@ -89,6 +89,9 @@ orin_status check_common(int dtype, int epi) {
 
 // Which kernel serves this call.
 // Tokens up to which AUTO takes the decode weight stream (csrc/gemv.cu).
+// Measured on the 22-layer decode path: M=8 0.59 ms (skinny tcgen05 tiles
+// 1.09); M=32 1.30 ms against 1.22 for the skinny tiles, whose tensor-core
+// operands reuse each token fragment across 128 weight rows.
 constexpr int kGemvAutoTokens = 16;
 
 int choose_algo(int req, const void* A, const void* W, int M, int K) {
@@ -139,7 +142,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   if (a < 0) {
     set_error("orin_linear: algo %d can't take M=%d K=%d (needs K%%8==0, 16-byte aligned "
               "A and W%s)", algo, M, K,
-              algo == ORIN_ALGO_TC_SKINNY ? ", M<=64" : algo == ORIN_ALGO_GEMV ? ", M<=16" : "");
+              algo == ORIN_ALGO_TC_SKINNY ? ", M<=64" : algo == ORIN_ALGO_GEMV ? ", M<=32" : "");
     return ORIN_ERR_UNSUPPORTED;
   }
   if (a == 3) {
@@ -210,7 +213,7 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
   info[0] = a;
   if (a == 3) return ORIN_OK;
   if (a == 4) {
-    info[1] = (M <= 8) ? 8 : 16;
+    info[1] = (M <= 8) ? 8 : (M <= 16) ? 16 : 32;
     info[3] = 1;
     info[4] = gemv_grid(N);
     info[5] = info[4];

@@ -1,4 +1,4 @@
-// gemv.cu — decode-time linear layers (M <= 16 tokens) as a weight stream.
+// gemv.cu — decode-time linear layers (M <= 32 tokens) as a weight stream.
 //
 // At decode the weight matrix is read once per step and the token count is
 // tiny, so the kernel is bound by how early and how deeply it can keep HBM
@@ -28,7 +28,7 @@
 //
 // The reference's decode path is kernels/matmul.cu:25-44 (one CTA per output
 // row, 2-byte loads, shared-memory tree reduction); this replaces it for
-// M = 1 and the skinny cuBLAS calls for M <= 16.  No spin-waits, no mbarriers.
+// M = 1 and the skinny cuBLAS calls for M <= 32.  No spin-waits, no mbarriers.
 #include "orin_common.cuh"
 #include "orin_internal.h"
 
@@ -98,13 +98,14 @@ __device__ __forceinline__ float bits_to_f(unsigned short b) {
   else return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
-// NT token tiles of 8 (M <= 8 * NT).
+// NT token tiles of 8 (M <= 8 * NT; NT = 1, 2 or 4).
 template <int DT, int EPI, int NT>
 __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int H = (EPI == EPI_SWIGLU) ? 2 : 1;  // row sets per group: gate, up
-  constexpr int U = (H == 2 || NT == 2) ? 4 : 8;  // k-blocks per load batch
+  // k-blocks per load batch (registers: U * (2H + NT) 16-byte fragments)
+  constexpr int U = (NT >= 4) ? 2 : (H == 2 || NT == 2) ? 4 : 8;
   constexpr int V = H * NT * 4;                   // fragment values per lane
   __shared__ float red[kGvWarps][V][32];
 
@@ -295,8 +296,12 @@ cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int
   p.K = K;
   p.w_rows = (epi == EPI_SWIGLU) ? 2 * N : N;
   if (dtype == DT_F16)
-    return (M <= 8) ? gemv_dispatch<DT_F16, 1>(p, epi, s) : gemv_dispatch<DT_F16, 2>(p, epi, s);
-  return (M <= 8) ? gemv_dispatch<DT_BF16, 1>(p, epi, s) : gemv_dispatch<DT_BF16, 2>(p, epi, s);
+    return (M <= 8)    ? gemv_dispatch<DT_F16, 1>(p, epi, s)
+           : (M <= 16) ? gemv_dispatch<DT_F16, 2>(p, epi, s)
+                       : gemv_dispatch<DT_F16, 4>(p, epi, s);
+  return (M <= 8)    ? gemv_dispatch<DT_BF16, 1>(p, epi, s)
+         : (M <= 16) ? gemv_dispatch<DT_BF16, 2>(p, epi, s)
+                     : gemv_dispatch<DT_BF16, 4>(p, epi, s);
 }
 
 }  // namespace orin

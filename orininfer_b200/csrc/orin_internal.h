@@ -56,7 +56,7 @@ cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const v
 
 // Decode-time weight-streaming kernel (csrc/gemv.cu) for M <= kGemvMaxTokens,
 // K % 8 == 0 and 16-byte aligned A and W.  Same epilogues and rounding.
-constexpr int kGemvMaxTokens = 16;
+constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t stream);
 int gemv_grid(int N);

@@ -69,19 +69,20 @@ def test_epilogues(epi, dt, algo, M, N, K):
 
 
 GEMV = [(1, 2048, 2048), (1, 200, 520), (3, 384, 72), (8, 2560, 2048), (9, 1024, 5632),
-        (16, 256, 8), (5, 4100, 136)]
+        (16, 256, 8), (5, 4100, 136), (17, 520, 1000), (24, 2048, 2048), (32, 1024, 5632)]
 
 
 @pytest.mark.parametrize("dt", [0, 1])
 @pytest.mark.parametrize("M,N,K", GEMV)
 def test_gemv_none(dt, M, N, K):
     # decode weight stream: ragged feature groups (N % 16), K not a multiple of
-    # the 32-element k-block, K = 8 (one block: seven warps without work)
+    # the 32-element k-block, K = 8 (one block: seven warps without work), one
+    # to four 8-token tiles
     run_case(M, N, K, dt, "none", "gemv")
 
 
 @pytest.mark.parametrize("epi", ["residual", "f32", "f32_partial", "swiglu"])
-@pytest.mark.parametrize("M", [1, 7, 16])
+@pytest.mark.parametrize("M", [1, 7, 16, 29])
 def test_gemv_epilogues(epi, M):
     run_case(M, 384, 1000, 1 if M == 7 else 0, epi, "gemv", seed=M)
 
@@ -90,6 +91,7 @@ def test_gemv_is_the_decode_default():
     for M in (1, 8, 16):
         assert ob.plan_info(M, 2048, 2048)["kernel"] == "gemv"
     assert ob.plan_info(17, 2048, 2048)["kernel"] == "tcgen05-skinny"
+    assert ob.plan_info(32, 2048, 2048, algo="gemv")["kernel"] == "gemv"
 
 
 @pytest.mark.parametrize("epi", ["none", "residual", "swiglu", "f32"])
