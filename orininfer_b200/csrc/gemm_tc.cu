@@ -275,7 +275,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
           if (mval && n < p.N) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              v[j] = silu_f32(E::round(v[j])) * E::round(u[j]);
+              v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
             store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, p.N - n, vec);
           }
         }
@@ -325,7 +325,7 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
           for (int j = 0; j < CW; ++j) {
             const int m = qcol0 + c + j;
             if (m < p.M) {
-              const float o = silu_f32(E::round(v[j])) * xch[lr * 32 + j];
+              const float o = silu_fast(E::round(v[j])) * xch[lr * 32 + j];
               static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o);
             }
           }
@@ -449,7 +449,7 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
           tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
           tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = silu_f32(E::round(v[j])) * E::round(u[j]);
+          for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
         } else {
           tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
         }
@@ -630,7 +630,7 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
       const int n = qcol0 / 2 + (u / 2) * 64 + (u % 2) * 32;
       if (n >= p.N) continue;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = silu_f32(E::round(v[i])) * E::round(w[i]);
+      for (int i = 0; i < 32; ++i) v[i] = silu_fast(E::round(v[i])) * E::round(w[i]);
       store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, p.N - n, vec);
     } else {
       const int n = qcol0 + c;
@@ -685,8 +685,8 @@ __device__ __forceinline__ void out_group(const TcParams& p, int prow0, int qcol
       const int n = qcol0 / 2 + (col / 128) * 64 + (col % 128);
       if (m >= p.M || n >= p.N) return;
       const float4 u = *up;
-      float o[4] = {silu_f32(E::round(a.x)) * E::round(u.x), silu_f32(E::round(a.y)) * E::round(u.y),
-                    silu_f32(E::round(a.z)) * E::round(u.z), silu_f32(E::round(a.w)) * E::round(u.w)};
+      float o[4] = {silu_fast(E::round(a.x)) * E::round(u.x), silu_fast(E::round(a.y)) * E::round(u.y),
+                    silu_fast(E::round(a.z)) * E::round(u.z), silu_fast(E::round(a.w)) * E::round(u.w)};
       T* dst = static_cast<T*>(p.C) + m * p.ldc + n;
       if (vec && n + 4 <= p.N) {
         *reinterpret_cast<uint2*>(dst) = make_uint2(E::pack2(o[0], o[1]), E::pack2(o[2], o[3]));
@@ -746,7 +746,7 @@ __device__ __forceinline__ void out_group(const TcParams& p, int prow0, int qcol
       for (int j = 0; j < 4; ++j) {
         const int m = qcol0 + col + j;
         if (m < p.M)
-          static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(silu_f32(E::round(o[j])) * E::round(uo[j]));
+          static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(silu_fast(E::round(o[j])) * E::round(uo[j]));
       }
     } else {
       const int n = prow0 + row;

@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
         static_cast<float*>(p.C)[o] = a;
       } else {
         const float u = s[(NT + t) * 4 + i];
-        static_cast<T*>(p.C)[o] = E::from_f(silu_f32(E::round(a)) * E::round(u));
+        static_cast<T*>(p.C)[o] = E::from_f(silu_fast(E::round(a)) * E::round(u));
       }
     }
   }
