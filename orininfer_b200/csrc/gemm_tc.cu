@@ -397,13 +397,15 @@ __device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, int et,
 
 // Store one tile held in tensor memory: for each 128-byte-wide chunk of
 // output columns, every thread writes its row into a swizzled staging buffer
-// and one thread issues the TMA store.  The residual chunk, if any, is first
-// TMA-loaded into the same buffer.  Rows and columns outside C are clipped by
-// the TMA unit.
+// and one thread issues the TMA store.  Chunks go in rounds of two, one per
+// staging buffer; a round starts once every earlier store has read its
+// buffer, and for RESIDUAL both chunks' residual tiles are TMA-loaded into the
+// buffers at once (one barrier, one wait per round).  Rows and columns
+// outside C are clipped by the TMA unit.
 template <int DT, int BN, int EPI>
 __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr, int prow0,
                                               int qcol0, int lr, int et, uint32_t outbuf,
-                                              int& obuf, const void* tm_c, const void* tm_r,
+                                              const void* tm_c, const void* tm_r,
                                               uint32_t res_bar, uint32_t& res_phase,
                                               volatile int* abort_flag, volatile int* flag) {
   using E = Elem<DT>;
@@ -413,15 +415,16 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
   constexpr int NCH = OUT_COLS / CH;
   const int ocol0 = (EPI == EPI_SWIGLU) ? qcol0 / 2 : qcol0;
 #pragma unroll 1
-  for (int oc = 0; oc < NCH; ++oc) {
-    const uint32_t buf = outbuf + static_cast<uint32_t>(obuf * kOutBuf);
-    const int ocol = ocol0 + oc * CH;
-    // the store that last used this buffer must have read it
-    if (et == 0) bulk_wait_group_read<1>();
+  for (int oc0 = 0; oc0 < NCH; oc0 += 2) {
+    const int n_round = (NCH - oc0) < 2 ? (NCH - oc0) : 2;
+    // every earlier store has read its staging buffer
+    if (et == 0) bulk_wait_group_read<0>();
     if constexpr (EPI == EPI_RESIDUAL) {
       if (et == 0) {
-        mbar_arrive_expect_tx(res_bar, kOutBuf);
-        tma_load_2d_plain(buf, tm_r, res_bar, ocol, prow0);
+        mbar_arrive_expect_tx(res_bar, static_cast<uint32_t>(n_round * kOutBuf));
+        for (int b = 0; b < n_round; ++b)
+          tma_load_2d_plain(outbuf + static_cast<uint32_t>(b * kOutBuf), tm_r, res_bar,
+                            ocol0 + (oc0 + b) * CH, prow0);
       }
     }
     named_bar_sync(1, kEpiThreads);
@@ -429,58 +432,64 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
       if (!epi_wait(res_bar, res_phase, et, abort_flag, p.err, flag)) return false;
       res_phase ^= 1u;
     }
-    if constexpr (F32) {
-      float v[32];
-      tmem_ld_32x32b_x32(taddr + oc * 32, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float o[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) o[t] = (EPI == EPI_F32_OUT) ? E::round(v[4 * j + t]) : v[4 * j + t];
-        st_smem_f4(buf + sw128(lr, j), o[0], o[1], o[2], o[3]);
-      }
-    } else {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+#pragma unroll 1
+    for (int b = 0; b < n_round; ++b) {
+      const int oc = oc0 + b;
+      const uint32_t buf = outbuf + static_cast<uint32_t>(b * kOutBuf);
+      const int ocol = ocol0 + oc * CH;
+      if constexpr (F32) {
         float v[32];
-        if constexpr (EPI == EPI_SWIGLU) {
-          // output chunk oc <- packed group oc: gate cols [128oc, 128oc+64), up +64
-          float u[32];
-          tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
-          tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
+        tmem_ld_32x32b_x32(taddr + oc * 32, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
-        } else {
-          tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
+        for (int j = 0; j < 8; ++j) {
+          float o[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            o[t] = (EPI == EPI_F32_OUT) ? E::round(v[4 * j + t]) : v[4 * j + t];
+          st_smem_f4(buf + sw128(lr, j), o[0], o[1], o[2], o[3]);
         }
+      } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t a = buf + sw128(lr, 4 * h + j);
-          if constexpr (EPI == EPI_RESIDUAL) {
-            uint4 r;
-            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                         : "r"(a));
-            float2 f;
-            f = E::unpack2(r.x); v[8 * j + 0] = f.x + E::round(v[8 * j + 0]); v[8 * j + 1] = f.y + E::round(v[8 * j + 1]);
-            f = E::unpack2(r.y); v[8 * j + 2] = f.x + E::round(v[8 * j + 2]); v[8 * j + 3] = f.y + E::round(v[8 * j + 3]);
-            f = E::unpack2(r.z); v[8 * j + 4] = f.x + E::round(v[8 * j + 4]); v[8 * j + 5] = f.y + E::round(v[8 * j + 5]);
-            f = E::unpack2(r.w); v[8 * j + 6] = f.x + E::round(v[8 * j + 6]); v[8 * j + 7] = f.y + E::round(v[8 * j + 7]);
+        for (int h = 0; h < 2; ++h) {
+          float v[32];
+          if constexpr (EPI == EPI_SWIGLU) {
+            // output chunk oc <- packed group oc: gate cols [128oc, 128oc+64), up +64
+            float u[32];
+            tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
+            tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
+          } else {
+            tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
           }
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                       "r"(E::pack2(v[8 * j + 0], v[8 * j + 1])), "r"(E::pack2(v[8 * j + 2], v[8 * j + 3])),
-                       "r"(E::pack2(v[8 * j + 4], v[8 * j + 5])), "r"(E::pack2(v[8 * j + 6], v[8 * j + 7]))
-                       : "memory");
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = buf + sw128(lr, 4 * h + j);
+            if constexpr (EPI == EPI_RESIDUAL) {
+              uint4 r;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                           : "r"(a));
+              float2 f;
+              f = E::unpack2(r.x); v[8 * j + 0] = f.x + E::round(v[8 * j + 0]); v[8 * j + 1] = f.y + E::round(v[8 * j + 1]);
+              f = E::unpack2(r.y); v[8 * j + 2] = f.x + E::round(v[8 * j + 2]); v[8 * j + 3] = f.y + E::round(v[8 * j + 3]);
+              f = E::unpack2(r.z); v[8 * j + 4] = f.x + E::round(v[8 * j + 4]); v[8 * j + 5] = f.y + E::round(v[8 * j + 5]);
+              f = E::unpack2(r.w); v[8 * j + 6] = f.x + E::round(v[8 * j + 6]); v[8 * j + 7] = f.y + E::round(v[8 * j + 7]);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                         "r"(E::pack2(v[8 * j + 0], v[8 * j + 1])), "r"(E::pack2(v[8 * j + 2], v[8 * j + 3])),
+                         "r"(E::pack2(v[8 * j + 4], v[8 * j + 5])), "r"(E::pack2(v[8 * j + 6], v[8 * j + 7]))
+                         : "memory");
+          }
         }
       }
+      fence_proxy_async_smem();
+      named_bar_sync(1, kEpiThreads);
+      if (et == 0) {
+        tma_store_2d(tm_c, buf, ocol, prow0);
+        bulk_commit_group();
+      }
     }
-    fence_proxy_async_smem();
-    named_bar_sync(1, kEpiThreads);
-    if (et == 0) {
-      tma_store_2d(tm_c, buf, ocol, prow0);
-      bulk_commit_group();
-    }
-    obuf ^= 1;
   }
   return true;
 }
@@ -610,6 +619,14 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
     const int u = u0 + ui;
     const int c = unit_col<EPI>(u);
     float v[32], w[32];
+    // the residual row segment (global memory) first: its latency overlaps
+    // the tensor-memory and shared-memory reads below
+    float r[32];
+    if constexpr (EPI == EPI_RESIDUAL) {
+      const int n = qcol0 + c;
+      if (m < p.M && n < p.N)
+        load16_row<DT>(static_cast<const T*>(p.R) + m * p.ldr + n, r, 32, p.N - n, vec);
+    }
     tmem_ld_32x32b_x32(taddr + c, v);
     if constexpr (EPI == EPI_SWIGLU) tmem_ld_32x32b_x32(taddr + c + 64, w);
 #pragma unroll 1
@@ -639,8 +656,6 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
       if constexpr (EPI == EPI_NONE) {
         store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
       } else if constexpr (EPI == EPI_RESIDUAL) {
-        float r[32];
-        load16_row<DT>(static_cast<const T*>(p.R) + m * p.ldr + n, r, 32, valid, vec);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = r[i] + E::round(v[i]);
         store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
@@ -1145,7 +1160,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         PAIR ? mapa_shared(smem_u32(&tempty_bar[0]), lead_rank) : smem_u32(&tempty_bar[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
-    int obuf = 0;
     uint32_t res_phase = 0;
     UnitIter it;
     it.init(p, GROUP);
@@ -1165,8 +1179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (S == 1) {
         if constexpr (!SWAP) {
           if (p.out_tma) {
-            ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, obuf, &tm_c,
-                                            &tm_r, smem_u32(&res_bar), res_phase, &abort_flag,
+            ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, &tm_c, &tm_r,
+                                            smem_u32(&res_bar), res_phase, &abort_flag,
                                             &epi_flag);
           } else {
             TmemChunks<CW> src{taddr};
