@@ -614,19 +614,39 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
   const uint32_t slot_bytes = static_cast<uint32_t>(128 * n_j * UC * 4);
   const int m = prow0 + lr;
   const bool vec = p.vec_ok != 0;
-#pragma unroll 1
-  for (int ui = 0; ui < n_j; ++ui) {
+  // every owned unit's residual row segment (16-bit words) is loaded first:
+  // the loads are in flight together while the tensor-memory and
+  // shared-memory reads below run (an owner holds at most U/2 units)
+  constexpr int MAXU = (U + 1) / 2;
+  uint32_t rw[(EPI == EPI_RESIDUAL) ? MAXU : 1][16];
+  if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+    for (int ui = 0; ui < MAXU; ++ui) {
+      const int n = qcol0 + unit_col<EPI>(u0 + ui);
+      const int valid = p.N - n;
+      const T* src = static_cast<const T*>(p.R) + m * p.ldr + n;
+      if (ui < n_j && m < p.M && valid >= 32 && vec) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 t = reinterpret_cast<const uint4*>(src)[q];
+          rw[ui][4 * q] = t.x; rw[ui][4 * q + 1] = t.y; rw[ui][4 * q + 2] = t.z; rw[ui][4 * q + 3] = t.w;
+        }
+      } else if (ui < n_j && m < p.M && valid > 0) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float lo = (2 * q < valid) ? E::to_f(src[2 * q]) : 0.f;
+          const float hi = (2 * q + 1 < valid) ? E::to_f(src[2 * q + 1]) : 0.f;
+          rw[ui][q] = E::pack2(lo, hi);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int ui = 0; ui < MAXU; ++ui) {
+    if (ui >= n_j) break;
     const int u = u0 + ui;
     const int c = unit_col<EPI>(u);
     float v[32], w[32];
-    // the residual row segment (global memory) first: its latency overlaps
-    // the tensor-memory and shared-memory reads below
-    float r[32];
-    if constexpr (EPI == EPI_RESIDUAL) {
-      const int n = qcol0 + c;
-      if (m < p.M && n < p.N)
-        load16_row<DT>(static_cast<const T*>(p.R) + m * p.ldr + n, r, 32, p.N - n, vec);
-    }
     tmem_ld_32x32b_x32(taddr + c, v);
     if constexpr (EPI == EPI_SWIGLU) tmem_ld_32x32b_x32(taddr + c + 64, w);
 #pragma unroll 1
@@ -657,7 +677,11 @@ __device__ __forceinline__ void reduce_received(const TcParams& p, uint32_t ring
         store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
       } else if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = r[i] + E::round(v[i]);
+        for (int q = 0; q < 16; ++q) {
+          const float2 f = E::unpack2(rw[ui][q]);
+          v[2 * q] = f.x + E::round(v[2 * q]);
+          v[2 * q + 1] = f.y + E::round(v[2 * q + 1]);
+        }
         store16_row<DT>(static_cast<T*>(p.C) + m * p.ldc + n, v, 32, valid, vec);
       } else if constexpr (EPI == EPI_F32_OUT) {
 #pragma unroll
