@@ -124,6 +124,24 @@ orin_status orin_pack_gate_up(void* w_packed, const void* w_gate,
                               const void* w_up, int IM, int K, int dtype,
                               void* stream);
 
+/*
+ * Greedy next token of each of M rows (no separate logits pass): replaces
+ * the LM head matmul + bf16_to_fp32 (src/model.cu:113-131) followed by
+ * kernels::argmax (include/kernels.h:118-125, kernels/softmax.cu:52-73,
+ * src/sampler.cu:24-27).  token[m] = argmax over v < V of
+ * f32(round16(h[m] . W[v])), ties resolved exactly as the reference's
+ * 512-thread sampler resolves them: among the positions of the maximum, the
+ * one whose residue v mod 512 has the smallest 9-bit bit-reversal, then the
+ * smallest v; -inf and NaN never win; if nothing counts, 0.
+ *   token  [M] int32 (device)      h [M, K] 16-bit      W [V, K] 16-bit
+ *   keys   caller scratch of M 64-bit words (device), overwritten
+ * Needs K % 8 == 0 and 16-byte aligned h and W.  Rows go through the decode
+ * weight-stream kernel 32 at a time.
+ */
+orin_status orin_lm_head_argmax(int* token, const void* h, const void* W,
+                                int M, int V, int K, int dtype,
+                                unsigned long long* keys, void* stream);
+
 /* out = round16(silu(f32(gate)) * f32(up)), n elements; out may alias gate.
  * Replaces kernels::fused_silu_mul (include/kernels.h:88-94). */
 orin_status orin_silu_mul(void* out, const void* gate, const void* up,

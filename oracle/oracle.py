@@ -138,6 +138,57 @@ def round16(x: np.ndarray, dt: int) -> np.ndarray:
     return out
 
 
+def argmax_reference(x: np.ndarray, threads: int = 512) -> int:
+    """The reference's greedy sampler (kernels/softmax.cu:52-73, launched with
+    512 threads at :108-110), restated step by step: thread t scans
+    i = t, t+512, ... keeping the first strictly greater value (start -FLT_MAX,
+    index 0), then a halving tree where slot t takes slot t+s only if strictly
+    greater.  x: float32 logits of one row."""
+    x = np.asarray(x, dtype=np.float32)
+    neg = np.float32(-3.4028234663852886e38)
+    val = np.full(threads, neg, dtype=np.float32)
+    idx = np.zeros(threads, dtype=np.int64)
+    for t in range(threads):
+        for i in range(t, x.shape[0], threads):
+            if x[i] > val[t]:
+                val[t], idx[t] = x[i], i
+    s = threads // 2
+    while s > 0:
+        for t in range(s):
+            if val[t + s] > val[t]:
+                val[t], idx[t] = val[t + s], idx[t + s]
+        s //= 2
+    return int(idx[0])
+
+
+def argmax_key_order(x: np.ndarray) -> int:
+    """The same choice as argmax_reference, stated as an order: among the
+    positions of the maximum (values > -FLT_MAX only; none -> 0), the one whose
+    residue i mod 512 has the smallest 9-bit bit-reversal (ties in the tree
+    meet at their lowest differing bit, where the 0 side wins), then the
+    smallest i.  This is the order the fused LM-head argmax packs into its
+    64-bit keys."""
+    x = np.asarray(x, dtype=np.float32)
+    ok = x > np.float32(-3.4028234663852886e38)
+    if not ok.any():
+        return 0
+    best = x[ok].max()
+    cand = np.nonzero(ok & (x == best))[0]
+
+    def rev9(t: int) -> int:
+        return int(format(t, "09b")[::-1], 2)
+
+    return int(min(cand, key=lambda i: (rev9(int(i) % 512), int(i))))
+
+
+def lm_head_argmax(h: np.ndarray, W: np.ndarray, dt: int) -> np.ndarray:
+    """Greedy next token per row of h: the LM head with the reference's
+    rounding (16-bit logits widened to fp32, src/model.cu:125-130) followed by
+    argmax_reference."""
+    logits = linear(h, W, dt, "f32")
+    return np.array([argmax_reference(row) for row in logits], dtype=np.int32)
+
+
 def pack_gate_up(wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
     wg = np.ascontiguousarray(wg, dtype=np.uint16)
     wu = np.ascontiguousarray(wu, dtype=np.uint16)

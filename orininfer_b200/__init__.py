@@ -8,7 +8,7 @@ import importlib
 
 __all__ = [
     "OrinError", "add", "bf16_to_fp32", "device_check", "fused_silu_mul", "linear",
-    "linear_into", "matmul", "pack_gate_up", "plan_info",
+    "linear_into", "lm_head_argmax", "matmul", "pack_gate_up", "plan_info",
 ]
 __version__ = "0.1.0"
 

@@ -234,6 +234,23 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
   return ORIN_OK;
 }
 
+orin_status orin_lm_head_argmax(int* token, const void* h, const void* W, int M, int V, int K,
+                                int dtype, unsigned long long* keys, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (!token || !h || !W || !keys || M < 1 || V < 1 || K < 1) {
+    set_error("orin_lm_head_argmax: null pointer or non-positive size");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (K % 8 != 0 || !aligned16(h) || !aligned16(W)) {
+    set_error("orin_lm_head_argmax: needs K %% 8 == 0 and 16-byte aligned h and W (K=%d)", K);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_lm_head_argmax(token, h, W, M, V, K, dtype, keys, s);
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_lm_head_argmax");
+}
+
 orin_status orin_linear(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epilogue, const void* residual, void* stream) {
   return orin_linear_ex(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, stream);

@@ -92,6 +92,23 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
   }
 }
 
+// Greedy-argmax key of logit v at vocabulary position n: larger is better.
+// The reference's sampler (kernels/softmax.cu:52-73, one CTA of 512 threads)
+// picks, among the positions of the maximum, the one whose residue n mod 512
+// has the smallest 9-bit bit-reversal (its tree keeps the lower slot on ties,
+// and two tied threads meet at their lowest differing bit), then the smallest
+// n; values not above -FLT_MAX never count (key 0, which decodes to token 0,
+// as the reference returns when nothing counts).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+  if (!(v > -3.402823466e38f)) return 0ull;
+  // the reference compares with '>': -0 and +0 tie
+  const uint32_t b = (v == 0.f) ? 0u : __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  const uint32_t rev = __brev(static_cast<uint32_t>(n) & 511u) >> 23;
+  const uint32_t lo = ~((rev << 22) | (static_cast<uint32_t>(n) >> 9));
+  return (static_cast<unsigned long long>(ord) << 32) | lo;
+}
+
 template <int DT>
 __device__ __forceinline__ float bits_to_f(unsigned short b) {
   if constexpr (DT == DT_F16) return __half2float(__ushort_as_half(b));
@@ -225,6 +242,32 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
     for (int ww = 1; ww < kGvWarps; ++ww) a += red[ww][v][lane];
     s[v] = a;
   }
+  if constexpr (EPI == EPI_ARGMAX) {
+    // per token: the best key of the CTA's 16 positions (the 8 lanes of equal
+    // q hold them), then one atomicMax per token
+    unsigned long long* keys = static_cast<unsigned long long*>(p.C);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        unsigned long long k = 0ull;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int n = f0 + g + 8 * r;
+          const unsigned long long kr = (n < p.N) ? argmax_key(E::round(s[t * 4 + 2 * r + j]), n) : 0ull;
+          k = kr > k ? kr : k;
+        }
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+          k = o > k ? o : k;
+        }
+        const int m = 8 * t + 2 * q + j;
+        if (g == 0 && m < p.M && k != 0ull) atomicMax(keys + m, k);
+      }
+    }
+    return;
+  }
   // fragment value i of tile t: row g + 8*(i/2), token 8t + 2q + (i%2)
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
@@ -275,13 +318,43 @@ cudaError_t gemv_dispatch(const GvParams& p, int epi, cudaStream_t s) {
     case EPI_RESIDUAL: return gemv_launch<DT, EPI_RESIDUAL, NT>(p, s);
     case EPI_F32_OUT: return gemv_launch<DT, EPI_F32_OUT, NT>(p, s);
     case EPI_F32_PARTIAL: return gemv_launch<DT, EPI_F32_PARTIAL, NT>(p, s);
+    case EPI_ARGMAX: return gemv_launch<DT, EPI_ARGMAX, NT>(p, s);
   }
   return cudaErrorInvalidValue;
+}
+
+// token[m] = the vocabulary position encoded in keys[m] (0 when nothing counted).
+__global__ void argmax_decode_kernel(int* token, const unsigned long long* keys, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  const unsigned long long k = keys[m];
+  if (k == 0ull) {
+    token[m] = 0;
+    return;
+  }
+  const uint32_t lo = ~static_cast<uint32_t>(k);
+  const uint32_t residue = __brev(lo >> 22) >> 23;
+  token[m] = static_cast<int>(((lo & 0x3fffffu) << 9) | residue);
 }
 
 }  // namespace
 
 int gemv_grid(int N) { return (N + kGvRows - 1) / kGvRows; }
+
+cudaError_t launch_lm_head_argmax(int* token, const void* A, const void* W, int M, int V, int K,
+                                  int dtype, unsigned long long* keys, cudaStream_t s) {
+  const size_t esz = 2;
+  for (int r0 = 0; r0 < M; r0 += kGemvMaxTokens) {
+    const int rows = (M - r0) < kGemvMaxTokens ? (M - r0) : kGemvMaxTokens;
+    cudaError_t e = cudaMemsetAsync(keys + r0, 0, rows * sizeof(unsigned long long), s);
+    if (e != cudaSuccess) return e;
+    e = launch_gemv(keys + r0, static_cast<const char*>(A) + static_cast<size_t>(r0) * K * esz, W,
+                    rows, V, K, dtype, EPI_ARGMAX, nullptr, s);
+    if (e != cudaSuccess) return e;
+  }
+  argmax_decode_kernel<<<(M + 127) / 128, 128, 0, s>>>(token, keys, M);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t s) {

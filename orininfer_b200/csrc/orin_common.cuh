@@ -17,7 +17,10 @@ enum : int {
   EPI_SWIGLU = 1,
   EPI_RESIDUAL = 2,
   EPI_F32_OUT = 3,
-  EPI_F32_PARTIAL = 4
+  EPI_F32_PARTIAL = 4,
+  // internal: the LM head's greedy argmax (orin_lm_head_argmax); C holds one
+  // 64-bit key per row, combined with atomicMax
+  EPI_ARGMAX = 5
 };
 
 // Device-side error codes written to the per-device error word.

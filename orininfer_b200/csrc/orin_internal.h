@@ -60,6 +60,9 @@ constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t stream);
 int gemv_grid(int N);
+// LM head + greedy argmax per row (keys: caller scratch of M 64-bit words).
+cudaError_t launch_lm_head_argmax(int* token, const void* A, const void* W, int M, int V, int K,
+                                  int dtype, unsigned long long* keys, cudaStream_t stream);
 
 // CUDA-core GEMM for shapes the tcgen05 path can't take (K % 8 != 0,
 // unaligned rows).  Same epilogues and rounding.

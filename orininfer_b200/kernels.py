@@ -45,7 +45,7 @@ _ALGOS = {
 
 __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
-    "pack_gate_up", "device_check", "plan_info",
+    "pack_gate_up", "device_check", "plan_info", "lm_head_argmax",
 ]
 
 
@@ -141,6 +141,26 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
         odt = torch.float32 if epilogue in ("f32", "f32_partial") else x.dtype
         out = torch.empty((M, N), dtype=odt, device=x.device)
     return linear_into(out, x, w, epilogue=epilogue, residual=residual, algo=algo, stream=stream)
+
+
+def lm_head_argmax(h: torch.Tensor, w: torch.Tensor, *, keys: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None,
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Greedy next token per row of h [M, K] through the LM head w [V, K]
+    (orin_lm_head_argmax: the reference's LM head + bf16_to_fp32 + argmax,
+    src/model.cu:113-131 and kernels/softmax.cu:52-73, with its tie-break)."""
+    _need_cuda(h, w, keys, out)
+    if w.dtype != h.dtype:
+        raise ValueError("h and w must share one dtype")
+    M, K = h.shape
+    V = w.shape[0]
+    if keys is None:
+        keys = torch.empty(M, dtype=torch.int64, device=h.device)
+    if out is None:
+        out = torch.empty(M, dtype=torch.int32, device=h.device)
+    check(_lib.lib.orin_lm_head_argmax(_ptr(out), _ptr(h), _ptr(w), M, V, K, _dtype_code(h),
+                                       _ptr(keys), _stream(stream)))
+    return out
 
 
 def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,

@@ -180,6 +180,57 @@ def test_decode_lm_head_f32(M):
     run_case(M, 32000, 2048, 0, "f32", seed=700 + M)
 
 
+def _gpu_logits(h, w, dt):
+    """The weight-stream kernel's own fp32 logits (F32_OUT: round16 then
+    widen), 32 rows at a time — the same accumulation as the fused argmax."""
+    rows = [ob.linear(h[r:r + 32], w, epilogue="f32", algo="gemv") for r in range(0, h.shape[0], 32)]
+    return torch.cat(rows).cpu().numpy()
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("M", [1, 5, 33])
+def test_lm_head_argmax(dt, M):
+    """Greedy token per row == the reference sampler's choice over the same
+    logits (its tie-break included), and the logits match the oracle."""
+    tdt = TORCH_DT[dt]
+    V, K = 32000, 2048
+    h = seeded((M, K), 40 + M, 1.0, tdt).to(DEV)
+    w = seeded((V, K), 41, 0.02, tdt).to(DEV)
+    tok = ob.lm_head_argmax(h, w)
+    ob.device_check()
+    logits = _gpu_logits(h, w, dt)
+    for m in range(M):
+        assert int(tok[m]) == orc.argmax_reference(logits[m]), m
+    ref = orc.linear(bits(h[:2].cpu()), bits(w.cpu()), dt, "f32")
+    assert_close(torch.from_numpy(logits[:2]), torch.from_numpy(ref), "lm head logits",
+                 exact_min=EXACT_MIN)
+
+
+def test_lm_head_argmax_ties():
+    """Planted exact ties: identical weight rows give identical logits, and
+    the winner follows the reference's order (bit-reversed residue mod 512,
+    then position), not simply the first position."""
+    V, K, M = 4096, 512, 3
+    h = seeded((M, K), 50, 1.0)
+    w = seeded((V, K), 51, 0.02)
+    top = (seeded((1, K), 52, 1.0).float() * 0.5)[0]
+    for m in (0, 2):                                  # the planted rows win on rows 0 and 2
+        if float(h[m].float() @ top) < 0:
+            h[m] = -h[m]
+    h[1] = 0.0                                        # every logit +-0 on row 1: all tie
+    for pos in (1, 2, 257, 1026, 3000):               # residues 1, 2, 257, 2, 440
+        w[pos] = top.half()
+    h, w = h.to(DEV), w.to(DEV)
+    tok = ob.lm_head_argmax(h, w)
+    ob.device_check()
+    logits = _gpu_logits(h, w, 0)
+    for m in range(M):
+        assert int(tok[m]) == orc.argmax_reference(logits[m]), m
+    # 9-bit reversals of the residues: 256, 128, 257, 128, 59 -> position 3000;
+    # all-zero logits: residue 0 reverses to 0 -> position 0
+    assert [int(t) for t in tok] == [3000, 0, 3000]
+
+
 def test_reference_entry_points_drop_in():
     """kernels::matmul / fused_silu_mul / add / bf16_to_fp32 / launch_gemm_cute
     with the reference's exact C++ signatures (bf16, default stream)."""

@@ -153,3 +153,21 @@ def test_golden_fixtures_present():
     assert {"matmul", "silu_mul", "add", "bf16_to_fp32"} <= kinds, (
         "tests/golden is missing reference fixtures; regenerate with "
         "tests/golden/make_golden.py on a GPU")
+
+
+def test_argmax_key_order_matches_the_reference_sampler():
+    """The fused LM-head argmax packs the reference sampler's choice into an
+    order (value, bit-reversed residue mod 512, position); check that order
+    against the literal restatement of the 512-thread kernel on tie-heavy rows
+    (few distinct values, -inf, NaN, nothing valid)."""
+    rng = np.random.default_rng(5)
+    for trial in range(200):
+        n = int(rng.integers(1, 2600))
+        x = rng.integers(-3, 4, size=n).astype(np.float32)
+        if trial % 5 == 0:
+            x[rng.integers(0, n, size=n // 3)] = -np.inf
+        if trial % 9 == 0:
+            x[rng.integers(0, n, size=n // 4)] = np.nan
+        if trial % 17 == 0:
+            x[:] = -np.inf
+        assert orc.argmax_reference(x) == orc.argmax_key_order(x), trial
