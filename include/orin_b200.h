@@ -218,6 +218,19 @@ orin_status orin_tp_linear_row_static(void* comm, void* C, const void* A_shard,
 long long orin_tp_static_partial_capacity(void);
 
 /*
+ * Vocabulary-parallel LM head + greedy argmax: this rank holds rows
+ * [v_offset, v_offset + V_shard) of the LM head (any split, ragged allowed);
+ * every rank gets the same token[m] as orin_lm_head_argmax over the whole
+ * vocabulary, tie-break included: each rank reduces its shard to one 64-bit
+ * key per row (the order the tie-break defines), one ncclAllReduce(max) of
+ * M keys combines them.  keys: caller scratch of M 64-bit words.
+ */
+orin_status orin_tp_lm_head_argmax(void* comm, int* token, const void* h,
+                                   const void* W_shard, int M, int V_shard,
+                                   int v_offset, int K, int dtype,
+                                   unsigned long long* keys, void* stream);
+
+/*
  * Give the communicator a peer-memory reduction for row-parallel calls
  * (no counterpart in the reference).  Collective: every rank calls it with
  * the same max_elems.  Each rank allocates one region (fp32 partials and

@@ -247,7 +247,8 @@ orin_status orin_lm_head_argmax(int* token, const void* h, const void* W, int M,
     return ORIN_ERR_UNSUPPORTED;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_lm_head_argmax(token, h, W, M, V, K, dtype, keys, s);
+  cudaError_t e = launch_argmax_keys(keys, h, W, M, V, K, dtype, 0, s);
+  if (e == cudaSuccess) e = launch_argmax_decode(token, keys, M, s);
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_lm_head_argmax");
 }
 

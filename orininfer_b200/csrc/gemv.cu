@@ -47,6 +47,7 @@ struct GvParams {
   const void* R;
   int M, N, K;
   int w_rows;  // rows of W: N, or 2N for the packed gate/up weight
+  int n_offset;  // EPI_ARGMAX: vocabulary position of row 0 (a tensor-parallel shard)
 };
 
 __device__ __forceinline__ uint4 ld_weights(const void* p) {
@@ -254,7 +255,8 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int n = f0 + g + 8 * r;
-          const unsigned long long kr = (n < p.N) ? argmax_key(E::round(s[t * 4 + 2 * r + j]), n) : 0ull;
+          const unsigned long long kr =
+              (n < p.N) ? argmax_key(E::round(s[t * 4 + 2 * r + j]), n + p.n_offset) : 0ull;
           k = kr > k ? kr : k;
         }
 #pragma unroll
@@ -341,25 +343,31 @@ __global__ void argmax_decode_kernel(int* token, const unsigned long long* keys,
 
 int gemv_grid(int N) { return (N + kGvRows - 1) / kGvRows; }
 
-cudaError_t launch_lm_head_argmax(int* token, const void* A, const void* W, int M, int V, int K,
-                                  int dtype, unsigned long long* keys, cudaStream_t s) {
+cudaError_t launch_argmax_keys(unsigned long long* keys, const void* A, const void* W, int M,
+                               int V, int K, int dtype, int v_offset, cudaStream_t s) {
   const size_t esz = 2;
   for (int r0 = 0; r0 < M; r0 += kGemvMaxTokens) {
     const int rows = (M - r0) < kGemvMaxTokens ? (M - r0) : kGemvMaxTokens;
     cudaError_t e = cudaMemsetAsync(keys + r0, 0, rows * sizeof(unsigned long long), s);
     if (e != cudaSuccess) return e;
     e = launch_gemv(keys + r0, static_cast<const char*>(A) + static_cast<size_t>(r0) * K * esz, W,
-                    rows, V, K, dtype, EPI_ARGMAX, nullptr, s);
+                    rows, V, K, dtype, EPI_ARGMAX, nullptr, s, v_offset);
     if (e != cudaSuccess) return e;
   }
+  return cudaSuccess;
+}
+
+cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int M,
+                                 cudaStream_t s) {
   argmax_decode_kernel<<<(M + 127) / 128, 128, 0, s>>>(token, keys, M);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
-                        int epi, const void* R, cudaStream_t s) {
+                        int epi, const void* R, cudaStream_t s, int n_offset) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
   GvParams p;
+  p.n_offset = n_offset;
   p.W = W;
   p.X = A;
   p.C = C;

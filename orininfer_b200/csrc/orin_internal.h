@@ -58,11 +58,15 @@ cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const v
 // K % 8 == 0 and 16-byte aligned A and W.  Same epilogues and rounding.
 constexpr int kGemvMaxTokens = 32;
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
-                        int epi, const void* R, cudaStream_t stream);
+                        int epi, const void* R, cudaStream_t stream, int n_offset = 0);
 int gemv_grid(int N);
-// LM head + greedy argmax per row (keys: caller scratch of M 64-bit words).
-cudaError_t launch_lm_head_argmax(int* token, const void* A, const void* W, int M, int V, int K,
-                                  int dtype, unsigned long long* keys, cudaStream_t stream);
+// LM head + greedy argmax per row: keys[m] = the best 64-bit argmax key of
+// row m over the V vocabulary rows of W (positions v_offset + v), then
+// token[m] = its position (keys: caller scratch of M words).
+cudaError_t launch_argmax_keys(unsigned long long* keys, const void* A, const void* W, int M,
+                               int V, int K, int dtype, int v_offset, cudaStream_t stream);
+cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int M,
+                                 cudaStream_t stream);
 
 // CUDA-core GEMM for shapes the tcgen05 path can't take (K % 8 != 0,
 // unaligned rows).  Same epilogues and rounding.

@@ -219,6 +219,47 @@ orin_status orin_tp_linear_row(void* comm, void* C, const void* A_shard, const v
   return ORIN_OK;
 }
 
+orin_status orin_tp_lm_head_argmax(void* comm, int* token, const void* h, const void* W_shard,
+                                   int M, int V_shard, int v_offset, int K, int dtype,
+                                   unsigned long long* keys, void* stream) {
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (!c || !token || !h || !W_shard || !keys || M < 1 || V_shard < 1 || K < 1 || v_offset < 0 ||
+      (dtype != ORIN_F16 && dtype != ORIN_BF16)) {
+    set_error("orin_tp_lm_head_argmax: bad arguments");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (static_cast<long long>(v_offset) + V_shard > 0x7fffffffLL) {
+    set_error("orin_tp_lm_head_argmax: vocabulary positions beyond 2^31");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (K % 8 != 0 || reinterpret_cast<uintptr_t>(h) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(W_shard) % 16 != 0) {
+    set_error("orin_tp_lm_head_argmax: needs K %% 8 == 0 and 16-byte aligned h and W_shard");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (c->aborted) {
+    set_error("orin_tp_lm_head_argmax: communicator was aborted");
+    return ORIN_ERR_NCCL;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_argmax_keys(keys, h, W_shard, M, V_shard, K, dtype, v_offset, s);
+  if (e != cudaSuccess) {
+    set_error("orin_tp_lm_head_argmax: %s", cudaGetErrorString(e));
+    return ORIN_ERR_CUDA;
+  }
+  // the keys order (value, tie-break) globally: the best of the ranks' bests
+  ncclResult_t r = ncclAllReduce(keys, keys, static_cast<size_t>(M), ncclUint64, ncclMax, c->comm,
+                                 s);
+  orin_status st = settle(c, r, "orin_tp_lm_head_argmax: ncclAllReduce");
+  if (st != ORIN_OK) return st;
+  e = launch_argmax_decode(token, keys, M, s);
+  if (e != cudaSuccess) {
+    set_error("orin_tp_lm_head_argmax: %s", cudaGetErrorString(e));
+    return ORIN_ERR_CUDA;
+  }
+  return ORIN_OK;
+}
+
 orin_status orin_tp_enable_p2p(void* comm, long long max_elems, void* stream) {
   TpComm* c = static_cast<TpComm*>(comm);
   if (!c || max_elems < 8) {

@@ -150,6 +150,22 @@ class TPComm:
                                           _ptr(partial), _stream(stream)))
         return out
 
+    def lm_head_argmax(self, h: torch.Tensor, w_shard: torch.Tensor, v_offset: int, *,
+                       keys: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                       stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Greedy token per row of h with the LM head split by vocabulary rows:
+        this rank holds rows [v_offset, v_offset + len(w_shard)) (orin_tp_lm_head_argmax)."""
+        _need_cuda(h, w_shard, keys, out)
+        M, K = h.shape
+        if keys is None:
+            keys = torch.empty(M, dtype=torch.int64, device=h.device)
+        if out is None:
+            out = torch.empty(M, dtype=torch.int32, device=h.device)
+        check(_lib.lib.orin_tp_lm_head_argmax(self._h, _ptr(out), _ptr(h), _ptr(w_shard), M,
+                                              w_shard.shape[0], int(v_offset), K,
+                                              _dtype_code(h), _ptr(keys), _stream(stream)))
+        return out
+
     def enable_p2p(self, max_elems: int, stream: Optional[torch.cuda.Stream] = None) -> None:
         """Collective: reduce row-parallel calls of up to max_elems outputs over
         NVLink peer memory instead of NCCL (orin_tp_enable_p2p)."""

@@ -100,6 +100,27 @@ def _worker(rank, world, port, q):
         ref7 = orc.linear(bits(a7), bits(wd), 0, "none")
         assert_close(o7.cpu().float(), from_bits(ref7, torch.float16).float(),
                      f"p2p no residual M=7 rank {rank}", exact_min=EXACT_MIN)
+        # vocabulary-parallel LM head + greedy argmax over ragged shards, with
+        # exact ties planted in different shards: 9-bit reversals of residues
+        # 1, 2, 257, 88, 487 are 256, 128, 257, 52, 463 -> position 600
+        V, Kv = 1000, 512
+        hv = seeded((3, Kv), 60, 1.0)
+        wv = seeded((V, Kv), 61, 0.02)
+        top = (seeded((1, Kv), 62, 1.0).float() * 0.5)[0]
+        for m in (0, 2):
+            if float(hv[m].float() @ top) < 0:
+                hv[m] = -hv[m]
+        for pos in (1, 2, 257, 600, 999):
+            wv[pos] = top.half()
+        lo, hi = tp.ragged_split(V, world)[rank]
+        hv_dev = hv.to(dev)
+        tok = comm.lm_head_argmax(hv_dev, wv[lo:hi].contiguous().to(dev), lo)
+        whole = ob.lm_head_argmax(hv_dev, wv.to(dev))
+        comm.wait()
+        ob.device_check()
+        assert torch.equal(tok, whole), (tok, whole)
+        assert int(tok[0]) == 600 and int(tok[2]) == 600, tok
+
         # column-parallel gate/up with SwiGLU on this rank's packed shard
         wg = seeded((IM, H), 4, 0.02)
         wu = seeded((IM, H), 5, 0.02)
