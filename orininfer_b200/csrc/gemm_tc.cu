@@ -1,35 +1,41 @@
 // gemm_tc.cu — the sm_100a linear-layer kernel: C = epilogue(A · W^T).
 //
-// One kernel template covers both shapes of the hot path:
-//   * wide tiles (prefill, M > 64): 128 tokens x {128,256} weight rows;
-//   * skinny tiles (decode, M <= 64): 128 weight rows x {16,32,64} tokens
-//     ("swap AB": the weight matrix feeds the 128-lane side of the MMA,
-//     so a one-token GEMV still streams weights through the tensor core at
-//     full HBM speed, with no CUDA-core fp16->fp32 conversions).
+// One kernel template covers both tensor-core shapes of the hot path:
+//   * wide tiles (prefill, M > 64): 128 tokens x {128,256} weight rows per
+//     CTA, or 256 tokens x {128,256} on a tcgen05 CTA pair (cta_group::2:
+//     each CTA of the pair loads its 128 A rows and half the B rows, the
+//     leader issues M=256 MMAs);
+//   * skinny tiles (decode, 17-64 tokens; 1-16 go to gemv.cu): 128 weight
+//     rows x {16,32,64} tokens ("swap AB": the weight matrix feeds the
+//     128-lane side of the MMA).  With <= 32 token columns a CTA takes at most
+//     113 KB of shared memory, so two fit on an SM and the next kernel's CTAs
+//     are resident (programmatic dependent launch) while this one finishes.
 //
-// Per CTA (one per SM, 192 threads):
-//   warp 0    TMA producer: 2-D tiled loads, 128-byte swizzle, into a
-//             STAGES-deep shared-memory ring guarded by mbarriers.  Weight
-//             tiles of the first ring pass are issued before the grid waits
-//             on the previous kernel (programmatic dependent launch), so a
-//             chain of layers keeps HBM busy across kernel boundaries.
-//   warp 1    MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::f16
-//             (fp16/bf16 in, fp32 accumulate) into a double-buffered tensor
-//             memory accumulator, tcgen05.commit frees ring slots.
-//   warps 2-5 epilogue: tcgen05.ld (32 lanes x 32 columns per warp), the
-//             fused epilogue (SwiGLU / residual / fp32 widen), global stores.
+// Per CTA, 192 threads (one CTA per SM for wide tiles):
+//   warp 0    TMA producer: 2-D tiled loads, 128-byte swizzle, into a ring of
+//             stage pairs guarded by mbarriers (one full/empty barrier per
+//             pair).  Weight tiles of the first ring pass are issued before
+//             the grid waits on the previous kernel; skinny tiles also
+//             prefetch the rest of their first unit's weight boxes into L2.
+//   warp 1    MMA issuer: one thread issues tcgen05.mma kind::f16 (fp16/bf16
+//             in, fp32 accumulate) into a double-buffered tensor-memory
+//             accumulator; tcgen05.commit frees ring slots.
+//   warps 2-5 epilogue: tcgen05.ld, the fused epilogue (SwiGLU / residual /
+//             fp32), stores — through 128-byte-swizzled staging and TMA stores
+//             for wide tiles, per element (coalesced) for skinny tiles.
 //
-// Scheduling (chosen on the host per problem):
-//   * split 1 — persistent: CTA c takes tiles c, c+grid, ... over the full K;
-//     the next tile's mainloop overlaps this tile's epilogue.  Tiles are
-//     rastered in groups of P tiles so concurrent CTAs share panels in L2.
-//   * split S (2..8) — for problems with fewer tiles than SMs: each tile's
-//     K range is split over a thread-block cluster of S CTAs.  Each CTA
-//     stages its fp32 partial tile in its own shared memory (the operand ring,
-//     idle by then); after a cluster barrier every CTA sums a slice of rows
-//     over all S partials through distributed shared memory, in rank order
-//     (deterministic), applies the epilogue and stores with coalesced writes.
-//     No global workspace, no atomics.
+// Scheduling (chosen on the host per problem, gemm_tc.cu plan_tc):
+//   * split 1 — persistent: CTA (pair) c takes tiles c, c+grid, ... over the
+//     full K; the next tile's mainloop overlaps this tile's epilogue.  Tiles
+//     are rastered in groups of P tiles so concurrent CTAs share L2 panels.
+//   * split S — fewer tiles than SMs: each tile's K range is split over a
+//     thread-block cluster of S CTAs (or S pairs).  Wide tiles: every CTA
+//     stages the 32-column units other CTAs own in shared memory and sends
+//     each owner its block with one bulk DSMEM copy; owners add them to their
+//     own units in rank order.  Skinny tiles: every CTA pushes each partial
+//     row straight from tensor memory into the shared memory of the CTA that
+//     owns that feature; one cluster barrier, then owners sum in rank order.
+//     Deterministic, no global workspace, no atomics.
 //
 // Every mbarrier wait is bounded (orin_common.cuh): after 2 s the CTA records
 // an error code in the device error word and unwinds instead of hanging.

@@ -8,9 +8,12 @@ Layout (one process per GPU, rank r of W):
   * gate/up — column-parallel by intermediate feature (IM/W per rank), packed
     per shard so the fused SwiGLU stays local to the rank.
   * o/down — row-parallel (split along K).  Each rank produces an fp32 partial
-    [M, H]; one all-reduce sums them, then the residual add and the single
-    rounding to 16 bits follow (orin_tp_linear_row).
-  * LM head — column-parallel by vocabulary row (any split, ragged tail ok).
+    [M, H]; the partials are summed over the ranks (over NVLink peer memory
+    after TPComm.enable_p2p, else ncclAllReduce), then the residual add and
+    the single rounding to 16 bits follow (orin_tp_linear_row).
+  * LM head — column-parallel by vocabulary row (any split, ragged tail ok);
+    greedy decoding reduces each rank's best token to one 64-bit key and
+    combines the ranks' keys with one max all-reduce (TPComm.lm_head_argmax).
 
 The reference is single-GPU (include/kv_cache.h:7); this module has no
 counterpart there.  Sharding helpers are plain torch and run on any device.

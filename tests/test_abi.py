@@ -91,6 +91,24 @@ def test_tp_rejects_bad_arguments():
     assert L.orin_tp_allreduce_f32(None, 16, 4, None) == _lib.ERR_INVALID_ARG
     assert L.orin_tp_linear_row(None, 16, 16, 16, 1, 1, 1, 0, None, None, None) == _lib.ERR_INVALID_ARG
     assert L.orin_tp_destroy(None) == _lib.OK
+    assert L.orin_tp_enable_p2p(None, 1 << 20, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_tp_lm_head_argmax(None, 16, 16, 16, 1, 10, 0, 64, 0, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    dummy = ctypes.c_void_p(16)
+    assert L.orin_tp_enable_p2p(dummy, 4, None) == _lib.ERR_INVALID_ARG         # < 8 elements
+    assert L.orin_tp_lm_head_argmax(dummy, 16, 16, 16, 1, 10, -1, 64, 0, 16, None) == \
+        _lib.ERR_INVALID_ARG                                                    # negative offset
+
+
+def test_lm_head_argmax_rejects_bad_arguments_on_host():
+    L = _lib.lib
+    assert L.orin_lm_head_argmax(None, 16, 16, 1, 10, 64, 0, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_lm_head_argmax(16, 16, 16, 0, 10, 64, 0, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_lm_head_argmax(16, 16, 16, 1, 10, 64, 7, 16, None) == _lib.ERR_INVALID_ARG
+    # K % 8 != 0: the weight stream can't take it
+    assert L.orin_lm_head_argmax(16, 16, 16, 1, 10, 12, 0, 16, None) == _lib.ERR_UNSUPPORTED
+    # unaligned h
+    assert L.orin_lm_head_argmax(16, 18, 16, 1, 10, 64, 0, 16, None) == _lib.ERR_UNSUPPORTED
 
 
 def test_python_mirror_rejects_cpu_tensors():
