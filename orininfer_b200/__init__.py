@@ -16,6 +16,6 @@ __version__ = "0.1.0"
 def __getattr__(name):
     if name in __all__:
         return getattr(importlib.import_module(".kernels", __name__), name)
-    if name in ("kernels", "tp", "synth", "_lib"):
+    if name in ("kernels", "tp", "synth", "weights", "_lib"):
         return importlib.import_module("." + name, __name__)
     raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
