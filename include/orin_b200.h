@@ -247,6 +247,16 @@ orin_status orin_tp_lm_head_argmax(void* comm, int* token, const void* h,
  */
 orin_status orin_tp_enable_p2p(void* comm, long long max_elems, void* stream);
 
+/*
+ * Diagnostic of the cross-GPU watchdog, on one GPU: runs the peer-memory
+ * reduction kernel against a "peer" that never signals (a plain buffer).
+ * The kernel must give up its bounded wait after 2 s and record a timeout in
+ * the device error word; the next orin_device_check then returns
+ * ORIN_ERR_TIMEOUT (and clears it) while the context stays usable.  Returns
+ * after the kernel has finished.
+ */
+orin_status orin_p2p_watchdog_selftest(void* stream);
+
 /* Block until every collective of comm issued on stream is done or the
  * timeout passes (then the communicator is aborted). */
 orin_status orin_tp_wait(void* comm, void* stream);

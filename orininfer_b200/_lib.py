@@ -71,6 +71,7 @@ SIGNATURES = {
     "orin_tp_linear_row_static": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "orin_tp_static_partial_capacity": (_ll, []),
     "orin_tp_enable_p2p": (_i, [_vp, _ll, _vp]),
+    "orin_p2p_watchdog_selftest": (_i, [_vp]),
     "orin_tp_lm_head_argmax": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "orin_tp_wait": (_i, [_vp, _vp]),
     "orin_tp_destroy": (_i, [_vp]),

@@ -260,6 +260,61 @@ orin_status orin_tp_lm_head_argmax(void* comm, int* token, const void* h, const 
   return ORIN_OK;
 }
 
+orin_status orin_p2p_watchdog_selftest(void* stream) {
+  // A two-rank view on one GPU whose "peer" is a plain buffer: the reduction
+  // kernel signals into it and waits on a local flag that nothing sets, so
+  // its bounded wait must give up and record DEVERR_TIMEOUT_PEER.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  DeviceCtx* ctx = (e == cudaSuccess) ? device_ctx(dev, &e) : nullptr;
+  if (!ctx) {
+    set_error("orin_p2p_watchdog_selftest: device set-up: %s", cudaGetErrorString(e));
+    return ORIN_ERR_CUDA;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  constexpr int M = 2, N = 8;
+  char* buf = nullptr;
+  const size_t flags_b = kP2PFlagBytes, part_b = 256, epoch_b = kP2PMaxBlocks * sizeof(int);
+  const size_t total = 2 * flags_b + 4 * part_b + epoch_b;
+  if ((e = cudaMalloc(&buf, total)) != cudaSuccess) {
+    set_error("orin_p2p_watchdog_selftest: cudaMalloc: %s", cudaGetErrorString(e));
+    return ORIN_ERR_CUDA;
+  }
+  cudaMemset(buf, 0, total);
+  P2PView v = {};
+  v.rank = 0;
+  v.world = 2;
+  v.N = N;
+  v.row0[0] = 0;
+  v.row0[1] = 1;
+  v.row0[2] = M;
+  char* p = buf;
+  v.flags[0] = reinterpret_cast<int*>(p);      // this rank's flags: nothing writes them
+  v.local_flags = v.flags[0];
+  p += flags_b;
+  v.flags[1] = reinterpret_cast<int*>(p);      // the "peer": receives our signal only
+  p += flags_b;
+  v.partial[0] = reinterpret_cast<const float*>(p);
+  v.partial[1] = reinterpret_cast<const float*>(p + part_b);
+  v.result[0] = p + 2 * part_b;
+  v.result[1] = p + 2 * part_b;
+  v.result_local = p + 2 * part_b;
+  v.C = p + 3 * part_b;
+  v.R = nullptr;
+  p += 4 * part_b;
+  v.epoch = reinterpret_cast<int*>(p);
+  v.err = ctx->err;
+  e = launch_p2p_reduce(v, ORIN_F16, s);
+  cudaError_t e2 = cudaStreamSynchronize(s);
+  cudaFree(buf);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    set_error("orin_p2p_watchdog_selftest: %s",
+              cudaGetErrorString(e != cudaSuccess ? e : e2));
+    return ORIN_ERR_CUDA;
+  }
+  return ORIN_OK;
+}
+
 orin_status orin_tp_enable_p2p(void* comm, long long max_elems, void* stream) {
   TpComm* c = static_cast<TpComm*>(comm);
   if (!c || max_elems < 8) {
