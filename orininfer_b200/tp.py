@@ -187,11 +187,3 @@ class TPComm:
             self.close()
         except Exception:
             pass
-
-
-def sum_shards_reference(parts: Sequence[torch.Tensor]) -> torch.Tensor:
-    """Sum of per-rank fp32 partials in rank order (host-side check helper)."""
-    out = parts[0].clone()
-    for p in parts[1:]:
-        out += p
-    return out
