@@ -157,6 +157,55 @@ orin_status orin_add(void* x, const void* y, long long n, int dtype,
 orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype,
                            void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Sink + sliding-window GQA attention over the ring KV pool (the callers of */
+/* the linear layers on either side: q/k/v come from the q/k/v projection,   */
+/* the output feeds o_proj).                                                 */
+
+/*
+ * The KV pool of one layer, as the reference lays it out (include/kv_cache.h:
+ * 12-25, src/kv_cache.cu:21-41): K and V pools of n_sink + window_size slots,
+ * each [slot][num_kv_heads][head_dim]; logical position p is stored in slot
+ * p (p < n_sink) or n_sink + (p - n_sink) % window_size.
+ *
+ * Scatter seq_len new rows (k_src, v_src: [seq_len][kv_dim]) of positions
+ * start_pos .. start_pos + seq_len - 1 into their slots.  Replaces
+ * KVCache::append_kv (include/kv_cache.h:37-40, src/kv_cache.cu:95-111) with
+ * the pools passed explicitly.  seq_len > n_sink + window_size is
+ * ORIN_ERR_INVALID_ARG, as the reference throws.  When more than window_size
+ * window positions arrive in one call, the later of two tokens sharing a
+ * slot is the one stored (the reference leaves that to launch order).
+ */
+orin_status orin_kv_append(void* k_pool, void* v_pool, const void* k_src,
+                           const void* v_src, int seq_len, int start_pos,
+                           int n_sink, int window_size, int kv_dim, int dtype,
+                           void* stream);
+
+/*
+ * out[t, h, :] = round16( sum_p softmax_p(scale * q[t, h] . K[p, h / G]) V[p, h / G] )
+ * over the positions p query token t sees: with ap = cache_len - seq_len + t,
+ * p <= ap and (p < n_sink or p >= ap + 1 - window_size), each read through
+ * its pool slot.  q, out: [seq_len][num_heads][head_dim]; G = num_heads /
+ * num_kv_heads; fp32 scores, softmax and sums.  Replaces kernels::attention
+ * (include/kernels.h:58-80, kernels/attention.cu:27-175).
+ *
+ * head_dim 64 or 128 (else ORIN_ERR_UNSUPPORTED); all pointers 16-byte
+ * aligned.  workspace (device, may be NULL) lets few-token calls split the
+ * keys across CTAs; orin_attention_workspace_bytes gives the size that
+ * unlocks every split, a smaller one splits less.  Calls that share a
+ * workspace must be ordered on one stream.
+ */
+orin_status orin_attention(void* out, const void* q, const void* k_pool,
+                           const void* v_pool, int seq_len, int cache_len,
+                           int num_heads, int num_kv_heads, int head_dim,
+                           float scale, int n_sink, int window_size, int dtype,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream);
+orin_status orin_attention_workspace_bytes(size_t* bytes, int seq_len,
+                                           int cache_len, int num_heads,
+                                           int num_kv_heads, int head_dim,
+                                           int n_sink, int window_size);
+
 /*
  * Synchronise stream and report device-side failures of this library's
  * kernels: every spin-wait inside them gives up after a bounded time and

@@ -35,6 +35,14 @@ void add(__nv_bfloat16* x, const __nv_bfloat16* y, int n);
  * kernels/softmax.cu:117-120. */
 void bf16_to_fp32(float* out, const __nv_bfloat16* in, int n);
 
+/* Sink + sliding-window GQA attention over the ring KV pool (orin_attention).
+ * Reference: include/kernels.h:58-80, kernels/attention.cu:140-175.  Split-key
+ * partials of few-token calls use a 4 MB static device array. */
+void attention(__nv_bfloat16* out, const __nv_bfloat16* q,
+               const __nv_bfloat16* k_pool, const __nv_bfloat16* v_pool,
+               int seq_len, int cache_len, int num_heads, int num_kv_heads,
+               int head_dim, float scale, int n_sink, int window_size);
+
 }  // namespace kernels
 
 /* Reference: kernels/gemm_cute.cu:295-324 (declared at kernels/matmul.cu:9-12).

@@ -198,6 +198,96 @@ def pack_gate_up(wg: np.ndarray, wu: np.ndarray) -> np.ndarray:
     return out
 
 
+def ring_slot(pos, n_sink: int, window: int):
+    """Pool slot of logical position pos (src/kv_cache.cu:29-31)."""
+    pos = np.asarray(pos, dtype=np.int64)
+    return np.where(pos < n_sink, pos, n_sink + (pos - n_sink) % window)
+
+
+def kv_append(k_pool: np.ndarray, v_pool: np.ndarray, k_src: np.ndarray, v_src: np.ndarray,
+              start_pos: int, n_sink: int, window: int) -> None:
+    """KVCache::append_kv (src/kv_cache.cu:95-111, kernel :21-41): row t of the
+    call goes to the slot of position start_pos + t, in place; rows taken in
+    call order, so of two rows sharing a slot the later one stays.
+    Pools [slots, kv_dim], sources [seq_len, kv_dim] (any dtype)."""
+    seq_len = k_src.shape[0]
+    if seq_len > n_sink + window:
+        raise ValueError("seq_len exceeds n_sink + window (src/kv_cache.cu:99-103)")
+    slots = ring_slot(start_pos + np.arange(seq_len), n_sink, window)
+    for t in range(seq_len):
+        k_pool[slots[t]] = k_src[t]
+        v_pool[slots[t]] = v_src[t]
+
+
+def attention(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, seq_len: int,
+              cache_len: int, num_heads: int, num_kv_heads: int, head_dim: int, scale: float,
+              n_sink: int, window: int, dt: int) -> np.ndarray:
+    """Sink + sliding-window GQA attention (kernels/attention.cu:27-138), vectorised.
+
+    q: uint16 bits [seq_len, num_heads, head_dim]; pools: uint16 bits
+    [n_sink + window, num_kv_heads, head_dim]; returns uint16 bits of out
+    [seq_len, num_heads, head_dim].  Query token t (attend_pos
+    ap = cache_len - seq_len + t, :47) sees positions p <= ap with p < n_sink
+    (the sink, :48) or p >= ap + 1 - window (the window, :49-55), each read
+    from its ring slot; scores scale * q.k (:66-82), softmax (:87-118) and the
+    weighted sum of V (:121-137) in float64 here (fp32 in the reference), one
+    rounding of the result to the 16-bit type (:137)."""
+    G = num_heads // num_kv_heads
+    qf = widen(q, dt).reshape(seq_len, num_heads, head_dim).astype(np.float64)
+    kf = widen(k_pool, dt).reshape(-1, num_kv_heads, head_dim).astype(np.float64)
+    vf = widen(v_pool, dt).reshape(-1, num_kv_heads, head_dim).astype(np.float64)
+    ap = cache_len - seq_len + np.arange(seq_len)
+    sink_hi = min(n_sink, int(ap[-1]) + 1)
+    win_lo = max(n_sink, int(ap[0]) + 1 - window)
+    pos = np.concatenate([np.arange(sink_hi), np.arange(win_lo, int(ap[-1]) + 1)])
+    slot = ring_slot(pos, n_sink, window)
+    ok = (pos[None, :] <= ap[:, None]) & (
+        (pos[None, :] < n_sink) | (pos[None, :] >= ap[:, None] + 1 - window))
+    out = np.empty((seq_len, num_heads, head_dim), dtype=np.float64)
+    for h in range(num_kv_heads):
+        K = kf[slot, h]  # [U, hd]
+        V = vf[slot, h]
+        Q = qf[:, h * G:(h + 1) * G]  # [seq, G, hd]
+        s = np.einsum("tgd,ud->tgu", Q, K) * scale
+        s = np.where(ok[:, None, :], s, -np.inf)
+        m = s.max(axis=-1, keepdims=True)
+        e = np.exp(s - m)
+        out[:, h * G:(h + 1) * G] = np.einsum("tgu,ud->tgd", e, V) / e.sum(axis=-1)[..., None]
+    return round16(out.astype(np.float32), dt)
+
+
+def attention_literal(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, seq_len: int,
+                      cache_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                      scale: float, n_sink: int, window: int, dt: int) -> np.ndarray:
+    """The same, step by step as one CTA of kernels/attention.cu:27-138 runs it
+    (small cases only): sink_len, window_len, the oldest window position and
+    the ring offset win_offset, physical slot n_sink + (win_offset + w) %
+    window of the w-th window token; fp32 scores, max, exp, sum and the
+    normalised weighted sum of V."""
+    G = num_heads // num_kv_heads
+    qf = widen(q, dt).reshape(seq_len, num_heads, head_dim)
+    kf = widen(k_pool, dt).reshape(-1, num_kv_heads, head_dim)
+    vf = widen(v_pool, dt).reshape(-1, num_kv_heads, head_dim)
+    out = np.empty((seq_len, num_heads, head_dim), dtype=np.float32)
+    f32 = np.float32
+    for qi in range(seq_len):
+        for h in range(num_heads):
+            kv_h = h // G
+            attend_pos = cache_len - seq_len + qi
+            sink_len = min(n_sink, attend_pos + 1)
+            window_len = min(max(attend_pos + 1 - n_sink, 0), window)
+            oldest_w = attend_pos + 1 - window_len
+            win_offset = (oldest_w - n_sink) % window if window_len > 0 else 0
+            phys = list(range(sink_len)) + [n_sink + (win_offset + w) % window
+                                            for w in range(window_len)]
+            scores = np.array([f32(np.dot(qf[qi, h], kf[ph, kv_h])) * f32(scale) for ph in phys],
+                              dtype=np.float32)
+            e = np.exp(scores - scores.max()).astype(np.float32)
+            p = e * (f32(1.0) / e.sum(dtype=np.float32))
+            out[qi, h] = (p[:, None] * vf[phys, kv_h]).sum(axis=0, dtype=np.float32)
+    return round16(out, dt)
+
+
 class RefKernels:
     """The reference's own bf16 kernels (built from its sources; GPU only).
 
@@ -214,8 +304,10 @@ class RefKernels:
         L.ref_fused_silu_mul.argtypes = [_vp, _vp, _vp, _i, _i]
         L.ref_add.argtypes = [_vp, _vp, _i]
         L.ref_bf16_to_fp32.argtypes = [_vp, _vp, _i]
+        L.ref_attention.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float,
+                                    _i, _i]
         for n in ("ref_matmul", "ref_gemm_cute", "ref_fused_silu_mul", "ref_add",
-                  "ref_bf16_to_fp32", "ref_sync"):
+                  "ref_bf16_to_fp32", "ref_attention", "ref_sync"):
             getattr(L, n).restype = _i
 
     def _ok(self, rc: int, what: str) -> None:
@@ -236,6 +328,13 @@ class RefKernels:
 
     def bf16_to_fp32(self, out: int, inp: int, n: int) -> None:
         self._ok(self.lib.ref_bf16_to_fp32(out, inp, n), "kernels::bf16_to_fp32")
+
+    def attention(self, out: int, q: int, k_pool: int, v_pool: int, seq_len: int,
+                  cache_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                  scale: float, n_sink: int, window: int) -> None:
+        self._ok(self.lib.ref_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
+                                        num_kv_heads, head_dim, scale, n_sink, window),
+                 "kernels::attention")
 
     def sync(self) -> None:
         self._ok(self.lib.ref_sync(), "cudaDeviceSynchronize")

@@ -2,7 +2,8 @@
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
 // the reference's unmodified sources (kernels/matmul.cu, kernels/gemm_cute.cu,
-// kernels/fused_swiglu.cu, kernels/softmax.cu) into oracle/_ref/.  The tests
+// kernels/fused_swiglu.cu, kernels/softmax.cu, kernels/attention.cu) into
+// oracle/_ref/.  The tests
 // use it to pin the CPU oracle to what the reference computes; nothing in the
 // product links it.
 #include <cuda_runtime.h>
@@ -43,6 +44,18 @@ int ref_add(void* x, const void* y, int n) {
 
 int ref_bf16_to_fp32(float* out, const void* in, int n) {
   kernels::bf16_to_fp32(out, static_cast<const __nv_bfloat16*>(in), n);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// kernels::attention: sink + sliding-window GQA attention over the ring pool
+// (one CTA of 128 threads per query token and head).
+int ref_attention(void* out, const void* q, const void* k_pool, const void* v_pool, int seq_len,
+                  int cache_len, int num_heads, int num_kv_heads, int head_dim, float scale,
+                  int n_sink, int window_size) {
+  kernels::attention(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
+                     static_cast<const __nv_bfloat16*>(k_pool),
+                     static_cast<const __nv_bfloat16*>(v_pool), seq_len, cache_len, num_heads,
+                     num_kv_heads, head_dim, scale, n_sink, window_size);
   return static_cast<int>(cudaGetLastError());
 }
 

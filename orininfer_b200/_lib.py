@@ -63,6 +63,10 @@ SIGNATURES = {
     "orin_silu_mul": (_i, [_vp, _vp, _vp, _ll, _i, _vp]),
     "orin_add": (_i, [_vp, _vp, _ll, _i, _vp]),
     "orin_widen_f32": (_i, [_vp, _vp, _ll, _i, _vp]),
+    "orin_kv_append": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "orin_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _i, _i,
+                            _vp, _sz, _vp]),
+    "orin_attention_workspace_bytes": (_i, [ctypes.POINTER(_sz), _i, _i, _i, _i, _i, _i, _i]),
     "orin_device_check": (_i, [_vp]),
     "orin_tp_unique_id": (_i, [_vp]),
     "orin_tp_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i, _i, ctypes.c_double]),
@@ -84,6 +88,7 @@ SHIM_SYMBOLS = {
     "kernels::add": "_ZN7kernels3addEP13__nv_bfloat16PKS0_i",
     "kernels::bf16_to_fp32": "_ZN7kernels12bf16_to_fp32EPfPK13__nv_bfloat16i",
     "launch_gemm_cute": "_Z16launch_gemm_cuteP13__nv_bfloat16PKS_S2_iii",
+    "kernels::attention": "_ZN7kernels9attentionEP13__nv_bfloat16PKS0_S3_S3_iiiiifii",
 }
 
 
@@ -111,6 +116,7 @@ def _load() -> ctypes.CDLL:
         "kernels::add": [_vp, _vp, _i],
         "kernels::bf16_to_fp32": [_vp, _vp, _i],
         "launch_gemm_cute": [_vp, _vp, _vp, _i, _i, _i],
+        "kernels::attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _i],
     }
     for name, sym in SHIM_SYMBOLS.items():
         fn = getattr(lib, sym)

@@ -308,6 +308,101 @@ orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype, v
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_widen_f32");
 }
 
+namespace {
+
+// Shared argument checks of the attention entry points.
+orin_status check_attention(const char* fn, int seq_len, int cache_len, int num_heads,
+                            int num_kv_heads, int head_dim, int n_sink, int window) {
+  if (seq_len < 0 || cache_len < seq_len || num_heads < 1 || num_kv_heads < 1 ||
+      num_heads % num_kv_heads != 0 || n_sink < 0 || window < 1) {
+    set_error("%s: needs 0 <= seq_len <= cache_len, num_heads a multiple of num_kv_heads, "
+              "n_sink >= 0, window_size >= 1 (seq_len=%d cache_len=%d heads=%d/%d n_sink=%d "
+              "window=%d)",
+              fn, seq_len, cache_len, num_heads, num_kv_heads, n_sink, window);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (head_dim != 64 && head_dim != 128) {
+    set_error("%s: head_dim %d (64 and 128 are built)", fn, head_dim);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (static_cast<long long>(n_sink) + window > 0x7fffffffLL / 2) {
+    set_error("%s: n_sink + window_size too large", fn);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  return ORIN_OK;
+}
+
+}  // namespace
+
+orin_status orin_attention_workspace_bytes(size_t* bytes, int seq_len, int cache_len,
+                                           int num_heads, int num_kv_heads, int head_dim,
+                                           int n_sink, int window_size) {
+  if (!bytes) {
+    set_error("orin_attention_workspace_bytes: null output");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  orin_status st = check_attention("orin_attention_workspace_bytes", seq_len, cache_len,
+                                   num_heads, num_kv_heads, head_dim, n_sink, window_size);
+  if (st != ORIN_OK) return st;
+  *bytes = seq_len == 0 ? 0
+                        : plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim,
+                                         n_sink, window_size, ~static_cast<size_t>(0))
+                              .workspace_bytes;
+  return ORIN_OK;
+}
+
+orin_status orin_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
+                           int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                           int head_dim, float scale, int n_sink, int window_size, int dtype,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  st = check_attention("orin_attention", seq_len, cache_len, num_heads, num_kv_heads, head_dim,
+                       n_sink, window_size);
+  if (st != ORIN_OK) return st;
+  if (seq_len == 0) return ORIN_OK;
+  if (!out || !q || !k_pool || !v_pool) {
+    set_error("orin_attention: null pointer");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (!aligned16(out) || !aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) ||
+      (workspace && !aligned16(workspace))) {
+    set_error("orin_attention: out, q, the pools and the workspace must be 16-byte aligned");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
+                                   num_kv_heads, head_dim, scale, n_sink, window_size, dtype,
+                                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention");
+}
+
+orin_status orin_kv_append(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
+                           int seq_len, int start_pos, int n_sink, int window_size, int kv_dim,
+                           int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (seq_len < 0 || start_pos < 0 || n_sink < 0 || window_size < 1 || kv_dim < 1 ||
+      (seq_len > 0 && (!k_pool || !v_pool || !k_src || !v_src))) {
+    set_error("orin_kv_append: null pointer or bad size (seq_len=%d start_pos=%d n_sink=%d "
+              "window=%d kv_dim=%d)",
+              seq_len, start_pos, n_sink, window_size, kv_dim);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (static_cast<long long>(seq_len) > static_cast<long long>(n_sink) + window_size) {
+    // the reference's precondition (src/kv_cache.cu:99-103)
+    set_error("orin_kv_append: seq_len %d exceeds n_sink + window_size (%d)", seq_len,
+              n_sink + window_size);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (static_cast<long long>(start_pos) + seq_len > 0x7fffffffLL) {
+    set_error("orin_kv_append: positions past 2^31");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_kv_scatter(k_pool, v_pool, k_src, v_src, seq_len, start_pos, n_sink,
+                                    window_size, kv_dim, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_kv_append");
+}
+
 orin_status orin_device_check(void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(s);

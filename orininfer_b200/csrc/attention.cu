@@ -1,0 +1,590 @@
+// attention.cu — sink + sliding-window GQA attention over the ring KV pool,
+// and the scatter of a call's new K/V rows into that pool.
+//
+// Pool layout (the reference's, src/kv_cache.cu:21-41): per layer one K and
+// one V pool of n_sink + W slots, slot-major [slot][num_kv_heads][head_dim].
+// Logical position p lives in slot p (p < n_sink) or n_sink + (p - n_sink) % W.
+//
+// Attention (kernels/attention.cu:27-138): query token qi of a call with
+// seq_len new tokens and cache_len positions in total sits at
+// ap = cache_len - seq_len + qi and attends to every position p with
+//   p <= ap  and  (p < n_sink  or  p >= ap + 1 - W),
+// read through its slot after the call's own tokens were scattered (so a
+// chunk that wraps the ring reads its own later tokens in the wrapped slots,
+// as the reference does):
+//   out[qi, h] = round16( sum_p softmax_p(scale * q[qi, h] . k[p, h / G]) v[p, h / G] )
+// with G = num_heads / num_kv_heads, fp32 scores, fp32 softmax and fp32 sums.
+//
+// Kernel: one CTA (4 warps) per (row block, kv head, key split).  A row is one
+// (token, query head) pair; the heads of one GQA group share the K/V tiles, so
+// a row block stacks tokens x group heads (16 rows per warp, the m16n8k16 tile).
+// Keys stream through shared memory in 64-key tiles (cp.async, two stages,
+// rows padded by 16 bytes so the fragment loads are bank-conflict free) in the
+// order of their logical positions: the sink range, then the window range.
+// S = Q K^T and O += P V run on mma.sync m16n8k16 with an online softmax in
+// registers.  Prefill blocks put 4 warps on 64 rows; decode blocks put the 4
+// warps on one 16-row group and split each key tile between them, and split
+// the key range across CTAs; partials (running max, sum, unnormalised O)
+// merge in shared memory and, across CTAs, in attn_combine_kernel.
+#include "orin_common.cuh"
+#include "orin_internal.h"
+
+namespace orin {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kKeyTile = 64;
+
+struct AttnParams {
+  void* out;           // [seq_len, num_heads, head_dim] 16-bit
+  const void* q;       // [seq_len, num_heads, head_dim] 16-bit
+  const void* k_pool;  // [n_sink + W, num_kv_heads, head_dim] 16-bit
+  const void* v_pool;
+  float* ws;           // split partials (splits > 1): O [splits][rows][HD], then (m, l) pairs
+  int seq_len, cache_len, num_heads, num_kv_heads, n_sink, window;
+  float scale;
+  int group;   // G = num_heads / num_kv_heads
+  int hpb;     // group heads per row block
+  int tpb;     // tokens per row block
+  int hsb;     // row blocks per (token block, group) when G > rows per block
+  int splits;  // key splits (grid z)
+};
+
+// Pool slot of logical position p (src/kv_cache.cu:29-31).
+__device__ __forceinline__ int ring_slot(int p, int n_sink, int window) {
+  return p < n_sink ? p : n_sink + (p - n_sink) % window;
+}
+
+__device__ __forceinline__ void cp_async_16(void* smem, const void* gmem, bool full) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const int n = full ? 16 : 0;  // 0 bytes read: the 16 bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint16_t* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+// Four 8x8 16-bit matrices, transposed: lane l gives the row address of
+// matrix l / 8, row l % 8; register i receives matrix i's elements
+// (2 * (lane % 4) + {0, 1}, lane / 4).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const uint16_t* p) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+
+// D += A B, m16n8k16, fp32 accumulate.  Fragments (lane = 4 g + q):
+//   A: a0 = (g, 2q..2q+1), a1 = (g+8, 2q..), a2 = (g, 2q+8..), a3 = (g+8, 2q+8..)
+//   B: b0 = (k 2q..2q+1, n g), b1 = (k 2q+8..2q+9, n g)
+//   D: d0, d1 = (g, 2q..2q+1), d2, d3 = (g+8, 2q..2q+1)
+template <int DT>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (DT == DT_F16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Key ranges of one row block: tokens [t_lo, t_hi] attend to the sink range
+// [0, sink_cnt) and the window range [win_lo, win_lo + win_cnt).
+struct KeyRanges {
+  int sink_cnt, win_lo, win_cnt, tiles_sink, tiles;
+};
+
+__device__ __host__ __forceinline__ KeyRanges key_ranges(int ap_lo, int ap_hi, int n_sink,
+                                                        int window) {
+  KeyRanges r;
+  r.sink_cnt = ap_hi + 1 < n_sink ? ap_hi + 1 : n_sink;
+  int lo = ap_lo + 1 - window;
+  if (lo < n_sink) lo = n_sink;
+  r.win_lo = lo;
+  r.win_cnt = ap_hi >= lo ? ap_hi - lo + 1 : 0;
+  r.tiles_sink = (r.sink_cnt + kKeyTile - 1) / kKeyTile;
+  r.tiles = r.tiles_sink + (r.win_cnt + kKeyTile - 1) / kKeyTile;
+  return r;
+}
+
+template <int HD>
+constexpr int attn_pitch() { return HD + 8; }  // 16-bit elements per staged key row
+template <int HD>
+constexpr int attn_stage_elems() { return kKeyTile * attn_pitch<HD>(); }
+template <int HD>
+constexpr int attn_smem_bytes() {
+  return 4 * attn_stage_elems<HD>() * 2;  // 2 stages x (K, V)
+}
+
+// RW = warps stacked on rows (4: 64 rows, prefill), the other 4 / RW warps
+// split each key tile.
+template <int DT, int HD, int RW>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_kernel(const AttnParams p) {
+  using E = Elem<DT>;
+  constexpr int KW = 4 / RW;          // warps sharing a row group
+  constexpr int KC = kKeyTile / KW;   // keys per warp per tile
+  constexpr int NB = KC / 8;          // S n-blocks per warp
+  constexpr int KS = HD / 16;         // k-steps of Q K^T
+  constexpr int ON = HD / 8;          // O n-blocks
+  constexpr int PITCH = attn_pitch<HD>();
+  constexpr int R = 16 * RW;          // rows per block
+  constexpr int OP = HD + 4;          // fp32 pitch of the merge area
+  static_assert(KC % 16 == 0, "a warp's key slice must cover whole k-steps");
+  static_assert(KW * R * OP * 4 <= attn_smem_bytes<HD>(), "merge area must fit the stages");
+
+  extern __shared__ __align__(16) uint16_t attn_smem[];
+  __shared__ float s_m[KW * R];
+  __shared__ float s_l[KW * R];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int rw = warp % RW, kw = warp / RW;
+
+  const int kvh = blockIdx.y;
+  const int tb = blockIdx.x / p.hsb, hs = blockIdx.x % p.hsb;
+  const int t_lo = tb * p.tpb;
+  int t_hi = t_lo + p.tpb - 1;
+  if (t_hi > p.seq_len - 1) t_hi = p.seq_len - 1;
+  const int base = p.cache_len - p.seq_len;
+  const KeyRanges kr = key_ranges(base + t_lo, base + t_hi, p.n_sink, p.window);
+  const int per = (kr.tiles + p.splits - 1) / p.splits;
+  const int tile0 = blockIdx.z * per;
+  int tile1 = tile0 + per;
+  if (tile1 > kr.tiles) tile1 = kr.tiles;
+
+  // The two rows of this lane: warp rows g and g + 8 of row group rw.
+  int tok[2], head[2], ap[2];
+  bool rv[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = rw * 16 + g + 8 * i;
+    const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
+    tok[i] = t_lo + tr;
+    head[i] = kvh * p.group + hr;
+    rv[i] = tr < p.tpb && tok[i] < p.seq_len && hr < p.group;
+    ap[i] = base + tok[i];
+  }
+
+  const uint16_t* kpool = static_cast<const uint16_t*>(p.k_pool);
+  const uint16_t* vpool = static_cast<const uint16_t*>(p.v_pool);
+  // stage s: K at 2 s, V at 2 s + 1 (in units of one staged tile)
+  auto sK = [&](int stage) { return attn_smem + (2 * stage) * attn_stage_elems<HD>(); };
+  auto sV = [&](int stage) { return attn_smem + (2 * stage + 1) * attn_stage_elems<HD>(); };
+
+  pdl_wait();  // q and the pools come from the previous kernels
+
+  auto tile_start = [&](int t, int& end) {
+    if (t < kr.tiles_sink) {
+      end = kr.sink_cnt;
+      return t * kKeyTile;
+    }
+    end = kr.win_lo + kr.win_cnt;
+    return kr.win_lo + (t - kr.tiles_sink) * kKeyTile;
+  };
+  auto load_tile = [&](int t, int stage) {
+    int end;
+    const int start = tile_start(t, end);
+    constexpr int CPR = HD / 8;  // 16-byte chunks per key row
+    for (int c = tid; c < kKeyTile * CPR; c += kAttnThreads) {
+      const int row = c / CPR, col = (c % CPR) * 8;
+      const int pos = start + row;
+      const bool ok = pos < end;
+      size_t off = 0;
+      if (ok)
+        off = (static_cast<size_t>(ring_slot(pos, p.n_sink, p.window)) * p.num_kv_heads + kvh) *
+                  HD + col;
+      cp_async_16(sK(stage) + row * PITCH + col, kpool + off, ok);
+      cp_async_16(sV(stage) + row * PITCH + col, vpool + off, ok);
+    }
+  };
+
+  if (tile0 < tile1) load_tile(tile0, 0);
+  cp_async_commit();
+
+  // Q fragments of the two rows, straight from global memory.
+  uint32_t qa[KS][4];
+  {
+    const uint16_t* qb = static_cast<const uint16_t*>(p.q);
+    const uint16_t* q0 =
+        rv[0] ? qb + (static_cast<size_t>(tok[0]) * p.num_heads + head[0]) * HD : nullptr;
+    const uint16_t* q1 =
+        rv[1] ? qb + (static_cast<size_t>(tok[1]) * p.num_heads + head[1]) * HD : nullptr;
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int c = 16 * s + 2 * q4;
+      qa[s][0] = q0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[s][1] = q1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[s][2] = q0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[s][3] = q1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+  }
+
+  float o[ON][4];
+#pragma unroll
+  for (int j = 0; j < ON; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+
+  for (int t = tile0; t < tile1; ++t) {
+    const int stage = (t - tile0) & 1;
+    if (t + 1 < tile1) load_tile(t + 1, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+
+    int end;
+    const int start = tile_start(t, end);
+    const uint16_t* k_s = sK(stage) + (kw * KC) * PITCH;
+    const uint16_t* v_s = sV(stage) + (kw * KC) * PITCH;
+
+    // S = Q K^T over this warp's KC keys
+    float s[NB][4];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+      const uint16_t* kr_row = k_s + (8 * j + g) * PITCH + 2 * q4;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks)
+        mma16816<DT>(s[j], qa[ks], lds32(kr_row + 16 * ks), lds32(kr_row + 16 * ks + 8));
+    }
+
+    // mask, scale and the online softmax of the two rows
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = e >> 1;
+        const int pos = start + kw * KC + 8 * j + 2 * q4 + (e & 1);
+        const bool ok = rv[i] && pos < end && pos <= ap[i] &&
+                        (pos < p.n_sink || pos >= ap[i] + 1 - p.window);
+        s[j][e] = ok ? s[j][e] * p.scale : -INFINITY;
+        mx[i] = fmaxf(mx[i], s[j][e]);
+      }
+    float alpha[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+      const float m_new = fmaxf(m_run[i], mx[i]);
+      // a row with nothing valid yet keeps m = -inf and adds nothing
+      alpha[i] = m_new == -INFINITY ? 1.f : __expf(m_run[i] - m_new);
+      mx[i] = m_new == -INFINITY ? 0.f : m_new;
+      m_run[i] = m_new;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = e >> 1;
+        const float v = __expf(s[j][e] - mx[i]);  // exp(-inf) = 0 for masked keys
+        s[j][e] = v;
+        rs[i] += v;
+      }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) l_run[i] = l_run[i] * alpha[i] + rs[i];
+#pragma unroll
+    for (int j = 0; j < ON; ++j) {
+      o[j][0] *= alpha[0];
+      o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1];
+      o[j][3] *= alpha[1];
+    }
+
+    // O += P V: the S accumulators of n-blocks 2u, 2u+1 are the A fragment of
+    // k-step u; V's B fragments come transposed from shared memory.
+#pragma unroll
+    for (int u = 0; u < KC / 16; ++u) {
+      uint32_t pa[4];
+      pa[0] = E::pack2(s[2 * u][0], s[2 * u][1]);
+      pa[1] = E::pack2(s[2 * u][2], s[2 * u][3]);
+      pa[2] = E::pack2(s[2 * u + 1][0], s[2 * u + 1][1]);
+      pa[3] = E::pack2(s[2 * u + 1][2], s[2 * u + 1][3]);
+      const int mi = lane >> 3;
+      const uint16_t* vrow = v_s + (16 * u + (mi & 1) * 8 + (lane & 7)) * PITCH + (mi >> 1) * 8;
+#pragma unroll
+      for (int jp = 0; jp < ON / 2; ++jp) {
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, vrow + 16 * jp);
+        mma16816<DT>(o[2 * jp], pa, b[0], b[1]);
+        mma16816<DT>(o[2 * jp + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();  // this stage is refilled by the next iteration's load
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // Partials of every warp into shared memory (the stages are free now).
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
+  }
+  float* s_o = reinterpret_cast<float*>(attn_smem);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = kw * R + rw * 16 + g + 8 * i;
+#pragma unroll
+    for (int j = 0; j < ON; ++j)
+      *reinterpret_cast<float2*>(s_o + r * OP + 8 * j + 2 * q4) =
+          make_float2(o[j][2 * i], o[j][2 * i + 1]);
+    if (q4 == 0) {
+      s_m[r] = m_run[i];
+      s_l[r] = l_run[i];
+    }
+  }
+  __syncthreads();
+
+  // Merge the KW partials of each row; write the row (one split) or this
+  // split's partial.
+  const int rows_total = p.seq_len * p.num_heads;
+  for (int idx = tid; idx < R * (HD / 2); idx += kAttnThreads) {
+    const int r = idx / (HD / 2), d = (idx % (HD / 2)) * 2;
+    const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
+    const int tk = t_lo + tr;
+    if (!(tr < p.tpb && tk < p.seq_len && hr < p.group)) continue;
+    const int orow = tk * p.num_heads + kvh * p.group + hr;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < KW; ++w) m = fmaxf(m, s_m[w * R + r]);
+    float l = 0.f, ox = 0.f, oy = 0.f;
+#pragma unroll
+    for (int w = 0; w < KW; ++w) {
+      const float mw = s_m[w * R + r];
+      const float f = mw == -INFINITY ? 0.f : __expf(mw - m);
+      l += f * s_l[w * R + r];
+      const float2 v = *reinterpret_cast<const float2*>(s_o + (w * R + r) * OP + d);
+      ox += f * v.x;
+      oy += f * v.y;
+    }
+    if (p.splits == 1) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.out) +
+                                   static_cast<size_t>(orow) * HD + d) =
+          E::pack2(ox * inv, oy * inv);
+    } else {
+      const size_t prow = static_cast<size_t>(blockIdx.z) * rows_total + orow;
+      *reinterpret_cast<float2*>(p.ws + prow * HD + d) = make_float2(ox, oy);
+      if (d == 0) {
+        float* ml = p.ws + static_cast<size_t>(p.splits) * rows_total * HD + prow * 2;
+        ml[0] = m;
+        ml[1] = l;
+      }
+    }
+  }
+}
+
+// out[row] = round16( sum_s f_s O_s / sum_s f_s l_s ), f_s = exp(m_s - max m):
+// one warp per output row.
+template <int DT, int HD>
+__global__ void __launch_bounds__(128)
+    attn_combine_kernel(void* out, const float* ws, int rows_total, int splits) {
+  using E = Elem<DT>;
+  pdl_wait();
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows_total) return;
+  const float* ml = ws + static_cast<size_t>(splits) * rows_total * HD;
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, ml[(static_cast<size_t>(s) * rows_total + row) * 2]);
+  constexpr int DPL = HD / 32;  // dims per lane (2 or 4)
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  float l = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const size_t pr = static_cast<size_t>(s) * rows_total + row;
+    const float ms = ml[pr * 2];
+    const float f = ms == -INFINITY ? 0.f : __expf(ms - m);
+    l += f * ml[pr * 2 + 1];
+    const float* os = ws + pr * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] += f * os[i];
+  }
+  pdl_launch_dependents();
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  uint16_t* dst = static_cast<uint16_t*>(out) + static_cast<size_t>(row) * HD + lane * DPL;
+#pragma unroll
+  for (int i = 0; i < DPL; i += 2)
+    *reinterpret_cast<uint32_t*>(dst + i) = E::pack2(acc[i] * inv, acc[i + 1] * inv);
+}
+
+// The call's new K/V rows into their pool slots (src/kv_cache.cu:21-41).  When
+// more than W window positions land in one call, two tokens share a slot; the
+// later token is the one kept (what a sequential append leaves), so the
+// earlier one is skipped.  One CTA per token, 16-byte copies when the rows
+// allow them.
+__global__ void __launch_bounds__(128)
+    kv_scatter_kernel(uint16_t* k_pool, uint16_t* v_pool, const uint16_t* k_src,
+                      const uint16_t* v_src, int seq_len, int start_pos, int n_sink, int window,
+                      int kv_dim, int vec) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int pos = start_pos + t;
+  if (pos >= n_sink && t + window < seq_len) return;  // a later token owns the slot
+  const size_t dst = static_cast<size_t>(ring_slot(pos, n_sink, window)) * kv_dim;
+  const size_t src = static_cast<size_t>(t) * kv_dim;
+  if (vec) {
+    for (int c = threadIdx.x; c < kv_dim / 8; c += blockDim.x) {
+      reinterpret_cast<uint4*>(k_pool + dst)[c] = reinterpret_cast<const uint4*>(k_src + src)[c];
+      reinterpret_cast<uint4*>(v_pool + dst)[c] = reinterpret_cast<const uint4*>(v_src + src)[c];
+    }
+  } else {
+    for (int c = threadIdx.x; c < kv_dim; c += blockDim.x) {
+      k_pool[dst + c] = k_src[src + c];
+      v_pool[dst + c] = v_src[src + c];
+    }
+  }
+  pdl_launch_dependents();
+}
+
+template <class... KArgs, class... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <int DT, int HD, int RW>
+cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t s) {
+  auto kern = attn_kernel<DT, HD, RW>;
+  constexpr int smem = attn_smem_bytes<HD>();
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  return launch_ex(kern, dim3(row_blocks, p.num_kv_heads, p.splits), dim3(kAttnThreads), smem,
+                   s, p);
+}
+
+template <int DT, int HD>
+cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStream_t s) {
+  cudaError_t e = rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
+                          : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int rows_total = p.seq_len * p.num_heads;
+  return launch_ex(attn_combine_kernel<DT, HD>, dim3((rows_total + 3) / 4), dim3(128), 0, s,
+                   p.out, static_cast<const float*>(p.ws), rows_total, p.splits);
+}
+
+}  // namespace
+
+AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                        int head_dim, int n_sink, int window, size_t workspace_bytes) {
+  AttnPlan pl = {};
+  const int group = num_heads / num_kv_heads;
+  pl.rw = static_cast<long long>(seq_len) * group <= 32 ? 1 : 4;
+  const int rows = 16 * pl.rw;
+  pl.hpb = group < rows ? group : rows;
+  pl.tpb = rows / pl.hpb;
+  pl.hsb = (group + pl.hpb - 1) / pl.hpb;
+  const long long token_blocks = (seq_len + pl.tpb - 1) / pl.tpb;
+  pl.row_blocks = token_blocks * pl.hsb;
+  // Split the keys across CTAs only when the row blocks leave SMs idle.
+  const long long ctas = pl.row_blocks * num_kv_heads;
+  int splits = 1;
+  if (ctas < 148) {
+    // key tiles of the row block with the most keys (the last one)
+    const int last_lo = static_cast<int>((token_blocks - 1) * pl.tpb);
+    const int base = cache_len - seq_len;
+    const KeyRanges kr = key_ranges(base + last_lo, cache_len - 1, n_sink, window);
+    long long want = (2 * 148 + ctas - 1) / ctas;
+    if (want > kr.tiles) want = kr.tiles;
+    if (want > 256) want = 256;
+    splits = want < 1 ? 1 : static_cast<int>(want);
+    const size_t per_split =
+        static_cast<size_t>(seq_len) * num_heads * (head_dim + 2) * sizeof(float);
+    while (splits > 1 && static_cast<size_t>(splits) * per_split > workspace_bytes) --splits;
+  }
+  pl.splits = splits;
+  pl.workspace_bytes = splits > 1 ? static_cast<size_t>(splits) * seq_len * num_heads *
+                                        (head_dim + 2) * sizeof(float)
+                                  : 0;
+  return pl;
+}
+
+cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
+                             int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                             int head_dim, float scale, int n_sink, int window, int dtype,
+                             void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (seq_len <= 0) return cudaSuccess;
+  const AttnPlan pl = plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim,
+                                     n_sink, window, workspace ? workspace_bytes : 0);
+  if (pl.row_blocks > 0x7fffffffLL || num_kv_heads > 65535) return cudaErrorInvalidConfiguration;
+  AttnParams p;
+  p.out = out;
+  p.q = q;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.ws = static_cast<float*>(workspace);
+  p.seq_len = seq_len;
+  p.cache_len = cache_len;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.n_sink = n_sink;
+  p.window = window;
+  p.scale = scale;
+  p.group = num_heads / num_kv_heads;
+  p.hpb = pl.hpb;
+  p.tpb = pl.tpb;
+  p.hsb = pl.hsb;
+  p.splits = pl.splits;
+  const int rb = static_cast<int>(pl.row_blocks);
+  if (dtype == DT_F16)
+    return head_dim == 64 ? attn_dispatch<DT_F16, 64>(p, pl.rw, rb, s)
+                          : attn_dispatch<DT_F16, 128>(p, pl.rw, rb, s);
+  return head_dim == 64 ? attn_dispatch<DT_BF16, 64>(p, pl.rw, rb, s)
+                        : attn_dispatch<DT_BF16, 128>(p, pl.rw, rb, s);
+}
+
+cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
+                              int seq_len, int start_pos, int n_sink, int window, int kv_dim,
+                              cudaStream_t s) {
+  if (seq_len <= 0) return cudaSuccess;
+  const bool vec = kv_dim % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
+                     reinterpret_cast<uintptr_t>(k_src) | reinterpret_cast<uintptr_t>(v_src)) &
+                    15) == 0;
+  return launch_ex(kv_scatter_kernel, dim3(seq_len), dim3(128), 0, s,
+                   static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool),
+                   static_cast<const uint16_t*>(k_src), static_cast<const uint16_t*>(v_src),
+                   seq_len, start_pos, n_sink, window, kv_dim, vec ? 1 : 0);
+}
+
+}  // namespace orin

@@ -84,6 +84,25 @@ cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM
 cudaError_t launch_finish_rows(void* C, const float* S, const void* R, long long n, int dtype,
                                cudaStream_t s);
 
+// Sink + sliding-window GQA attention over the ring KV pool and the K/V
+// scatter into it (csrc/attention.cu).  head_dim 64 or 128.
+struct AttnPlan {
+  int rw;                  // warps stacked on rows (1: decode blocks, 4: prefill)
+  int hpb, tpb, hsb;       // group heads / tokens per row block; row blocks per group
+  int splits;              // key splits across CTAs (1: no workspace used)
+  long long row_blocks;
+  size_t workspace_bytes;  // what `splits` needs
+};
+AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                        int head_dim, int n_sink, int window, size_t workspace_bytes);
+cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
+                             int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                             int head_dim, float scale, int n_sink, int window, int dtype,
+                             void* workspace, size_t workspace_bytes, cudaStream_t s);
+cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
+                              int seq_len, int start_pos, int n_sink, int window, int kv_dim,
+                              cudaStream_t s);
+
 // Row-parallel reduction over peer memory (csrc/tp_p2p.cu).  Each rank's
 // shared region starts with a flag block of ints written by the peers, one
 // per (block, rank): "partial ready" at kP2PArrive + b * kP2PMaxRanks + rank,

@@ -1,9 +1,14 @@
-// shim.cu — the reference's C++ GEMM entry points (include/kernels.h:51-108,
-// kernels/gemm_cute.cu:295-324) implemented on the C ABI, so a program built
-// against the reference's headers links this library unchanged.  Everything
-// runs on the legacy default stream in bf16, as in the reference.
+// shim.cu — the reference's C++ entry points of the linear-layer path and of
+// its attention (include/kernels.h:51-108, kernels/gemm_cute.cu:295-324)
+// implemented on the C ABI, so a program built against the reference's headers
+// links this library unchanged.  Everything runs on the legacy default stream
+// in bf16, as in the reference.
 #include "orin_b200.h"
 #include "orin_kernels.h"
+
+namespace {
+__device__ __align__(16) float g_attn_workspace[1 << 20];
+}  // namespace
 
 namespace kernels {
 
@@ -24,6 +29,18 @@ void add(__nv_bfloat16* x, const __nv_bfloat16* y, int n) {
 
 void bf16_to_fp32(float* out, const __nv_bfloat16* in, int n) {
   orin_widen_f32(out, in, n, ORIN_BF16, nullptr);
+}
+
+void attention(__nv_bfloat16* out, const __nv_bfloat16* q, const __nv_bfloat16* k_pool,
+               const __nv_bfloat16* v_pool, int seq_len, int cache_len, int num_heads,
+               int num_kv_heads, int head_dim, float scale, int n_sink, int window_size) {
+  // the split-key partials of few-token calls go to a static device array
+  // (calls are ordered on the default stream, as in the reference)
+  void* ws = nullptr;
+  if (cudaGetSymbolAddress(&ws, g_attn_workspace) != cudaSuccess) ws = nullptr;
+  orin_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads, num_kv_heads, head_dim,
+                 scale, n_sink, window_size, ORIN_BF16, ws, ws ? sizeof(g_attn_workspace) : 0,
+                 nullptr);
 }
 
 }  // namespace kernels

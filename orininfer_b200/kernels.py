@@ -11,7 +11,11 @@ streams), each a direct call into liborin_b200.so:
     bf16_to_fp32(out, inp, n)                  kernels::bf16_to_fp32
 
 plus the fused entry points that replace the reference's call pairs in
-src/model.cu (``linear`` with an epilogue) and the gate/up packer.  fp16 and
+src/model.cu (``linear`` with an epilogue), the gate/up packer, and the
+attention between the q/k/v and o projections:
+
+    attention(out, q, k_pool, v_pool, ...)     kernels::attention
+    kv_append(k_pool, v_pool, k, v, ...)       KVCache::append_kv (pools explicit)  fp16 and
 bf16 are both accepted; the reference itself is bf16-only.
 
 Errors raise ``OrinError`` (the library's status and message).  There is no
@@ -45,7 +49,8 @@ _ALGOS = {
 
 __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
-    "pack_gate_up", "device_check", "plan_info", "lm_head_argmax",
+    "pack_gate_up", "device_check", "plan_info", "lm_head_argmax", "attention",
+    "attention_workspace_bytes", "kv_append",
 ]
 
 
@@ -161,6 +166,61 @@ def lm_head_argmax(h: torch.Tensor, w: torch.Tensor, *, keys: Optional[torch.Ten
     check(_lib.lib.orin_lm_head_argmax(_ptr(out), _ptr(h), _ptr(w), M, V, K, _dtype_code(h),
                                        _ptr(keys), _stream(stream)))
     return out
+
+
+def kv_append(k_pool: torch.Tensor, v_pool: torch.Tensor, k_src: torch.Tensor,
+              v_src: torch.Tensor, seq_len: int, start_pos: int, n_sink: int,
+              window_size: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """KVCache::append_kv with the pools passed explicitly (orin_kv_append):
+    rows [seq_len, kv_dim] of positions start_pos.. into pool slots
+    p (p < n_sink) or n_sink + (p - n_sink) % window_size
+    (src/kv_cache.cu:21-41, 95-111)."""
+    _need_cuda(k_pool, v_pool, k_src, v_src)
+    if len({k_pool.dtype, v_pool.dtype, k_src.dtype, v_src.dtype}) != 1:
+        raise ValueError("pools and sources must share one dtype")
+    kv_dim = k_src.numel() // max(seq_len, 1)
+    check(_lib.lib.orin_kv_append(_ptr(k_pool), _ptr(v_pool), _ptr(k_src), _ptr(v_src), seq_len,
+                                  start_pos, n_sink, window_size, kv_dim, _dtype_code(k_src),
+                                  _stream(stream)))
+
+
+def attention_workspace_bytes(seq_len: int, cache_len: int, num_heads: int, num_kv_heads: int,
+                              head_dim: int, n_sink: int, window_size: int) -> int:
+    """Device workspace that lets orin_attention split every few-token call."""
+    n = ctypes.c_size_t(0)
+    check(_lib.lib.orin_attention_workspace_bytes(ctypes.byref(n), seq_len, cache_len, num_heads,
+                                                  num_kv_heads, head_dim, n_sink, window_size))
+    return int(n.value)
+
+
+def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+              seq_len: int, cache_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+              scale: float, n_sink: int, window_size: int, *,
+              workspace: Optional[torch.Tensor] = None, split: bool = True,
+              stream: Optional[torch.cuda.Stream] = None) -> None:
+    """kernels::attention (include/kernels.h:58-80, kernels/attention.cu:27-175):
+    sink + sliding-window GQA attention of q [seq_len, num_heads, head_dim]
+    over the ring pools [n_sink + window_size, num_kv_heads, head_dim] into
+    out.  With split (the default) few-token calls split their keys across
+    CTAs through `workspace` (allocated here when not given)."""
+    _need_cuda(out, q, k_pool, v_pool, workspace)
+    if len({out.dtype, q.dtype, k_pool.dtype, v_pool.dtype}) != 1:
+        raise ValueError("out, q and the pools must share one dtype")
+    ws_bytes = 0
+    if split:
+        if workspace is None:
+            need = attention_workspace_bytes(seq_len, cache_len, num_heads, num_kv_heads,
+                                             head_dim, n_sink, window_size)
+            if need:
+                workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        if workspace is not None:
+            ws_bytes = workspace.numel() * workspace.element_size()
+    else:
+        workspace = None
+    check(_lib.lib.orin_attention(_ptr(out), _ptr(q), _ptr(k_pool), _ptr(v_pool), seq_len,
+                                  cache_len, num_heads, num_kv_heads, head_dim, float(scale),
+                                  n_sink, window_size, _dtype_code(q), _ptr(workspace), ws_bytes,
+                                  _stream(stream)))
 
 
 def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,

@@ -29,7 +29,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_library_exports_reference_cxx_entry_points():
     hdr = open(os.path.join(ROOT, "include", "orin_kernels.h")).read()
-    for name in ("matmul", "fused_silu_mul", "add", "bf16_to_fp32", "launch_gemm_cute"):
+    for name in ("matmul", "fused_silu_mul", "add", "bf16_to_fp32", "launch_gemm_cute",
+                 "attention"):
         assert re.search(rf"\b{name}\s*\(", hdr)
     for name, sym in _lib.SHIM_SYMBOLS.items():
         assert hasattr(_lib.lib, sym), f"{name} ({sym}) not exported"
@@ -118,3 +119,41 @@ def test_python_mirror_rejects_cpu_tensors():
         K.linear(x, w)
     with pytest.raises(ValueError):
         K.matmul(torch.zeros(4, 128, dtype=torch.float16), x, w, 4, 128, 64)
+
+
+def test_attention_and_kv_append_reject_bad_arguments_on_host():
+    L = _lib.lib
+    f = ctypes.c_float(0.125)
+    ok = dict(out=16, q=16, k=16, v=16, S=1, C=10, nh=32, nkv=4, hd=64, ns=4, W=1024, dt=0)
+
+    def att(**kw):
+        a = dict(ok, **kw)
+        return L.orin_attention(a["out"], a["q"], a["k"], a["v"], a["S"], a["C"], a["nh"],
+                                a["nkv"], a["hd"], f, a["ns"], a["W"], a["dt"], None, 0, None)
+
+    assert att(nkv=5) == _lib.ERR_INVALID_ARG        # heads not a multiple of kv heads
+    assert att(C=0) == _lib.ERR_INVALID_ARG          # cache_len < seq_len
+    assert att(W=0) == _lib.ERR_INVALID_ARG
+    assert att(ns=-1) == _lib.ERR_INVALID_ARG
+    assert att(dt=3) == _lib.ERR_INVALID_ARG
+    assert att(q=0) == _lib.ERR_INVALID_ARG
+    assert att(hd=96) == _lib.ERR_UNSUPPORTED
+    assert att(k=24) == _lib.ERR_UNSUPPORTED         # pool not 16-byte aligned
+    assert att(S=0, C=0, out=0) == _lib.OK           # nothing to do
+    assert L.orin_kv_append(16, 16, 16, 16, 1029, 0, 4, 1024, 256, 0, None) == \
+        _lib.ERR_INVALID_ARG                          # seq_len > n_sink + window (reference throws)
+    assert L.orin_kv_append(0, 16, 16, 16, 4, 0, 4, 1024, 256, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_kv_append(16, 16, 16, 16, 4, -1, 4, 1024, 256, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_kv_append(16, 16, 16, 16, 0, 0, 4, 1024, 256, 0, None) == _lib.OK
+
+
+def test_attention_workspace_plan():
+    """Few-token calls split their keys across CTAs; prefill-sized calls don't.
+    The split count for TinyLlama decode (32 heads over 4 KV heads, window
+    1024 + 4 sinks) is one per 64-key tile: 17."""
+    ws = K.attention_workspace_bytes
+    assert ws(1, 2048, 32, 4, 64, 4, 1024) == 17 * 32 * (64 + 2) * 4
+    assert ws(1, 3, 32, 4, 64, 4, 1024) == 0            # one key tile: nothing to split
+    assert ws(1028, 1028, 32, 4, 64, 4, 1024) == 0      # 516 CTAs without splitting
+    assert ws(1, 3000, 32, 8, 128, 4, 1024) == 17 * 32 * (128 + 2) * 4
+    assert ws(0, 0, 32, 4, 64, 4, 1024) == 0
