@@ -157,6 +157,45 @@ orin_status orin_add(void* x, const void* y, long long n, int dtype,
 orin_status orin_widen_f32(float* out, const void* in, long long n, int dtype,
                            void* stream);
 
+/* out[t, :] = table[token_ids[t], :] (16-bit rows of hidden elements; token_ids
+ * int32 on the device).  An id outside [0, vocab_size) gives a zero row.
+ * Replaces kernels::embedding (include/kernels.h:12-19, kernels/embedding.cu:4-21). */
+orin_status orin_embedding(void* out, const void* table, const int* token_ids,
+                           int seq_len, int hidden, int vocab_size, void* stream);
+
+/* out = round16(x * r * w) per row of dim elements, r = rsqrtf(sum(x^2)/dim + eps),
+ * fp32.  out may alias x.  Replaces kernels::rmsnorm (include/kernels.h:22-31,
+ * kernels/rmsnorm.cu:7-41). */
+orin_status orin_rmsnorm(void* out, const void* x, const void* weight, int rows,
+                         int dim, float eps, int dtype, void* stream);
+
+/* Rotary embedding in place on q [seq_len][num_heads][head_dim] and
+ * k [seq_len][num_kv_heads][head_dim]: pairs (i, i + head_dim/2) of each head
+ * at position start_pos + t rotate by (start_pos + t) * powf(theta,
+ * -2i/head_dim), each result rounded to 16 bits.  Replaces kernels::rope
+ * (include/kernels.h:33-45, kernels/rope.cu:7-60). */
+orin_status orin_rope(void* q, void* k, int seq_len, int num_heads,
+                      int num_kv_heads, int head_dim, int start_pos, float theta,
+                      int dtype, void* stream);
+
+/*
+ * The steps between this library's fused q/k/v projection and the attention,
+ * in one launch.  qkv: token rows [q (num_heads*head_dim) | k | v
+ * (num_kv_heads*head_dim each)], as orin_linear writes them with the q, k and
+ * v weights stacked.  Per head: the optional RMSNorm with q_norm / k_norm
+ * [head_dim] (Qwen3, src/model.cu:64-67; both NULL for Llama), the rotation of
+ * orin_rope, then q -> q_out [seq_len][num_heads][head_dim] and k, v into their
+ * ring slots as orin_kv_append places them (src/model.cu:70-73).  Rounding
+ * points are the reference's (normed value, then each rotated value).
+ * head_dim 64 or 128.
+ */
+orin_status orin_qkv_rope_append(void* q_out, const void* qkv, const void* q_norm,
+                                 const void* k_norm, void* k_pool, void* v_pool,
+                                 int seq_len, int start_pos, int num_heads,
+                                 int num_kv_heads, int head_dim, float eps,
+                                 float theta, int n_sink, int window_size,
+                                 int dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sink + sliding-window GQA attention over the ring KV pool (the callers of */
 /* the linear layers on either side: q/k/v come from the q/k/v projection,   */

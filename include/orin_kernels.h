@@ -1,9 +1,11 @@
 /*
- * orin_kernels.h — C++ link-compatible replacements for the reference's GEMM
- * entry points, implemented by liborin_b200.so on top of the C ABI in
- * orin_b200.h.  A program compiled against the reference's include/kernels.h
- * links these instead of kernels/matmul.cu, kernels/fused_swiglu.cu and the
- * add / bf16_to_fp32 part of kernels/softmax.cu.
+ * orin_kernels.h — C++ link-compatible replacements for the reference's
+ * entry points of the linear-layer path and of the attention around it,
+ * implemented by liborin_b200.so on top of the C ABI in orin_b200.h.  A
+ * program compiled against the reference's include/kernels.h links these
+ * instead of kernels/matmul.cu, kernels/fused_swiglu.cu, kernels/embedding.cu,
+ * kernels/rmsnorm.cu, kernels/rope.cu, kernels/attention.cu and the add /
+ * bf16_to_fp32 part of kernels/softmax.cu.
  *
  * Like the originals they take raw bf16 device pointers, run on the legacy
  * default stream and return nothing.  A failure is recorded (read it with
@@ -13,6 +15,7 @@
 #define ORIN_KERNELS_H
 
 #include <cuda_bf16.h>
+#include <stdint.h>
 
 namespace kernels {
 
@@ -34,6 +37,21 @@ void add(__nv_bfloat16* x, const __nv_bfloat16* y, int n);
 /* out = float(in).  Reference: include/kernels.h:104-108,
  * kernels/softmax.cu:117-120. */
 void bf16_to_fp32(float* out, const __nv_bfloat16* in, int n);
+
+/* out[t] = table[token_ids[t]] (orin_embedding).  Reference:
+ * include/kernels.h:12-19, kernels/embedding.cu:14-21. */
+void embedding(__nv_bfloat16* out, const __nv_bfloat16* table,
+               const int32_t* token_ids, int seq_len, int hidden_size);
+
+/* out = rmsnorm(x) per row (orin_rmsnorm).  Reference: include/kernels.h:22-31,
+ * kernels/rmsnorm.cu:7-41. */
+void rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x,
+             const __nv_bfloat16* weight, int seq_len, int dim, float eps);
+
+/* Rotary embedding in place on q and k (orin_rope).  Reference:
+ * include/kernels.h:33-45, kernels/rope.cu:7-60. */
+void rope(__nv_bfloat16* q, __nv_bfloat16* k, int seq_len, int num_heads,
+          int num_kv_heads, int head_dim, int start_pos, float theta);
 
 /* Sink + sliding-window GQA attention over the ring KV pool (orin_attention).
  * Reference: include/kernels.h:58-80, kernels/attention.cu:140-175.  Split-key

@@ -288,6 +288,75 @@ def attention_literal(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, seq
     return round16(out, dt)
 
 
+def rmsnorm(x: np.ndarray, w: np.ndarray, dt: int, eps: float) -> np.ndarray:
+    """kernels/rmsnorm.cu:7-34 per row of the last axis: r = rsqrt(sum(x^2) / dim
+    + eps) in fp32 (the sum in float64 here), out = round16(x * r * w) in fp32."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    xf = widen(x, dt)
+    wf = widen(np.ascontiguousarray(w, dtype=np.uint16), dt)
+    dim = x.shape[-1]
+    ss = (xf.astype(np.float64) ** 2).sum(axis=-1).astype(np.float32)
+    r = (np.float32(1.0) / np.sqrt(ss / np.float32(dim) + np.float32(eps))).astype(np.float32)
+    return round16((xf * r[..., None]) * wf, dt)
+
+
+def rope(x: np.ndarray, start_pos: int, theta: float, dt: int) -> np.ndarray:
+    """kernels/rope.cu:7-37 on x [seq, heads, head_dim] (bits): pair (i, i + hd/2)
+    of token t rotates by (start_pos + t) * theta^(-2i/hd), fp32 angle, each
+    result rounded to 16 bits."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    seq, heads, hd = x.shape
+    half = hd // 2
+    xf = widen(x, dt)
+    i = np.arange(half, dtype=np.float32)
+    inv = np.power(np.float32(theta), (np.float32(-2.0) * i) / np.float32(hd)).astype(np.float32)
+    pos = (start_pos + np.arange(seq)).astype(np.float32)
+    ang = (pos[:, None] * inv[None, :]).astype(np.float32)
+    c = np.cos(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    sn = np.sin(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    x0, x1 = xf[..., :half], xf[..., half:]
+    out = np.empty_like(x)
+    out[..., :half] = round16(x0 * c - x1 * sn, dt)
+    out[..., half:] = round16(x0 * sn + x1 * c, dt)
+    return out
+
+
+def transformer_layer(x: np.ndarray, L: dict, k_pool: np.ndarray, v_pool: np.ndarray,
+                      start_pos: int, cfg: dict, dt: int) -> np.ndarray:
+    """Model::transformer_layer (src/model.cu:37-111) on seq_len = len(x) tokens:
+    x [seq, H] bits -> new x; the pools [n_sink + W, kv_dim] bits are appended
+    in place.  L holds bits of input_layernorm, q/k/v/o_proj, post_attention_layernorm,
+    gate/up/down_proj and, for Qwen3, q_norm / k_norm (absent: Llama, no
+    q/k norm).  cfg: num_attention_heads, num_key_value_heads, head_dim,
+    rms_norm_eps, rope_theta, n_sink, window."""
+    nh, nkv, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    eps, theta = cfg["rms_norm_eps"], cfg["rope_theta"]
+    ns, W = cfg["n_sink"], cfg["window"]
+    seq = x.shape[0]
+    xn = rmsnorm(x, L["input_layernorm"], dt, eps)                        # :53
+    q = linear(xn, L["q_proj"], dt)                                       # :59-61
+    k = linear(xn, L["k_proj"], dt)
+    v = linear(xn, L["v_proj"], dt)
+    if L.get("q_norm") is not None:                                       # :64-67
+        q = rmsnorm(q.reshape(-1, hd), L["q_norm"], dt, eps)
+        k = rmsnorm(k.reshape(-1, hd), L["k_norm"], dt, eps)
+    q = rope(q.reshape(seq, nh, hd), start_pos, theta, dt)                # :70-73
+    k = rope(k.reshape(seq, nkv, hd), start_pos, theta, dt)
+    kv_append(k_pool, v_pool, k.reshape(seq, nkv * hd), v.reshape(seq, nkv * hd),
+              start_pos, ns, W)                                           # :75
+    att = attention(q, k_pool.reshape(-1, nkv, hd), v_pool.reshape(-1, nkv, hd), seq,
+                    start_pos + seq, nh, nkv, hd, float(np.float32(1.0) / np.sqrt(np.float32(hd))),
+                    ns, W, dt)                                            # :79-84
+    o = linear(att.reshape(seq, nh * hd), L["o_proj"], dt)                # :87
+    x = add(x, o, dt)                                                     # :90
+    xn = rmsnorm(x, L["post_attention_layernorm"], dt, eps)               # :95
+    g = linear(xn, L["gate_proj"], dt)                                    # :100-101
+    u = linear(xn, L["up_proj"], dt)
+    h = silu_mul(g, u, dt)                                                # :104
+    d = linear(h, L["down_proj"], dt)                                     # :107
+    return add(x, d, dt)                                                  # :110
+
+
 class RefKernels:
     """The reference's own bf16 kernels (built from its sources; GPU only).
 
@@ -297,7 +366,7 @@ class RefKernels:
         path = REF_CUTE if cute else REF_CUBLAS
         if not path.exists():
             raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
-        self.lib = ctypes.CDLL(os.fspath(path))
+        self.lib = ctypes.CDLL(os.fspath(path), mode=os.RTLD_LOCAL | os.RTLD_NOW)
         L = self.lib
         L.ref_matmul.argtypes = [_vp, _vp, _vp, _i, _i, _i]
         L.ref_gemm_cute.argtypes = [_vp, _vp, _vp, _i, _i, _i]
@@ -306,8 +375,12 @@ class RefKernels:
         L.ref_bf16_to_fp32.argtypes = [_vp, _vp, _i]
         L.ref_attention.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float,
                                     _i, _i]
+        L.ref_rmsnorm.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_float]
+        L.ref_rope.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float]
+        L.ref_embedding.argtypes = [_vp, _vp, _vp, _i, _i]
         for n in ("ref_matmul", "ref_gemm_cute", "ref_fused_silu_mul", "ref_add",
-                  "ref_bf16_to_fp32", "ref_attention", "ref_sync"):
+                  "ref_bf16_to_fp32", "ref_attention", "ref_rmsnorm", "ref_rope",
+                  "ref_embedding", "ref_sync"):
             getattr(L, n).restype = _i
 
     def _ok(self, rc: int, what: str) -> None:
@@ -335,6 +408,17 @@ class RefKernels:
         self._ok(self.lib.ref_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
                                         num_kv_heads, head_dim, scale, n_sink, window),
                  "kernels::attention")
+
+    def rmsnorm(self, out: int, x: int, w: int, rows: int, dim: int, eps: float) -> None:
+        self._ok(self.lib.ref_rmsnorm(out, x, w, rows, dim, eps), "kernels::rmsnorm")
+
+    def rope(self, q: int, k: int, seq_len: int, num_heads: int, num_kv_heads: int,
+             head_dim: int, start_pos: int, theta: float) -> None:
+        self._ok(self.lib.ref_rope(q, k, seq_len, num_heads, num_kv_heads, head_dim, start_pos,
+                                   theta), "kernels::rope")
+
+    def embedding(self, out: int, table: int, ids: int, seq_len: int, hidden: int) -> None:
+        self._ok(self.lib.ref_embedding(out, table, ids, seq_len, hidden), "kernels::embedding")
 
     def sync(self) -> None:
         self._ok(self.lib.ref_sync(), "cudaDeviceSynchronize")

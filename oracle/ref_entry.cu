@@ -2,8 +2,8 @@
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
 // the reference's unmodified sources (kernels/matmul.cu, kernels/gemm_cute.cu,
-// kernels/fused_swiglu.cu, kernels/softmax.cu, kernels/attention.cu) into
-// oracle/_ref/.  The tests
+// kernels/fused_swiglu.cu, kernels/softmax.cu, kernels/attention.cu,
+// kernels/rmsnorm.cu, kernels/rope.cu, kernels/embedding.cu) into oracle/_ref/.  The tests
 // use it to pin the CPU oracle to what the reference computes; nothing in the
 // product links it.
 #include <cuda_runtime.h>
@@ -56,6 +56,25 @@ int ref_attention(void* out, const void* q, const void* k_pool, const void* v_po
                      static_cast<const __nv_bfloat16*>(k_pool),
                      static_cast<const __nv_bfloat16*>(v_pool), seq_len, cache_len, num_heads,
                      num_kv_heads, head_dim, scale, n_sink, window_size);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int ref_rmsnorm(void* out, const void* x, const void* w, int rows, int dim, float eps) {
+  kernels::rmsnorm(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(x),
+                   static_cast<const __nv_bfloat16*>(w), rows, dim, eps);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int ref_rope(void* q, void* k, int seq_len, int num_heads, int num_kv_heads, int head_dim,
+             int start_pos, float theta) {
+  kernels::rope(static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), seq_len,
+                num_heads, num_kv_heads, head_dim, start_pos, theta);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int ref_embedding(void* out, const void* table, const int* ids, int seq_len, int hidden) {
+  kernels::embedding(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(table),
+                     ids, seq_len, hidden);
   return static_cast<int>(cudaGetLastError());
 }
 

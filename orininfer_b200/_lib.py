@@ -64,6 +64,11 @@ SIGNATURES = {
     "orin_add": (_i, [_vp, _vp, _ll, _i, _vp]),
     "orin_widen_f32": (_i, [_vp, _vp, _ll, _i, _vp]),
     "orin_kv_append": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "orin_embedding": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "orin_rmsnorm": (_i, [_vp, _vp, _vp, _i, _i, ctypes.c_float, _i, _vp]),
+    "orin_rope": (_i, [_vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _vp]),
+    "orin_qkv_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                  ctypes.c_float, ctypes.c_float, _i, _i, _i, _vp]),
     "orin_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _i, _i,
                             _vp, _sz, _vp]),
     "orin_attention_workspace_bytes": (_i, [ctypes.POINTER(_sz), _i, _i, _i, _i, _i, _i, _i]),
@@ -89,6 +94,9 @@ SHIM_SYMBOLS = {
     "kernels::bf16_to_fp32": "_ZN7kernels12bf16_to_fp32EPfPK13__nv_bfloat16i",
     "launch_gemm_cute": "_Z16launch_gemm_cuteP13__nv_bfloat16PKS_S2_iii",
     "kernels::attention": "_ZN7kernels9attentionEP13__nv_bfloat16PKS0_S3_S3_iiiiifii",
+    "kernels::rmsnorm": "_ZN7kernels7rmsnormEP13__nv_bfloat16PKS0_S3_iif",
+    "kernels::embedding": "_ZN7kernels9embeddingEP13__nv_bfloat16PKS0_PKiii",
+    "kernels::rope": "_ZN7kernels4ropeEP13__nv_bfloat16S1_iiiiif",
 }
 
 
@@ -105,7 +113,9 @@ def _load() -> ctypes.CDLL:
         raise ImportError(
             f"{LIB_PATH} is missing: build it with `python -m orininfer_b200.build` "
             "(there is no CPU fallback)")
-    lib = ctypes.CDLL(os.fspath(LIB_PATH), mode=ctypes.RTLD_GLOBAL)
+    # RTLD_LOCAL: the library's C++ drop-in symbols (kernels::matmul, ...) must
+    # not become the global definitions other libraries in this process bind to
+    lib = ctypes.CDLL(os.fspath(LIB_PATH), mode=os.RTLD_LOCAL | os.RTLD_NOW)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = res
@@ -117,6 +127,9 @@ def _load() -> ctypes.CDLL:
         "kernels::bf16_to_fp32": [_vp, _vp, _i],
         "launch_gemm_cute": [_vp, _vp, _vp, _i, _i, _i],
         "kernels::attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _i],
+        "kernels::rmsnorm": [_vp, _vp, _vp, _i, _i, ctypes.c_float],
+        "kernels::embedding": [_vp, _vp, _vp, _i, _i],
+        "kernels::rope": [_vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float],
     }
     for name, sym in SHIM_SYMBOLS.items():
         fn = getattr(lib, sym)

@@ -403,6 +403,82 @@ orin_status orin_kv_append(void* k_pool, void* v_pool, const void* k_src, const 
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_kv_append");
 }
 
+orin_status orin_embedding(void* out, const void* table, const int* token_ids, int seq_len,
+                           int hidden, int vocab_size, void* stream) {
+  if (seq_len < 0 || hidden < 1 || vocab_size < 1 ||
+      (seq_len > 0 && (!out || !table || !token_ids))) {
+    set_error("orin_embedding: null pointer or bad size (seq_len=%d hidden=%d vocab=%d)", seq_len,
+              hidden, vocab_size);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_embedding(out, table, token_ids, seq_len, hidden, vocab_size,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_embedding");
+}
+
+orin_status orin_rmsnorm(void* out, const void* x, const void* weight, int rows, int dim,
+                         float eps, int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (rows < 0 || dim < 1 || (rows > 0 && (!out || !x || !weight))) {
+    set_error("orin_rmsnorm: null pointer or bad size (rows=%d dim=%d)", rows, dim);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_rmsnorm(out, x, weight, rows, dim, eps, dtype,
+                                 static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_rmsnorm");
+}
+
+orin_status orin_rope(void* q, void* k, int seq_len, int num_heads, int num_kv_heads,
+                      int head_dim, int start_pos, float theta, int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (seq_len < 0 || num_heads < 1 || num_kv_heads < 0 || head_dim < 2 || head_dim % 2 != 0 ||
+      start_pos < 0 || (seq_len > 0 && (!q || (num_kv_heads > 0 && !k)))) {
+    set_error("orin_rope: null pointer or bad size (seq_len=%d heads=%d/%d head_dim=%d "
+              "start_pos=%d)",
+              seq_len, num_heads, num_kv_heads, head_dim, start_pos);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  cudaError_t e = launch_rope(q, k, seq_len, num_heads, num_kv_heads, head_dim, start_pos, theta,
+                              dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_rope");
+}
+
+orin_status orin_qkv_rope_append(void* q_out, const void* qkv, const void* q_norm,
+                                 const void* k_norm, void* k_pool, void* v_pool, int seq_len,
+                                 int start_pos, int num_heads, int num_kv_heads, int head_dim,
+                                 float eps, float theta, int n_sink, int window_size, int dtype,
+                                 void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (seq_len < 0 || start_pos < 0 || num_heads < 1 || num_kv_heads < 1 ||
+      num_heads % num_kv_heads != 0 || n_sink < 0 || window_size < 1 ||
+      (seq_len > 0 && (!q_out || !qkv || !k_pool || !v_pool)) ||
+      (q_norm == nullptr) != (k_norm == nullptr)) {
+    set_error("orin_qkv_rope_append: null pointer or bad size (seq_len=%d start_pos=%d "
+              "heads=%d/%d n_sink=%d window=%d; q_norm and k_norm both or neither)",
+              seq_len, start_pos, num_heads, num_kv_heads, n_sink, window_size);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (static_cast<long long>(seq_len) > static_cast<long long>(n_sink) + window_size ||
+      static_cast<long long>(start_pos) + seq_len > 0x7fffffffLL) {
+    set_error("orin_qkv_rope_append: seq_len %d exceeds n_sink + window_size, or positions "
+              "past 2^31",
+              seq_len);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (head_dim != 64 && head_dim != 128) {
+    set_error("orin_qkv_rope_append: head_dim %d (64 and 128 are built)", head_dim);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_qkv_rope_append(q_out, qkv, q_norm, k_norm, k_pool, v_pool, seq_len,
+                                         start_pos, num_heads, num_kv_heads, head_dim, eps, theta,
+                                         n_sink, window_size, dtype,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_qkv_rope_append");
+}
+
 orin_status orin_device_check(void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(s);

@@ -103,6 +103,20 @@ cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, con
                               int seq_len, int start_pos, int n_sink, int window, int kv_dim,
                               cudaStream_t s);
 
+// RMSNorm over rows, rotary embedding, and the fused per-head norm + rotation
+// + K/V scatter that follows this library's q/k/v projection (csrc/norm_rope.cu).
+cudaError_t launch_embedding(void* out, const void* table, const int* ids, int seq_len,
+                             int hidden, int vocab, cudaStream_t s);
+cudaError_t launch_rmsnorm(void* out, const void* x, const void* w, int rows, int dim, float eps,
+                           int dtype, cudaStream_t s);
+cudaError_t launch_rope(void* q, void* k, int seq_len, int num_heads, int num_kv_heads,
+                        int head_dim, int start_pos, float theta, int dtype, cudaStream_t s);
+cudaError_t launch_qkv_rope_append(void* q_out, const void* qkv, const void* q_norm,
+                                   const void* k_norm, void* k_pool, void* v_pool, int seq_len,
+                                   int start_pos, int num_heads, int num_kv_heads, int head_dim,
+                                   float eps, float theta, int n_sink, int window, int dtype,
+                                   cudaStream_t s);
+
 // Row-parallel reduction over peer memory (csrc/tp_p2p.cu).  Each rank's
 // shared region starts with a flag block of ints written by the peers, one
 // per (block, rank): "partial ready" at kP2PArrive + b * kP2PMaxRanks + rank,

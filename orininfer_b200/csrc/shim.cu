@@ -31,6 +31,23 @@ void bf16_to_fp32(float* out, const __nv_bfloat16* in, int n) {
   orin_widen_f32(out, in, n, ORIN_BF16, nullptr);
 }
 
+void embedding(__nv_bfloat16* out, const __nv_bfloat16* table, const int32_t* token_ids,
+               int seq_len, int hidden_size) {
+  // the reference passes no vocabulary size: ids are trusted, as there
+  orin_embedding(out, table, token_ids, seq_len, hidden_size, 0x7fffffff, nullptr);
+}
+
+void rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* weight,
+             int seq_len, int dim, float eps) {
+  orin_rmsnorm(out, x, weight, seq_len, dim, eps, ORIN_BF16, nullptr);
+}
+
+void rope(__nv_bfloat16* q, __nv_bfloat16* k, int seq_len, int num_heads, int num_kv_heads,
+          int head_dim, int start_pos, float theta) {
+  orin_rope(q, k, seq_len, num_heads, num_kv_heads, head_dim, start_pos, theta, ORIN_BF16,
+            nullptr);
+}
+
 void attention(__nv_bfloat16* out, const __nv_bfloat16* q, const __nv_bfloat16* k_pool,
                const __nv_bfloat16* v_pool, int seq_len, int cache_len, int num_heads,
                int num_kv_heads, int head_dim, float scale, int n_sink, int window_size) {

@@ -15,7 +15,11 @@ src/model.cu (``linear`` with an epilogue), the gate/up packer, and the
 attention between the q/k/v and o projections:
 
     attention(out, q, k_pool, v_pool, ...)     kernels::attention
-    kv_append(k_pool, v_pool, k, v, ...)       KVCache::append_kv (pools explicit)  fp16 and
+    kv_append(k_pool, v_pool, k, v, ...)       KVCache::append_kv (pools explicit)
+    embedding(out, table, ids, seq, hidden)    kernels::embedding
+    rmsnorm(out, x, w, seq, dim, eps)          kernels::rmsnorm
+    rope(q, k, seq, heads, kv_heads, ...)      kernels::rope
+    qkv_rope_append(q_out, qkv, pools, ...)    q/k norm + rope + append in one launch  fp16 and
 bf16 are both accepted; the reference itself is bf16-only.
 
 Errors raise ``OrinError`` (the library's status and message).  There is no
@@ -50,7 +54,8 @@ _ALGOS = {
 __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
     "pack_gate_up", "device_check", "plan_info", "lm_head_argmax", "attention",
-    "attention_workspace_bytes", "kv_append",
+    "attention_workspace_bytes", "kv_append", "rmsnorm", "rope", "qkv_rope_append",
+    "embedding",
 ]
 
 
@@ -166,6 +171,53 @@ def lm_head_argmax(h: torch.Tensor, w: torch.Tensor, *, keys: Optional[torch.Ten
     check(_lib.lib.orin_lm_head_argmax(_ptr(out), _ptr(h), _ptr(w), M, V, K, _dtype_code(h),
                                        _ptr(keys), _stream(stream)))
     return out
+
+
+def embedding(out: torch.Tensor, table: torch.Tensor, token_ids: torch.Tensor, seq_len: int,
+              hidden_size: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """kernels::embedding (include/kernels.h:12-19): out[t] = table[token_ids[t]]
+    (int32 ids; an id outside the table gives a zero row)."""
+    _need_cuda(out, table, token_ids)
+    if token_ids.dtype != torch.int32:
+        raise ValueError("token_ids must be int32")
+    check(_lib.lib.orin_embedding(_ptr(out), _ptr(table), _ptr(token_ids), seq_len, hidden_size,
+                                  table.shape[0], _stream(stream)))
+
+
+def rmsnorm(out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, seq_len: int, dim: int,
+            eps: float, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """kernels::rmsnorm (include/kernels.h:22-31): out = round16(x * r * w) per
+    row, r = rsqrt(mean(x^2) + eps) (orin_rmsnorm)."""
+    _need_cuda(out, x, weight)
+    check(_lib.lib.orin_rmsnorm(_ptr(out), _ptr(x), _ptr(weight), seq_len, dim, float(eps),
+                                _dtype_code(x), _stream(stream)))
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, seq_len: int, num_heads: int, num_kv_heads: int,
+         head_dim: int, start_pos: int, theta: float,
+         stream: Optional[torch.cuda.Stream] = None) -> None:
+    """kernels::rope (include/kernels.h:33-45): rotate-half rotary embedding
+    in place on q [seq, heads, hd] and k [seq, kv_heads, hd] (orin_rope)."""
+    _need_cuda(q, k)
+    check(_lib.lib.orin_rope(_ptr(q), _ptr(k), seq_len, num_heads, num_kv_heads, head_dim,
+                             start_pos, float(theta), _dtype_code(q), _stream(stream)))
+
+
+def qkv_rope_append(q_out: torch.Tensor, qkv: torch.Tensor, k_pool: torch.Tensor,
+                    v_pool: torch.Tensor, seq_len: int, start_pos: int, num_heads: int,
+                    num_kv_heads: int, head_dim: int, theta: float, n_sink: int,
+                    window_size: int, *, q_norm: Optional[torch.Tensor] = None,
+                    k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+    """After the fused q/k/v projection (token rows [q | k | v]): optional
+    per-head q/k RMSNorm, rotary embedding, q into q_out and k/v into their
+    ring slots, in one launch (orin_qkv_rope_append)."""
+    _need_cuda(q_out, qkv, k_pool, v_pool, q_norm, k_norm)
+    check(_lib.lib.orin_qkv_rope_append(_ptr(q_out), _ptr(qkv), _ptr(q_norm), _ptr(k_norm),
+                                        _ptr(k_pool), _ptr(v_pool), seq_len, start_pos,
+                                        num_heads, num_kv_heads, head_dim, float(eps),
+                                        float(theta), n_sink, window_size, _dtype_code(qkv),
+                                        _stream(stream)))
 
 
 def kv_append(k_pool: torch.Tensor, v_pool: torch.Tensor, k_src: torch.Tensor,

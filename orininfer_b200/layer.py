@@ -1,0 +1,139 @@
+"""The reference's transformer layer and model step on this library's kernels.
+
+``DecoderLayer`` runs Model::transformer_layer (src/model.cu:37-111) for one
+call of seq_len tokens at start_pos, on one GPU, in eight launches where the
+reference makes fifteen:
+
+    orin_rmsnorm(xn, x)                          :53
+    orin_linear(qkv, xn, W_qkv)                  :59-61  (q/k/v weights stacked: one GEMM)
+    orin_qkv_rope_append(q, qkv, pools)          :64-75  (Qwen3 q/k norm, RoPE, K/V append)
+    orin_attention(att, q, pools)                :79-84  (+ the split-key combine for decode)
+    orin_linear(x, att, W_o, RESIDUAL, x)        :87-90
+    orin_rmsnorm(xn, x)                          :95
+    orin_linear(h, xn, W_gate_up, SWIGLU)        :100-104
+    orin_linear(x, h, W_down, RESIDUAL, x)       :107-110
+
+with the reference's rounding points (the residual and SwiGLU epilogues round
+where its separate add and fused_silu_mul kernels do).  ``Decoder`` adds the
+embedding gather (:25), the final RMSNorm and the LM head with the greedy
+argmax (:113-131 plus the sampler's argmax, one fused launch), i.e. one
+Model::forward + greedy sample per call.  Every buffer is allocated once, so
+a decode step can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import math
+from typing import Mapping, Optional
+
+import torch
+
+from . import kernels
+
+
+class DecoderLayer:
+    """One layer; `w` from weights.layer_for_device, `cfg` the model's
+    config.json keys.  qk_norm applies q_norm / k_norm (Qwen3; the reference
+    always does); Llama-family models (TinyLlama) have none."""
+
+    def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, *, n_sink: int, window: int,
+                 max_tokens: int, qk_norm: bool = False,
+                 workspace: Optional[torch.Tensor] = None):
+        self.w = dict(w)
+        self.nh = int(cfg["num_attention_heads"])
+        self.nkv = int(cfg["num_key_value_heads"])
+        self.hd = int(cfg.get("head_dim", cfg["hidden_size"] // self.nh))
+        self.H = int(cfg["hidden_size"])
+        self.IM = int(cfg["intermediate_size"])
+        self.eps = float(cfg["rms_norm_eps"])
+        self.theta = float(cfg["rope_theta"])
+        self.n_sink, self.window = int(n_sink), int(window)
+        if max_tokens > self.n_sink + self.window:
+            raise ValueError("max_tokens exceeds n_sink + window (src/kv_cache.cu:99-103)")
+        self.qk_norm = bool(qk_norm)
+        if self.qk_norm and ("q_norm" not in self.w or "k_norm" not in self.w):
+            raise ValueError("qk_norm needs q_norm and k_norm weights")
+        qkv = self.w["qkv"]
+        dev, dt = qkv.device, qkv.dtype
+        QD, KVD = self.nh * self.hd, self.nkv * self.hd
+        self.k_pool = torch.zeros((self.n_sink + self.window, KVD), dtype=dt, device=dev)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.xn = torch.empty((max_tokens, self.H), dtype=dt, device=dev)
+        self.qkv = torch.empty((max_tokens, QD + 2 * KVD), dtype=dt, device=dev)
+        self.q = torch.empty((max_tokens, QD), dtype=dt, device=dev)
+        self.att = torch.empty((max_tokens, QD), dtype=dt, device=dev)
+        self.h = torch.empty((max_tokens, self.IM), dtype=dt, device=dev)
+        self.scale = 1.0 / math.sqrt(self.hd)
+        self.workspace = workspace
+
+    @staticmethod
+    def workspace_bytes(cfg: Mapping, n_sink: int, window: int) -> int:
+        """Split-key workspace a decode step needs (shareable by all layers)."""
+        nh = int(cfg["num_attention_heads"])
+        hd = int(cfg.get("head_dim", cfg["hidden_size"] // nh))
+        return kernels.attention_workspace_bytes(1, n_sink + window + 64, nh,
+                                                 int(cfg["num_key_value_heads"]), hd, n_sink,
+                                                 window)
+
+    def forward(self, x: torch.Tensor, start_pos: int,
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """x [seq_len, H] (the residual stream) is updated in place and returned."""
+        S = x.shape[0]
+        w = self.w
+        xn, qkv, q, att, h = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S], self.h[:S]
+        kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
+        kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+        kernels.qkv_rope_append(q, qkv, self.k_pool, self.v_pool, S, start_pos, self.nh, self.nkv,
+                                self.hd, self.theta, self.n_sink, self.window,
+                                q_norm=w.get("q_norm") if self.qk_norm else None,
+                                k_norm=w.get("k_norm") if self.qk_norm else None,
+                                eps=self.eps, stream=stream)
+        kernels.attention(att, q, self.k_pool, self.v_pool, S, start_pos + S, self.nh, self.nkv,
+                          self.hd, self.scale, self.n_sink, self.window,
+                          workspace=self.workspace, stream=stream)
+        kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x, stream=stream)
+        kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps, stream=stream)
+        kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", stream=stream)
+        kernels.linear_into(x, h, w["down"], epilogue="residual", residual=x, stream=stream)
+        return x
+
+
+class Decoder:
+    """Model::forward + greedy sampling (src/model.cu:20-131): embedding,
+    the layers, final RMSNorm and the LM head argmax of the last token."""
+
+    def __init__(self, tensors: Mapping[str, torch.Tensor], cfg: Mapping, device, *,
+                 n_sink: int, window: int, max_tokens: int, qk_norm: bool = False):
+        from .weights import layer_for_device
+
+        self.cfg = dict(cfg)
+        self.H = int(cfg["hidden_size"])
+        self.eps = float(cfg["rms_norm_eps"])
+        self.embed = tensors["model.embed_tokens.weight"].to(device)
+        self.final_norm = tensors["model.norm.weight"].to(device)
+        self.lm_head = tensors["lm_head.weight"].to(device)
+        dt = self.embed.dtype
+        ws = DecoderLayer.workspace_bytes(cfg, n_sink, window)
+        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.layers = [
+            DecoderLayer(layer_for_device(tensors, i, cfg, device), cfg, n_sink=n_sink,
+                         window=window, max_tokens=max_tokens, qk_norm=qk_norm,
+                         workspace=self.workspace)
+            for i in range(int(cfg["num_hidden_layers"]))
+        ]
+        self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
+        self.xn = torch.empty((1, self.H), dtype=dt, device=device)
+        self.keys = torch.empty(1, dtype=torch.int64, device=device)
+        self.token = torch.empty(1, dtype=torch.int32, device=device)
+
+    def step(self, token_ids: torch.Tensor, start_pos: int,
+             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """token_ids int32 [seq_len] on the device -> next token id [1] (device)."""
+        S = token_ids.shape[0]
+        x = self.x[:S]
+        kernels.embedding(x, self.embed, token_ids, S, self.H, stream=stream)
+        for layer in self.layers:
+            layer.forward(x, start_pos, stream=stream)
+        kernels.rmsnorm(self.xn, x[S - 1:S], self.final_norm, 1, self.H, self.eps, stream=stream)
+        kernels.lm_head_argmax(self.xn, self.lm_head, keys=self.keys, out=self.token,
+                               stream=stream)
+        return self.token

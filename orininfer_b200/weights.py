@@ -154,7 +154,10 @@ def layer_for_device(tensors: Mapping[str, torch.Tensor], layer: int, cfg: Mappi
     """Layer `layer` in this library's layout on `device` (a CUDA device):
     "qkv" [q|k|v rows, H] (the reference's contiguous q/k/v scratch order,
     src/model.cu:56-58), "o_proj", "gate_up" (packed for the SwiGLU epilogue),
-    "down"; with world > 1, this rank's tensor-parallel shard of each."""
+    "down"; with world > 1, this rank's tensor-parallel shard of each.  The
+    norm weights ride along unsharded: "input_layernorm",
+    "post_attention_layernorm" and, where the file has them, "q_norm" /
+    "k_norm"."""
     from . import kernels, tp
 
     p = f"model.layers.{layer}"
@@ -176,4 +179,10 @@ def layer_for_device(tensors: Mapping[str, torch.Tensor], layer: int, cfg: Mappi
     else:
         out["o_proj"] = tp.shard_cols(wo, rank, world).to(device)
         out["down"] = tp.shard_cols(wd, rank, world).to(device)
+    for name in ("input_layernorm", "post_attention_layernorm"):
+        out[name] = tensors[f"{p}.{name}.weight"].to(device)
+    for name in ("q_norm", "k_norm"):
+        t = tensors.get(f"{p}.self_attn.{name}.weight")
+        if t is not None:
+            out[name] = t.to(device)
     return out

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
 def test_library_exports_reference_cxx_entry_points():
     hdr = open(os.path.join(ROOT, "include", "orin_kernels.h")).read()
     for name in ("matmul", "fused_silu_mul", "add", "bf16_to_fp32", "launch_gemm_cute",
-                 "attention"):
+                 "attention", "rmsnorm", "rope", "embedding"):
         assert re.search(rf"\b{name}\s*\(", hdr)
     for name, sym in _lib.SHIM_SYMBOLS.items():
         assert hasattr(_lib.lib, sym), f"{name} ({sym}) not exported"
@@ -157,3 +157,31 @@ def test_attention_workspace_plan():
     assert ws(1028, 1028, 32, 4, 64, 4, 1024) == 0      # 516 CTAs without splitting
     assert ws(1, 3000, 32, 8, 128, 4, 1024) == 17 * 32 * (128 + 2) * 4
     assert ws(0, 0, 32, 4, 64, 4, 1024) == 0
+
+
+def test_norm_and_rope_reject_bad_arguments_on_host():
+    L = _lib.lib
+    f = ctypes.c_float
+    assert L.orin_embedding(16, 16, 16, 1, 64, 0, None) == _lib.ERR_INVALID_ARG    # no vocab
+    assert L.orin_embedding(None, 16, 16, 1, 64, 10, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_embedding(16, 16, 16, 0, 64, 10, None) == _lib.OK
+    assert L.orin_rmsnorm(16, 16, 16, 1, 0, f(1e-5), 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_rmsnorm(None, 16, 16, 1, 64, f(1e-5), 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_rmsnorm(16, 16, 16, 0, 64, f(1e-5), 0, None) == _lib.OK
+    assert L.orin_rope(16, 16, 1, 4, 2, 63, 0, f(1e4), 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_rope(16, 16, 1, 4, 2, 64, -1, f(1e4), 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_rope(None, 16, 1, 4, 2, 64, 0, f(1e4), 0, None) == _lib.ERR_INVALID_ARG
+
+    def fused(**kw):
+        a = dict(qo=16, qkv=16, qn=0, kn=0, kp=16, vp=16, S=1, pos=0, nh=32, nkv=4, hd=64,
+                 ns=4, W=1024, dt=0)
+        a.update(kw)
+        return L.orin_qkv_rope_append(a["qo"], a["qkv"], a["qn"], a["kn"], a["kp"], a["vp"],
+                                      a["S"], a["pos"], a["nh"], a["nkv"], a["hd"], f(1e-6),
+                                      f(1e4), a["ns"], a["W"], a["dt"], None)
+
+    assert fused(qn=16) == _lib.ERR_INVALID_ARG       # q_norm without k_norm
+    assert fused(nkv=5) == _lib.ERR_INVALID_ARG
+    assert fused(S=1029) == _lib.ERR_INVALID_ARG      # more than n_sink + window
+    assert fused(hd=96) == _lib.ERR_UNSUPPORTED
+    assert fused(S=0) == _lib.OK

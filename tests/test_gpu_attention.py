@@ -116,13 +116,18 @@ def test_oracle_matches_reference_attention_kernel(S, C, shape, ns, W):
                   hd ** -0.5, ns, W)
     ref.sync()
     r = O.attention(q, kp, vp, S, C, nh, nkv, hd, hd ** -0.5, ns, W, dt)
-    # both sides compute in fp32/fp64 from the same 16-bit inputs with the
-    # same weights (no 16-bit softmax weights): at most one-ulp flips
-    mr, mae, exact = assert_close(out.cpu().float(), from_bits(r, torch.bfloat16).float(),
-                                  "reference kernel vs oracle", max_rel=4e-3, mae=2e-4)
-    assert exact >= 0.97
+    # same fp32 arithmetic on both sides (fp64 in the oracle): one-unit
+    # rounding flips at most
+    _, _, exact = assert_close(out.cpu().float(), from_bits(r, torch.bfloat16).float(),
+                               "reference kernel vs oracle", max_rel=4e-3, mae=2e-4)
+    assert exact >= 0.95
     # and this library against the reference kernel directly
-    check(ours(q, kp, vp, S, C, nh, nkv, hd, ns, W, dt), bits(out.cpu()), dt, "ours vs reference")
+    mine = ours(q, kp, vp, S, C, nh, nkv, hd, ns, W, dt)
+    check(mine, bits(out.cpu()), dt, "ours vs reference")
+    if C > 64:
+        # this library rounds the softmax weights to 16 bits for the tensor
+        # cores and the reference does not: two implementations are compared
+        assert (bits(mine) != bits(out.cpu())).any()
 
 
 @pytest.mark.parametrize("start,S,ns,W,kv_dim", [
@@ -130,7 +135,7 @@ def test_oracle_matches_reference_attention_kernel(S, C, shape, ns, W):
     (1028, 1020, 4, 1024, 256),  # second chunk, wraps
     (5000, 1, 4, 1024, 256),    # one decode token
     (2, 1028, 4, 1024, 256),    # more window positions than slots: later token kept
-    (3, 40, 2, 16, 12),         # rows not a multiple of 16 bytes (scalar copies)
+    (3, 18, 2, 16, 12),         # rows not a multiple of 16 bytes (scalar copies), slot reuse
 ])
 def test_kv_append_bit_exact(start, S, ns, W, kv_dim):
     rng = np.random.default_rng(start + S)

@@ -171,3 +171,46 @@ def test_argmax_key_order_matches_the_reference_sampler():
         if trial % 17 == 0:
             x[:] = -np.inf
         assert orc.argmax_reference(x) == orc.argmax_key_order(x), trial
+
+
+def _elf_dynamic_flags(path):
+    """(DT_FLAGS value, DT_SYMBOLIC present) from an ELF64 little-endian file."""
+    import struct
+    data = open(path, "rb").read()
+    assert data[:4] == b"\x7fELF" and data[4] == 2 and data[5] == 1
+    e_phoff, = struct.unpack_from("<Q", data, 0x20)
+    e_phentsize, e_phnum = struct.unpack_from("<HH", data, 0x36)
+    flags, symbolic = 0, False
+    for i in range(e_phnum):
+        p_type, _, p_offset, _, _, p_filesz = struct.unpack_from("<IIQQQQ", data,
+                                                                 e_phoff + i * e_phentsize)
+        if p_type != 2:  # PT_DYNAMIC
+            continue
+        for j in range(p_filesz // 16):
+            tag, val = struct.unpack_from("<qQ", data, p_offset + 16 * j)
+            if tag == 0:
+                break
+            if tag == 30:  # DT_FLAGS
+                flags = val
+            if tag == 16:  # DT_SYMBOLIC
+                symbolic = True
+    return flags, symbolic
+
+
+@pytest.mark.parametrize("path", [orc.REF_CUBLAS, orc.REF_CUTE])
+def test_reference_checkers_bind_their_own_kernels(path):
+    """The checkers built from the reference's sources define the same
+    kernels:: names as liborin_b200.so's drop-in entry points; linked with
+    -Bsymbolic, their entry points reach the reference's kernels even in a
+    process that also loaded liborin_b200.so."""
+    if not path.exists():
+        pytest.skip(f"{path.name} not built")
+    flags, symbolic = _elf_dynamic_flags(path)
+    assert symbolic or (flags & 0x2), f"{path.name} is not linked -Bsymbolic"
+
+
+def test_library_symbols_stay_out_of_the_global_scope():
+    import ctypes
+    from orininfer_b200 import _lib
+    assert hasattr(_lib.lib, "orin_linear")
+    assert not hasattr(ctypes.CDLL(None), "orin_linear")
