@@ -801,6 +801,104 @@ def run_one_kernel(args):
             "plan": ob_plan(m, n_out, kk, epi)}
 
 
+def run_model_decode(args) -> dict:
+    """Greedy generation through the whole model (config 5 of the workload set):
+    a 22-layer TinyLlama-shaped model (seeded random-init fp16 weights made on
+    the device, 2.07 GB), sink + window KV cache (4 + 1024), a 2048-token prompt
+    prefilled in the reference's chunks of n_sink + W = 1028 and 1020 tokens,
+    then one decode step (embedding, 22 x eight launches + the split-key
+    combine, final norm, LM head + argmax, the token fed back on the device)
+    captured in a CUDA graph at position 2048 (a full window) and replayed
+    `args.model_decode` times.  Every replay does a full step's work: the same
+    ring slot is rewritten and the same 1028 positions are attended."""
+    from orininfer_b200 import weights as Wt
+    from orininfer_b200.layer import Decoder
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = dict(Wt.TINYLLAMA)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2024)
+    tensors = {}
+    for name in Wt.reference_tensor_names(cfg["num_hidden_layers"]):
+        if name.endswith("norm.weight"):
+            dim = cfg["head_dim"] if ("q_norm" in name or "k_norm" in name) else cfg["hidden_size"]
+            tensors[name] = torch.ones(dim, dtype=torch.float16, device=dev)
+            continue
+        shape = {"embed_tokens": (cfg["vocab_size"], H), "lm_head": (cfg["vocab_size"], H),
+                 "q_proj": (H, H), "k_proj": (KVD, H), "v_proj": (KVD, H), "o_proj": (H, H),
+                 "gate_proj": (IM, H), "up_proj": (IM, H), "down_proj": (H, IM)}
+        key = next(k for k in shape if k in name)
+        tensors[name] = (torch.randn(shape[key], generator=gen, device=dev) * 0.02).half()
+    n_sink, window = 4, 1024
+    model = Decoder(tensors, cfg, dev, n_sink=n_sink, window=window, max_tokens=n_sink + window)
+    del tensors
+    prompt = torch.randint(0, cfg["vocab_size"], (2048,), generator=gen, device=dev,
+                           dtype=torch.int32)
+    # prefill (eager launches), timed with events
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    model.step(prompt[:1028], 0)
+    model.step(prompt[1028:], 1028)
+    b.record()
+    torch.cuda.synchronize()
+    prefill_ms = a.elapsed_time(b)
+    ids = model.token.clone()
+    pos = 2048
+
+    def decode():
+        model.step(ids, pos)
+        ids.copy_(model.token)
+
+    # eager step (host launch cost included)
+    for _ in range(3):
+        decode()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(10):
+        decode()
+    b.record()
+    torch.cuda.synchronize()
+    eager_ms = a.elapsed_time(b) / 10
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            decode()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(args.model_decode):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.model_decode
+    import orininfer_b200 as ob
+    ob.device_check()
+    del g
+    L = cfg["num_hidden_layers"]
+    w_bytes = 2 * (L * ((H + 2 * KVD) * H + H * H + 2 * IM * H + H * IM) + cfg["vocab_size"] * H)
+    kv_bytes = L * 2 * (n_sink + window) * KVD * 2
+    peaks, _ = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    gbs = (w_bytes + kv_bytes) / (ms / 1e3) / 1e9
+    return {"metric": "greedy decode tokens/s, 22-layer TinyLlama, batch 1, 1028-position window",
+            "value": round(1e3 / ms, 1), "unit": "tokens/s", "ms_per_token": round(ms, 4),
+            "eager_ms_per_token": round(eager_ms, 4),
+            "prefill_ms_2048_tokens": round(prefill_ms, 3),
+            "prefill_tokens_per_s": round(2048 / (prefill_ms / 1e3), 1),
+            "bytes_per_token": w_bytes + kv_bytes, "gbs": round(gbs, 1),
+            "hbm_frac": round(gbs / hbm, 4), "peak_hbm_gbs": hbm,
+            "launches_per_token": L * 9 + 6, "steps": args.model_decode,
+            "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
+            "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,
+                       "window": window, "prompt": 2048, "graph": True}}
+
+
 # ---------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -894,6 +992,10 @@ def main():
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,
                     help="run only this projection, eagerly, warmup+steps times, and print "
                          "its event-timed average (a small case for profilers)")
+    ap.add_argument("--model-decode", type=int, default=0,
+                    help="instead of the layer bench: time this many graph-replayed greedy "
+                         "decode steps of the whole 22-layer model (prefill of a 2048-token "
+                         "prompt first) and print that line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="with --kernel: token rows M of that projection (default: the "
                          "workload's 512; 1..64 is the decode GEMV / skinny path)")
@@ -907,6 +1009,9 @@ def main():
 
     if args.kernel is not None:
         print(json.dumps(run_one_kernel(args)), flush=True)
+        return 0
+    if args.model_decode > 0:
+        print(json.dumps(run_model_decode(args)), flush=True)
         return 0
 
     if args.impl == "reference":
