@@ -806,8 +806,9 @@ def run_model_decode(args) -> dict:
     a 22-layer TinyLlama-shaped model (seeded random-init fp16 weights made on
     the device, 2.07 GB), sink + window KV cache (4 + 1024), a 2048-token prompt
     prefilled in the reference's chunks of n_sink + W = 1028 and 1020 tokens,
-    then one decode step (embedding, 22 x eight launches + the split-key
-    combine, final norm, LM head + argmax, the token fed back on the device)
+    then one decode step (embedding, 22 x the layer's eight launches + the
+    split-key combine, final norm, LM head + argmax, the token fed back on the
+    device)
     captured in a CUDA graph at position 2048 (a full window) and replayed
     `args.model_decode` times.  Every replay does a full step's work: the same
     ring slot is rewritten and the same 1028 positions are attended."""
@@ -893,6 +894,9 @@ def run_model_decode(args) -> dict:
             "prefill_tokens_per_s": round(2048 / (prefill_ms / 1e3), 1),
             "bytes_per_token": w_bytes + kv_bytes, "gbs": round(gbs, 1),
             "hbm_frac": round(gbs / hbm, 4), "peak_hbm_gbs": hbm,
+            # per layer: norm, q/k/v, RoPE + append, attention, combine, o_proj,
+            # norm, gate/up, down; then embedding, final norm, LM head (key
+            # reset, weight stream, decode), token copy
             "launches_per_token": L * 9 + 6, "steps": args.model_decode,
             "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
             "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,

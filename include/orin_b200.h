@@ -142,6 +142,28 @@ orin_status orin_lm_head_argmax(int* token, const void* h, const void* W,
                                 int M, int V, int K, int dtype,
                                 unsigned long long* keys, void* stream);
 
+/*
+ * The projection that follows an RMSNorm, with the norm folded in:
+ *   C = epilogue( round16(A * r * norm_w) · W^T ),  r = rsqrtf(sum(A_row^2)/K + eps)
+ * per token row of A, the normalised row rounded to 16 bits exactly as
+ * orin_rmsnorm stores it (kernels/rmsnorm.cu:7-34), so the result equals
+ * orin_rmsnorm followed by orin_linear.  Replaces the reference's
+ * rmsnorm + matmul pairs (src/model.cu:53,59-61 and :95,100-101) at decode:
+ * the decode weight stream, M <= 32 tokens, epilogue NONE or SWIGLU, K % 8 == 0,
+ * 16-byte aligned A, W and norm_w; ORIN_ERR_UNSUPPORTED otherwise (use
+ * orin_rmsnorm + orin_linear).
+ */
+orin_status orin_linear_rmsnorm(void* C, const void* A, const void* W,
+                                const void* norm_w, float eps, int M, int N,
+                                int K, int dtype, int epilogue, void* stream);
+
+/* orin_lm_head_argmax of the RMS-normalised rows of h (the final norm of
+ * src/model.cu:116-117 folded in, rounded as orin_rmsnorm stores it). */
+orin_status orin_lm_head_argmax_rmsnorm(int* token, const void* h, const void* W,
+                                        const void* norm_w, float eps, int M,
+                                        int V, int K, int dtype,
+                                        unsigned long long* keys, void* stream);
+
 /* out = round16(silu(f32(gate)) * f32(up)), n elements; out may alias gate.
  * Replaces kernels::fused_silu_mul (include/kernels.h:88-94). */
 orin_status orin_silu_mul(void* out, const void* gate, const void* up,

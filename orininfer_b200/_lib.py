@@ -58,6 +58,9 @@ SIGNATURES = {
     "orin_linear": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "orin_linear_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "orin_lm_head_argmax": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "orin_linear_rmsnorm": (_i, [_vp, _vp, _vp, _vp, ctypes.c_float, _i, _i, _i, _i, _i, _vp]),
+    "orin_lm_head_argmax_rmsnorm": (_i, [_vp, _vp, _vp, _vp, ctypes.c_float, _i, _i, _i, _i, _vp,
+                                         _vp]),
     "orin_pack_gate_up": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "orin_plan_info": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]),
     "orin_silu_mul": (_i, [_vp, _vp, _vp, _ll, _i, _vp]),

@@ -196,6 +196,56 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   return ORIN_OK;
 }
 
+orin_status orin_linear_rmsnorm(void* C, const void* A, const void* W, const void* norm_w,
+                                float eps, int M, int N, int K, int dtype, int epilogue,
+                                void* stream) {
+  orin_status st = check_common(dtype, epilogue);
+  if (st != ORIN_OK) return st;
+  if (!C || !A || !W || !norm_w || M < 1 || N < 1 || K < 1) {
+    set_error("orin_linear_rmsnorm: null pointer or non-positive size (M=%d N=%d K=%d)", M, N,
+              K);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (epilogue != ORIN_EPI_NONE && epilogue != ORIN_EPI_SWIGLU) {
+    set_error("orin_linear_rmsnorm: epilogue %d (NONE and SWIGLU follow a norm)", epilogue);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (epilogue == ORIN_EPI_SWIGLU && N % 64 != 0) {
+    set_error("orin_linear_rmsnorm: SWIGLU needs N=%d to be a multiple of 64", N);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (M > kGemvMaxTokens || K % 8 != 0 || !aligned16(A) || !aligned16(W) || !aligned16(norm_w)) {
+    set_error("orin_linear_rmsnorm: the folded norm runs on the decode weight stream: needs "
+              "M <= %d, K %% 8 == 0 and 16-byte aligned A, W and norm_w (M=%d K=%d); use "
+              "orin_rmsnorm + orin_linear otherwise",
+              kGemvMaxTokens, M, K);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_gemv(C, A, W, M, N, K, dtype, epilogue, nullptr,
+                              static_cast<cudaStream_t>(stream), 0, norm_w, eps);
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_linear_rmsnorm");
+}
+
+orin_status orin_lm_head_argmax_rmsnorm(int* token, const void* h, const void* W,
+                                        const void* norm_w, float eps, int M, int V, int K,
+                                        int dtype, unsigned long long* keys, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (!token || !h || !W || !norm_w || !keys || M < 1 || V < 1 || K < 1) {
+    set_error("orin_lm_head_argmax_rmsnorm: null pointer or non-positive size");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (K % 8 != 0 || !aligned16(h) || !aligned16(W) || !aligned16(norm_w)) {
+    set_error("orin_lm_head_argmax_rmsnorm: needs K %% 8 == 0 and 16-byte aligned h, W and "
+              "norm_w (K=%d)", K);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_argmax_keys(keys, h, W, M, V, K, dtype, 0, s, norm_w, eps);
+  if (e == cudaSuccess) e = launch_argmax_decode(token, keys, M, s);
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_lm_head_argmax_rmsnorm");
+}
+
 orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int algo, int info[6]) {
   orin_status st = check_common(dtype, epilogue);
   if (st != ORIN_OK) return st;

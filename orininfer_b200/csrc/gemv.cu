@@ -48,6 +48,8 @@ struct GvParams {
   int M, N, K;
   int w_rows;  // rows of W: N, or 2N for the packed gate/up weight
   int n_offset;  // EPI_ARGMAX: vocabulary position of row 0 (a tensor-parallel shard)
+  const void* norm;  // NORM: RMSNorm weight [K] applied to every token row of X first
+  float eps;
 };
 
 __device__ __forceinline__ uint4 ld_weights(const void* p) {
@@ -116,8 +118,30 @@ __device__ __forceinline__ float bits_to_f(unsigned short b) {
   else return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
-// NT token tiles of 8 (M <= 8 * NT; NT = 1, 2 or 4).
-template <int DT, int EPI, int NT>
+// x * r * w for the 8 16-bit values of one fragment word set, rounded as the
+// RMSNorm kernel rounds its output.
+template <int DT>
+__device__ __forceinline__ uint4 rmsnorm8(uint4 x, float r, uint4 w) {
+  using E = Elem<DT>;
+  const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 a = E::unpack2(xs[i]);
+    const float2 b = E::unpack2(ws[i]);
+    o[i] = E::pack2(a.x * r * b.x, a.y * r * b.y);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// NT token tiles of 8 (M <= 8 * NT; NT = 1, 2 or 4).  NORM: the token rows are
+// RMS-normalised on the way in (the reference's RMSNorm before the projection,
+// kernels/rmsnorm.cu:7-34): every CTA sums the squares of the rows it reads
+// anyway (fp32, fixed order), then multiplies each loaded fragment by r and the
+// norm weight and rounds it to 16 bits, exactly what the separate kernel
+// would have stored.
+template <int DT, int EPI, int NT, bool NORM = false>
 __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   using E = Elem<DT>;
   using T = typename E::T;
@@ -168,6 +192,46 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
       for (int i = 0; i < 4; ++i) acc[h][t][i] = 0.f;
 
   bool waited = false;
+  __shared__ float s_r[NORM ? kGemvMaxTokens : 1];
+  if constexpr (NORM) {
+    __shared__ float s_ss[kGvWarps][kGemvMaxTokens];
+    // this warp's k-range of every row of the group into L2 while the
+    // previous kernel finishes, then the row statistics
+    if (kb0 < kb1 && lane < kGvRows * H) {
+      const int row = wrow[lane / kGvRows] + lane % kGvRows;
+      const int k_end = (kb1 * kGvBlockK < p.K) ? kb1 * kGvBlockK : p.K;
+      if (row < p.w_rows)
+        prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + kb0 * kGvBlockK,
+                          static_cast<uint32_t>((k_end - kb0 * kGvBlockK) * 2));
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    waited = true;
+    for (int m = 0; m < p.M; ++m) {
+      float ss = 0.f;
+      for (int c = threadIdx.x; c < p.K / 8; c += kGvThreads) {
+        const uint4 v = ld_l2_v4(X + static_cast<long long>(m) * p.K + 8 * c);
+        const uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = E::unpack2(vs[i]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_ss[warp][m] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < p.M) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGvWarps; ++w) tot += s_ss[w][threadIdx.x];
+      s_r[threadIdx.x] = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
+    }
+    __syncthreads();
+  }
+  const T* NW = static_cast<const T*>(p.norm);
   for (int kb = kb0; kb < kb1; kb += U) {
     uint4 w[U][H][2];
 #pragma unroll
@@ -205,6 +269,16 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
         const int tok = 8 * t + g;
         x[u][t] = (kin && tok < p.M) ? ld_l2_v4(X + static_cast<long long>(tok) * p.K + k)
                                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+      if constexpr (NORM) {
+        if (kin) {
+          const uint4 nw = ld_weights(NW + k);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int tok = 8 * t + g;
+            if (tok < p.M) x[u][t] = rmsnorm8<DT>(x[u][t], s_r[tok], nw);
+          }
+        }
       }
     }
 #pragma unroll
@@ -297,7 +371,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   }
 }
 
-template <int DT, int EPI, int NT>
+template <int DT, int EPI, int NT, bool NORM = false>
 cudaError_t gemv_launch(const GvParams& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N + kGvRows - 1) / kGvRows);
@@ -309,11 +383,19 @@ cudaError_t gemv_launch(const GvParams& p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<DT, EPI, NT>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<DT, EPI, NT, NORM>, p);
 }
 
 template <int DT, int NT>
 cudaError_t gemv_dispatch(const GvParams& p, int epi, cudaStream_t s) {
+  if (p.norm) {  // RMSNorm folded in: the projections that follow a norm
+    switch (epi) {
+      case EPI_NONE: return gemv_launch<DT, EPI_NONE, NT, true>(p, s);
+      case EPI_SWIGLU: return gemv_launch<DT, EPI_SWIGLU, NT, true>(p, s);
+      case EPI_ARGMAX: return gemv_launch<DT, EPI_ARGMAX, NT, true>(p, s);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (epi) {
     case EPI_NONE: return gemv_launch<DT, EPI_NONE, NT>(p, s);
     case EPI_SWIGLU: return gemv_launch<DT, EPI_SWIGLU, NT>(p, s);
@@ -344,14 +426,15 @@ __global__ void argmax_decode_kernel(int* token, const unsigned long long* keys,
 int gemv_grid(int N) { return (N + kGvRows - 1) / kGvRows; }
 
 cudaError_t launch_argmax_keys(unsigned long long* keys, const void* A, const void* W, int M,
-                               int V, int K, int dtype, int v_offset, cudaStream_t s) {
+                               int V, int K, int dtype, int v_offset, cudaStream_t s,
+                               const void* norm, float eps) {
   const size_t esz = 2;
   for (int r0 = 0; r0 < M; r0 += kGemvMaxTokens) {
     const int rows = (M - r0) < kGemvMaxTokens ? (M - r0) : kGemvMaxTokens;
     cudaError_t e = cudaMemsetAsync(keys + r0, 0, rows * sizeof(unsigned long long), s);
     if (e != cudaSuccess) return e;
     e = launch_gemv(keys + r0, static_cast<const char*>(A) + static_cast<size_t>(r0) * K * esz, W,
-                    rows, V, K, dtype, EPI_ARGMAX, nullptr, s, v_offset);
+                    rows, V, K, dtype, EPI_ARGMAX, nullptr, s, v_offset, norm, eps);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -364,10 +447,14 @@ cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int
 }
 
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
-                        int epi, const void* R, cudaStream_t s, int n_offset) {
+                        int epi, const void* R, cudaStream_t s, int n_offset, const void* norm,
+                        float eps) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
+  if (norm && K % 8 != 0) return cudaErrorInvalidValue;
   GvParams p;
   p.n_offset = n_offset;
+  p.norm = norm;
+  p.eps = eps;
   p.W = W;
   p.X = A;
   p.C = C;

@@ -57,14 +57,18 @@ cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const v
 // Decode-time weight-streaming kernel (csrc/gemv.cu) for M <= kGemvMaxTokens,
 // K % 8 == 0 and 16-byte aligned A and W.  Same epilogues and rounding.
 constexpr int kGemvMaxTokens = 32;
+// norm (optional): RMSNorm weight [K] applied to the rows of A first (eps);
+// epilogues NONE, SWIGLU and ARGMAX only.
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
-                        int epi, const void* R, cudaStream_t stream, int n_offset = 0);
+                        int epi, const void* R, cudaStream_t stream, int n_offset = 0,
+                        const void* norm = nullptr, float eps = 0.f);
 int gemv_grid(int N);
 // LM head + greedy argmax per row: keys[m] = the best 64-bit argmax key of
 // row m over the V vocabulary rows of W (positions v_offset + v), then
 // token[m] = its position (keys: caller scratch of M words).
 cudaError_t launch_argmax_keys(unsigned long long* keys, const void* A, const void* W, int M,
-                               int V, int K, int dtype, int v_offset, cudaStream_t stream);
+                               int V, int K, int dtype, int v_offset, cudaStream_t stream,
+                               const void* norm = nullptr, float eps = 0.f);
 cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int M,
                                  cudaStream_t stream);
 

@@ -55,7 +55,7 @@ __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
     "pack_gate_up", "device_check", "plan_info", "lm_head_argmax", "attention",
     "attention_workspace_bytes", "kv_append", "rmsnorm", "rope", "qkv_rope_append",
-    "embedding",
+    "embedding", "linear_rmsnorm",
 ]
 
 
@@ -153,13 +153,32 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
     return linear_into(out, x, w, epilogue=epilogue, residual=residual, algo=algo, stream=stream)
 
 
+def linear_rmsnorm(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, norm: torch.Tensor,
+                   eps: float, *, epilogue: str = "none",
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """out = epilogue(rmsnorm(x; norm, eps) · w^T) with the norm folded into the
+    decode weight stream (orin_linear_rmsnorm; M <= 32, epilogue "none" or
+    "swiglu"): bit for bit rmsnorm() then linear_into()."""
+    _need_cuda(out, x, w, norm)
+    if len({x.dtype, w.dtype, norm.dtype}) != 1:
+        raise ValueError("x, w and norm must share one dtype")
+    M, K = x.shape
+    check(_lib.lib.orin_linear_rmsnorm(_ptr(out), _ptr(x), _ptr(w), _ptr(norm), float(eps), M,
+                                       out.shape[-1], K, _dtype_code(x), _EPILOGUES[epilogue],
+                                       _stream(stream)))
+    return out
+
+
 def lm_head_argmax(h: torch.Tensor, w: torch.Tensor, *, keys: Optional[torch.Tensor] = None,
-                   out: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None, norm: Optional[torch.Tensor] = None,
+                   eps: float = 1e-5,
                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """Greedy next token per row of h [M, K] through the LM head w [V, K]
     (orin_lm_head_argmax: the reference's LM head + bf16_to_fp32 + argmax,
-    src/model.cu:113-131 and kernels/softmax.cu:52-73, with its tie-break)."""
-    _need_cuda(h, w, keys, out)
+    src/model.cu:113-131 and kernels/softmax.cu:52-73, with its tie-break).
+    With `norm`, the final RMSNorm of h is folded in
+    (orin_lm_head_argmax_rmsnorm)."""
+    _need_cuda(h, w, keys, out, norm)
     if w.dtype != h.dtype:
         raise ValueError("h and w must share one dtype")
     M, K = h.shape
@@ -168,6 +187,11 @@ def lm_head_argmax(h: torch.Tensor, w: torch.Tensor, *, keys: Optional[torch.Ten
         keys = torch.empty(M, dtype=torch.int64, device=h.device)
     if out is None:
         out = torch.empty(M, dtype=torch.int32, device=h.device)
+    if norm is not None:
+        check(_lib.lib.orin_lm_head_argmax_rmsnorm(_ptr(out), _ptr(h), _ptr(w), _ptr(norm),
+                                                   float(eps), M, V, K, _dtype_code(h),
+                                                   _ptr(keys), _stream(stream)))
+        return out
     check(_lib.lib.orin_lm_head_argmax(_ptr(out), _ptr(h), _ptr(w), M, V, K, _dtype_code(h),
                                        _ptr(keys), _stream(stream)))
     return out

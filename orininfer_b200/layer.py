@@ -14,11 +14,16 @@ reference makes fifteen:
     orin_linear(x, h, W_down, RESIDUAL, x)       :107-110
 
 with the reference's rounding points (the residual and SwiGLU epilogues round
-where its separate add and fused_silu_mul kernels do).  ``Decoder`` adds the
-embedding gather (:25), the final RMSNorm and the LM head with the greedy
-argmax (:113-131 plus the sampler's argmax, one fused launch), i.e. one
-Model::forward + greedy sample per call.  Every buffer is allocated once, so
-a decode step can be captured in a CUDA graph.
+where its separate add and fused_silu_mul kernels do).  With fold_norm, calls
+of up to 16 tokens (decode) fold each RMSNorm into the projection after it
+(orin_linear_rmsnorm: the decode weight stream normalises the rows it reads,
+bit for bit the separate kernel's output), six launches; that is faster for
+eagerly launched steps, but inside a CUDA graph the separate norm kernel
+lets the projection stream its weights while the norm runs, so it is off by
+default.  ``Decoder`` adds the embedding gather (:25), the final RMSNorm and
+the LM head with the greedy argmax (:113-131 plus the sampler's argmax), i.e.
+one Model::forward + greedy sample per call.  Every buffer is allocated once,
+so a decode step can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
@@ -37,8 +42,9 @@ class DecoderLayer:
 
     def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, *, n_sink: int, window: int,
                  max_tokens: int, qk_norm: bool = False,
-                 workspace: Optional[torch.Tensor] = None):
+                 workspace: Optional[torch.Tensor] = None, fold_norm: bool = False):
         self.w = dict(w)
+        self.fold_norm = bool(fold_norm)
         self.nh = int(cfg["num_attention_heads"])
         self.nkv = int(cfg["num_key_value_heads"])
         self.hd = int(cfg.get("head_dim", cfg["hidden_size"] // self.nh))
@@ -74,14 +80,22 @@ class DecoderLayer:
                                                  int(cfg["num_key_value_heads"]), hd, n_sink,
                                                  window)
 
+    # calls of at most this many tokens fold the norms into the weight stream
+    FOLD_NORM_TOKENS = 16
+
     def forward(self, x: torch.Tensor, start_pos: int,
                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """x [seq_len, H] (the residual stream) is updated in place and returned."""
         S = x.shape[0]
         w = self.w
         xn, qkv, q, att, h = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S], self.h[:S]
-        kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
-        kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+        fold = self.fold_norm and S <= self.FOLD_NORM_TOKENS
+        if fold:
+            kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
+                                   stream=stream)
+        else:
+            kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
+            kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
         kernels.qkv_rope_append(q, qkv, self.k_pool, self.v_pool, S, start_pos, self.nh, self.nkv,
                                 self.hd, self.theta, self.n_sink, self.window,
                                 q_norm=w.get("q_norm") if self.qk_norm else None,
@@ -91,8 +105,13 @@ class DecoderLayer:
                           self.hd, self.scale, self.n_sink, self.window,
                           workspace=self.workspace, stream=stream)
         kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x, stream=stream)
-        kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps, stream=stream)
-        kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", stream=stream)
+        if fold:
+            kernels.linear_rmsnorm(h, x, w["gate_up"], w["post_attention_layernorm"], self.eps,
+                                   epilogue="swiglu", stream=stream)
+        else:
+            kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps,
+                            stream=stream)
+            kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", stream=stream)
         kernels.linear_into(x, h, w["down"], epilogue="residual", residual=x, stream=stream)
         return x
 
@@ -102,9 +121,11 @@ class Decoder:
     the layers, final RMSNorm and the LM head argmax of the last token."""
 
     def __init__(self, tensors: Mapping[str, torch.Tensor], cfg: Mapping, device, *,
-                 n_sink: int, window: int, max_tokens: int, qk_norm: bool = False):
+                 n_sink: int, window: int, max_tokens: int, qk_norm: bool = False,
+                 fold_norm: bool = False):
         from .weights import layer_for_device
 
+        self.fold_norm = bool(fold_norm)
         self.cfg = dict(cfg)
         self.H = int(cfg["hidden_size"])
         self.eps = float(cfg["rms_norm_eps"])
@@ -117,7 +138,7 @@ class Decoder:
         self.layers = [
             DecoderLayer(layer_for_device(tensors, i, cfg, device), cfg, n_sink=n_sink,
                          window=window, max_tokens=max_tokens, qk_norm=qk_norm,
-                         workspace=self.workspace)
+                         workspace=self.workspace, fold_norm=fold_norm)
             for i in range(int(cfg["num_hidden_layers"]))
         ]
         self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
@@ -133,7 +154,12 @@ class Decoder:
         kernels.embedding(x, self.embed, token_ids, S, self.H, stream=stream)
         for layer in self.layers:
             layer.forward(x, start_pos, stream=stream)
-        kernels.rmsnorm(self.xn, x[S - 1:S], self.final_norm, 1, self.H, self.eps, stream=stream)
-        kernels.lm_head_argmax(self.xn, self.lm_head, keys=self.keys, out=self.token,
-                               stream=stream)
+        if self.fold_norm:
+            kernels.lm_head_argmax(x[S - 1:S], self.lm_head, keys=self.keys, out=self.token,
+                                   norm=self.final_norm, eps=self.eps, stream=stream)
+        else:
+            kernels.rmsnorm(self.xn, x[S - 1:S], self.final_norm, 1, self.H, self.eps,
+                            stream=stream)
+            kernels.lm_head_argmax(self.xn, self.lm_head, keys=self.keys, out=self.token,
+                                   stream=stream)
         return self.token

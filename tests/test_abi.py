@@ -185,3 +185,22 @@ def test_norm_and_rope_reject_bad_arguments_on_host():
     assert fused(S=1029) == _lib.ERR_INVALID_ARG      # more than n_sink + window
     assert fused(hd=96) == _lib.ERR_UNSUPPORTED
     assert fused(S=0) == _lib.OK
+
+
+def test_folded_norm_entry_points_reject_bad_arguments_on_host():
+    L = _lib.lib
+    f = ctypes.c_float(1e-5)
+    # C, A, W, norm, eps, M, N, K, dtype, epilogue
+    assert L.orin_linear_rmsnorm(16, 16, 16, 0, f, 1, 64, 64, 0, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_linear_rmsnorm(16, 16, 16, 16, f, 33, 64, 64, 0, 0, None) == \
+        _lib.ERR_UNSUPPORTED                                   # more tokens than the stream takes
+    assert L.orin_linear_rmsnorm(16, 16, 16, 16, f, 1, 64, 60, 0, 0, None) == \
+        _lib.ERR_UNSUPPORTED                                   # K % 8 != 0
+    assert L.orin_linear_rmsnorm(16, 16, 16, 16, f, 1, 64, 64, 0, 2, None) == \
+        _lib.ERR_UNSUPPORTED                                   # residual does not follow a norm
+    assert L.orin_linear_rmsnorm(16, 16, 16, 16, f, 1, 100, 64, 0, 1, None) == \
+        _lib.ERR_UNSUPPORTED                                   # SwiGLU needs N % 64 == 0
+    assert L.orin_lm_head_argmax_rmsnorm(16, 16, 16, 0, f, 1, 10, 64, 0, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    assert L.orin_lm_head_argmax_rmsnorm(16, 16, 16, 24, f, 1, 10, 64, 0, 16, None) == \
+        _lib.ERR_UNSUPPORTED                                   # unaligned norm weight

@@ -142,6 +142,49 @@ def test_qkv_rope_append(dt, qk_norm, S, start, nh, nkv, hd, ns, W):
     assert np.array_equal(bits(dv.cpu()), vp)  # v is copied, never rounded
 
 
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("M", [1, 5, 16, 32])
+@pytest.mark.parametrize("N,Kd,epi", [(2560, 2048, "none"), (5632, 2048, "swiglu"),
+                                      (100, 72, "none")])
+def test_linear_rmsnorm_equals_norm_then_linear(dt, M, N, Kd, epi):
+    """The norm folded into the weight stream gives what orin_rmsnorm then
+    orin_linear give (same per-row sum, same rounding of the normed row), and
+    matches the oracle."""
+    rng = np.random.default_rng(M * 7 + Kd)
+    x = rand16(rng, (M, Kd), dt)
+    nw = rand16(rng, (Kd,), dt, 0.5)
+    w = rand16(rng, (2 * N if epi == "swiglu" else N, Kd), dt, 0.02)
+    dx, dn, dw = dev(x, dt), dev(nw, dt), dev(w, dt)
+    fused = torch.empty((M, N), dtype=TORCH_DT[dt], device="cuda")
+    K.linear_rmsnorm(fused, dx, dw, dn, 1e-5, epilogue=epi)
+    xn = torch.empty_like(dx)
+    K.rmsnorm(xn, dx, dn, M, Kd, 1e-5)
+    plain = torch.empty_like(fused)
+    K.linear_into(plain, xn, dw, epilogue=epi, algo="gemv")
+    K.device_check()
+    assert (bits(fused.cpu()) == bits(plain.cpu())).mean() >= 0.99
+    r = O.linear(O.rmsnorm(x, nw, dt, 1e-5), w, dt, epi)
+    close(fused.cpu(), r, dt, f"linear_rmsnorm M={M} N={N} K={Kd} {epi}")
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_lm_head_argmax_with_folded_norm(M):
+    dt = 1
+    rng = np.random.default_rng(M)
+    h = rand16(rng, (M, 2048), dt)
+    nw = rand16(rng, (2048,), dt, 0.5)
+    w = rand16(rng, (32000, 2048), dt, 0.02)
+    dh, dn, dw = dev(h, dt), dev(nw, dt), dev(w, dt)
+    tok = K.lm_head_argmax(dh, dw, norm=dn, eps=1e-5)
+    hn = torch.empty_like(dh)
+    K.rmsnorm(hn, dh, dn, M, 2048, 1e-5)
+    tok2 = K.lm_head_argmax(hn, dw)
+    K.device_check()
+    assert tok.cpu().tolist() == tok2.cpu().tolist()
+    r = O.lm_head_argmax(O.rmsnorm(h, nw, dt, 1e-5), w, dt)
+    assert tok.cpu().tolist() == r.tolist()
+
+
 SMALL = dict(hidden_size=512, intermediate_size=1408, num_attention_heads=8,
              num_key_value_heads=2, head_dim=64, vocab_size=3000, rms_norm_eps=1e-5,
              rope_theta=10000.0)
@@ -157,12 +200,14 @@ def layer_bits(tensors, i, dt):
     return {k: bits(tensors[f"{p}.{v}.weight"]) for k, v in names.items()}
 
 
+@pytest.mark.parametrize("fold_norm", [False, True])
 @pytest.mark.parametrize("dims,qk_norm,dt", [
     (dict(), False, 0),                # TinyLlama layer
     (SMALL, True, 1),                  # Qwen3-style q/k norm, bf16
 ])
-def test_decoder_layer_matches_oracle(dims, qk_norm, dt):
-    """A 100-token prefill then 3 decode tokens through one layer."""
+def test_decoder_layer_matches_oracle(dims, qk_norm, dt, fold_norm):
+    """A 100-token prefill then 3 decode tokens through one layer (the decode
+    tokens with and without the norms folded into the weight stream)."""
     torch_dt = TORCH_DT[dt]
     tensors, cfg = Wt.synthetic_model(1, seed=3, dtype=torch_dt, **dims)
     if qk_norm:  # non-trivial norm weights
@@ -173,7 +218,7 @@ def test_decoder_layer_matches_oracle(dims, qk_norm, dt):
                 (1 + 0.3 * torch.randn(t.shape, generator=g)).to(torch_dt)
     ns, W = 4, 64
     layer = DecoderLayer(Wt.layer_for_device(tensors, 0, cfg, "cuda"), cfg, n_sink=ns, window=W,
-                         max_tokens=ns + W, qk_norm=qk_norm)
+                         max_tokens=ns + W, qk_norm=qk_norm, fold_norm=fold_norm)
     L = layer_bits(tensors, 0, dt)
     if not qk_norm:
         L["q_norm"] = L["k_norm"] = None
@@ -192,13 +237,15 @@ def test_decoder_layer_matches_oracle(dims, qk_norm, dt):
         pos += S
 
 
-def test_decoder_greedy_step():
+@pytest.mark.parametrize("fold_norm", [False, True])
+def test_decoder_greedy_step(fold_norm):
     """Two layers, prefill then decode: each token the library picks has an
     oracle logit within the tolerance of the oracle's best."""
     dt = 1
     tensors, cfg = Wt.synthetic_model(2, seed=5, dtype=torch.bfloat16, **SMALL)
     ns, W = 4, 60
-    model = Decoder(tensors, cfg, "cuda", n_sink=ns, window=W, max_tokens=ns + W)
+    model = Decoder(tensors, cfg, "cuda", n_sink=ns, window=W, max_tokens=ns + W,
+                    fold_norm=fold_norm)
     Ls = [layer_bits(tensors, i, dt) for i in range(2)]
     for L in Ls:
         L["q_norm"] = L["k_norm"] = None
