@@ -116,6 +116,61 @@ class DecoderLayer:
         return x
 
 
+class TPDecoderLayer(DecoderLayer):
+    """DecoderLayer on one rank of a tensor-parallel group (one process per
+    GPU), sharded as orininfer_b200.tp lays the projections out: this rank's
+    query heads and their KV head(s) (replicated when ranks outnumber KV
+    heads), with this rank's own ring pools; attention stays local; o_proj and
+    down are row-parallel through `comm` (orin_tp_linear_row: fp32 partials
+    summed over the ranks, then the residual add and one rounding, every rank
+    receiving the whole [seq, H] result); gate/up is this rank's packed shard.
+    `w` from weights.layer_for_device(..., rank, world)."""
+
+    def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, comm, *, n_sink: int,
+                 window: int, max_tokens: int, qk_norm: bool = False,
+                 workspace: Optional[torch.Tensor] = None):
+        from . import tp
+
+        rank, world = comm.rank, comm.world
+        nh = int(cfg["num_attention_heads"])
+        nkv = int(cfg["num_key_value_heads"])
+        local = dict(cfg)
+        local["num_attention_heads"] = tp.even_split(nh, world, "query heads")
+        local["num_key_value_heads"] = len(tp.kv_heads_of(rank, world, nkv))
+        local["intermediate_size"] = tp.even_split(int(cfg["intermediate_size"]), world,
+                                                   "intermediate size")
+        local["head_dim"] = int(cfg.get("head_dim", cfg["hidden_size"] // nh))
+        super().__init__(w, local, n_sink=n_sink, window=window, max_tokens=max_tokens,
+                         qk_norm=qk_norm, workspace=workspace)
+        self.comm = comm
+        self.partial = torch.empty((max_tokens, self.H), dtype=torch.float32,
+                                   device=self.w["qkv"].device)
+
+    def forward(self, x: torch.Tensor, start_pos: int,
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """x [seq_len, H], the same on every rank, updated in place."""
+        S = x.shape[0]
+        w = self.w
+        xn, qkv, q, att, h = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S], self.h[:S]
+        partial = self.partial[:S]
+        kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
+        kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+        kernels.qkv_rope_append(q, qkv, self.k_pool, self.v_pool, S, start_pos, self.nh, self.nkv,
+                                self.hd, self.theta, self.n_sink, self.window,
+                                q_norm=w.get("q_norm") if self.qk_norm else None,
+                                k_norm=w.get("k_norm") if self.qk_norm else None,
+                                eps=self.eps, stream=stream)
+        kernels.attention(att, q, self.k_pool, self.v_pool, S, start_pos + S, self.nh, self.nkv,
+                          self.hd, self.scale, self.n_sink, self.window,
+                          workspace=self.workspace, stream=stream)
+        self.comm.linear_row(att, w["o_proj"], residual=x, out=x, partial=partial,
+                             stream=stream)
+        kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps, stream=stream)
+        kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", stream=stream)
+        self.comm.linear_row(h, w["down"], residual=x, out=x, partial=partial, stream=stream)
+        return x
+
+
 class Decoder:
     """Model::forward + greedy sampling (src/model.cu:20-131): embedding,
     the layers, final RMSNorm and the LM head argmax of the last token."""
