@@ -740,6 +740,15 @@ def run_ours(args, rank, world, local_rank):
             else None
         if args.decode_reps > 0:
             line["decode"] = decode_path(dev, args.decode_reps, args.cublas_bar)
+        if args.model_decode_reps > 0:
+            # the whole model's greedy decode step; reported beside the layer
+            # line, which stands on its own if this part fails
+            try:
+                line["model_decode"] = run_model_decode(
+                    argparse.Namespace(model_decode=args.model_decode_reps, warmup=5))
+            except Exception as e:  # noqa: BLE001
+                line["model_decode"] = {"error": f"{type(e).__name__}: {e}"}
+            torch.cuda.empty_cache()
     if args.llama3_reps > 0:
         line["llama3_tp"] = llama3_tp_layer(rank, world, dev, comm, args.llama3_reps)
     if comm is not None:
@@ -802,7 +811,7 @@ def run_one_kernel(args):
 
 
 def run_model_decode(args) -> dict:
-    """Greedy generation through the whole model (config 5 of the workload set):
+    """Greedy generation through the whole model:
     a 22-layer TinyLlama-shaped model (seeded random-init fp16 weights made on
     the device, 2.07 GB), sink + window KV cache (4 + 1024), a 2048-token prompt
     prefilled in the reference's chunks of n_sink + W = 1028 and 1020 tokens,
@@ -996,6 +1005,9 @@ def main():
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,
                     help="run only this projection, eagerly, warmup+steps times, and print "
                          "its event-timed average (a small case for profilers)")
+    ap.add_argument("--model-decode-reps", type=int, default=50,
+                    help="graph replays of the whole-model greedy decode step reported as the "
+                         "line's model_decode object (0: skip)")
     ap.add_argument("--model-decode", type=int, default=0,
                     help="instead of the layer bench: time this many graph-replayed greedy "
                          "decode steps of the whole 22-layer model (prefill of a 2048-token "
