@@ -126,12 +126,12 @@ class TPDecoderLayer(DecoderLayer):
     receiving the whole [seq, H] result); gate/up is this rank's packed shard.
     `w` from weights.layer_for_device(..., rank, world)."""
 
-    def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, comm, *, n_sink: int,
-                 window: int, max_tokens: int, qk_norm: bool = False,
-                 workspace: Optional[torch.Tensor] = None):
+    @staticmethod
+    def local_config(cfg: Mapping, rank: int, world: int) -> dict:
+        """The config this rank's shard looks like: its query heads, its KV
+        head(s), its intermediate features (hidden size unchanged)."""
         from . import tp
 
-        rank, world = comm.rank, comm.world
         nh = int(cfg["num_attention_heads"])
         nkv = int(cfg["num_key_value_heads"])
         local = dict(cfg)
@@ -140,6 +140,12 @@ class TPDecoderLayer(DecoderLayer):
         local["intermediate_size"] = tp.even_split(int(cfg["intermediate_size"]), world,
                                                    "intermediate size")
         local["head_dim"] = int(cfg.get("head_dim", cfg["hidden_size"] // nh))
+        return local
+
+    def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, comm, *, n_sink: int,
+                 window: int, max_tokens: int, qk_norm: bool = False,
+                 workspace: Optional[torch.Tensor] = None):
+        local = self.local_config(cfg, comm.rank, comm.world)
         super().__init__(w, local, n_sink=n_sink, window=window, max_tokens=max_tokens,
                          qk_norm=qk_norm, workspace=workspace)
         self.comm = comm
@@ -217,4 +223,57 @@ class Decoder:
                             stream=stream)
             kernels.lm_head_argmax(self.xn, self.lm_head, keys=self.keys, out=self.token,
                                    stream=stream)
+        return self.token
+
+
+class TPDecoder(Decoder):
+    """Decoder on one rank of a tensor-parallel group: the embedding and the
+    final RMSNorm replicated, the layers as TPDecoderLayer, the LM head split by
+    vocabulary rows (tp.ragged_split) with the greedy argmax combined over the
+    ranks as one 64-bit key per token (TPComm.lm_head_argmax), so every rank
+    gets the unsharded model's token."""
+
+    def __init__(self, tensors: Mapping[str, torch.Tensor], cfg: Mapping, comm, device, *,
+                 n_sink: int, window: int, max_tokens: int, qk_norm: bool = False):
+        from . import tp
+        from .weights import layer_for_device
+
+        rank, world = comm.rank, comm.world
+        self.comm = comm
+        self.fold_norm = False
+        self.cfg = dict(cfg)
+        self.H = int(cfg["hidden_size"])
+        self.eps = float(cfg["rms_norm_eps"])
+        self.embed = tensors["model.embed_tokens.weight"].to(device)
+        self.final_norm = tensors["model.norm.weight"].to(device)
+        head = tensors["lm_head.weight"]
+        lo, hi = tp.ragged_split(head.shape[0], world)[rank]
+        self.v_offset = lo
+        self.lm_head = head[lo:hi].contiguous().to(device)
+        dt = self.embed.dtype
+        local = TPDecoderLayer.local_config(cfg, rank, world)
+        ws = DecoderLayer.workspace_bytes(local, n_sink, window)
+        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.layers = [
+            TPDecoderLayer(layer_for_device(tensors, i, cfg, device, rank, world), cfg, comm,
+                           n_sink=n_sink, window=window, max_tokens=max_tokens,
+                           qk_norm=qk_norm, workspace=self.workspace)
+            for i in range(int(cfg["num_hidden_layers"]))
+        ]
+        self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
+        self.xn = torch.empty((1, self.H), dtype=dt, device=device)
+        self.keys = torch.empty(1, dtype=torch.int64, device=device)
+        self.token = torch.empty(1, dtype=torch.int32, device=device)
+
+    def step(self, token_ids: torch.Tensor, start_pos: int,
+             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """token_ids int32 [seq_len] (the same on every rank) -> next token [1]."""
+        S = token_ids.shape[0]
+        x = self.x[:S]
+        kernels.embedding(x, self.embed, token_ids, S, self.H, stream=stream)
+        for layer in self.layers:
+            layer.forward(x, start_pos, stream=stream)
+        kernels.rmsnorm(self.xn, x[S - 1:S], self.final_norm, 1, self.H, self.eps, stream=stream)
+        self.comm.lm_head_argmax(self.xn, self.lm_head, self.v_offset, keys=self.keys,
+                                 out=self.token, stream=stream)
         return self.token

@@ -3,7 +3,9 @@ GPUs, one process per GPU: a TinyLlama layer split by heads (its 4 KV heads
 replicated on pairs of ranks at 8), local ring pools, row-parallel o_proj and
 down reduced over NVLink peer memory.  A 64-token prefill and three decode
 tokens on every rank must give the unsharded oracle layer's output, and the
-same bits on every rank."""
+same bits on every rank.  Then the model step (TPDecoder, two layers, the LM
+head split by vocabulary rows): every rank picks the same greedy token, one
+whose oracle logit is within the tolerance of the oracle's best."""
 import os
 import socket
 
@@ -76,6 +78,46 @@ def _worker(rank, world, port, q):
             pos += S
         torch.cuda.synchronize()
         del layer
+
+        # the model step: two layers, vocabulary-parallel LM head with the greedy
+        # argmax combined over the ranks
+        from orininfer_b200.layer import TPDecoder
+        dims = dict(vocab_size=3000)
+        tensors, cfg = Wt.synthetic_model(2, seed=9, dtype=torch.float16, **dims)
+        model = TPDecoder(tensors, cfg, comm, dev, n_sink=ns, window=W, max_tokens=ns + W)
+        Ls = []
+        for i in range(2):
+            pi = f"model.layers.{i}"
+            Ls.append({k: bits(tensors[f"{pi}.{v}.weight"]) for k, v in {
+                "input_layernorm": "input_layernorm",
+                "post_attention_layernorm": "post_attention_layernorm",
+                "q_proj": "self_attn.q_proj", "k_proj": "self_attn.k_proj",
+                "v_proj": "self_attn.v_proj", "o_proj": "self_attn.o_proj",
+                "gate_proj": "mlp.gate_proj", "up_proj": "mlp.up_proj",
+                "down_proj": "mlp.down_proj"}.items()})
+        pools = [(np.zeros((ns + W, kvd), np.uint16), np.zeros((ns + W, kvd), np.uint16))
+                 for _ in range(2)]
+        emb = bits(tensors["model.embed_tokens.weight"])
+        fnorm = bits(tensors["model.norm.weight"])
+        head = bits(tensors["lm_head.weight"])
+        ids = np.random.default_rng(2).integers(0, cfg["vocab_size"], 20).astype(np.int32)
+        pos = 0
+        for step in range(3):
+            x = emb[ids]
+            for Lw, (kp_, vp_) in zip(Ls, pools):
+                x = O.transformer_layer(x, Lw, kp_, vp_, pos, dict(cfg, n_sink=ns, window=W), 0)
+            logits = O.linear(O.rmsnorm(x[-1:], fnorm, 0, cfg["rms_norm_eps"]), head, 0, "f32")[0]
+            tok = int(model.step(torch.from_numpy(ids).to(dev), pos).item())
+            comm.wait()
+            ob.device_check()
+            assert logits[tok] >= logits.max() - 0.02 * np.abs(logits).max(), (rank, step)
+            toks = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+            dist.all_gather(toks, torch.tensor([tok]))
+            assert all(int(t_) == tok for t_ in toks), "ranks picked different tokens"
+            pos += len(ids)
+            ids = np.array([tok], dtype=np.int32)
+        torch.cuda.synchronize()
+        del model
         comm.close()
         dist.destroy_process_group()
         q.put((rank, "ok"))

@@ -49,3 +49,14 @@ def test_tensor_parallel_local_heads_tinyllama(world, kv_local):
         kv = tp.kv_heads_of(rank, world, nkv)
         assert len(kv) == kv_local
         assert sorted({h // G for h in heads}) == kv
+
+
+def test_local_config_of_a_rank():
+    from orininfer_b200.layer import TPDecoderLayer
+    cfg = dict(hidden_size=2048, intermediate_size=5632, num_attention_heads=32,
+               num_key_value_heads=4, head_dim=64)
+    loc = TPDecoderLayer.local_config(cfg, 5, 8)
+    assert (loc["num_attention_heads"], loc["num_key_value_heads"],
+            loc["intermediate_size"], loc["hidden_size"]) == (4, 1, 704, 2048)
+    with pytest.raises(ValueError):
+        TPDecoderLayer.local_config(cfg, 0, 3)   # 32 heads don't split over 3 ranks
