@@ -461,22 +461,6 @@ __global__ void __launch_bounds__(128)
   pdl_launch_dependents();
 }
 
-template <class... KArgs, class... Args>
-cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                      cudaStream_t s, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
 template <int DT, int HD, int RW>
 cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t s) {
   auto kern = attn_kernel<DT, HD, RW>;
@@ -489,8 +473,8 @@ cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  return launch_ex(kern, dim3(row_blocks, p.num_kv_heads, p.splits), dim3(kAttnThreads), smem,
-                   s, p);
+  return launch_pdl_smem(kern, dim3(row_blocks, p.num_kv_heads, p.splits), dim3(kAttnThreads),
+                         smem, s, p);
 }
 
 template <int DT, int HD>
@@ -499,8 +483,8 @@ cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStrea
                           : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
   if (e != cudaSuccess || p.splits == 1) return e;
   const int rows_total = p.seq_len * p.num_heads;
-  return launch_ex(attn_combine_kernel<DT, HD>, dim3((rows_total + 3) / 4), dim3(128), 0, s,
-                   p.out, static_cast<const float*>(p.ws), rows_total, p.splits);
+  return launch_pdl_smem(attn_combine_kernel<DT, HD>, dim3((rows_total + 3) / 4), dim3(128), 0,
+                         s, p.out, static_cast<const float*>(p.ws), rows_total, p.splits);
 }
 
 }  // namespace
@@ -516,15 +500,17 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
   pl.hsb = (group + pl.hpb - 1) / pl.hpb;
   const long long token_blocks = (seq_len + pl.tpb - 1) / pl.tpb;
   pl.row_blocks = token_blocks * pl.hsb;
-  // Split the keys across CTAs only when the row blocks leave SMs idle.
+  // Split the keys across CTAs only when the row blocks leave SMs idle
+  // (aiming at two CTAs per SM of a B200's 148).
+  constexpr int kSMs = 148;
   const long long ctas = pl.row_blocks * num_kv_heads;
   int splits = 1;
-  if (ctas < 148) {
+  if (ctas < kSMs) {
     // key tiles of the row block with the most keys (the last one)
     const int last_lo = static_cast<int>((token_blocks - 1) * pl.tpb);
     const int base = cache_len - seq_len;
     const KeyRanges kr = key_ranges(base + last_lo, cache_len - 1, n_sink, window);
-    long long want = (2 * 148 + ctas - 1) / ctas;
+    long long want = (2 * kSMs + ctas - 1) / ctas;
     if (want > kr.tiles) want = kr.tiles;
     if (want > 256) want = 256;
     splits = want < 1 ? 1 : static_cast<int>(want);
@@ -581,10 +567,10 @@ cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, con
                    ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
                      reinterpret_cast<uintptr_t>(k_src) | reinterpret_cast<uintptr_t>(v_src)) &
                     15) == 0;
-  return launch_ex(kv_scatter_kernel, dim3(seq_len), dim3(128), 0, s,
-                   static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool),
-                   static_cast<const uint16_t*>(k_src), static_cast<const uint16_t*>(v_src),
-                   seq_len, start_pos, n_sink, window, kv_dim, vec ? 1 : 0);
+  return launch_pdl_smem(kv_scatter_kernel, dim3(seq_len), dim3(128), 0, s,
+                         static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool),
+                         static_cast<const uint16_t*>(k_src), static_cast<const uint16_t*>(v_src),
+                         seq_len, start_pos, n_sink, window, kv_dim, vec ? 1 : 0);
 }
 
 }  // namespace orin

@@ -214,21 +214,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-template <class... KArgs, class... Args>
-cudaError_t launch_pdl_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
-                              Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
 template <int DT>
 cudaError_t rmsnorm_t(void* out, const void* x, const void* w, int rows, int dim, float eps,
                       cudaStream_t s) {
@@ -237,9 +222,9 @@ cudaError_t rmsnorm_t(void* out, const void* x, const void* w, int rows, int dim
                    ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
                      reinterpret_cast<uintptr_t>(w)) &
                     15) == 0;
-  return launch_pdl_kernel(rmsnorm_kernel<DT>, dim3(rows), dim3(kNormThreads), s,
-                           static_cast<T*>(out), static_cast<const T*>(x),
-                           static_cast<const T*>(w), dim, eps, vec ? 1 : 0);
+  return launch_pdl_smem(rmsnorm_kernel<DT>, dim3(rows), dim3(kNormThreads), 0, s,
+                         static_cast<T*>(out), static_cast<const T*>(x),
+                         static_cast<const T*>(w), dim, eps, vec ? 1 : 0);
 }
 
 template <int DT>
@@ -250,7 +235,7 @@ cudaError_t rope_t(void* q, void* k, int seq_len, int num_heads, int num_kv_head
       static_cast<long long>(seq_len) * (num_heads + num_kv_heads) * (head_dim / 2);
   const long long blocks = (n + 255) / 256;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  return launch_pdl_kernel(rope_kernel<DT>, dim3(static_cast<unsigned>(blocks)), dim3(256), s,
+  return launch_pdl_smem(rope_kernel<DT>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
                            static_cast<T*>(q), static_cast<T*>(k), seq_len, num_heads,
                            num_kv_heads, head_dim, start_pos, theta);
 }
@@ -264,11 +249,11 @@ cudaError_t qkv_rope_append_t(void* q_out, const void* qkv, const void* q_norm,
   const long long warps = static_cast<long long>(seq_len) * (num_heads + 2 * num_kv_heads);
   const long long blocks = (warps + 7) / 8;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  return launch_pdl_kernel(qkv_rope_append_kernel<DT, HD>, dim3(static_cast<unsigned>(blocks)),
-                           dim3(256), s, static_cast<T*>(q_out), static_cast<const T*>(qkv),
-                           static_cast<const T*>(q_norm), static_cast<const T*>(k_norm),
-                           static_cast<T*>(k_pool), static_cast<T*>(v_pool), seq_len, start_pos,
-                           num_heads, num_kv_heads, eps, theta, n_sink, window);
+  return launch_pdl_smem(qkv_rope_append_kernel<DT, HD>, dim3(static_cast<unsigned>(blocks)),
+                         dim3(256), 0, s, static_cast<T*>(q_out), static_cast<const T*>(qkv),
+                         static_cast<const T*>(q_norm), static_cast<const T*>(k_norm),
+                         static_cast<T*>(k_pool), static_cast<T*>(v_pool), seq_len, start_pos,
+                         num_heads, num_kv_heads, eps, theta, n_sink, window);
 }
 
 }  // namespace
@@ -279,7 +264,7 @@ cudaError_t launch_embedding(void* out, const void* table, const int* ids, int s
   const bool vec = hidden % 8 == 0 &&
                    ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(table)) &
                     15) == 0;
-  return launch_pdl_kernel(embedding_kernel, dim3(seq_len), dim3(256), s,
+  return launch_pdl_smem(embedding_kernel, dim3(seq_len), dim3(256), 0, s,
                            static_cast<uint16_t*>(out), static_cast<const uint16_t*>(table),
                            reinterpret_cast<const int32_t*>(ids), hidden, vocab, vec ? 1 : 0);
 }

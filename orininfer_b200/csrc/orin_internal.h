@@ -145,6 +145,25 @@ struct P2PView {
 };
 cudaError_t launch_p2p_reduce(const P2PView& v, int dtype, cudaStream_t s);
 
+// Launch `kern` with programmatic dependent launch allowed (it may start while
+// the previous kernel on the stream finishes; it orders itself with
+// griddepcontrol.wait) and `smem` bytes of dynamic shared memory.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Record a failure message for orin_last_error().
 void set_error(const char* fmt, ...);
 
