@@ -92,3 +92,54 @@ def test_wrapped_chunk_reads_its_own_later_tokens():
     # the chunk's last query sees exactly the positions it should
     last = direct(q[7, 0], [0, 1, 10, 11, 12, 13, 14, 15, 16, 17])
     assert np.abs(out[7, 0] - last).max() < 2e-3
+
+
+@pytest.mark.parametrize("dt", [F16, BF16])
+def test_constant_values_come_back_exactly(dt):
+    """Softmax weights sum to one: if every V row is the same vector, every
+    output is that vector (one rounding of an exact value)."""
+    rng = np.random.default_rng(1)
+    S, C, nh, nkv, hd, ns, W = 9, 300, 8, 2, 64, 4, 100
+    q = rand16(rng, (S, nh, hd), dt)
+    kp = rand16(rng, (ns + W, nkv, hd), dt)
+    row = rand16(rng, (1, 1, hd), dt)
+    vp = np.broadcast_to(row, (ns + W, nkv, hd)).copy()
+    out = O.attention(q, kp, vp, S, C, nh, nkv, hd, hd ** -0.5, ns, W, dt)
+    assert np.array_equal(out, np.broadcast_to(row, (S, nh, hd)))
+
+
+@pytest.mark.parametrize("dt", [F16, BF16])
+def test_no_sink_and_a_long_window_is_causal_attention(dt):
+    """With n_sink = 0 and a window longer than the sequence nothing is
+    evicted: plain causal softmax attention over positions 0..ap."""
+    rng = np.random.default_rng(2)
+    S, nh, hd = 20, 4, 64
+    q = rand16(rng, (S, nh, hd), dt)
+    k = rand16(rng, (S, nh, hd), dt)
+    v = rand16(rng, (S, nh, hd), dt)
+    W = 64
+    kp = np.zeros((W, nh, hd), np.uint16)
+    vp = np.zeros_like(kp)
+    O.kv_append(kp.reshape(W, -1), vp.reshape(W, -1), k.reshape(S, -1), v.reshape(S, -1), 0, 0, W)
+    out = O.widen(O.attention(q, kp, vp, S, S, nh, nh, hd, hd ** -0.5, 0, W, dt), dt)
+    qf, kf, vf = (O.widen(a, dt).astype(np.float64) for a in (q, k, v))
+    s = np.einsum("thd,uhd->htu", qf, kf) * hd ** -0.5
+    s = np.where(np.tril(np.ones((S, S), bool))[None], s, -np.inf)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    ref = np.einsum("htu,uhd->thd", p / p.sum(-1, keepdims=True), vf)
+    assert np.abs(out - ref).max() <= 2 ** -7 * np.abs(ref).max()
+
+
+def test_grouped_query_heads_equal_repeated_kv_heads():
+    """G query heads sharing a KV head give what G copies of that KV head would."""
+    dt = BF16
+    rng = np.random.default_rng(3)
+    S, C, nh, nkv, hd, ns, W = 5, 70, 8, 2, 64, 4, 32
+    q = rand16(rng, (S, nh, hd), dt)
+    kp = rand16(rng, (ns + W, nkv, hd), dt)
+    vp = rand16(rng, (ns + W, nkv, hd), dt)
+    gqa = O.attention(q, kp, vp, S, C, nh, nkv, hd, hd ** -0.5, ns, W, dt)
+    G = nh // nkv
+    mha = O.attention(q, np.repeat(kp, G, axis=1), np.repeat(vp, G, axis=1), S, C, nh, nh, hd,
+                      hd ** -0.5, ns, W, dt)
+    assert np.array_equal(gqa, mha)
