@@ -46,7 +46,8 @@ __nv_bfloat16* upload(std::mt19937& g, size_t n, float scale, bool ones = false)
 }
 
 struct Layer {
-  __nv_bfloat16 *in_norm, *q, *k, *v, *o, *post_norm, *gate, *up, *down, *k_pool, *v_pool;
+  __nv_bfloat16 *in_norm, *q, *k, *v, *q_norm, *k_norm, *o, *post_norm, *gate, *up, *down,
+      *k_pool, *v_pool;
 };
 
 }  // namespace
@@ -63,6 +64,8 @@ int main(int argc, char** argv) {
     l.q = upload(g, size_t(QD) * H, 0.02f);
     l.k = upload(g, size_t(KVD) * H, 0.02f);
     l.v = upload(g, size_t(KVD) * H, 0.02f);
+    l.q_norm = upload(g, HD, 0.f, true);
+    l.k_norm = upload(g, HD, 0.f, true);
     l.o = upload(g, size_t(H) * QD, 0.02f);
     l.post_norm = upload(g, H, 0.f, true);
     l.gate = upload(g, size_t(IM) * H, 0.02f);
@@ -101,6 +104,8 @@ int main(int argc, char** argv) {
       kernels::matmul(q, buf_b, l.q, seq, QD, H);
       kernels::matmul(k, buf_b, l.k, seq, KVD, H);
       kernels::matmul(v, buf_b, l.v, seq, KVD, H);
+      kernels::rmsnorm(q, q, l.q_norm, seq * NH, HD, EPS);
+      kernels::rmsnorm(k, k, l.k_norm, seq * NKV, HD, EPS);
       kernels::rope(q, k, seq, NH, NKV, HD, start, THETA);
       if (orin_kv_append(l.k_pool, l.v_pool, k, v, seq, start, N_SINK, WINDOW, KVD, ORIN_BF16,
                          nullptr) != ORIN_OK)
