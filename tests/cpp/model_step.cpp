@@ -1,8 +1,8 @@
 // model_step.cpp — the reference's per-token call sequence (Model::forward,
 // src/model.cu:20-131: embedding, per layer RMSNorm, q/k/v matmuls, the
 // per-head q/k RMSNorm, RoPE, the K/V append, attention, o_proj + add, RMSNorm,
-// gate/up matmuls, SwiGLU, down
-// + add, then the final RMSNorm, LM head and bf16 -> fp32 logits) written
+// gate/up matmuls, SwiGLU, down + add, then the final RMSNorm, LM head and
+// bf16 -> fp32 logits) written
 // against include/orin_kernels.h, the C++ drop-in signatures liborin_b200.so
 // exports, plus orin_kv_append for the append KVCache::append_kv does.
 //
