@@ -35,6 +35,15 @@ import torch
 from . import kernels
 
 
+def prefill_chunks(prompt_len: int, chunk: int) -> list[tuple[int, int]]:
+    """(start position, length) of each prefill call: chunks of the KV cache's
+    capacity n_sink + window, as Engine::generate splits a long prompt
+    (src/engine.cpp:67-81)."""
+    if chunk < 1:
+        raise ValueError("chunk must be >= 1")
+    return [(pos, min(chunk, prompt_len - pos)) for pos in range(0, prompt_len, chunk)]
+
+
 class DecoderLayer:
     """One layer; `w` from weights.layer_for_device, `cfg` the model's
     config.json keys.  qk_norm applies q_norm / k_norm (Qwen3; the reference
@@ -206,6 +215,35 @@ class Decoder:
         self.xn = torch.empty((1, self.H), dtype=dt, device=device)
         self.keys = torch.empty(1, dtype=torch.int64, device=device)
         self.token = torch.empty(1, dtype=torch.int32, device=device)
+
+    def generate(self, prompt: list[int], max_new_tokens: int,
+                 eos_ids: tuple[int, ...] = ()) -> list[int]:
+        """Greedy generation as Engine::generate runs it (src/engine.cpp:55-115):
+        the prompt prefilled in chunks of the cache's capacity, then one token
+        per step until max_new_tokens or an end token.  Returns the generated
+        ids; self.stats holds the prefill and decode times (ms)."""
+        import time
+
+        if not prompt or max_new_tokens < 1:
+            return []
+        dev = self.x.device
+        ids = torch.tensor(prompt, dtype=torch.int32, device=dev)
+        capacity = self.layers[0].n_sink + self.layers[0].window
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for pos, n in prefill_chunks(len(prompt), min(capacity, self.x.shape[0])):
+            tok = self.step(ids[pos:pos + n], pos)
+        out = [int(tok.item())]
+        t1 = time.perf_counter()
+        step_ids = torch.empty(1, dtype=torch.int32, device=dev)
+        while len(out) < max_new_tokens and out[-1] not in eos_ids:
+            step_ids.fill_(out[-1])
+            tok = self.step(step_ids, len(prompt) + len(out) - 1)
+            out.append(int(tok.item()))
+        t2 = time.perf_counter()
+        self.stats = {"prompt_tokens": len(prompt), "prefill_ms": (t1 - t0) * 1e3,
+                      "generated_tokens": len(out), "decode_ms": (t2 - t1) * 1e3}
+        return out
 
     def step(self, token_ids: torch.Tensor, start_pos: int,
              stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:

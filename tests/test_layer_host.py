@@ -60,3 +60,14 @@ def test_local_config_of_a_rank():
             loc["intermediate_size"], loc["hidden_size"]) == (4, 1, 704, 2048)
     with pytest.raises(ValueError):
         TPDecoderLayer.local_config(cfg, 0, 3)   # 32 heads don't split over 3 ranks
+
+
+def test_prefill_chunks_follow_the_reference_engine():
+    from orininfer_b200.layer import prefill_chunks
+    # a 2048-token prompt with a 4 + 1024 cache: 1028 then 1020
+    assert prefill_chunks(2048, 1028) == [(0, 1028), (1028, 1020)]
+    assert prefill_chunks(5, 1028) == [(0, 5)]
+    assert prefill_chunks(2056, 1028) == [(0, 1028), (1028, 1028)]
+    assert prefill_chunks(0, 1028) == []
+    with pytest.raises(ValueError):
+        prefill_chunks(10, 0)
