@@ -3,8 +3,16 @@
  *
  * Every entry point takes plain device pointers, element counts and an opaque
  * CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream).
- * Nothing is allocated: split-K partial sums stay on chip (thread-block
- * clusters combine them through distributed shared memory).  The first GEMM
+ * The GEMM entry points allocate no workspace: split-K partial sums stay on
+ * chip (thread-block clusters combine them through distributed shared memory).
+ * The library does own a few file-scope device arrays, present on every
+ * device that loads it until exit: a 4-byte error word per device, the 4 MB
+ * split-key array behind the kernels::attention drop-in, and the 64 MiB
+ * partial-sum array of orin_tp_linear_row_static.  orin_attention and
+ * orin_tp_linear_row take their workspace from the caller.  The tensor-parallel
+ * set-up allocates: orin_tp_enable_p2p the peer-memory region it maps (freed by
+ * orin_tp_destroy, which also uses a 4-byte buffer for its closing barrier),
+ * orin_p2p_watchdog_selftest a small buffer for the duration of the call.  The first GEMM
  * call on a device does a one-time set-up (device attributes, the device
  * error word); it must not be inside CUDA stream capture, later calls may be
  * captured into graphs.

@@ -26,11 +26,20 @@ EPI = {"none": 0, "swiglu": 1, "residual": 2, "f32": 3, "f32_partial": 4}
 _vp, _i, _ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
 
 
+def reference_tree() -> Path | None:
+    """The reference source tree the checkers are compiled from: $ORIN_REFERENCE_TREE,
+    else the Makefile's default REF; None where it is absent (a machine that only
+    runs the prebuilt files)."""
+    ref = Path(os.environ.get("ORIN_REFERENCE_TREE", "/root/reference"))
+    return ref if (ref / "kernels" / "matmul.cu").exists() else None
+
+
 def build() -> None:
     """Compile liborc.so (and the reference checkers when the reference tree exists)."""
     subprocess.run(["make", "-s", "-C", os.fspath(HERE), "orc"], check=True)
-    if Path("/root/reference/kernels/matmul.cu").exists():
-        subprocess.run(["make", "-s", "-C", os.fspath(HERE), "ref"], check=True)
+    ref = reference_tree()
+    if ref is not None:
+        subprocess.run(["make", "-s", "-C", os.fspath(HERE), f"REF={ref}", "ref"], check=True)
 
 
 def _load() -> ctypes.CDLL:
@@ -357,19 +366,31 @@ def transformer_layer(x: np.ndarray, L: dict, k_pool: np.ndarray, v_pool: np.nda
     return add(x, d, dt)                                                  # :110
 
 
+REF_REFUSED_CUTE = -2  # ref_entry.cu: the call would have reached the CuTe kernel
+
+
+def cute_refused(M: int, N: int, K: int) -> bool:
+    """True for the shapes that the reference's build without cuBLAS sends to its
+    CuTe kernel (kernels/matmul.cu:71, alignment test kernels/gemm_cute.cu:302).
+    That kernel made an illegal address access on a B200 (its 128-thread copy
+    layouts under a 256-thread MMA, kernels/gemm_cute.cu:211-249), so those calls
+    are refused before any launch; the per-row GEMV fallback stays usable."""
+    return M > 1 and M % 128 == 0 and N % 128 == 0 and K % 32 == 0
+
+
 class RefKernels:
     """The reference's own bf16 kernels (built from its sources; GPU only).
 
     Pointers are raw device addresses (ints)."""
 
     def __init__(self, cute: bool = False):
+        self.cute = cute
         path = REF_CUTE if cute else REF_CUBLAS
         if not path.exists():
             raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
         self.lib = ctypes.CDLL(os.fspath(path), mode=os.RTLD_LOCAL | os.RTLD_NOW)
         L = self.lib
         L.ref_matmul.argtypes = [_vp, _vp, _vp, _i, _i, _i]
-        L.ref_gemm_cute.argtypes = [_vp, _vp, _vp, _i, _i, _i]
         L.ref_fused_silu_mul.argtypes = [_vp, _vp, _vp, _i, _i]
         L.ref_add.argtypes = [_vp, _vp, _i]
         L.ref_bf16_to_fp32.argtypes = [_vp, _vp, _i]
@@ -378,7 +399,7 @@ class RefKernels:
         L.ref_rmsnorm.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_float]
         L.ref_rope.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float]
         L.ref_embedding.argtypes = [_vp, _vp, _vp, _i, _i]
-        for n in ("ref_matmul", "ref_gemm_cute", "ref_fused_silu_mul", "ref_add",
+        for n in ("ref_matmul", "ref_fused_silu_mul", "ref_add",
                   "ref_bf16_to_fp32", "ref_attention", "ref_rmsnorm", "ref_rope",
                   "ref_embedding", "ref_sync"):
             getattr(L, n).restype = _i
@@ -388,10 +409,14 @@ class RefKernels:
             raise RuntimeError(f"{what}: CUDA error {rc}")
 
     def matmul(self, C: int, A: int, B: int, M: int, N: int, K: int) -> None:
-        self._ok(self.lib.ref_matmul(C, A, B, M, N, K), "kernels::matmul")
-
-    def gemm_cute(self, C: int, A: int, B: int, M: int, N: int, K: int) -> bool:
-        return bool(self.lib.ref_gemm_cute(C, A, B, M, N, K))
+        if self.cute and cute_refused(M, N, K):
+            raise ValueError(
+                f"kernels::matmul {M}x{N}x{K} without cuBLAS would launch the reference's CuTe "
+                "kernel (gemm_multi_stage), which accessed illegal addresses on a B200; refused")
+        rc = self.lib.ref_matmul(C, A, B, M, N, K)
+        if rc == REF_REFUSED_CUTE:
+            raise ValueError(f"ref_matmul refused {M}x{N}x{K}: CuTe kernel shape")
+        self._ok(rc, "kernels::matmul")
 
     def fused_silu_mul(self, out: int, g: int, u: int, seq: int, im: int) -> None:
         self._ok(self.lib.ref_fused_silu_mul(out, g, u, seq, im), "kernels::fused_silu_mul")

@@ -10,25 +10,28 @@
 
 #include "kernels.h"  // the reference's include/kernels.h
 
-extern bool launch_gemm_cute(__nv_bfloat16* C, const __nv_bfloat16* A, const __nv_bfloat16* B,
-                             int M, int N, int K);
-
 extern "C" {
 
+// Returned instead of launching when a call of the build without USE_CUBLAS would
+// reach the reference's CuTe kernel.
+#define REF_REFUSED_CUTE (-2)
+
 // kernels::matmul: M == 1 -> gemv_kernel; M > 1 -> cuBLAS (USE_CUBLAS build) or
-// CuTe / per-row GEMV (the other build).
+// the per-row GEMV fallback (the other build).
+//
+// Without USE_CUBLAS, kernels::matmul sends tile-aligned shapes (M % 128, N % 128,
+// K % 32 all zero; kernels/gemm_cute.cu:302) to gemm_multi_stage.  That kernel
+// made an illegal address access on a B200: its copy layouts cover 128 threads
+// (kernels/gemm_cute.cu:211-249) while the block has 256, so the upper half reads
+// past A and writes past the C tile on the last k-tile.  Those shapes are refused
+// here before anything is launched; only the per-row GEMV fallback stays callable.
 int ref_matmul(void* C, const void* A, const void* B, int M, int N, int K) {
+#ifndef USE_CUBLAS
+  if (M > 1 && M % 128 == 0 && N % 128 == 0 && K % 32 == 0) return REF_REFUSED_CUTE;
+#endif
   kernels::matmul(static_cast<__nv_bfloat16*>(C), static_cast<const __nv_bfloat16*>(A),
                   static_cast<const __nv_bfloat16*>(B), M, N, K);
   return static_cast<int>(cudaGetLastError());
-}
-
-// The CuTe sm80 kernel alone; returns 1 if it launched (tile-aligned shapes).
-int ref_gemm_cute(void* C, const void* A, const void* B, int M, int N, int K) {
-  return launch_gemm_cute(static_cast<__nv_bfloat16*>(C), static_cast<const __nv_bfloat16*>(A),
-                          static_cast<const __nv_bfloat16*>(B), M, N, K)
-             ? 1
-             : 0;
 }
 
 int ref_fused_silu_mul(void* out, const void* gate, const void* up, int seq, int im) {

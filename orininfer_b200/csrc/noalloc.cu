@@ -15,7 +15,10 @@
 // different communicators, without an ordering between them) write the same
 // scratch and corrupt each other's sums; calls on one device must be ordered,
 // e.g. issued on a single stream.  The first call on a device performs the
-// look-up (it may load the module) and must happen outside stream capture.
+// look-up (it may load the module) and must happen outside stream capture; a
+// first call made under capture is refused with ORIN_ERR_INVALID_ARG.  The
+// array used is the one of the communicator's device, which must be the
+// current device (the kernels run there).
 #include "orin_b200.h"
 #include "orin_internal.h"
 
@@ -33,14 +36,24 @@ constexpr int kMaxDevices = 64;
 float* g_partial_addr[kMaxDevices] = {};
 std::mutex g_partial_mutex;
 
-// This device's address of g_tp_partial (looked up once per device).
-float* static_partial(int device, const char** why) {
+// This device's address of g_tp_partial (looked up once per device, with the
+// device current).  A look-up under stream capture is refused: it may load the
+// module, which would invalidate the capture.
+float* static_partial(int device, cudaStream_t s, orin_status* st, const char** why) {
+  *st = ORIN_ERR_CUDA;
   if (device < 0 || device >= kMaxDevices) {
     *why = "device ordinal out of range";
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(g_partial_mutex);
   if (!g_partial_addr[device]) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) {
+      *st = ORIN_ERR_INVALID_ARG;
+      *why = "the first call on a device looks the array up and must not be stream-captured; "
+             "make one uncaptured call first";
+      return nullptr;
+    }
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_tp_partial);
     if (e != cudaSuccess) {
@@ -79,11 +92,18 @@ orin_status orin_tp_linear_row_static(void* comm, void* C, const void* A_shard,
     set_error("orin_tp_linear_row_static: cudaGetDevice: %s", cudaGetErrorString(e));
     return ORIN_ERR_CUDA;
   }
+  const int comm_device = tp_comm_device(comm);
+  if (device != comm_device) {
+    set_error("orin_tp_linear_row_static: the current device (%d) is not the communicator's "
+              "(%d); make the communicator's device current", device, comm_device);
+    return ORIN_ERR_INVALID_ARG;
+  }
   const char* why = "";
-  float* partial = static_partial(device, &why);
+  orin_status st = ORIN_OK;
+  float* partial = static_partial(device, static_cast<cudaStream_t>(stream), &st, &why);
   if (!partial) {
     set_error("orin_tp_linear_row_static: static scratch look-up failed: %s", why);
-    return ORIN_ERR_CUDA;
+    return st;
   }
   return orin_tp_linear_row(comm, C, A_shard, W_shard, M, N, K_shard, dtype, residual, partial,
                             stream);

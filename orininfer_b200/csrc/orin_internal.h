@@ -167,4 +167,8 @@ cudaError_t launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
 // Record a failure message for orin_last_error().
 void set_error(const char* fmt, ...);
 
+// The CUDA device ordinal a tensor-parallel communicator (orin_tp_init's
+// handle) was created on (csrc/tp.cu).
+int tp_comm_device(const void* comm);
+
 }  // namespace orin

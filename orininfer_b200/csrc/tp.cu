@@ -87,6 +87,8 @@ orin_status settle(TpComm* c, ncclResult_t r, const char* what) {
 
 }  // namespace
 
+int orin::tp_comm_device(const void* comm) { return static_cast<const TpComm*>(comm)->device; }
+
 extern "C" {
 
 orin_status orin_tp_unique_id(void* id_out) {

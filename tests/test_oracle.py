@@ -214,3 +214,30 @@ def test_library_symbols_stay_out_of_the_global_scope():
     from orininfer_b200 import _lib
     assert hasattr(_lib.lib, "orin_linear")
     assert not hasattr(ctypes.CDLL(None), "orin_linear")
+
+
+def test_reference_cute_kernel_is_not_launchable():
+    """The reference's CuTe kernel (gemm_multi_stage) made an illegal address
+    access on a B200, so nothing here may launch it: the checker library exports
+    no entry for it, and the build without cuBLAS refuses every shape that
+    kernels::matmul would send to it (tile-aligned M, N, K), both in Python and
+    in the C entry point, before any CUDA call.  Unaligned shapes keep the
+    per-row GEMV fallback that the rowgemv fixture pins."""
+    import ctypes
+    assert orc.cute_refused(128, 256, 512)
+    assert orc.cute_refused(4096, 4096, 4096)
+    assert not orc.cute_refused(3, 64, 96)      # the rowgemv fixture's shape
+    assert not orc.cute_refused(1, 128, 128)    # M == 1 is the GEMV
+    assert not orc.cute_refused(128, 100, 64)
+    if not orc.REF_CUTE.exists():
+        pytest.skip("libref_cute.so not built")
+    raw = ctypes.CDLL(str(orc.REF_CUTE), mode=os.RTLD_LOCAL | os.RTLD_NOW)
+    assert not hasattr(raw, "ref_gemm_cute")
+    raw.ref_matmul.restype = ctypes.c_int
+    raw.ref_matmul.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3
+    # null pointers: the refusal returns before anything touches them or the GPU
+    assert raw.ref_matmul(None, None, None, 128, 256, 512) == orc.REF_REFUSED_CUTE
+    rk = orc.RefKernels(cute=True)
+    assert not hasattr(rk, "gemm_cute")
+    with pytest.raises(ValueError, match="CuTe"):
+        rk.matmul(0, 0, 0, 256, 128, 64)

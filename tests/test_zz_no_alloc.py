@@ -68,3 +68,53 @@ def test_static_scratch_matches_caller_scratch_on_two_calls():
     finally:
         torch.cuda.synchronize()
         comm.close()
+
+
+_CAPTURE_PROBE = r"""
+import ctypes, sys, torch
+sys.path.insert(0, sys.argv[1])
+from orininfer_b200 import _lib, tp
+dev = torch.device("cuda", 0)
+torch.cuda.set_device(dev)
+comm = tp.TPComm(0, 1, 0, tp.TPComm.unique_id(), timeout_s=30.0)
+M, N, K = 16, 256, 128
+x = torch.randn(M, K, device=dev).half()
+w = (torch.randn(N, K, device=dev) * 0.02).half()
+out = torch.empty(M, N, device=dev, dtype=torch.float16)
+args = lambda s: (comm._h, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(x.data_ptr()),
+                  ctypes.c_void_p(w.data_ptr()), M, N, K, 0, None, ctypes.c_void_p(s.cuda_stream))
+s = torch.cuda.Stream()
+g = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g, stream=s):
+    st = _lib.lib.orin_tp_linear_row_static(*args(s))
+msg = _lib.lib.orin_last_error()
+assert st == _lib.ERR_INVALID_ARG, (st, msg)
+assert b"stream-captured" in (msg if isinstance(msg, bytes) else str(msg).encode()), msg
+# outside capture the look-up succeeds and the call computes
+with torch.cuda.stream(s):
+    st = _lib.lib.orin_tp_linear_row_static(*args(s))
+assert st == _lib.OK, _lib.lib.orin_last_error()
+comm.wait()
+ref = torch.nn.functional.linear(x.float(), w.float())
+assert (out.float() - ref).abs().max().item() < 2e-2
+torch.cuda.synchronize()
+del g
+comm.close()
+print("CAPTURE_PROBE_OK")
+"""
+
+
+@pytest.mark.gpu
+def test_first_static_call_under_capture_is_refused():
+    """The first call on a device looks the array's address up, which may load
+    the module; made inside stream capture it would break the capture, so it is
+    refused with ORIN_ERR_INVALID_ARG and a message, and the next uncaptured
+    call works.  Runs in a fresh process, where no earlier call did the
+    look-up."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _CAPTURE_PROBE, root], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and "CAPTURE_PROBE_OK" in r.stdout, r.stdout + r.stderr
