@@ -226,6 +226,23 @@ orin_status orin_qkv_rope_append(void* q_out, const void* qkv, const void* q_nor
                                  float theta, int n_sink, int window_size,
                                  int dtype, void* stream);
 
+/*
+ * orin_qkv_rope_append for `batch` sequences of seq_len tokens each at the
+ * same positions (batched decode; no counterpart in the single-sequence
+ * reference): qkv and q_out rows are [batch][seq_len]; sequence b's K/V go
+ * into the pools at k_pool / v_pool + b * pool_stride elements
+ * (pool_stride >= (n_sink + window_size) * num_kv_heads * head_dim).  Each
+ * sequence's results are those of its own orin_qkv_rope_append call.
+ */
+orin_status orin_qkv_rope_append_batch(void* q_out, const void* qkv,
+                                       const void* q_norm, const void* k_norm,
+                                       void* k_pool, void* v_pool, int batch,
+                                       long long pool_stride, int seq_len,
+                                       int start_pos, int num_heads,
+                                       int num_kv_heads, int head_dim, float eps,
+                                       float theta, int n_sink, int window_size,
+                                       int dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sink + sliding-window GQA attention over the ring KV pool (the callers of */
 /* the linear layers on either side: q/k/v come from the q/k/v projection,   */
@@ -274,6 +291,26 @@ orin_status orin_attention_workspace_bytes(size_t* bytes, int seq_len,
                                            int cache_len, int num_heads,
                                            int num_kv_heads, int head_dim,
                                            int n_sink, int window_size);
+
+/*
+ * orin_attention over `batch` independent sequences in one launch (batched
+ * decode; the reference's engine is single-sequence, include/kv_cache.h:7, so
+ * this has no counterpart there).  Every sequence has seq_len new tokens at
+ * the same positions (cache_len); q and out hold [batch][seq_len][num_heads]
+ * [head_dim]; sequence b's pools start pool_stride elements after sequence
+ * b-1's (pool_stride >= (n_sink + window_size) * num_kv_heads * head_dim,
+ * a multiple of 8).  Each sequence is computed exactly as its own
+ * orin_attention call would be (same key splits, same summation order), so
+ * its output is bit-identical to that call's; the workspace for that is batch
+ * times orin_attention_workspace_bytes (a smaller one splits less).
+ */
+orin_status orin_attention_batch(void* out, const void* q, const void* k_pool,
+                                 const void* v_pool, int batch, long long pool_stride,
+                                 int seq_len, int cache_len, int num_heads,
+                                 int num_kv_heads, int head_dim, float scale,
+                                 int n_sink, int window_size, int dtype,
+                                 void* workspace, size_t workspace_bytes,
+                                 void* stream);
 
 /*
  * Synchronise stream and report device-side failures of this library's

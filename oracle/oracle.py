@@ -399,9 +399,10 @@ class RefKernels:
         L.ref_rmsnorm.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_float]
         L.ref_rope.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float]
         L.ref_embedding.argtypes = [_vp, _vp, _vp, _i, _i]
+        L.ref_argmax.argtypes = [_vp, _vp, _i]
         for n in ("ref_matmul", "ref_fused_silu_mul", "ref_add",
                   "ref_bf16_to_fp32", "ref_attention", "ref_rmsnorm", "ref_rope",
-                  "ref_embedding", "ref_sync"):
+                  "ref_embedding", "ref_argmax", "ref_sync"):
             getattr(L, n).restype = _i
 
     def _ok(self, rc: int, what: str) -> None:
@@ -444,6 +445,9 @@ class RefKernels:
 
     def embedding(self, out: int, table: int, ids: int, seq_len: int, hidden: int) -> None:
         self._ok(self.lib.ref_embedding(out, table, ids, seq_len, hidden), "kernels::embedding")
+
+    def argmax(self, out: int, logits: int, n: int) -> None:
+        self._ok(self.lib.ref_argmax(out, logits, n), "kernels::argmax")
 
     def sync(self) -> None:
         self._ok(self.lib.ref_sync(), "cudaDeviceSynchronize")

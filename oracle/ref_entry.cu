@@ -81,6 +81,12 @@ int ref_embedding(void* out, const void* table, const int* ids, int seq_len, int
   return static_cast<int>(cudaGetLastError());
 }
 
+// kernels::argmax: the greedy sampler (one CTA of 512 threads, kernels/softmax.cu:52-73).
+int ref_argmax(int* out, const float* logits, int n) {
+  kernels::argmax(reinterpret_cast<int32_t*>(out), logits, n);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int ref_sync(void) { return static_cast<int>(cudaDeviceSynchronize()); }
 
 }  // extern "C"

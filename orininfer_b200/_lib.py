@@ -75,6 +75,10 @@ SIGNATURES = {
     "orin_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _i, _i, _i,
                             _vp, _sz, _vp]),
     "orin_attention_workspace_bytes": (_i, [ctypes.POINTER(_sz), _i, _i, _i, _i, _i, _i, _i]),
+    "orin_attention_batch": (_i, [_vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i, _i,
+                                  ctypes.c_float, _i, _i, _i, _vp, _sz, _vp]),
+    "orin_qkv_rope_append_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i,
+                                        _i, ctypes.c_float, ctypes.c_float, _i, _i, _i, _vp]),
     "orin_device_check": (_i, [_vp]),
     "orin_tp_unique_id": (_i, [_vp]),
     "orin_tp_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i, _i, ctypes.c_double]),

@@ -426,6 +426,45 @@ orin_status orin_attention(void* out, const void* q, const void* k_pool, const v
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention");
 }
 
+orin_status orin_attention_batch(void* out, const void* q, const void* k_pool, const void* v_pool,
+                                 int batch, long long pool_stride, int seq_len, int cache_len,
+                                 int num_heads, int num_kv_heads, int head_dim, float scale,
+                                 int n_sink, int window_size, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  st = check_attention("orin_attention_batch", seq_len, cache_len, num_heads, num_kv_heads,
+                       head_dim, n_sink, window_size);
+  if (st != ORIN_OK) return st;
+  const long long pool_elems =
+      (static_cast<long long>(n_sink) + window_size) * num_kv_heads * head_dim;
+  if (batch < 0 || (batch > 1 && pool_stride < pool_elems)) {
+    set_error("orin_attention_batch: batch %d, pool_stride %lld (at least one pool, %lld "
+              "elements, apart)", batch, pool_stride, pool_elems);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (seq_len == 0 || batch == 0) return ORIN_OK;
+  if (!out || !q || !k_pool || !v_pool) {
+    set_error("orin_attention_batch: null pointer");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (!aligned16(out) || !aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) ||
+      (workspace && !aligned16(workspace)) || (pool_stride * 2) % 16 != 0) {
+    set_error("orin_attention_batch: out, q, the pools, the pool stride and the workspace must "
+              "be 16-byte aligned");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  if (static_cast<long long>(num_kv_heads) * batch > 65535) {
+    set_error("orin_attention_batch: batch * num_kv_heads above 65535");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
+                                   num_kv_heads, head_dim, scale, n_sink, window_size, dtype,
+                                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                                   batch, pool_stride);
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention_batch");
+}
+
 orin_status orin_kv_append(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
                            int seq_len, int start_pos, int n_sink, int window_size, int kv_dim,
                            int dtype, void* stream) {
@@ -527,6 +566,53 @@ orin_status orin_qkv_rope_append(void* q_out, const void* qkv, const void* q_nor
                                          n_sink, window_size, dtype,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_qkv_rope_append");
+}
+
+orin_status orin_qkv_rope_append_batch(void* q_out, const void* qkv, const void* q_norm,
+                                       const void* k_norm, void* k_pool, void* v_pool, int batch,
+                                       long long pool_stride, int seq_len, int start_pos,
+                                       int num_heads, int num_kv_heads, int head_dim, float eps,
+                                       float theta, int n_sink, int window_size, int dtype,
+                                       void* stream) {
+  const long long pool_elems =
+      (static_cast<long long>(n_sink) + window_size) * num_kv_heads * head_dim;
+  if (batch < 0 || (batch > 1 && pool_stride < pool_elems)) {
+    set_error("orin_qkv_rope_append_batch: batch %d, pool_stride %lld (at least one pool, %lld "
+              "elements, apart)", batch, pool_stride, pool_elems);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (batch == 0) return ORIN_OK;
+  if (batch == 1)
+    return orin_qkv_rope_append(q_out, qkv, q_norm, k_norm, k_pool, v_pool, seq_len, start_pos,
+                                num_heads, num_kv_heads, head_dim, eps, theta, n_sink,
+                                window_size, dtype, stream);
+  // the single-sequence checks hold for every sequence of the batch
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  if (seq_len < 0 || start_pos < 0 || num_heads < 1 || num_kv_heads < 1 ||
+      num_heads % num_kv_heads != 0 || n_sink < 0 || window_size < 1 ||
+      (seq_len > 0 && (!q_out || !qkv || !k_pool || !v_pool)) ||
+      (q_norm == nullptr) != (k_norm == nullptr)) {
+    set_error("orin_qkv_rope_append_batch: null pointer or bad size (seq_len=%d start_pos=%d "
+              "heads=%d/%d n_sink=%d window=%d; q_norm and k_norm both or neither)",
+              seq_len, start_pos, num_heads, num_kv_heads, n_sink, window_size);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (static_cast<long long>(seq_len) > static_cast<long long>(n_sink) + window_size ||
+      static_cast<long long>(start_pos) + seq_len > 0x7fffffffLL) {
+    set_error("orin_qkv_rope_append_batch: seq_len %d exceeds n_sink + window_size, or "
+              "positions past 2^31", seq_len);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  if (head_dim != 64 && head_dim != 128) {
+    set_error("orin_qkv_rope_append_batch: head_dim %d (64 and 128 are built)", head_dim);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_qkv_rope_append(q_out, qkv, q_norm, k_norm, k_pool, v_pool, seq_len,
+                                         start_pos, num_heads, num_kv_heads, head_dim, eps, theta,
+                                         n_sink, window_size, dtype,
+                                         static_cast<cudaStream_t>(stream), batch, pool_stride);
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_qkv_rope_append_batch");
 }
 
 orin_status orin_device_check(void* stream) {

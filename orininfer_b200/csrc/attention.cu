@@ -49,6 +49,8 @@ struct AttnParams {
   int tpb;     // tokens per row block
   int hsb;     // row blocks per (token block, group) when G > rows per block
   int splits;  // key splits (grid z)
+  int batch;   // sequences (grid y = batch * num_kv_heads); rows [batch][seq_len][heads]
+  long long pool_stride;  // elements from one sequence's pools to the next
 };
 
 // Pool slot of logical position p (src/kv_cache.cu:29-31).
@@ -160,7 +162,8 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int g = lane >> 2, q4 = lane & 3;
   const int rw = warp % RW, kw = warp / RW;
 
-  const int kvh = blockIdx.y;
+  const int kvh = blockIdx.y % p.num_kv_heads;
+  const int bseq = blockIdx.y / p.num_kv_heads;  // sequence of this CTA
   const int tb = blockIdx.x / p.hsb, hs = blockIdx.x % p.hsb;
   const int t_lo = tb * p.tpb;
   int t_hi = t_lo + p.tpb - 1;
@@ -185,8 +188,10 @@ __global__ void __launch_bounds__(kAttnThreads)
     ap[i] = base + tok[i];
   }
 
-  const uint16_t* kpool = static_cast<const uint16_t*>(p.k_pool);
-  const uint16_t* vpool = static_cast<const uint16_t*>(p.v_pool);
+  const uint16_t* kpool = static_cast<const uint16_t*>(p.k_pool) + bseq * p.pool_stride;
+  const uint16_t* vpool = static_cast<const uint16_t*>(p.v_pool) + bseq * p.pool_stride;
+  // this sequence's first q / out row
+  const size_t row_base = static_cast<size_t>(bseq) * p.seq_len * p.num_heads;
   // stage s: K at 2 s, V at 2 s + 1 (in units of one staged tile)
   auto sK = [&](int stage) { return attn_smem + (2 * stage) * attn_stage_elems<HD>(); };
   auto sV = [&](int stage) { return attn_smem + (2 * stage + 1) * attn_stage_elems<HD>(); };
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   // Q fragments of the two rows, straight from global memory.
   uint32_t qa[KS][4];
   {
-    const uint16_t* qb = static_cast<const uint16_t*>(p.q);
+    const uint16_t* qb = static_cast<const uint16_t*>(p.q) + row_base * HD;
     const uint16_t* q0 =
         rv[0] ? qb + (static_cast<size_t>(tok[0]) * p.num_heads + head[0]) * HD : nullptr;
     const uint16_t* q1 =
@@ -360,13 +365,13 @@ __global__ void __launch_bounds__(kAttnThreads)
 
   // Merge the KW partials of each row; write the row (one split) or this
   // split's partial.
-  const int rows_total = p.seq_len * p.num_heads;
+  const int rows_total = p.batch * p.seq_len * p.num_heads;
   for (int idx = tid; idx < R * (HD / 2); idx += kAttnThreads) {
     const int r = idx / (HD / 2), d = (idx % (HD / 2)) * 2;
     const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
     const int tk = t_lo + tr;
     if (!(tr < p.tpb && tk < p.seq_len && hr < p.group)) continue;
-    const int orow = tk * p.num_heads + kvh * p.group + hr;
+    const int orow = static_cast<int>(row_base) + tk * p.num_heads + kvh * p.group + hr;
     float m = -INFINITY;
 #pragma unroll
     for (int w = 0; w < KW; ++w) m = fmaxf(m, s_m[w * R + r]);
@@ -473,8 +478,8 @@ cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  return launch_pdl_smem(kern, dim3(row_blocks, p.num_kv_heads, p.splits), dim3(kAttnThreads),
-                         smem, s, p);
+  return launch_pdl_smem(kern, dim3(row_blocks, p.num_kv_heads * p.batch, p.splits),
+                         dim3(kAttnThreads), smem, s, p);
 }
 
 template <int DT, int HD>
@@ -482,7 +487,7 @@ cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStrea
   cudaError_t e = rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
                           : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
   if (e != cudaSuccess || p.splits == 1) return e;
-  const int rows_total = p.seq_len * p.num_heads;
+  const int rows_total = p.batch * p.seq_len * p.num_heads;
   return launch_pdl_smem(attn_combine_kernel<DT, HD>, dim3((rows_total + 3) / 4), dim3(128), 0,
                          s, p.out, static_cast<const float*>(p.ws), rows_total, p.splits);
 }
@@ -528,11 +533,15 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
 cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
-                             void* workspace, size_t workspace_bytes, cudaStream_t s) {
-  if (seq_len <= 0) return cudaSuccess;
+                             void* workspace, size_t workspace_bytes, cudaStream_t s, int batch,
+                             long long pool_stride) {
+  if (seq_len <= 0 || batch <= 0) return cudaSuccess;
+  // each sequence plans alone, on its share of the workspace
   const AttnPlan pl = plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim,
-                                     n_sink, window, workspace ? workspace_bytes : 0);
-  if (pl.row_blocks > 0x7fffffffLL || num_kv_heads > 65535) return cudaErrorInvalidConfiguration;
+                                     n_sink, window, workspace ? workspace_bytes / batch : 0);
+  if (pl.row_blocks > 0x7fffffffLL || static_cast<long long>(num_kv_heads) * batch > 65535 ||
+      static_cast<long long>(batch) * seq_len * num_heads > 0x7fffffffLL)
+    return cudaErrorInvalidConfiguration;
   AttnParams p;
   p.out = out;
   p.q = q;
@@ -551,6 +560,8 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
   p.tpb = pl.tpb;
   p.hsb = pl.hsb;
   p.splits = pl.splits;
+  p.batch = batch;
+  p.pool_stride = pool_stride;
   const int rb = static_cast<int>(pl.row_blocks);
   if (dtype == DT_F16)
     return head_dim == 64 ? attn_dispatch<DT_F16, 64>(p, pl.rw, rb, s)

@@ -146,7 +146,8 @@ __global__ void __launch_bounds__(256)
                            const typename Elem<DT>::T* q_norm, const typename Elem<DT>::T* k_norm,
                            typename Elem<DT>::T* k_pool, typename Elem<DT>::T* v_pool,
                            int seq_len, int start_pos, int num_heads, int num_kv_heads, float eps,
-                           float theta, int n_sink, int window) {
+                           float theta, int n_sink, int window, int batch,
+                           long long pool_stride) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int HALF = HD / 2;
@@ -155,13 +156,18 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int slots = num_heads + 2 * num_kv_heads;
-  if (wid >= static_cast<long long>(seq_len) * slots) return;
-  const int tok = static_cast<int>(wid / slots);
+  if (wid >= static_cast<long long>(batch) * seq_len * slots) return;
+  // row tg of the call = token tok of sequence b (sequences one after another)
+  const long long tg = wid / slots;
+  const int b = static_cast<int>(tg / seq_len);
+  const int tok = static_cast<int>(tg - static_cast<long long>(b) * seq_len);
   const int slot = static_cast<int>(wid % slots);
   const int pos = start_pos + tok;
+  k_pool += b * pool_stride;
+  v_pool += b * pool_stride;
   // a later token of this call that lands in the same ring slot owns it
   const bool pool_owner = !(pos >= n_sink && tok + window < seq_len);
-  const T* src = qkv + static_cast<size_t>(tok) * slots * HD + static_cast<size_t>(slot) * HD;
+  const T* src = qkv + static_cast<size_t>(tg) * slots * HD + static_cast<size_t>(slot) * HD;
   const size_t kv_dim = static_cast<size_t>(num_kv_heads) * HD;
   const size_t ring = static_cast<size_t>(pos < n_sink ? pos : n_sink + (pos - n_sink) % window);
 
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(256)
   }
   T* dst;
   if (is_q) {
-    dst = q_out + (static_cast<size_t>(tok) * num_heads + slot) * HD;
+    dst = q_out + (static_cast<size_t>(tg) * num_heads + slot) * HD;
   } else {
     if (!pool_owner) return;
     dst = k_pool + ring * kv_dim + static_cast<size_t>(slot - num_heads) * HD;
@@ -244,16 +250,18 @@ template <int DT, int HD>
 cudaError_t qkv_rope_append_t(void* q_out, const void* qkv, const void* q_norm,
                               const void* k_norm, void* k_pool, void* v_pool, int seq_len,
                               int start_pos, int num_heads, int num_kv_heads, float eps,
-                              float theta, int n_sink, int window, cudaStream_t s) {
+                              float theta, int n_sink, int window, int batch,
+                              long long pool_stride, cudaStream_t s) {
   using T = typename Elem<DT>::T;
-  const long long warps = static_cast<long long>(seq_len) * (num_heads + 2 * num_kv_heads);
+  const long long warps =
+      static_cast<long long>(batch) * seq_len * (num_heads + 2 * num_kv_heads);
   const long long blocks = (warps + 7) / 8;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   return launch_pdl_smem(qkv_rope_append_kernel<DT, HD>, dim3(static_cast<unsigned>(blocks)),
                          dim3(256), 0, s, static_cast<T*>(q_out), static_cast<const T*>(qkv),
                          static_cast<const T*>(q_norm), static_cast<const T*>(k_norm),
                          static_cast<T*>(k_pool), static_cast<T*>(v_pool), seq_len, start_pos,
-                         num_heads, num_kv_heads, eps, theta, n_sink, window);
+                         num_heads, num_kv_heads, eps, theta, n_sink, window, batch, pool_stride);
 }
 
 }  // namespace
@@ -289,11 +297,12 @@ cudaError_t launch_qkv_rope_append(void* q_out, const void* qkv, const void* q_n
                                    const void* k_norm, void* k_pool, void* v_pool, int seq_len,
                                    int start_pos, int num_heads, int num_kv_heads, int head_dim,
                                    float eps, float theta, int n_sink, int window, int dtype,
-                                   cudaStream_t s) {
-  if (seq_len <= 0) return cudaSuccess;
+                                   cudaStream_t s, int batch, long long pool_stride) {
+  if (seq_len <= 0 || batch <= 0) return cudaSuccess;
 #define ORIN_QKV_ROPE(DTV, HDV)                                                               \
   qkv_rope_append_t<DTV, HDV>(q_out, qkv, q_norm, k_norm, k_pool, v_pool, seq_len, start_pos, \
-                              num_heads, num_kv_heads, eps, theta, n_sink, window, s)
+                              num_heads, num_kv_heads, eps, theta, n_sink, window, batch,      \
+                              pool_stride, s)
   if (dtype == DT_F16) return head_dim == 64 ? ORIN_QKV_ROPE(DT_F16, 64) : ORIN_QKV_ROPE(DT_F16, 128);
   return head_dim == 64 ? ORIN_QKV_ROPE(DT_BF16, 64) : ORIN_QKV_ROPE(DT_BF16, 128);
 #undef ORIN_QKV_ROPE

@@ -99,10 +99,16 @@ struct AttnPlan {
 };
 AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
                         int head_dim, int n_sink, int window, size_t workspace_bytes);
+// `batch` sequences of seq_len tokens each, all at the same positions: q/out
+// rows [batch][seq_len][num_heads][head_dim], sequence b's pools at
+// k_pool/v_pool + b * pool_stride elements.  Every sequence gets the plan a
+// single-sequence call would (the workspace is divided among them), so each
+// sequence's result is bit-identical to its own batch-1 call.
 cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
-                             void* workspace, size_t workspace_bytes, cudaStream_t s);
+                             void* workspace, size_t workspace_bytes, cudaStream_t s,
+                             int batch = 1, long long pool_stride = 0);
 cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
                               int seq_len, int start_pos, int n_sink, int window, int kv_dim,
                               cudaStream_t s);
@@ -119,7 +125,7 @@ cudaError_t launch_qkv_rope_append(void* q_out, const void* qkv, const void* q_n
                                    const void* k_norm, void* k_pool, void* v_pool, int seq_len,
                                    int start_pos, int num_heads, int num_kv_heads, int head_dim,
                                    float eps, float theta, int n_sink, int window, int dtype,
-                                   cudaStream_t s);
+                                   cudaStream_t s, int batch = 1, long long pool_stride = 0);
 
 // Row-parallel reduction over peer memory (csrc/tp_p2p.cu).  Each rank's
 // shared region starts with a flag block of ints written by the peers, one

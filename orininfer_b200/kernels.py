@@ -55,7 +55,7 @@ __all__ = [
     "OrinError", "matmul", "fused_silu_mul", "add", "bf16_to_fp32", "linear", "linear_into",
     "pack_gate_up", "device_check", "plan_info", "lm_head_argmax", "attention",
     "attention_workspace_bytes", "kv_append", "rmsnorm", "rope", "qkv_rope_append",
-    "embedding", "linear_rmsnorm",
+    "embedding", "linear_rmsnorm", "attention_batch", "qkv_rope_append_batch",
 ]
 
 
@@ -297,6 +297,53 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
                                   cache_len, num_heads, num_kv_heads, head_dim, float(scale),
                                   n_sink, window_size, _dtype_code(q), _ptr(workspace), ws_bytes,
                                   _stream(stream)))
+
+
+def attention_batch(out: torch.Tensor, q: torch.Tensor, k_pools: torch.Tensor,
+                    v_pools: torch.Tensor, seq_len: int, cache_len: int, num_heads: int,
+                    num_kv_heads: int, head_dim: int, scale: float, n_sink: int,
+                    window_size: int, *, workspace: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+    """attention() over a batch of independent sequences in one launch
+    (orin_attention_batch): q/out [batch, seq_len, num_heads, head_dim], pools
+    [batch, n_sink + window_size, num_kv_heads, head_dim]; each sequence's
+    result is bit-identical to its own attention() call."""
+    _need_cuda(out, q, k_pools, v_pools, workspace)
+    if len({out.dtype, q.dtype, k_pools.dtype, v_pools.dtype}) != 1:
+        raise ValueError("out, q and the pools must share one dtype")
+    batch = k_pools.shape[0]
+    if v_pools.shape != k_pools.shape or k_pools.stride(0) != v_pools.stride(0):
+        raise ValueError("k_pools and v_pools must have one shape and stride")
+    if workspace is None:
+        need = batch * attention_workspace_bytes(seq_len, cache_len, num_heads, num_kv_heads,
+                                                 head_dim, n_sink, window_size)
+        if need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(_lib.lib.orin_attention_batch(_ptr(out), _ptr(q), _ptr(k_pools), _ptr(v_pools), batch,
+                                        k_pools.stride(0), seq_len, cache_len, num_heads,
+                                        num_kv_heads, head_dim, float(scale), n_sink, window_size,
+                                        _dtype_code(q), _ptr(workspace), ws_bytes,
+                                        _stream(stream)))
+
+
+def qkv_rope_append_batch(q_out: torch.Tensor, qkv: torch.Tensor, k_pools: torch.Tensor,
+                          v_pools: torch.Tensor, seq_len: int, start_pos: int, num_heads: int,
+                          num_kv_heads: int, head_dim: int, theta: float, n_sink: int,
+                          window_size: int, *, q_norm: Optional[torch.Tensor] = None,
+                          k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                          stream: Optional[torch.cuda.Stream] = None) -> None:
+    """qkv_rope_append() for a batch of sequences at the same positions
+    (orin_qkv_rope_append_batch): qkv/q_out rows [batch * seq_len], sequence
+    b's K/V into k_pools[b] / v_pools[b]."""
+    _need_cuda(q_out, qkv, k_pools, v_pools, q_norm, k_norm)
+    if v_pools.shape != k_pools.shape or k_pools.stride(0) != v_pools.stride(0):
+        raise ValueError("k_pools and v_pools must have one shape and stride")
+    check(_lib.lib.orin_qkv_rope_append_batch(
+        _ptr(q_out), _ptr(qkv), _ptr(q_norm), _ptr(k_norm), _ptr(k_pools), _ptr(v_pools),
+        k_pools.shape[0], k_pools.stride(0), seq_len, start_pos, num_heads, num_kv_heads,
+        head_dim, float(eps), float(theta), n_sink, window_size, _dtype_code(qkv),
+        _stream(stream)))
 
 
 def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,

@@ -47,11 +47,15 @@ def prefill_chunks(prompt_len: int, chunk: int) -> list[tuple[int, int]]:
 class DecoderLayer:
     """One layer; `w` from weights.layer_for_device, `cfg` the model's
     config.json keys.  qk_norm applies q_norm / k_norm (Qwen3; the reference
-    always does); Llama-family models (TinyLlama) have none."""
+    always does); Llama-family models (TinyLlama) have none.  With batch > 1
+    the layer keeps one pair of ring pools per sequence (k_pools / v_pools
+    [batch, n_sink + window, kv_dim]); forward(seq=b) runs sequence b alone
+    (prefill), forward_batch one decode token of every sequence in one pass."""
 
     def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, *, n_sink: int, window: int,
                  max_tokens: int, qk_norm: bool = False,
-                 workspace: Optional[torch.Tensor] = None, fold_norm: bool = False):
+                 workspace: Optional[torch.Tensor] = None, fold_norm: bool = False,
+                 batch: int = 1):
         self.w = dict(w)
         self.fold_norm = bool(fold_norm)
         self.nh = int(cfg["num_attention_heads"])
@@ -70,8 +74,13 @@ class DecoderLayer:
         qkv = self.w["qkv"]
         dev, dt = qkv.device, qkv.dtype
         QD, KVD = self.nh * self.hd, self.nkv * self.hd
-        self.k_pool = torch.zeros((self.n_sink + self.window, KVD), dtype=dt, device=dev)
-        self.v_pool = torch.zeros_like(self.k_pool)
+        if batch < 1:
+            raise ValueError("batch must be >= 1")
+        self.batch = int(batch)
+        self.k_pools = torch.zeros((self.batch, self.n_sink + self.window, KVD), dtype=dt,
+                                   device=dev)
+        self.v_pools = torch.zeros_like(self.k_pools)
+        self.k_pool, self.v_pool = self.k_pools[0], self.v_pools[0]
         self.xn = torch.empty((max_tokens, self.H), dtype=dt, device=dev)
         self.qkv = torch.empty((max_tokens, QD + 2 * KVD), dtype=dt, device=dev)
         self.q = torch.empty((max_tokens, QD), dtype=dt, device=dev)
@@ -81,23 +90,26 @@ class DecoderLayer:
         self.workspace = workspace
 
     @staticmethod
-    def workspace_bytes(cfg: Mapping, n_sink: int, window: int) -> int:
-        """Split-key workspace a decode step needs (shareable by all layers)."""
+    def workspace_bytes(cfg: Mapping, n_sink: int, window: int, batch: int = 1) -> int:
+        """Split-key workspace a decode step of `batch` sequences needs
+        (shareable by all layers)."""
         nh = int(cfg["num_attention_heads"])
         hd = int(cfg.get("head_dim", cfg["hidden_size"] // nh))
-        return kernels.attention_workspace_bytes(1, n_sink + window + 64, nh,
-                                                 int(cfg["num_key_value_heads"]), hd, n_sink,
-                                                 window)
+        return batch * kernels.attention_workspace_bytes(1, n_sink + window + 64, nh,
+                                                         int(cfg["num_key_value_heads"]), hd,
+                                                         n_sink, window)
 
     # calls of at most this many tokens fold the norms into the weight stream
     FOLD_NORM_TOKENS = 16
 
     def forward(self, x: torch.Tensor, start_pos: int,
-                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
-        """x [seq_len, H] (the residual stream) is updated in place and returned."""
+                stream: Optional[torch.cuda.Stream] = None, seq: int = 0) -> torch.Tensor:
+        """x [seq_len, H] (the residual stream of sequence `seq`) is updated in
+        place and returned."""
         S = x.shape[0]
         w = self.w
-        xn, qkv, q, att, h = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S], self.h[:S]
+        xn, qkv, q, att = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S]
+        k_pool, v_pool = self.k_pools[seq], self.v_pools[seq]
         fold = self.fold_norm and S <= self.FOLD_NORM_TOKENS
         if fold:
             kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
@@ -105,14 +117,51 @@ class DecoderLayer:
         else:
             kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
             kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
-        kernels.qkv_rope_append(q, qkv, self.k_pool, self.v_pool, S, start_pos, self.nh, self.nkv,
+        kernels.qkv_rope_append(q, qkv, k_pool, v_pool, S, start_pos, self.nh, self.nkv,
                                 self.hd, self.theta, self.n_sink, self.window,
                                 q_norm=w.get("q_norm") if self.qk_norm else None,
                                 k_norm=w.get("k_norm") if self.qk_norm else None,
                                 eps=self.eps, stream=stream)
-        kernels.attention(att, q, self.k_pool, self.v_pool, S, start_pos + S, self.nh, self.nkv,
+        kernels.attention(att, q, k_pool, v_pool, S, start_pos + S, self.nh, self.nkv,
                           self.hd, self.scale, self.n_sink, self.window,
                           workspace=self.workspace, stream=stream)
+        return self._mlp_tail(x, att, S, fold, stream)
+
+    def forward_batch(self, x: torch.Tensor, start_pos: int,
+                      stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """One decode token of each of the `batch` sequences, all at start_pos:
+        x [batch, H] (row b = sequence b's residual stream) updated in place.
+        The projections run once over all rows (the weights are streamed once
+        per step, not once per sequence); RoPE + append and attention use each
+        sequence's own pools.  Row b's result is bit-identical to
+        forward(x[b:b+1], start_pos, seq=b)."""
+        B = x.shape[0]
+        if B != self.batch:
+            raise ValueError(f"forward_batch takes {self.batch} rows, got {B}")
+        w = self.w
+        xn, qkv, q, att = self.xn[:B], self.qkv[:B], self.q[:B], self.att[:B]
+        fold = self.fold_norm and B <= self.FOLD_NORM_TOKENS
+        if fold:
+            kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
+                                   stream=stream)
+        else:
+            kernels.rmsnorm(xn, x, w["input_layernorm"], B, self.H, self.eps, stream=stream)
+            kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+        kernels.qkv_rope_append_batch(q, qkv, self.k_pools, self.v_pools, 1, start_pos, self.nh,
+                                      self.nkv, self.hd, self.theta, self.n_sink, self.window,
+                                      q_norm=w.get("q_norm") if self.qk_norm else None,
+                                      k_norm=w.get("k_norm") if self.qk_norm else None,
+                                      eps=self.eps, stream=stream)
+        kernels.attention_batch(att, q, self.k_pools, self.v_pools, 1, start_pos + 1, self.nh,
+                                self.nkv, self.hd, self.scale, self.n_sink, self.window,
+                                workspace=self.workspace, stream=stream)
+        return self._mlp_tail(x, att, B, fold, stream)
+
+    def _mlp_tail(self, x: torch.Tensor, att: torch.Tensor, S: int, fold: bool,
+                  stream: Optional[torch.cuda.Stream]) -> torch.Tensor:
+        """o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual."""
+        w = self.w
+        xn, h = self.xn[:S], self.h[:S]
         kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x, stream=stream)
         if fold:
             kernels.linear_rmsnorm(h, x, w["gate_up"], w["post_attention_layernorm"], self.eps,
@@ -192,10 +241,13 @@ class Decoder:
 
     def __init__(self, tensors: Mapping[str, torch.Tensor], cfg: Mapping, device, *,
                  n_sink: int, window: int, max_tokens: int, qk_norm: bool = False,
-                 fold_norm: bool = False):
+                 fold_norm: bool = False, batch: int = 1):
         from .weights import layer_for_device
 
+        if max_tokens < batch:
+            raise ValueError("max_tokens must cover one decode row per sequence")
         self.fold_norm = bool(fold_norm)
+        self.batch = int(batch)
         self.cfg = dict(cfg)
         self.H = int(cfg["hidden_size"])
         self.eps = float(cfg["rms_norm_eps"])
@@ -203,18 +255,19 @@ class Decoder:
         self.final_norm = tensors["model.norm.weight"].to(device)
         self.lm_head = tensors["lm_head.weight"].to(device)
         dt = self.embed.dtype
-        ws = DecoderLayer.workspace_bytes(cfg, n_sink, window)
+        ws = DecoderLayer.workspace_bytes(cfg, n_sink, window, self.batch)
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
         self.layers = [
             DecoderLayer(layer_for_device(tensors, i, cfg, device), cfg, n_sink=n_sink,
                          window=window, max_tokens=max_tokens, qk_norm=qk_norm,
-                         workspace=self.workspace, fold_norm=fold_norm)
+                         workspace=self.workspace, fold_norm=fold_norm, batch=self.batch)
             for i in range(int(cfg["num_hidden_layers"]))
         ]
         self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
-        self.xn = torch.empty((1, self.H), dtype=dt, device=device)
-        self.keys = torch.empty(1, dtype=torch.int64, device=device)
-        self.token = torch.empty(1, dtype=torch.int32, device=device)
+        self.xn = torch.empty((self.batch, self.H), dtype=dt, device=device)
+        self.keys = torch.empty(self.batch, dtype=torch.int64, device=device)
+        self.tokens = torch.empty(self.batch, dtype=torch.int32, device=device)
+        self.token = self.tokens[:1]
 
     def generate(self, prompt: list[int], max_new_tokens: int,
                  eos_ids: tuple[int, ...] = ()) -> list[int]:
@@ -246,22 +299,93 @@ class Decoder:
         return out
 
     def step(self, token_ids: torch.Tensor, start_pos: int,
-             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
-        """token_ids int32 [seq_len] on the device -> next token id [1] (device)."""
+             stream: Optional[torch.cuda.Stream] = None, seq: int = 0) -> torch.Tensor:
+        """token_ids int32 [seq_len] of sequence `seq` on the device -> its next
+        token id [1] (device)."""
         S = token_ids.shape[0]
         x = self.x[:S]
         kernels.embedding(x, self.embed, token_ids, S, self.H, stream=stream)
         for layer in self.layers:
-            layer.forward(x, start_pos, stream=stream)
+            layer.forward(x, start_pos, stream=stream, seq=seq)
+        return self._head(x[S - 1:S], self.xn[:1], self.keys[:1], self.tokens[seq:seq + 1],
+                          stream)
+
+    def step_batch(self, token_ids: torch.Tensor, start_pos: int,
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """One decode step of every sequence: token_ids int32 [batch] (token b
+        of sequence b, all at position start_pos) -> next tokens [batch]
+        (device).  Each projection streams its weights once for the whole
+        batch; token b equals what step(token_ids[b:b+1], start_pos, seq=b)
+        gives."""
+        B = token_ids.shape[0]
+        if B != self.batch:
+            raise ValueError(f"step_batch takes {self.batch} tokens, got {B}")
+        x = self.x[:B]
+        kernels.embedding(x, self.embed, token_ids, B, self.H, stream=stream)
+        for layer in self.layers:
+            layer.forward_batch(x, start_pos, stream=stream)
+        return self._head(x, self.xn, self.keys, self.tokens, stream)
+
+    def _head(self, rows: torch.Tensor, xn: torch.Tensor, keys: torch.Tensor,
+              out: torch.Tensor, stream: Optional[torch.cuda.Stream]) -> torch.Tensor:
+        """Final RMSNorm and the greedy LM head of `rows` into `out`."""
+        n = rows.shape[0]
         if self.fold_norm:
-            kernels.lm_head_argmax(x[S - 1:S], self.lm_head, keys=self.keys, out=self.token,
+            kernels.lm_head_argmax(rows, self.lm_head, keys=keys, out=out,
                                    norm=self.final_norm, eps=self.eps, stream=stream)
         else:
-            kernels.rmsnorm(self.xn, x[S - 1:S], self.final_norm, 1, self.H, self.eps,
-                            stream=stream)
-            kernels.lm_head_argmax(self.xn, self.lm_head, keys=self.keys, out=self.token,
-                                   stream=stream)
-        return self.token
+            kernels.rmsnorm(xn, rows, self.final_norm, n, self.H, self.eps, stream=stream)
+            kernels.lm_head_argmax(xn, self.lm_head, keys=keys, out=out, stream=stream)
+        return out
+
+    def generate_batch(self, prompts: list[list[int]], max_new_tokens: int,
+                       eos_ids: tuple[int, ...] = ()) -> list[list[int]]:
+        """Greedy generation for `batch` prompts of one length: each prompt
+        prefilled on its own (the chunks of generate()), then one batched
+        decode step per token for all sequences together.  A sequence that
+        emits an end token stops there (its row keeps being computed until
+        every sequence has stopped, and what it computes is dropped).  Returns
+        the generated ids per sequence; self.stats holds the times (ms)."""
+        import time
+
+        if len(prompts) != self.batch:
+            raise ValueError(f"generate_batch takes {self.batch} prompts, got {len(prompts)}")
+        lens = {len(p) for p in prompts}
+        if len(lens) != 1 or 0 in lens:
+            raise ValueError("the prompts of one batch must be non-empty and of one length")
+        if max_new_tokens < 1:
+            return [[] for _ in prompts]
+        P = lens.pop()
+        dev = self.x.device
+        capacity = self.layers[0].n_sink + self.layers[0].window
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for b, prompt in enumerate(prompts):
+            ids = torch.tensor(prompt, dtype=torch.int32, device=dev)
+            for pos, n in prefill_chunks(P, min(capacity, self.x.shape[0])):
+                self.step(ids[pos:pos + n], pos, seq=b)
+        out = [[t] for t in self.tokens.tolist()]
+        t1 = time.perf_counter()
+        done = [o[-1] in eos_ids for o in out]
+        step_ids = torch.empty(self.batch, dtype=torch.int32, device=dev)
+        steps = 0
+        while len(out[0]) < max_new_tokens and not all(done):
+            step_ids.copy_(torch.tensor([o[-1] for o in out], dtype=torch.int32))
+            tok = self.step_batch(step_ids, P + len(out[0]) - 1).tolist()
+            steps += 1
+            for b in range(self.batch):
+                out[b].append(tok[b])
+                done[b] = done[b] or tok[b] in eos_ids
+        for b in range(self.batch):
+            for i, t in enumerate(out[b]):
+                if t in eos_ids:
+                    del out[b][i + 1:]
+                    break
+        t2 = time.perf_counter()
+        self.stats = {"prompt_tokens": P * self.batch, "prefill_ms": (t1 - t0) * 1e3,
+                      "decode_steps": steps, "generated_tokens": sum(map(len, out)),
+                      "decode_ms": (t2 - t1) * 1e3}
+        return out
 
 
 class TPDecoder(Decoder):

@@ -147,6 +147,39 @@ def test_attention_and_kv_append_reject_bad_arguments_on_host():
     assert L.orin_kv_append(16, 16, 16, 16, 0, 0, 4, 1024, 256, 0, None) == _lib.OK
 
 
+def test_batched_attention_and_append_reject_bad_arguments_on_host():
+    """The batched decode entry points check the pool stride (at least one
+    pool apart) and the single-sequence arguments before any device work."""
+    L = _lib.lib
+    f = ctypes.c_float(0.125)
+    pool = (4 + 1024) * 4 * 64
+
+    def att(batch=2, stride=pool, **kw):
+        a = dict(dict(out=16, q=16, k=16, v=16, S=1, C=10, nh=32, nkv=4, hd=64, ns=4, W=1024,
+                      dt=0), **kw)
+        return L.orin_attention_batch(a["out"], a["q"], a["k"], a["v"], batch, stride, a["S"],
+                                      a["C"], a["nh"], a["nkv"], a["hd"], f, a["ns"], a["W"],
+                                      a["dt"], None, 0, None)
+
+    assert att(stride=pool - 8) == _lib.ERR_INVALID_ARG     # pools would overlap
+    assert att(batch=-1) == _lib.ERR_INVALID_ARG
+    assert att(nkv=5) == _lib.ERR_INVALID_ARG
+    assert att(stride=pool + 4) == _lib.ERR_UNSUPPORTED     # stride not 16-byte aligned
+    assert att(batch=20000) == _lib.ERR_UNSUPPORTED         # grid y above 65535
+    assert att(batch=0) == _lib.OK
+
+    def app(batch=2, stride=pool, S=1, start=7, q_out=16):
+        return L.orin_qkv_rope_append_batch(q_out, 16, None, None, 16, 16, batch, stride, S,
+                                            start, 32, 4, 64, ctypes.c_float(1e-5),
+                                            ctypes.c_float(1e4), 4, 1024, 0, None)
+
+    assert app(stride=pool - 1) == _lib.ERR_INVALID_ARG
+    assert app(S=1029) == _lib.ERR_INVALID_ARG              # more than n_sink + window
+    assert app(start=-1) == _lib.ERR_INVALID_ARG
+    assert app(q_out=0) == _lib.ERR_INVALID_ARG
+    assert app(batch=0) == _lib.OK
+
+
 def test_attention_workspace_plan():
     """Few-token calls split their keys across CTAs; prefill-sized calls don't.
     The split count for TinyLlama decode (32 heads over 4 KV heads, window

@@ -215,3 +215,51 @@ def test_attention_in_a_cuda_graph():
     torch.cuda.synchronize()
     r = O.attention(q, kp, vp, S, C, nh, nkv, hd, hd ** -0.5, ns, W, dt)
     check(out.cpu(), r, dt, "graph replay")
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("C,shape", [(1029, TINY), (2048 + 7, TINY), (300, LLAMA3), (3, TINY)])
+def test_attention_batch_equals_per_sequence_calls(dt, C, shape):
+    """orin_attention_batch over 5 sequences with their own pools: every
+    sequence's output bit-identical to its own orin_attention call (same key
+    splits and summation order), and within the bar of the oracle."""
+    B, ns, W = 5, 4, 1024
+    nh, nkv, hd = shape["nh"], shape["nkv"], shape["hd"]
+    rng = np.random.default_rng(77 + C)
+    q = [rand16(rng, (1, nh, hd), dt) for _ in range(B)]
+    kp = [rand16(rng, (ns + W, nkv, hd), dt) for _ in range(B)]
+    vp = [rand16(rng, (ns + W, nkv, hd), dt) for _ in range(B)]
+    qb = torch.stack([dev(a, dt) for a in q])
+    kb = torch.stack([dev(a, dt) for a in kp])
+    vb = torch.stack([dev(a, dt) for a in vp])
+    out = torch.empty((B, 1, nh, hd), dtype=TORCH_DT[dt], device="cuda")
+    K.attention_batch(out, qb, kb, vb, 1, C, nh, nkv, hd, hd ** -0.5, ns, W)
+    K.device_check()
+    for b in range(B):
+        single = ours(q[b], kp[b], vp[b], 1, C, nh, nkv, hd, ns, W, dt)
+        assert torch.equal(out[b].cpu().view(torch.int16), single.view(torch.int16)), b
+        r = O.attention(q[b], kp[b], vp[b], 1, C, nh, nkv, hd, hd ** -0.5, ns, W, dt)
+        check(out[b].cpu(), r, dt, f"batch seq {b}")
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+def test_qkv_rope_append_batch_equals_per_sequence_calls(dt):
+    """orin_qkv_rope_append_batch: 6 sequences' decode rows at one position,
+    each appended to its own pools; q rows and every pool bit-identical to
+    per-sequence orin_qkv_rope_append calls."""
+    B, nh, nkv, hd, ns, W, pos = 6, 32, 4, 64, 4, 1024, 1500
+    tdt = TORCH_DT[dt]
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn((B, (nh + 2 * nkv) * hd), generator=g).to(tdt).cuda()
+    kb = torch.randn((B, ns + W, nkv * hd), generator=g).to(tdt).cuda()
+    vb = torch.randn((B, ns + W, nkv * hd), generator=g).to(tdt).cuda()
+    k1, v1 = kb.clone(), vb.clone()
+    qo = torch.empty((B, nh * hd), dtype=tdt, device="cuda")
+    K.qkv_rope_append_batch(qo, qkv, kb, vb, 1, pos, nh, nkv, hd, 10000.0, ns, W)
+    q1 = torch.empty((1, nh * hd), dtype=tdt, device="cuda")
+    for b in range(B):
+        K.qkv_rope_append(q1, qkv[b:b + 1], k1[b], v1[b], 1, pos, nh, nkv, hd, 10000.0, ns, W)
+        assert torch.equal(qo[b:b + 1].view(torch.int16), q1.view(torch.int16)), b
+    K.device_check()
+    assert torch.equal(kb.view(torch.int16), k1.view(torch.int16))
+    assert torch.equal(vb.view(torch.int16), v1.view(torch.int16))
