@@ -247,6 +247,24 @@ def capture(step: Step, n: int, start: int = 0, events_per_step=None):
     return g
 
 
+_LIBCUDA = None
+
+
+def upload_graph(g) -> None:
+    """Upload an instantiated CUDA graph to the device (cuGraphUpload) on the
+    current stream, so that its first replay inside a timed region does not
+    pay the upload.  Nothing of the graph runs."""
+    global _LIBCUDA
+    if _LIBCUDA is None:
+        _LIBCUDA = ctypes.CDLL("libcuda.so.1")
+        _LIBCUDA.cuGraphUpload.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        _LIBCUDA.cuGraphUpload.restype = ctypes.c_int
+    rc = _LIBCUDA.cuGraphUpload(ctypes.c_void_p(g.raw_cuda_graph_exec()),
+                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc != 0:
+        raise RuntimeError(f"cuGraphUpload: CUresult {rc}")
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -273,6 +291,9 @@ def time_steps(step: Step, steps: int, warmup: int, world: int, dev_index: int):
     g_warm = capture(step, warmup) if warmup > 0 else None
     if g_warm is not None:
         g_warm.replay()
+    upload_graph(g)
+    if g_rem is not None:
+        upload_graph(g_rem)
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
@@ -537,6 +558,149 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
     return out
 
 
+def _graph_ms(fn, reps: int) -> float:
+    """Average ms of one call of fn, replayed `reps` times as one captured
+    CUDA graph (uploaded and warmed up first)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    upload_graph(g)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / reps
+
+
+def single_linear_m1(dev, reps: int) -> dict:
+    """Config 1: y = x . W^T with x [1, 2048], W [2048, 2048] fp16 (x ~ N(0,1),
+    W ~ N(0, 0.02^2)), fp32 accumulate, fp16 out.  One call streams 8.4 MB, about
+    1.3 us at the copy bandwidth, so 64 weight copies (537 MB, > 4x L2) rotate:
+    each call reads a W that is not in L2.  A captured graph of 64 calls is
+    replayed `reps` times; GB/s counts 2 (MK + NK + MN) bytes per call."""
+    import torch.nn.functional as F
+
+    import orininfer_b200 as ob
+
+    K_, N_, copies = 2048, 2048, 64
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    x = torch.randn((1, K_), generator=gen, device=dev).half()
+    Ws = [(torch.randn((N_, K_), generator=gen, device=dev) * 0.02).half()
+          for _ in range(copies)]
+    y = torch.empty((1, N_), dtype=torch.float16, device=dev)
+
+    def ours():
+        for W in Ws:
+            ob.linear_into(y, x, W)
+
+    def cublas():
+        for W in Ws:
+            F.linear(x, W, out=y)
+
+    per = 2 * (K_ + N_ * K_ + N_)
+    ms = _graph_ms(ours, reps) / copies
+    ob.device_check()
+    cms = _graph_ms(cublas, reps) / copies
+    peaks, _ = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    gbs = per / (ms / 1e3) / 1e9
+    out = {"workload": "single_linear_m1_2048x2048", "M": 1, "N": N_, "K": K_,
+           "bytes_per_call": per, "us_per_call": round(ms * 1e3, 3), "gbs": round(gbs, 1),
+           "hbm_frac": round(gbs / hbm, 4), "peak_hbm_gbs": hbm,
+           "cublas_us_per_call": round(cms * 1e3, 3),
+           "cublas_gbs": round(per / (cms / 1e3) / 1e9, 1),
+           "l2": f"{copies} rotating weight copies ({copies * N_ * K_ * 2 >> 20} MiB)",
+           "kernel": ob_plan(1, N_, K_, "none")}
+    del Ws
+    torch.cuda.empty_cache()
+    return out
+
+
+def llama3_decode(dev, reps: int) -> dict:
+    """Config 4 at decode: one Llama-3-8B-shaped layer's projections (q/k/v
+    6144x4096, o_proj 4096x4096 + residual, gate/up 28672x4096 + SwiGLU, down
+    4096x14336 + residual) and the LM head (128256x4096, fp32 logits) at M = 1
+    and 32 token rows, fp16, random-init weights (436 MB + 1050 MB, each far
+    above L2), one captured graph per M; next to torch.nn.functional.linear
+    (cuBLAS) with unfused epilogues.  GB/s = algorithmic bytes (weights once,
+    activations in and out) / time."""
+    import torch.nn.functional as F
+
+    import orininfer_b200 as ob
+
+    H_, IM_, V_ = L3_H, L3_IM, 128256
+    QKV_ = (L3_HEADS + 2 * L3_KV) * L3_HD
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(88)
+
+    def w(r, c):
+        return (torch.randn((r, c), generator=gen, device=dev) * 0.02).half()
+
+    Wqkv, Wo, Wgu, Wd, Wlm = w(QKV_, H_), w(H_, H_), w(2 * IM_, H_), w(H_, IM_), w(V_, H_)
+    w_layer = 2 * (QKV_ * H_ + H_ * H_ + 2 * IM_ * H_ + H_ * IM_)
+    w_head = 2 * V_ * H_
+    peaks, _ = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    out = {"workload": "llama3_8b_decode_layer_and_lm_head", "weight_bytes_layer": w_layer,
+           "weight_bytes_lm_head": w_head, "by_tokens": {}, "peak_hbm_gbs": hbm}
+    for m in (1, 32):
+        x = torch.randn((m, H_), generator=gen, device=dev).half()
+        attn = torch.randn((m, H_), generator=gen, device=dev).half()
+        h0 = torch.randn((m, H_), generator=gen, device=dev).half()
+        h = h0.clone()
+        qkv = torch.empty((m, QKV_), dtype=torch.float16, device=dev)
+        act = torch.empty((m, IM_), dtype=torch.float16, device=dev)
+        logits = torch.empty((m, V_), dtype=torch.float32, device=dev)
+
+        def ours():
+            h.copy_(h0)
+            ob.linear_into(qkv, x, Wqkv)
+            ob.linear_into(h, attn, Wo, epilogue="residual", residual=h)
+            ob.linear_into(act, x, Wgu, epilogue="swiglu")
+            ob.linear_into(h, act, Wd, epilogue="residual", residual=h)
+            ob.linear_into(logits, h, Wlm, epilogue="f32")
+
+        def cublas():
+            F.linear(x, Wqkv, out=qkv)
+            hh = h0 + F.linear(attn, Wo)
+            gu = F.linear(x, Wgu).view(m, IM_ // 64, 2, 64)
+            a_ = (F.silu(gu[:, :, 0].float()) * gu[:, :, 1].float()).half()
+            hh = hh + F.linear(a_.reshape(m, IM_), Wd)
+            logits.copy_(F.linear(hh, Wlm).float())
+
+        ms = _graph_ms(ours, reps)
+        ob.device_check()
+        cms = _graph_ms(cublas, reps)
+        a_bytes = 2 * m * (H_ + QKV_ + 4 * H_ + H_ + 2 * IM_ + H_) + 4 * m * V_
+        total = w_layer + w_head + a_bytes
+        gbs = total / (ms / 1e3) / 1e9
+        out["by_tokens"][str(m)] = {
+            "ms_per_step": round(ms, 4), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+            "cublas_ms_per_step": round(cms, 4),
+            "cublas_gbs": round(total / (cms / 1e3) / 1e9, 1),
+            "plans": {"qkv": ob_plan(m, QKV_, H_, "none"),
+                      "gate_up": ob_plan(m, IM_, H_, "swiglu"),
+                      "lm_head": ob_plan(m, V_, H_, "f32")}}
+        del x, attn, h0, h, qkv, act, logits
+    del Wqkv, Wo, Wgu, Wd, Wlm
+    torch.cuda.empty_cache()
+    return out
+
+
 L3_M, L3_H, L3_IM, L3_HEADS, L3_KV, L3_HD = 4096, 4096, 14336, 32, 8, 128
 L3_FLOPS = 2 * L3_M * ((L3_HEADS + 2 * L3_KV) * L3_HD * L3_H + L3_H * L3_H + 2 * L3_IM * L3_H
                        + L3_H * L3_IM)  # 1786.7 GFLOP
@@ -740,15 +904,19 @@ def run_ours(args, rank, world, local_rank):
             else None
         if args.decode_reps > 0:
             line["decode"] = decode_path(dev, args.decode_reps, args.cublas_bar)
+            line["single_linear_m1"] = single_linear_m1(dev, args.decode_reps)
+            line["llama3_decode"] = llama3_decode(dev, args.decode_reps)
         if args.model_decode_reps > 0:
             # the whole model's greedy decode step; reported beside the layer
             # line, which stands on its own if this part fails
-            try:
-                line["model_decode"] = run_model_decode(
-                    argparse.Namespace(model_decode=args.model_decode_reps, warmup=5))
-            except Exception as e:  # noqa: BLE001
-                line["model_decode"] = {"error": f"{type(e).__name__}: {e}"}
-            torch.cuda.empty_cache()
+            for key, batch in (("model_decode", 1), ("model_decode_b16", 16)):
+                try:
+                    line[key] = run_model_decode(
+                        argparse.Namespace(model_decode=args.model_decode_reps, warmup=5,
+                                           batch=batch))
+                except Exception as e:  # noqa: BLE001
+                    line[key] = {"error": f"{type(e).__name__}: {e}"}
+                torch.cuda.empty_cache()
     if args.llama3_reps > 0:
         line["llama3_tp"] = llama3_tp_layer(rank, world, dev, comm, args.llama3_reps)
     if comm is not None:
@@ -813,14 +981,15 @@ def run_one_kernel(args):
 def run_model_decode(args) -> dict:
     """Greedy generation through the whole model:
     a 22-layer TinyLlama-shaped model (seeded random-init fp16 weights made on
-    the device, 2.07 GB), sink + window KV cache (4 + 1024), a 2048-token prompt
-    prefilled in the reference's chunks of n_sink + W = 1028 and 1020 tokens,
-    then one decode step (embedding, 22 x the layer's eight launches + the
-    split-key combine, final norm, LM head + argmax, the token fed back on the
-    device)
-    captured in a CUDA graph at position 2048 (a full window) and replayed
-    `args.model_decode` times.  Every replay does a full step's work: the same
-    ring slot is rewritten and the same 1028 positions are attended."""
+    the device, 2.07 GB), sink + window KV cache (4 + 1024) per sequence,
+    `args.batch` (default 1) 2048-token prompts, each prefilled in the
+    reference's chunks of n_sink + W = 1028 and 1020 tokens, then one decode
+    step of all sequences (embedding, 22 x the layer's eight launches + the
+    split-key combine, final norm, LM head + argmax, the tokens fed back on
+    the device; the batch shares each weight stream) captured in a CUDA graph
+    at position 2048 (a full window) and replayed `args.model_decode` times.
+    Every replay does a full step's work: the same ring slot is rewritten and
+    the same 1028 positions are attended.  tokens/s = batch / step time."""
     from orininfer_b200 import weights as Wt
     from orininfer_b200.layer import Decoder
 
@@ -841,25 +1010,31 @@ def run_model_decode(args) -> dict:
         key = next(k for k in shape if k in name)
         tensors[name] = (torch.randn(shape[key], generator=gen, device=dev) * 0.02).half()
     n_sink, window = 4, 1024
-    model = Decoder(tensors, cfg, dev, n_sink=n_sink, window=window, max_tokens=n_sink + window)
+    B = int(getattr(args, "batch", 1))
+    model = Decoder(tensors, cfg, dev, n_sink=n_sink, window=window, max_tokens=n_sink + window,
+                    batch=B)
     del tensors
-    prompt = torch.randint(0, cfg["vocab_size"], (2048,), generator=gen, device=dev,
-                           dtype=torch.int32)
-    # prefill (eager launches), timed with events
+    prompts = [torch.randint(0, cfg["vocab_size"], (2048,), generator=gen, device=dev,
+                             dtype=torch.int32) for _ in range(B)]
+    # prefill of every sequence (eager launches), timed with events
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    model.step(prompt[:1028], 0)
-    model.step(prompt[1028:], 1028)
+    for seq, prompt in enumerate(prompts):
+        model.step(prompt[:1028], 0, seq=seq)
+        model.step(prompt[1028:], 1028, seq=seq)
     b.record()
     torch.cuda.synchronize()
     prefill_ms = a.elapsed_time(b)
-    ids = model.token.clone()
+    ids = model.tokens.clone()
     pos = 2048
 
     def decode():
-        model.step(ids, pos)
-        ids.copy_(model.token)
+        if B == 1:
+            model.step(ids, pos)
+        else:
+            model.step_batch(ids, pos)
+        ids.copy_(model.tokens)
 
     # eager step (host launch cost included)
     for _ in range(3):
@@ -895,21 +1070,24 @@ def run_model_decode(args) -> dict:
     kv_bytes = L * 2 * (n_sink + window) * KVD * 2
     peaks, _ = load_peaks()
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    kv_bytes *= B
     gbs = (w_bytes + kv_bytes) / (ms / 1e3) / 1e9
-    return {"metric": "greedy decode tokens/s, 22-layer TinyLlama, batch 1, 1028-position window",
-            "value": round(1e3 / ms, 1), "unit": "tokens/s", "ms_per_token": round(ms, 4),
-            "eager_ms_per_token": round(eager_ms, 4),
-            "prefill_ms_2048_tokens": round(prefill_ms, 3),
-            "prefill_tokens_per_s": round(2048 / (prefill_ms / 1e3), 1),
-            "bytes_per_token": w_bytes + kv_bytes, "gbs": round(gbs, 1),
+    return {"metric": f"greedy decode tokens/s, 22-layer TinyLlama, batch {B}, "
+                      "1028-position window",
+            "value": round(B * 1e3 / ms, 1), "unit": "tokens/s", "batch": B,
+            "ms_per_step": round(ms, 4), "ms_per_token": round(ms / B, 4),
+            "eager_ms_per_step": round(eager_ms, 4),
+            "prefill_ms_2048_tokens": round(prefill_ms / B, 3),
+            "prefill_tokens_per_s": round(B * 2048 / (prefill_ms / 1e3), 1),
+            "bytes_per_step": w_bytes + kv_bytes, "gbs": round(gbs, 1),
             "hbm_frac": round(gbs / hbm, 4), "peak_hbm_gbs": hbm,
             # per layer: norm, q/k/v, RoPE + append, attention, combine, o_proj,
             # norm, gate/up, down; then embedding, final norm, LM head (key
             # reset, weight stream, decode), token copy
-            "launches_per_token": L * 9 + 6, "steps": args.model_decode,
+            "launches_per_step": L * 9 + 6, "steps": args.model_decode,
             "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
             "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,
-                       "window": window, "prompt": 2048, "graph": True}}
+                       "window": window, "prompt": 2048, "batch": B, "graph": True}}
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -1012,6 +1190,9 @@ def main():
                     help="instead of the layer bench: time this many graph-replayed greedy "
                          "decode steps of the whole 22-layer model (prefill of a 2048-token "
                          "prompt first) and print that line")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="with --model-decode: sequences decoded together (per-sequence KV "
+                         "pools, one weight stream per step)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="with --kernel: token rows M of that projection (default: the "
                          "workload's 512; 1..64 is the decode GEMV / skinny path)")

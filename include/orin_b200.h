@@ -123,6 +123,35 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
                            int info[6]);
 
 /*
+ * orin_linear with a caller workspace (no counterpart in the reference, whose
+ * matmul takes none).  With a workspace of at least
+ * orin_linear_workspace_bytes() bytes, wide (prefill) problems may run a
+ * stream-K schedule: the tiles x K work is dealt to one CTA (pair) per SM in
+ * equal contiguous ranges, so no SM idles in a last partial wave; a CTA whose
+ * range starts inside a tile leaves that partial fp32 accumulator in the
+ * workspace and the CTA holding the tile's first k-blocks adds it (in a fixed
+ * order: deterministic) before its epilogue.  Same semantics and epilogues as
+ * orin_linear; without a workspace (NULL or too small) it is orin_linear.
+ * The workspace: 16-byte aligned device memory whose first 4 KB (flag words)
+ * are zero before its first use (cudaMemset once); every call leaves them
+ * zero again.  Calls that share a workspace must be ordered (one stream);
+ * after an ORIN_ERR_TIMEOUT from orin_device_check, zero it again.
+ */
+orin_status orin_linear_ws(void* C, const void* A, const void* W,
+                           int M, int N, int K, int dtype, int epilogue,
+                           const void* residual, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Workspace bytes that let orin_linear_ws choose any plan on the current
+ * device (one 128 x 256 fp32 slot per SM plus 4 KB of flags: 19 MB on B200). */
+orin_status orin_linear_workspace_bytes(size_t* bytes);
+
+/* orin_plan_info for orin_linear_ws with a workspace of workspace_bytes:
+ * info[0..5] as orin_plan_info, info[6] 1 for a stream-K schedule. */
+orin_status orin_plan_info_ws(int M, int N, int K, int dtype, int epilogue,
+                              int algo, size_t workspace_bytes, int info[7]);
+
+/*
  * Build the packed gate/up weight the SWIGLU epilogue reads:
  * rows [128g, 128g+64) = gate rows [64g, 64g+64), rows [128g+64, 128g+128) =
  * up rows [64g, 64g+64).  w_gate, w_up [IM, K] (include/weight_store.h:17-18);

@@ -8,7 +8,8 @@ import importlib
 
 __all__ = [
     "OrinError", "add", "bf16_to_fp32", "device_check", "fused_silu_mul", "linear",
-    "linear_into", "lm_head_argmax", "matmul", "pack_gate_up", "plan_info",
+    "linear_into", "lm_head_argmax", "matmul", "pack_gate_up", "plan_info", "linear_workspace",
+    "linear_workspace_bytes",
 ]
 __version__ = "0.1.0"
 

@@ -105,6 +105,10 @@ int choose_algo(int req, const void* A, const void* W, int M, int K) {
   return (M <= 64) ? 2 : 1;
 }
 
+orin_status linear_impl(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epilogue, const void* residual, int algo, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 }  // namespace
 
 extern "C" {
@@ -115,6 +119,42 @@ const char* orin_last_error(void) { return g_err; }
 
 orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                            int epilogue, const void* residual, int algo, void* stream) {
+  return linear_impl(C, A, W, M, N, K, dtype, epilogue, residual, algo, nullptr, 0, stream);
+}
+
+orin_status orin_linear_ws(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                           int epilogue, const void* residual, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (workspace && !aligned16(workspace)) {
+    set_error("orin_linear_ws: the workspace must be 16-byte aligned");
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  return linear_impl(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, workspace,
+                     workspace ? workspace_bytes : 0, stream);
+}
+
+orin_status orin_linear_workspace_bytes(size_t* bytes) {
+  if (!bytes) {
+    set_error("orin_linear_workspace_bytes: null output");
+    return ORIN_ERR_INVALID_ARG;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  *bytes = sk_workspace_max_bytes(sms);
+  return ORIN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+orin_status linear_impl(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
+                        int epilogue, const void* residual, int algo, void* workspace,
+                        size_t workspace_bytes, void* stream) {
   orin_status st = check_common(dtype, epilogue);
   if (st != ORIN_OK) return st;
   if (!C || !A || !W) {
@@ -176,7 +216,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
     return cuda_fail(e, "orin_linear: device set-up");
   }
   Plan pl;
-  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count);
+  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count, workspace_bytes);
   const size_t esz = (epilogue == ORIN_EPI_F32_OUT || epilogue == ORIN_EPI_F32_PARTIAL) ? 4 : 2;
   pl.p.C = C;
   pl.p.ldc = N;
@@ -185,7 +225,7 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   pl.p.vec_ok = aligned16(C) && ((N * esz) % 16 == 0) &&
                 (!residual || (aligned16(residual) && (N * 2) % 16 == 0));
   const char* why = nullptr;
-  e = launch_tc(pl, dtype, epilogue, A, W, ctx->err, s, &why);
+  e = launch_tc(pl, dtype, epilogue, A, W, ctx->err, s, &why, workspace);
   if (e != cudaSuccess) {
     if (why) {
       set_error("orin_linear: %s", why);
@@ -195,6 +235,10 @@ orin_status orin_linear_ex(void* C, const void* A, const void* W, int M, int N, 
   }
   return ORIN_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 orin_status orin_linear_rmsnorm(void* C, const void* A, const void* W, const void* norm_w,
                                 float eps, int M, int N, int K, int dtype, int epilogue,
@@ -247,6 +291,15 @@ orin_status orin_lm_head_argmax_rmsnorm(int* token, const void* h, const void* W
 }
 
 orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int algo, int info[6]) {
+  int full[7];
+  orin_status st = orin_plan_info_ws(M, N, K, dtype, epilogue, algo, 0, full);
+  if (st == ORIN_OK)
+    for (int i = 0; i < 6; ++i) info[i] = full[i];
+  return st;
+}
+
+orin_status orin_plan_info_ws(int M, int N, int K, int dtype, int epilogue, int algo,
+                              size_t workspace_bytes, int info[7]) {
   orin_status st = check_common(dtype, epilogue);
   if (st != ORIN_OK) return st;
   if (!info || M < 1 || N < 1 || K < 1) {
@@ -259,7 +312,7 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
     set_error("orin_plan_info: algo %d can't take M=%d K=%d", algo, M, K);
     return ORIN_ERR_UNSUPPORTED;
   }
-  for (int i = 0; i < 6; ++i) info[i] = 0;
+  for (int i = 0; i < 7; ++i) info[i] = 0;
   info[0] = a;
   if (a == 3) return ORIN_OK;
   if (a == 4) {
@@ -275,12 +328,13 @@ orin_status orin_plan_info(int M, int N, int K, int dtype, int epilogue, int alg
   DeviceCtx* ctx = device_ctx(dev, &e);
   if (!ctx) return cuda_fail(e, "orin_plan_info: device set-up");
   Plan pl;
-  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count);
+  plan_tc(pl, M, N, K, epilogue, a, ctx->sm_count, workspace_bytes);
   info[1] = pl.bn;
   info[2] = pl.pair;
   info[3] = pl.p.split;
   info[4] = pl.grid;
   info[5] = pl.p.tiles_p * pl.p.tiles_q;
+  info[6] = pl.p.sk;
   return ORIN_OK;
 }
 

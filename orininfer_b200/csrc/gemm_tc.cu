@@ -139,13 +139,36 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
+template <int GROUP>
+__device__ __forceinline__ int g_of_cta() {
+  return static_cast<int>(blockIdx.x) / GROUP;
+}
+
+// Stream-K range of CTA group g of G over W k-block pairs: [W g / G, W (g+1) / G).
+__device__ __forceinline__ long long sk_range_start(long long W, int g, int G) {
+  return W * g / G;
+}
+
 struct UnitIter {
   int tile, stride, tiles, k0, k1;
+  int kp;                // stream-K: k-block pairs per tile
+  long long cur, hi;     // stream-K: this group's remaining range of pairs
+  bool sk;
   // group: CTAs that share one tile's accumulator (2 for a CTA pair)
   __device__ __forceinline__ void init(const TcParams& p, int group) {
     const int kb = p.kb;
     tiles = p.tiles_p * p.tiles_q;
-    if (p.split == 1) {
+    sk = p.sk != 0;
+    if (sk) {
+      kp = kb / 2;
+      const long long W = static_cast<long long>(tiles) * kp;
+      const int G = gridDim.x / group, g = blockIdx.x / group;
+      cur = sk_range_start(W, g, G);
+      hi = sk_range_start(W, g + 1, G);
+      tile = 0;
+      stride = 0;
+      k0 = k1 = 0;
+    } else if (p.split == 1) {
       tile = blockIdx.x / group;
       stride = gridDim.x / group;
       k0 = 0;
@@ -161,6 +184,17 @@ struct UnitIter {
     }
   }
   __device__ __forceinline__ bool next(Unit& u) {
+    if (sk) {
+      if (cur >= hi) return false;
+      const int t = static_cast<int>(cur / kp);
+      const long long tile_end = static_cast<long long>(t + 1) * kp;
+      const long long e = hi < tile_end ? hi : tile_end;
+      u.tile = t;
+      u.k0 = 2 * static_cast<int>(cur - static_cast<long long>(t) * kp);
+      u.k1 = 2 * static_cast<int>(e - static_cast<long long>(t) * kp);
+      cur = e;
+      return true;
+    }
     if (tile >= tiles) return false;
     u.tile = tile;
     u.k0 = k0;
@@ -367,6 +401,105 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 }
 
 // ---------------------------------------------------------------------------
+// Stream-K partial accumulators
+// ---------------------------------------------------------------------------
+
+// A CTA's slot holds its kBM x BN fp32 partial accumulator as float4 columns
+// groups: float4 (c4, row) at index c4 * kBM + row, so that the 32 rows of a
+// warp touch 512 contiguous bytes per access (writer and reader alike).
+__device__ __forceinline__ int ld_acquire_gpu(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// Add the partial sums of `n` contributor slots (first at `slots`, then every
+// `stride` floats, in order) for columns [col, col + CNT) of this thread's
+// row to v.
+template <int CNT>
+__device__ __forceinline__ void sk_add(float* v, int col, int lr, const float* slots, int n,
+                                       long long stride) {
+  for (int j = 0; j < n; ++j) {
+    const float4* s = reinterpret_cast<const float4*>(slots + j * stride) + (col / 4) * kBM + lr;
+#pragma unroll
+    for (int i = 0; i < CNT / 4; ++i) {
+      const float4 t = __ldcg(s + i * kBM);
+      v[4 * i + 0] += t.x;
+      v[4 * i + 1] += t.y;
+      v[4 * i + 2] += t.z;
+      v[4 * i + 3] += t.w;
+    }
+  }
+}
+
+// Accumulator chunks from tensor memory plus stream-K partials.
+template <int CW>
+struct TmemChunksSk {
+  uint32_t taddr;
+  int lr;
+  const float* slots;
+  int n;
+  long long stride;
+  __device__ __forceinline__ void get(int col, float* v) const {
+    if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + col, v);
+    else tmem_ld_32x32b_x16(taddr + col, v);
+    sk_add<CW>(v, col, lr, slots, n, stride);
+  }
+};
+
+// Contributor: this CTA's partial accumulator (columns [0, BN) of its 128 rows)
+// into its slot, then its flag, released at GPU scope after every epilogue
+// thread's stores.
+template <int BN>
+__device__ __forceinline__ void sk_write_partial(const TcParams& p, uint32_t taddr, int lr,
+                                                 int et) {
+  float4* slot = reinterpret_cast<float4*>(p.sk_ws + static_cast<long long>(blockIdx.x) * kBM * BN) + lr;
+  float v[32];
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    tmem_ld_32x32b_x32(taddr + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      __stcg(slot + (c / 4 + i) * kBM, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+  }
+  __threadfence();
+  named_bar_sync(1, kEpiThreads);
+  if (et == 0) st_release_gpu(p.sk_flags + blockIdx.x, 1);
+}
+
+// Finisher: one thread waits (bounded) for the flags of the n contributor
+// CTAs first, first + stride, ...; the result reaches all 128 epilogue threads.
+__device__ __forceinline__ bool sk_wait(const int* flags, int first, int n, int stride, int et,
+                                        volatile int* abort_flag, int* err, volatile int* flag) {
+  if (et == 0) {
+    bool good = true;
+    const unsigned long long t0 = global_timer_ns();
+    for (int j = 0; j < n && good; ++j) {
+      while (ld_acquire_gpu(flags + first + j * stride) == 0) {
+        if (*abort_flag) {
+          good = false;
+          break;
+        }
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          *abort_flag = 1;
+          if (err) atomicCAS(err, 0, DEVERR_TIMEOUT_EPILOGUE);
+          good = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    *flag = good ? 1 : 0;
+  }
+  named_bar_sync(1, kEpiThreads);
+  __threadfence();
+  return *flag != 0;
+}
+
+// ---------------------------------------------------------------------------
 // Epilogue through TMA stores (wide tiles)
 // ---------------------------------------------------------------------------
 
@@ -413,7 +546,9 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
                                               int qcol0, int lr, int et, uint32_t outbuf,
                                               const void* tm_c, const void* tm_r,
                                               uint32_t res_bar, uint32_t& res_phase,
-                                              volatile int* abort_flag, volatile int* flag) {
+                                              volatile int* abort_flag, volatile int* flag,
+                                              const float* sk_slots, int sk_n,
+                                              long long sk_stride) {
   using E = Elem<DT>;
   constexpr bool F32 = (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL);
   constexpr int CH = F32 ? 32 : 64;  // output columns per 128-byte chunk
@@ -446,6 +581,7 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
       if constexpr (F32) {
         float v[32];
         tmem_ld_32x32b_x32(taddr + oc * 32, v);
+        sk_add<32>(v, oc * 32, lr, sk_slots, sk_n, sk_stride);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float o[4];
@@ -463,10 +599,13 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
             float u[32];
             tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
             tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
+            sk_add<32>(v, 128 * oc + 32 * h, lr, sk_slots, sk_n, sk_stride);
+            sk_add<32>(u, 128 * oc + 64 + 32 * h, lr, sk_slots, sk_n, sk_stride);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
           } else {
             tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
+            sk_add<32>(v, 64 * oc + 32 * h, lr, sk_slots, sk_n, sk_stride);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -1208,13 +1347,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       if (S == 1) {
         if constexpr (!SWAP) {
-          if (p.out_tma) {
-            ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, &tm_c, &tm_r,
-                                            smem_u32(&res_bar), res_phase, &abort_flag,
-                                            &epi_flag);
+          if (p.sk && u.k0 > 0) {
+            // stream-K: this group's range starts inside the tile; its part
+            // goes to the group that holds the tile's first k-blocks
+            sk_write_partial<BN>(p, taddr, lr, et);
           } else {
-            TmemChunks<CW> src{taddr};
-            emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
+            const float* sk_slots = nullptr;
+            int sk_n = 0;
+            long long sk_stride = 0;
+            if (p.sk && u.k1 < p.kb) {
+              // stream-K finisher: the contributors are the following groups
+              // whose ranges start inside this tile
+              const int G = static_cast<int>(gridDim.x) / GROUP;
+              const int g = static_cast<int>(blockIdx.x) / GROUP;
+              const long long W = static_cast<long long>(it.tiles) * it.kp;
+              const long long tile_end = static_cast<long long>(u.tile + 1) * it.kp;
+              while (g + 1 + sk_n < G && sk_range_start(W, g + 1 + sk_n, G) < tile_end) ++sk_n;
+              const long long slot_f = static_cast<long long>(kBM) * BN;
+              sk_slots = p.sk_ws + (static_cast<long long>(g + 1) * GROUP + half) * slot_f;
+              sk_stride = GROUP * slot_f;
+              ok = sk_wait(p.sk_flags, (g + 1) * GROUP + half, sk_n, GROUP, et, &abort_flag,
+                           p.err, &epi_flag);
+            }
+            if (ok) {
+              if (p.out_tma) {
+                ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, &tm_c,
+                                                &tm_r, smem_u32(&res_bar), res_phase,
+                                                &abort_flag, &epi_flag, sk_slots, sk_n,
+                                                sk_stride);
+              } else {
+                TmemChunksSk<CW> src{taddr, lr, sk_slots, sk_n, sk_stride};
+                emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
+              }
+            }
+            if (ok && sk_n > 0) {
+              // every thread has read the partials: clear the flags for the
+              // next call
+              named_bar_sync(1, kEpiThreads);
+              if (et == 0)
+                for (int j = 0; j < sk_n; ++j)
+                  p.sk_flags[(g_of_cta<GROUP>() + 1 + j) * GROUP + half] = 0;
+            }
           }
         } else {
           TmemChunks<CW> src{taddr};
@@ -1560,32 +1733,42 @@ int cluster_cap(int algo, int bn, int pair, int cluster) {
   return v;
 }
 
-// Optional tuning override "BN,SPLIT[,PAIR]" for wide tiles (ORIN_TC_PLAN).
-bool plan_override(int& bn, int& split, int& pair) {
-  static int o_bn = -1, o_split = -1, o_pair = 0;
+// Optional tuning override "BN,SPLIT[,PAIR[,SK]]" for wide tiles (ORIN_TC_PLAN).
+bool plan_override(int& bn, int& split, int& pair, int& sk) {
+  static int o_bn = -1, o_split = -1, o_pair = 0, o_sk = 0;
   static bool read = false;
   if (!read) {
     read = true;
     const char* e = getenv("ORIN_TC_PLAN");
     if (e) {
-      const int n = sscanf(e, "%d,%d,%d", &o_bn, &o_split, &o_pair);
+      const int n = sscanf(e, "%d,%d,%d,%d", &o_bn, &o_split, &o_pair, &o_sk);
       if (n < 2) o_bn = -1;
       if (n < 3) o_pair = 0;
+      if (n < 4) o_sk = 0;
     }
     if (o_bn != 128 && o_bn != 256) o_bn = -1;
     if (o_split < 1 || o_split > 8) o_bn = -1;
     if (o_pair && o_split > 4) o_bn = -1;
+    if (o_sk && o_split != 1) o_bn = -1;
   }
   if (o_bn < 0) return false;
   bn = o_bn;
   split = o_split;
   pair = o_pair;
+  sk = o_sk;
   return true;
 }
 
 }  // namespace
 
-void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
+size_t sk_workspace_bytes(int grid, int bn) {
+  return kSkFlagBytes + static_cast<size_t>(grid) * kBM * bn * sizeof(float);
+}
+
+size_t sk_workspace_max_bytes(int sm_count) { return sk_workspace_bytes(sm_count, 256); }
+
+void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count, int sk_groups = 0) {
+  const bool sk = sk_groups > 0;
   TcParams& p = pl.p;
   const int tile_p = pair ? 2 * kBM : kBM;
   const int group = pair ? 2 : 1;
@@ -1597,8 +1780,12 @@ void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
   p.kb += p.kb & 1;  // whole stage pairs; the extra block is zero-filled
   p.group_p = kGroupP;
   p.split = split;
+  p.sk = sk ? 1 : 0;
   const int tiles = p.tiles_p * p.tiles_q;
-  if (split == 1) {
+  if (sk) {
+    // every co-resident CTA group takes an equal share of tiles x K
+    pl.grid = group * sk_groups;
+  } else if (split == 1) {
     const int groups = sm_count / group;
     pl.grid = group * (tiles < groups ? tiles : groups);
   } else {
@@ -1614,7 +1801,7 @@ void fill_tiles(Plan& pl, int K, int bn, int split, int pair, int sm_count) {
 //   exchange split-K: staging, the cluster barriers and the bulk copies.
 // Tiles are dealt in waves of at most `groups` tiles; every wave pays its
 // k-blocks at the rate of its own CTA count.
-void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
+void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, size_t sk_bytes) {
   const int wrows = (epi == EPI_SWIGLU) ? 2 * N : N;  // rows of W
   TcParams& p = pl.p;
   p = TcParams{};
@@ -1646,8 +1833,34 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   }
   p.P = M;
   p.Q = wrows;
-  int obn = 0, osplit = 0, opair = 0;
-  if (plan_override(obn, osplit, opair) && !(epi == EPI_SWIGLU && obn % 128)) {
+  // a stream-K plan of tile shape (bn, pair) is possible when the workspace
+  // holds its slots and every CTA group gets at least one k-block pair
+  // The finishers wait on later groups, so every group of a stream-K grid must
+  // be resident at once: the grid is the co-resident count of this tile shape
+  // (one CTA, or one 2-CTA cluster, per SM pair), at most one group per SM.
+  auto sk_groups = [&](int bn, int pair) {
+    const int group = pair ? 2 : 1;
+    int n = cluster_cap(1, bn, pair, group);
+    if (n > G / group) n = G / group;
+    return n;
+  };
+  auto sk_possible = [&](int bn, int pair) {
+    if (sk_bytes == 0) return false;
+    const int group = pair ? 2 : 1;
+    const int tile_p = pair ? 2 * kBM : kBM;
+    const long long tiles =
+        static_cast<long long>((M + tile_p - 1) / tile_p) * ((wrows + bn - 1) / bn);
+    const int n = sk_groups(bn, pair);
+    const int grid = group * n;
+    return n > 0 && grid <= kSkMaxGrid && sk_bytes >= sk_workspace_bytes(grid, bn) &&
+           tiles * (kb / 2) >= n;
+  };
+  int obn = 0, osplit = 0, opair = 0, osk = 0;
+  if (plan_override(obn, osplit, opair, osk) && !(epi == EPI_SWIGLU && obn % 128)) {
+    if (osk && sk_possible(obn, opair)) {
+      fill_tiles(pl, K, obn, 1, opair, G, sk_groups(obn, opair));
+      return;
+    }
     const int units = (epi == EPI_SWIGLU) ? obn / 64 : obn / 32;
     int sp = osplit > kb / 2 ? kb / 2 : osplit;
     if (sp > units) sp = units;
@@ -1669,6 +1882,7 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
   };
   double best = 1e30;
   int best_bn = 256, best_split = 1, best_pair = 0;
+  int best_sk = 0;  // stream-K groups (0: no stream-K)
   for (const Shape& sh : shapes) {
     if (epi == EPI_SWIGLU && sh.bn % 128) continue;
     const int tile_p = sh.pair ? 2 * kBM : kBM;
@@ -1687,6 +1901,26 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
       best_bn = sh.bn;
       best_split = 1;
       best_pair = sh.pair;
+      best_sk = 0;
+    }
+    // stream-K: every group takes an equal share of tiles x k-block pairs,
+    // all at the full-machine rate; the groups that hold a tile's first
+    // k-blocks read the other groups' partials of that tile (fp32 slots of
+    // 128 x bn per CTA, ~1 us per 128 KB slot) before their last epilogue
+    if (sk_possible(sh.bn, sh.pair)) {
+      const long long W = tiles * (kb / 2);
+      const long long ng = sk_groups(sh.bn, sh.pair);
+      const long long per = (W + ng - 1) / ng;                   // pairs per group
+      const long long readers = (kb / 2 + per - 1) / per;          // groups per tile
+      const double fix = 0.5 + static_cast<double>(readers - 1) * 0.9 * sh.bn / 256.0;
+      cost = sh.launch + 2.0 * per * t_kb(sh, ng * group) + fix;
+      if (cost < best) {
+        best = cost;
+        best_bn = sh.bn;
+        best_split = 1;
+        best_pair = sh.pair;
+        best_sk = static_cast<int>(ng);
+      }
     }
     // split columns are handed out in units (32 accumulator columns, 64 for
     // SwiGLU pairs): at most one owner per unit
@@ -1704,15 +1938,24 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count) {
         best_bn = sh.bn;
         best_split = s;
         best_pair = sh.pair;
+        best_sk = 0;
       }
     }
   }
-  fill_tiles(pl, K, best_bn, best_split, best_pair, G);
+  fill_tiles(pl, K, best_bn, best_split, best_pair, G, best_sk);
 }
 
 cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const void* W,
-                      int* err, cudaStream_t stream, const char** why) {
+                      int* err, cudaStream_t stream, const char** why, void* sk_ws) {
   Plan pl = pl0;
+  if (pl.p.sk) {
+    if (!sk_ws) {
+      if (why) *why = "stream-K plan without a workspace";
+      return cudaErrorInvalidValue;
+    }
+    pl.p.sk_flags = static_cast<int*>(sk_ws);
+    pl.p.sk_ws = reinterpret_cast<float*>(static_cast<char*>(sk_ws) + kSkFlagBytes);
+  }
   const TcParams& p = pl.p;
   const bool swap = pl.algo == 2;
   const void* pptr = swap ? W : A;

@@ -27,6 +27,15 @@ struct TcParams {
   int* err;          // device error word
   int vec_ok;        // C / R rows are 16-byte aligned for vector stores
   int out_tma;       // wide tiles: stores (and the residual) go through TMA
+  // Stream-K (wide tiles, split == 1): the tiles x K work is dealt to the
+  // persistent CTA groups in equal contiguous ranges of k-block pairs, so a
+  // tile's K range may be shared by consecutive groups.  A group whose range
+  // starts inside a tile writes that partial accumulator to its slot of
+  // sk_ws (kBM x BN floats per CTA) and raises its flag; the group that holds
+  // the tile's first k-blocks adds those partials in group order and stores.
+  int sk;            // 1: stream-K schedule
+  float* sk_ws;      // gridDim.x slots of kBM * BN floats
+  int* sk_flags;     // gridDim.x flags, zero between calls
 };
 
 struct Plan {
@@ -48,11 +57,24 @@ DeviceCtx* device_ctx(int device, cudaError_t* e);
 bool device_ctx_ready(int device);
 
 // Fill the tiling / scheduling fields of a plan for the tcgen05 kernels.
-void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count);
+// sk_bytes: caller workspace available for a stream-K schedule (0: none).
+void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count,
+             size_t sk_bytes = 0);
+
+// Stream-K workspace layout: kSkFlagBytes of flag words (one per CTA, grids of
+// up to kSkMaxGrid CTAs, zero between calls) at the start, then one slot of
+// 128 x BN floats per CTA.  The flags sit at a fixed offset whatever the plan,
+// so slots written by one call never land on another call's flags.
+constexpr int kSkMaxGrid = 1024;
+constexpr size_t kSkFlagBytes = kSkMaxGrid * sizeof(int);
+size_t sk_workspace_bytes(int grid, int bn);
+// Bytes that unlock every stream-K plan on a device with sm_count SMs.
+size_t sk_workspace_max_bytes(int sm_count);
 
 // Launch the tcgen05 GEMM described by pl.
+// sk_ws: the caller's workspace when pl is a stream-K plan (else unused).
 cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const void* W,
-                      int* err, cudaStream_t stream, const char** why);
+                      int* err, cudaStream_t stream, const char** why, void* sk_ws = nullptr);
 
 // Decode-time weight-streaming kernel (csrc/gemv.cu) for M <= kGemvMaxTokens,
 // K % 8 == 0 and 16-byte aligned A and W.  Same epilogues and rounding.

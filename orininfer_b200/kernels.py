@@ -56,6 +56,7 @@ __all__ = [
     "pack_gate_up", "device_check", "plan_info", "lm_head_argmax", "attention",
     "attention_workspace_bytes", "kv_append", "rmsnorm", "rope", "qkv_rope_append",
     "embedding", "linear_rmsnorm", "attention_batch", "qkv_rope_append_batch",
+    "linear_workspace", "linear_workspace_bytes",
 ]
 
 
@@ -121,21 +122,51 @@ def bf16_to_fp32(out: torch.Tensor, inp: torch.Tensor, n: int,
 
 # ----------------------------------------------------------------- fused entry points
 
+def linear_workspace_bytes() -> int:
+    """Workspace bytes that let linear_into(..., workspace=) pick any plan on the
+    current GPU (orin_linear_workspace_bytes)."""
+    n = ctypes.c_size_t(0)
+    check(_lib.lib.orin_linear_workspace_bytes(ctypes.byref(n)))
+    return int(n.value)
+
+
+def linear_workspace(device=None) -> torch.Tensor:
+    """A zeroed workspace for linear_into(..., workspace=) on `device`: its flag
+    words must start at zero, and every call leaves them zero.  Calls sharing
+    one workspace must be ordered on one stream."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    with torch.cuda.device(dev):
+        n = linear_workspace_bytes()
+    return torch.zeros(n, dtype=torch.uint8, device=dev)
+
+
 def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
                 residual: Optional[torch.Tensor] = None, algo: str = "auto",
+                workspace: Optional[torch.Tensor] = None,
                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """out = epilogue(x · w^T) written into `out` (see include/orin_b200.h).
 
     x [M, K]; w [N, K] ([2N, K] packed gate/up for "swiglu"); out [M, N]
     (float32 for "f32" / "f32_partial", else x.dtype); residual [M, N].
+    With a workspace (linear_workspace()), prefill-sized problems may take the
+    stream-K schedule (orin_linear_ws); algo must then be "auto".
     """
-    _need_cuda(out, x, w, residual)
+    _need_cuda(out, x, w, residual, workspace)
     dt = _dtype_code(x)
     if w.dtype != x.dtype or (residual is not None and residual.dtype != x.dtype):
         raise ValueError("x, w and residual must share one dtype")
     epi = _EPILOGUES[epilogue]
     M, K = x.shape
     N = out.shape[-1]
+    if workspace is not None:
+        if algo != "auto":
+            raise ValueError("a workspace goes with algo='auto'")
+        check(_lib.lib.orin_linear_ws(_ptr(out), _ptr(x), _ptr(w), M, N, K, dt, epi,
+                                      _ptr(residual), _ptr(workspace),
+                                      workspace.numel() * workspace.element_size(),
+                                      _stream(stream)))
+        return out
     check(_lib.lib.orin_linear_ex(_ptr(out), _ptr(x), _ptr(w), M, N, K, dt, epi, _ptr(residual),
                                   _ALGOS[algo], _stream(stream)))
     return out
@@ -143,14 +174,16 @@ def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue
 
 def linear(x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-           algo: str = "auto", stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+           algo: str = "auto", workspace: Optional[torch.Tensor] = None,
+           stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """Allocating form of linear_into."""
     M = x.shape[0]
     N = w.shape[0] // 2 if epilogue == "swiglu" else w.shape[0]
     if out is None:
         odt = torch.float32 if epilogue in ("f32", "f32_partial") else x.dtype
         out = torch.empty((M, N), dtype=odt, device=x.device)
-    return linear_into(out, x, w, epilogue=epilogue, residual=residual, algo=algo, stream=stream)
+    return linear_into(out, x, w, epilogue=epilogue, residual=residual, algo=algo,
+                       workspace=workspace, stream=stream)
 
 
 def linear_rmsnorm(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, norm: torch.Tensor,
@@ -359,14 +392,15 @@ def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,
 
 
 def plan_info(M: int, N: int, K: int, dtype: torch.dtype = torch.float16,
-              epilogue: str = "none", algo: str = "auto") -> dict:
-    """The launch orin_linear would make for this problem on the current GPU."""
-    info = (ctypes.c_int * 6)()
-    check(_lib.lib.orin_plan_info(M, N, K, _DTYPES[dtype], _EPILOGUES[epilogue], _ALGOS[algo],
-                                  info))
+              epilogue: str = "none", algo: str = "auto", workspace_bytes: int = 0) -> dict:
+    """The launch orin_linear (with a workspace of workspace_bytes:
+    orin_linear_ws) would make for this problem on the current GPU."""
+    info = (ctypes.c_int * 7)()
+    check(_lib.lib.orin_plan_info_ws(M, N, K, _DTYPES[dtype], _EPILOGUES[epilogue], _ALGOS[algo],
+                                     workspace_bytes, info))
     kind = {1: "tcgen05-wide", 2: "tcgen05-skinny", 3: "cuda-core", 4: "gemv"}[info[0]]
     return {"kernel": kind, "tile_cols": info[1], "cta_pair": bool(info[2]), "split_k": info[3],
-            "grid": info[4], "tiles": info[5]}
+            "grid": info[4], "tiles": info[5], "stream_k": bool(info[6])}
 
 
 def device_check(stream: Optional[torch.cuda.Stream] = None) -> None:

@@ -1,6 +1,7 @@
 """Every wide-tile plan — tile width 128/256, one CTA or a tcgen05 CTA pair
-per tile, split-K 1..8 through thread-block clusters — against the oracle
-(B200 only).
+per tile, split-K 1..8 through thread-block clusters, and the stream-K
+schedule (a caller workspace; "BN,1,PAIR,1") — against the oracle (B200
+only).
 
 The plan is forced with the ORIN_TC_PLAN tuning override, which the library
 reads once per process, so each plan runs in its own subprocess."""
@@ -14,7 +15,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 # "BN,SPLIT" = one CTA per 128-row tile; "BN,SPLIT,1" = tcgen05 CTA pairs
 # (256-row tiles); SPLIT > 1 = k-split over a thread-block cluster
 PLANS = ["256,1", "128,1", "256,2", "128,2", "256,3", "128,4", "256,4", "128,3",
-         "256,1,1", "256,2,1", "256,3,1", "256,4,1", "128,1,1", "128,2,1", "128,4,1"]
+         "256,1,1", "256,2,1", "256,3,1", "256,4,1", "128,1,1", "128,2,1", "128,4,1",
+         "256,1,0,1", "128,1,0,1", "256,1,1,1", "128,1,1,1"]
 
 
 @pytest.mark.gpu
@@ -34,8 +36,17 @@ def _main() -> None:
     from tests._util import EXACT_MIN, assert_close, bits, from_bits, seeded
 
     dev = torch.device("cuda:0")
+    plan = os.environ.get("ORIN_TC_PLAN", "")
+    stream_k = plan.count(",") == 3 and plan.endswith(",1")
     cases = [(512, 2560, 2048, "none"), (200, 300, 520, "none"), (256, 640, 1024, "residual"),
              (130, 704, 512, "swiglu"), (512, 1000, 2048, "f32"), (96, 512, 4096, "f32_partial")]
+    ws = None
+    if stream_k:
+        # the layer's shapes: several groups share each tile's K range (down:
+        # K = 5632), the finisher adds up to four partial slots
+        cases += [(512, 2048, 5632, "residual"), (512, 5632, 2048, "swiglu"),
+                  (512, 2048, 2048, "residual")]
+        ws = ob.linear_workspace(dev)
     for dt in (0, 1):
         tdt = torch.float16 if dt == 0 else torch.bfloat16
         for i, (M, N, K, epi) in enumerate(cases):
@@ -43,14 +54,25 @@ def _main() -> None:
             x = seeded((M, K), 10 + i, 1.0, tdt)
             w = seeded((wrows, K), 20 + i, 0.02, tdt)
             r = seeded((M, N), 30 + i, 1.0, tdt) if epi == "residual" else None
-            y = ob.linear(x.to(dev), w.to(dev), epilogue=epi, algo="wide",
-                          residual=r.to(dev) if r is not None else None)
+            if ws is not None:
+                sk = ob.plan_info(M, N, K, tdt, epi, workspace_bytes=ws.numel())["stream_k"]
+                # stream-K needs at least one k-block pair per CTA group: the
+                # small cases keep the forced tile shape without it
+                assert sk or i < 6, (M, N, K)
+                y = ob.linear(x.to(dev), w.to(dev), epilogue=epi, workspace=ws,
+                              residual=r.to(dev) if r is not None else None)
+            else:
+                y = ob.linear(x.to(dev), w.to(dev), epilogue=epi, algo="wide",
+                              residual=r.to(dev) if r is not None else None)
             ob.device_check()
             ref = orc.linear(bits(x), bits(w), dt, epi, bits(r) if r is not None else None)
             ref_t = torch.from_numpy(ref) if epi in ("f32", "f32_partial") else from_bits(ref, tdt)
             assert_close(y.cpu().float(), ref_t.float(),
                          f"plan {os.environ.get('ORIN_TC_PLAN')} {epi} dt={dt} {M}x{N}x{K}",
                          exact_min=None if epi == "f32_partial" else EXACT_MIN)
+    if ws is not None:
+        # every call left the flag words zero for the next one
+        assert int(ws[:4096].count_nonzero()) == 0
     print("ok")
 
 
