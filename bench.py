@@ -179,7 +179,7 @@ def make_layers(rank: int, world: int, dev):
 class Step:
     """One layer pass (4 projections), on the current stream."""
 
-    def __init__(self, layers, rank, world, dev, comm=None):
+    def __init__(self, layers, rank, world, dev, comm=None, use_workspace=True):
         import orininfer_b200 as ob
         from orininfer_b200.synth import seeded
 
@@ -201,6 +201,8 @@ class Step:
         self.act = torch.empty((M, im_local), dtype=torch.float16, device=dev)
         self.x2 = torch.empty((M, H), dtype=torch.float16, device=dev)
         self.partial = torch.empty((M, H), dtype=torch.float32, device=dev)
+        # stream-K workspace shared by the step's GEMMs (one stream)
+        self.ws = ob.linear_workspace(dev) if use_workspace else None
         # our kernels per step: 4 GEMMs (+ 2 all-reduce finish kernels under TP)
         self.launches = 4 if world == 1 else 6
 
@@ -213,22 +215,25 @@ class Step:
             if events is not None:
                 events[name][which].record(s)
 
+        ws = self.ws
         mark("qkv", 0)
-        ob.linear_into(self.qkv, self.h, L["qkv"])
+        ob.linear_into(self.qkv, self.h, L["qkv"], workspace=ws)
         mark("qkv", 1)
         mark("o_proj", 0)
         if self.world == 1:
-            ob.linear_into(self.x1, self.attn, L["o_proj"], epilogue="residual", residual=self.x)
+            ob.linear_into(self.x1, self.attn, L["o_proj"], epilogue="residual", residual=self.x,
+                           workspace=ws)
         else:
             self.comm.linear_row(self.attn, L["o_proj"], residual=self.x, out=self.x1,
                                  partial=self.partial)
         mark("o_proj", 1)
         mark("gate_up", 0)
-        ob.linear_into(self.act, self.h2, L["gate_up"], epilogue="swiglu")
+        ob.linear_into(self.act, self.h2, L["gate_up"], epilogue="swiglu", workspace=ws)
         mark("gate_up", 1)
         mark("down", 0)
         if self.world == 1:
-            ob.linear_into(self.x2, self.act, L["down"], epilogue="residual", residual=self.x1)
+            ob.linear_into(self.x2, self.act, L["down"], epilogue="residual", residual=self.x1,
+                           workspace=ws)
         else:
             self.comm.linear_row(self.act, L["down"], residual=self.x1, out=self.x2,
                                  partial=self.partial)
@@ -815,10 +820,12 @@ def cpu_baseline_layer(budget_s: float = 10.0) -> dict:
                       f"{dt:.1f} s"}
 
 
-def ob_plan(M_, N_, K_, epi):
+def ob_plan(M_, N_, K_, epi, workspace_bytes=0):
     import orininfer_b200 as ob
-    p = ob.kernels.plan_info(M_, N_, K_, torch.float16, epi)
-    return f"{p['kernel']} {'pair ' if p['cta_pair'] else ''}{p['tile_cols']}-wide split{p['split_k']} grid{p['grid']}"
+    p = ob.kernels.plan_info(M_, N_, K_, torch.float16, epi, workspace_bytes=workspace_bytes)
+    sched = "stream-K" if p["stream_k"] else f"split{p['split_k']}"
+    return (f"{p['kernel']} {'pair ' if p['cta_pair'] else ''}{p['tile_cols']}-wide {sched} "
+            f"grid{p['grid']}")
 
 
 def run_ours(args, rank, world, local_rank):
@@ -836,7 +843,7 @@ def run_ours(args, rank, world, local_rank):
             # to ncclAllReduce only where a call does not fit)
             comm.enable_p2p(max(M * H, L3_M * L3_H))
     layers = make_layers(rank, world, dev)
-    step = Step(layers, rank, world, dev, comm)
+    step = Step(layers, rank, world, dev, comm, use_workspace=not args.no_workspace)
 
     ms, clocks = time_steps(step, args.steps, args.warmup, world, local_rank)
     ms_per_step = ms / args.steps
@@ -869,6 +876,7 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": "tp%d" % world if world > 1 else "single",
                    "tp_reduce": ("nccl" if args.nccl_reduce else "nvlink-p2p") if world > 1
                    else None,
+                   "gemm_workspace_bytes": step.ws.numel() if step.ws is not None else 0,
                    "l2": f"inputs larger than L2: {N_COPIES} rotating layer copies "
                          f"({N_COPIES * 88} MB of weights)"},
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
@@ -895,8 +903,9 @@ def run_ours(args, rank, world, local_rank):
             "avg_launch_ms": round(avg_ms, 5),
         }
         line["kernels_ms"] = {k: round(v, 5) for k, v in kt.items()}
+        wsb = step.ws.numel() if step.ws is not None else 0
         line["kernels_plan"] = {
-            k: ob_plan(M, n, kk, epi) for k, (n, kk, epi) in GEMMS.items()}
+            k: ob_plan(M, n, kk, epi, wsb) for k, (n, kk, epi) in GEMMS.items()}
         if bar is not None:
             line["cublas_bar"] = bar
         line["kernels_tflops"] = {k: round(FLOPS[k] / (kt[k] / 1e3) / 1e12, 1) for k in kt}
@@ -1178,6 +1187,8 @@ def main():
     ap.add_argument("--nccl-reduce", action="store_true",
                     help="N>1: reduce the row-parallel partial sums with ncclAllReduce instead "
                          "of the peer-memory kernels")
+    ap.add_argument("--no-workspace", action="store_true",
+                    help="run the projections without a GEMM workspace (no stream-K plans)")
     ap.add_argument("--no-cublas-bar", dest="cublas_bar", action="store_false",
                     help="skip timing the cuBLAS comparison bar")
     ap.add_argument("--kernel", choices=list(GEMMS), default=None,

@@ -401,6 +401,41 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
 }
 
 // ---------------------------------------------------------------------------
+// Epilogue through TMA stores (wide tiles)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_smem_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled buffer
+// (the layout TMA reads and writes with CU_TENSOR_MAP_SWIZZLE_128B).
+__device__ __forceinline__ uint32_t sw128(int r, int j) {
+  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// One thread of the 128 epilogue threads waits (bounded) on `bar`; the rest
+// park on a named barrier instead of polling.  Returns false on timeout, in
+// every thread.
+__device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, int et,
+                                         volatile int* abort_flag, int* err, volatile int* flag) {
+  if (et == 0) *flag = mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE) ? 1 : 0;
+  named_bar_sync(1, kEpiThreads);
+  return *flag != 0;
+}
+
+// ---------------------------------------------------------------------------
 // Stream-K partial accumulators
 // ---------------------------------------------------------------------------
 
@@ -416,39 +451,65 @@ __device__ __forceinline__ void st_release_gpu(int* f, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
 }
 
-// Add the partial sums of `n` contributor slots (first at `slots`, then every
-// `stride` floats, in order) for columns [col, col + CNT) of this thread's
-// row to v.
-template <int CNT>
-__device__ __forceinline__ void sk_add(float* v, int col, int lr, const float* slots, int n,
-                                       long long stride) {
-  for (int j = 0; j < n; ++j) {
-    const float4* s = reinterpret_cast<const float4*>(slots + j * stride) + (col / 4) * kBM + lr;
-#pragma unroll
-    for (int i = 0; i < CNT / 4; ++i) {
-      const float4 t = __ldcg(s + i * kBM);
-      v[4 * i + 0] += t.x;
-      v[4 * i + 1] += t.y;
-      v[4 * i + 2] += t.z;
-      v[4 * i + 3] += t.w;
+// Finisher: add the partial accumulators of n contributor slots (first at
+// `slots`, then every `stride` floats, in that order) to this CTA's tile in
+// tensor memory, before the ordinary epilogue reads it.  The operand ring is
+// idle by now (a finisher's unit is its group's last), so one thread moves the
+// slots into it with bulk copies, a column range of every slot at a time (as
+// wide as fits: n * cols * 512 bytes <= ring_bytes), and the 128 epilogue
+// threads add them from shared memory into their rows: tcgen05.ld, n adds in
+// slot order, tcgen05.st.  Slot layout: float4 (c4, row) at c4 * kBM + row,
+// so columns [c0, c0 + w) of a slot are one contiguous run of w * 512 bytes.
+template <int BN>
+__device__ __forceinline__ bool sk_fixup(uint32_t taddr, int lr, int et, uint32_t ring,
+                                         uint32_t ring_bytes, const float* slots, int n,
+                                         long long stride, uint32_t bar, uint32_t& phase,
+                                         volatile int* abort_flag, int* err, volatile int* flag) {
+  if (static_cast<uint32_t>(n) * 32u * 512u > ring_bytes) {
+    // the planner never makes such a plan; refuse rather than overrun the ring
+    if (et == 0) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, DEVERR_TIMEOUT_EPILOGUE);
     }
+    return false;
   }
+  int w = BN;
+  while (w > 32 && static_cast<uint32_t>(n) * w * 512u > ring_bytes) w >>= 1;
+  const uint32_t part = static_cast<uint32_t>(w) * 512u;  // bytes of one slot's column range
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += w) {
+    if (et == 0) {
+      // the ring's last readers were the MMAs (complete) or this loop's
+      // generic loads (finished at the barrier below)
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n) * part);
+      for (int j = 0; j < n; ++j)
+        bulk_copy_g2s(ring + j * part, slots + j * stride + static_cast<long long>(c0) * kBM,
+                      part, bar);
+    }
+    if (!epi_wait(bar, phase, et, abort_flag, err, flag)) return false;
+    phase ^= 1u;
+#pragma unroll 1
+    for (int c = c0; c < c0 + w; c += 32) {
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + c, v);
+      for (int j = 0; j < n; ++j) {
+        const uint32_t src = ring + j * part + static_cast<uint32_t>(((c - c0) / 4) * kBM + lr) * 16u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = ld_smem_f4(src + static_cast<uint32_t>(i * kBM * 16));
+          v[4 * i + 0] += t.x;
+          v[4 * i + 1] += t.y;
+          v[4 * i + 2] += t.z;
+          v[4 * i + 3] += t.w;
+        }
+      }
+      tmem_st_32x32b_x32(taddr + c, v);
+    }
+    named_bar_sync(1, kEpiThreads);
+  }
+  return true;
 }
-
-// Accumulator chunks from tensor memory plus stream-K partials.
-template <int CW>
-struct TmemChunksSk {
-  uint32_t taddr;
-  int lr;
-  const float* slots;
-  int n;
-  long long stride;
-  __device__ __forceinline__ void get(int col, float* v) const {
-    if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr + col, v);
-    else tmem_ld_32x32b_x16(taddr + col, v);
-    sk_add<CW>(v, col, lr, slots, n, stride);
-  }
-};
 
 // Contributor: this CTA's partial accumulator (columns [0, BN) of its 128 rows)
 // into its slot, then its flag, released at GPU scope after every epilogue
@@ -499,41 +560,6 @@ __device__ __forceinline__ bool sk_wait(const int* flags, int first, int n, int 
   return *flag != 0;
 }
 
-// ---------------------------------------------------------------------------
-// Epilogue through TMA stores (wide tiles)
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ float4 ld_smem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_smem_f4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
-
-// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled buffer
-// (the layout TMA reads and writes with CU_TENSOR_MAP_SWIZZLE_128B).
-__device__ __forceinline__ uint32_t sw128(int r, int j) {
-  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
-}
-
-// One thread of the 128 epilogue threads waits (bounded) on `bar`; the rest
-// park on a named barrier instead of polling.  Returns false on timeout, in
-// every thread.
-__device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, int et,
-                                         volatile int* abort_flag, int* err, volatile int* flag) {
-  if (et == 0) *flag = mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE) ? 1 : 0;
-  named_bar_sync(1, kEpiThreads);
-  return *flag != 0;
-}
-
 // Store one tile held in tensor memory: for each 128-byte-wide chunk of
 // output columns, every thread writes its row into a swizzled staging buffer
 // and one thread issues the TMA store.  Chunks go in rounds of two, one per
@@ -546,9 +572,7 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
                                               int qcol0, int lr, int et, uint32_t outbuf,
                                               const void* tm_c, const void* tm_r,
                                               uint32_t res_bar, uint32_t& res_phase,
-                                              volatile int* abort_flag, volatile int* flag,
-                                              const float* sk_slots, int sk_n,
-                                              long long sk_stride) {
+                                              volatile int* abort_flag, volatile int* flag) {
   using E = Elem<DT>;
   constexpr bool F32 = (EPI == EPI_F32_OUT || EPI == EPI_F32_PARTIAL);
   constexpr int CH = F32 ? 32 : 64;  // output columns per 128-byte chunk
@@ -581,7 +605,6 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
       if constexpr (F32) {
         float v[32];
         tmem_ld_32x32b_x32(taddr + oc * 32, v);
-        sk_add<32>(v, oc * 32, lr, sk_slots, sk_n, sk_stride);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float o[4];
@@ -599,13 +622,10 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
             float u[32];
             tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
             tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
-            sk_add<32>(v, 128 * oc + 32 * h, lr, sk_slots, sk_n, sk_stride);
-            sk_add<32>(u, 128 * oc + 64 + 32 * h, lr, sk_slots, sk_n, sk_stride);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
           } else {
             tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
-            sk_add<32>(v, 64 * oc + 32 * h, lr, sk_slots, sk_n, sk_stride);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -1330,6 +1350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t res_phase = 0;
+    uint32_t sk_phase = 0;  // recv_bar: stream-K fix-up copies (split == 1 only)
     UnitIter it;
     it.init(p, GROUP);
     Unit u;
@@ -1367,16 +1388,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               sk_slots = p.sk_ws + (static_cast<long long>(g + 1) * GROUP + half) * slot_f;
               sk_stride = GROUP * slot_f;
               ok = sk_wait(p.sk_flags, (g + 1) * GROUP + half, sk_n, GROUP, et, &abort_flag,
-                           p.err, &epi_flag);
+                           p.err, &epi_flag) &&
+                   sk_fixup<BN>(taddr, lr, et, ring, STAGES * STAGE_BYTES, sk_slots, sk_n,
+                                sk_stride, smem_u32(&recv_bar), sk_phase, &abort_flag, p.err,
+                                &epi_flag);
             }
             if (ok) {
               if (p.out_tma) {
                 ok = emit_tile_tma<DT, BN, EPI>(p, taddr, prow0, qcol0, lr, et, outbuf, &tm_c,
                                                 &tm_r, smem_u32(&res_bar), res_phase,
-                                                &abort_flag, &epi_flag, sk_slots, sk_n,
-                                                sk_stride);
+                                                &abort_flag, &epi_flag);
               } else {
-                TmemChunksSk<CW> src{taddr, lr, sk_slots, sk_n, sk_stride};
+                TmemChunks<CW> src{taddr};
                 emit_tile<DT, BN, EPI, SWAP, CW>(p, src, prow0, qcol0, lr, xch);
               }
             }
@@ -1844,6 +1867,22 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
     if (n > G / group) n = G / group;
     return n;
   };
+  // Most contributors any tile's finisher adds: groups g whose range starts
+  // strictly inside a tile.
+  auto sk_max_contributors = [&](long long tiles, int ng) {
+    const long long kpp = kb / 2, W = tiles * kpp;
+    int most = 0, run = 0;
+    long long run_tile = -1;
+    for (int g = 1; g < ng; ++g) {
+      const long long st = W * g / ng;
+      if (st % kpp == 0) continue;
+      const long long t = st / kpp;
+      run = (t == run_tile) ? run + 1 : 1;
+      run_tile = t;
+      if (run > most) most = run;
+    }
+    return most;
+  };
   auto sk_possible = [&](int bn, int pair) {
     if (sk_bytes == 0) return false;
     const int group = pair ? 2 : 1;
@@ -1852,8 +1891,13 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
         static_cast<long long>((M + tile_p - 1) / tile_p) * ((wrows + bn - 1) / bn);
     const int n = sk_groups(bn, pair);
     const int grid = group * n;
-    return n > 0 && grid <= kSkMaxGrid && sk_bytes >= sk_workspace_bytes(grid, bn) &&
-           tiles * (kb / 2) >= n;
+    if (n <= 0 || grid > kSkMaxGrid || sk_bytes < sk_workspace_bytes(grid, bn) ||
+        tiles * (kb / 2) < n)
+      return false;
+    // the finisher stages a 32-column slab (16 KB) of every contributor in its
+    // operand ring at once
+    const int ring_bytes = tc_stages(bn, pair != 0) * tc_stage_bytes(bn, pair != 0);
+    return sk_max_contributors(tiles, n) * 32 * 512 <= ring_bytes;
   };
   int obn = 0, osplit = 0, opair = 0, osk = 0;
   if (plan_override(obn, osplit, opair, osk) && !(epi == EPI_SWIGLU && obn % 128)) {
@@ -1909,10 +1953,12 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
     // 128 x bn per CTA, ~1 us per 128 KB slot) before their last epilogue
     if (sk_possible(sh.bn, sh.pair)) {
       const long long W = tiles * (kb / 2);
-      const long long ng = sk_groups(sh.bn, sh.pair);
+      const int ng = sk_groups(sh.bn, sh.pair);
       const long long per = (W + ng - 1) / ng;                   // pairs per group
-      const long long readers = (kb / 2 + per - 1) / per;          // groups per tile
-      const double fix = 0.5 + static_cast<double>(readers - 1) * 0.9 * sh.bn / 256.0;
+      const int readers = sk_max_contributors(tiles, ng);
+      // contributors write a slot (bn/256 x ~0.6 us); the finisher moves each
+      // slot into shared memory (~0.5 us per 128 KB) and adds it
+      const double fix = 0.6 * sh.bn / 256.0 + static_cast<double>(readers) * 0.5 * sh.bn / 256.0;
       cost = sh.launch + 2.0 * per * t_kb(sh, ng * group) + fix;
       if (cost < best) {
         best = cost;

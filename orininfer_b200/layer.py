@@ -55,8 +55,11 @@ class DecoderLayer:
     def __init__(self, w: Mapping[str, torch.Tensor], cfg: Mapping, *, n_sink: int, window: int,
                  max_tokens: int, qk_norm: bool = False,
                  workspace: Optional[torch.Tensor] = None, fold_norm: bool = False,
-                 batch: int = 1):
+                 batch: int = 1, gemm_workspace: Optional[torch.Tensor] = None):
         self.w = dict(w)
+        # stream-K workspace of the projections (kernels.linear_workspace),
+        # shareable by every layer of a model run on one stream
+        self.gemm_ws = gemm_workspace
         self.fold_norm = bool(fold_norm)
         self.nh = int(cfg["num_attention_heads"])
         self.nkv = int(cfg["num_key_value_heads"])
@@ -116,7 +119,7 @@ class DecoderLayer:
                                    stream=stream)
         else:
             kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
-            kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+            kernels.linear_into(qkv, xn, w["qkv"], workspace=self.gemm_ws, stream=stream)
         kernels.qkv_rope_append(q, qkv, k_pool, v_pool, S, start_pos, self.nh, self.nkv,
                                 self.hd, self.theta, self.n_sink, self.window,
                                 q_norm=w.get("q_norm") if self.qk_norm else None,
@@ -162,15 +165,18 @@ class DecoderLayer:
         """o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual."""
         w = self.w
         xn, h = self.xn[:S], self.h[:S]
-        kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x, stream=stream)
+        kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x,
+                            workspace=self.gemm_ws, stream=stream)
         if fold:
             kernels.linear_rmsnorm(h, x, w["gate_up"], w["post_attention_layernorm"], self.eps,
                                    epilogue="swiglu", stream=stream)
         else:
             kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps,
                             stream=stream)
-            kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", stream=stream)
-        kernels.linear_into(x, h, w["down"], epilogue="residual", residual=x, stream=stream)
+            kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", workspace=self.gemm_ws,
+                                stream=stream)
+        kernels.linear_into(x, h, w["down"], epilogue="residual", residual=x,
+                            workspace=self.gemm_ws, stream=stream)
         return x
 
 
@@ -257,10 +263,12 @@ class Decoder:
         dt = self.embed.dtype
         ws = DecoderLayer.workspace_bytes(cfg, n_sink, window, self.batch)
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.gemm_ws = kernels.linear_workspace(device)
         self.layers = [
             DecoderLayer(layer_for_device(tensors, i, cfg, device), cfg, n_sink=n_sink,
                          window=window, max_tokens=max_tokens, qk_norm=qk_norm,
-                         workspace=self.workspace, fold_norm=fold_norm, batch=self.batch)
+                         workspace=self.workspace, fold_norm=fold_norm, batch=self.batch,
+                         gemm_workspace=self.gemm_ws)
             for i in range(int(cfg["num_hidden_layers"]))
         ]
         self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
