@@ -319,6 +319,58 @@ def time_steps(step: Step, steps: int, warmup: int, world: int, dev_index: int):
     return ms, clk.summary()
 
 
+def parity_report(step: Step) -> dict:
+    """One step's four outputs against a plain PyTorch fp32 reference computed
+    on the GPU from the same 16-bit inputs, with the reference's rounding
+    points (kernels/matmul.cu:43, fused_swiglu.cu:11-15, softmax.cu:81): per
+    projection the normwise max relative error max|y-r| / max|r|, the
+    elementwise one max |y-r|/|r| over |r| >= 1e-2 max|r|, the mean absolute
+    error and the share of bit-identical outputs.  Outside the timed region."""
+    import torch.nn.functional as F
+
+    if step.world != 1:
+        return {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        step.run(0)
+        torch.cuda.synchronize()
+        L = step.layers[0]
+        dt = step.h.dtype
+
+        def r16(t):
+            return t.to(dt).float()
+
+        gu = L["gate_up"].view(IM // 64, 2, 64, H)
+        wg, wu = gu[:, 0].reshape(IM, H), gu[:, 1].reshape(IM, H)
+        g = r16(F.linear(step.h2.float(), wg.float()))
+        u = r16(F.linear(step.h2.float(), wu.float()))
+        refs = {
+            "qkv": (step.qkv, r16(F.linear(step.h.float(), L["qkv"].float()))),
+            "o_proj": (step.x1, r16(step.x.float() + r16(F.linear(step.attn.float(),
+                                                                  L["o_proj"].float())))),
+            "gate_up": (step.act, r16(g / (1.0 + torch.exp(-g)) * u)),
+            "down": (step.x2, r16(step.x1.float() + r16(F.linear(step.act.float(),
+                                                                 L["down"].float())))),
+        }
+        out = {}
+        for k, (y, r) in refs.items():
+            y = y.float()
+            d = (y - r).abs()
+            ra = r.abs()
+            mx = float(ra.max())
+            keep = ra >= 1e-2 * mx
+            out[k] = {"max_rel_normwise": float(d.max()) / mx,
+                      "max_rel_elementwise": float((d[keep] / ra[keep]).max()),
+                      "mae": float(d.mean()), "exact": float((d == 0).double().mean())}
+            out[k] = {kk: round(v, 6) for kk, v in out[k].items()}
+        out["reference"] = "torch fp32 GEMM on the GPU, 16-bit rounding at the reference's points"
+        out["bar"] = "max relative error <= 1e-2, mean absolute error <= 1e-3"
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def kernel_breakdown(step: Step, n: int):
     """Average device time per launch of each projection (CUDA events on the
     launching stream, inside a captured graph of n steps)."""
@@ -850,6 +902,7 @@ def run_ours(args, rank, world, local_rank):
     value = STEP_FLOPS * args.steps / (ms / 1e3) / 1e12
 
     kt = kernel_breakdown(step, args.breakdown_steps) if world == 1 else None
+    parity = parity_report(step) if world == 1 else None
     bar = cublas_bar(step, args.steps) if world == 1 and args.cublas_bar else None
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     e2e_ms, h2d, d2h = e2e_through_abi(step, e2e_steps, dev)
@@ -887,6 +940,8 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": step.launches * args.steps,
         "clocks": clocks,
     }
+    if parity:
+        line["parity"] = parity
     if kt is not None:
         dom = "gate_up"
         avg_ms = kt[dom]
