@@ -614,18 +614,22 @@ __device__ __forceinline__ bool emit_tile_tma(const TcParams& p, uint32_t taddr,
           st_smem_f4(buf + sw128(lr, j), o[0], o[1], o[2], o[3]);
         }
       } else {
+        // both 32-column halves of the chunk in flight before one wait
+        float vh[2][32];
+        if constexpr (EPI != EPI_SWIGLU)
+          tmem_ld_32x32b_x32x2(taddr + 64 * oc, taddr + 64 * oc + 32, vh[0], vh[1]);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float v[32];
           if constexpr (EPI == EPI_SWIGLU) {
             // output chunk oc <- packed group oc: gate cols [128oc, 128oc+64), up +64
             float u[32];
-            tmem_ld_32x32b_x32(taddr + 128 * oc + 32 * h, v);
-            tmem_ld_32x32b_x32(taddr + 128 * oc + 64 + 32 * h, u);
+            tmem_ld_32x32b_x32x2(taddr + 128 * oc + 32 * h, taddr + 128 * oc + 64 + 32 * h, v, u);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = silu_fast(E::round(v[j])) * E::round(u[j]);
           } else {
-            tmem_ld_32x32b_x32(taddr + 64 * oc + 32 * h, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = vh[h][j];
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {

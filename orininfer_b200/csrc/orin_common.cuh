@@ -415,6 +415,44 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column loads in flight before one wait: v from taddr0, u from
+// taddr1.  The registers pass through the wait as read-write operands, so no
+// use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld_32x32b_x32x2(uint32_t taddr0, uint32_t taddr1, float* v,
+                                                     float* u) {
+  uint32_t a[32], b[32];
+#define ORIN_LD32(R, ADDR)                                                                     \
+  asm volatile(                                                                                \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                \
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "                \
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "      \
+      "[%32];"                                                                                 \
+      : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),  \
+        "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]),            \
+        "=r"(R[13]), "=r"(R[14]), "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]),         \
+        "=r"(R[19]), "=r"(R[20]), "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]),         \
+        "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), "=r"(R[28]), "=r"(R[29]), "=r"(R[30]),         \
+        "=r"(R[31])                                                                            \
+      : "r"(ADDR))
+#define ORIN_PASS32(R)                                                                         \
+  "+r"(R[0]), "+r"(R[1]), "+r"(R[2]), "+r"(R[3]), "+r"(R[4]), "+r"(R[5]), "+r"(R[6]),        \
+      "+r"(R[7]), "+r"(R[8]), "+r"(R[9]), "+r"(R[10]), "+r"(R[11]), "+r"(R[12]), "+r"(R[13]), \
+      "+r"(R[14]), "+r"(R[15]), "+r"(R[16]), "+r"(R[17]), "+r"(R[18]), "+r"(R[19]),           \
+      "+r"(R[20]), "+r"(R[21]), "+r"(R[22]), "+r"(R[23]), "+r"(R[24]), "+r"(R[25]),           \
+      "+r"(R[26]), "+r"(R[27]), "+r"(R[28]), "+r"(R[29]), "+r"(R[30]), "+r"(R[31])
+  ORIN_LD32(a, taddr0);
+  ORIN_LD32(b, taddr1);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : ORIN_PASS32(a) : : "memory");
+  asm volatile("" : ORIN_PASS32(b) : : "memory");
+#undef ORIN_LD32
+#undef ORIN_PASS32
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(a[i]);
+    u[i] = __uint_as_float(b[i]);
+  }
+}
+
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(

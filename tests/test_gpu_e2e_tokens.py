@@ -27,9 +27,11 @@ and asserts:
   * every step whose reference top-2 gap exceeds twice that step's band picks
     the reference's token: every mismatch is a near-tie the band explains;
   * the logits stay within 5e-2 of the largest logit at every step (a guard
-    against gross errors; the printed control, the same library with another
-    fp32 summation order in its decode attention, shows how far summation
-    order alone moves this model's logits);
+    against gross errors), and their median band against the reference is at
+    most twice that of a control: this library against itself with another
+    fp32 summation order in its decode attention, i.e. how far summation order
+    alone moves this model's logits (measured: 0.084 against the reference,
+    0.0845 for the control);
   * free-running generation (each side feeding back its own tokens) agrees
     with the reference up to its first divergence, which is such a near-tie.
 Batch 16 has no counterpart in the single-sequence reference
@@ -158,6 +160,9 @@ def test_teacher_forced_tokens_match_the_reference_outside_near_ties(e2e):
     # not a precision claim: 22 bf16 layers of random weights amplify
     # summation-order differences to a few per cent of the logits
     assert worst_rel <= 5e-2
+    # the distance to the reference is the model's own sensitivity to fp32
+    # summation order (measured ratio ~1), not an error of this library
+    assert np.median(bands) <= 2.0 * np.median(ctrl_bands)
     assert agree >= 0.9 * NEW
 
 
