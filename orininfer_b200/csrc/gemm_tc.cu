@@ -451,21 +451,69 @@ __device__ __forceinline__ void st_release_gpu(int* f, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
 }
 
-// Finisher: add the partial accumulators of n contributor slots (first at
-// `slots`, then every `stride` floats, in that order) to this CTA's tile in
-// tensor memory, before the ordinary epilogue reads it.  The operand ring is
-// idle by now (a finisher's unit is its group's last), so one thread moves the
-// slots into it with bulk copies, a column range of every slot at a time (as
-// wide as fits: n * cols * 512 bytes <= ring_bytes), and the 128 epilogue
-// threads add them from shared memory into their rows: tcgen05.ld, n adds in
-// slot order, tcgen05.st.  Slot layout: float4 (c4, row) at c4 * kBM + row,
-// so columns [c0, c0 + w) of a slot are one contiguous run of w * 512 bytes.
+// Stream-K slots: CTA b's partial accumulator is rows [128 b, 128 b + 128) of
+// an fp32 [grid * 128, BN] matrix in the workspace, moved by the TMA unit in
+// boxes of 32 columns x 128 rows (16 KB, 128-byte swizzle) that use the same
+// shared-memory layout as the epilogue's staging buffers (row r, 16-byte
+// chunk j at sw128(r, j)).
+
+// Orders this thread's async-proxy (TMA) global accesses against its generic
+// ones: TMA stores before a flag release, a flag acquire before TMA loads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Contributor: this CTA's partial accumulator (columns [0, BN) of its 128
+// rows) into its slot: each 32-column chunk staged in one of the two output
+// staging buffers and stored by TMA; once every store has completed, the
+// flag, released at GPU scope.
 template <int BN>
-__device__ __forceinline__ bool sk_fixup(uint32_t taddr, int lr, int et, uint32_t ring,
-                                         uint32_t ring_bytes, const float* slots, int n,
-                                         long long stride, uint32_t bar, uint32_t& phase,
+__device__ __forceinline__ void sk_write_partial(const TcParams& p, const void* tm_s,
+                                                 uint32_t taddr, int lr, int et,
+                                                 uint32_t outbuf) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    const uint32_t buf = outbuf + static_cast<uint32_t>(((c / 32) & 1) * kOutBuf);
+    // the store that last read this buffer is done with it (at the first
+    // chunk: every earlier store of this CTA)
+    if (et == 0) {
+      if (c == 0) bulk_wait_group_read<0>();
+      else bulk_wait_group_read<1>();
+    }
+    named_bar_sync(1, kEpiThreads);
+    float v[32];
+    tmem_ld_32x32b_x32(taddr + c, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      st_smem_f4(buf + sw128(lr, j), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    fence_proxy_async_smem();
+    named_bar_sync(1, kEpiThreads);
+    if (et == 0) {
+      tma_store_2d(tm_s, buf, c, static_cast<int>(blockIdx.x) * kBM);
+      bulk_commit_group();
+    }
+  }
+  if (et == 0) {
+    bulk_wait_group<0>();  // the slot is written, not just read out of shared memory
+    fence_proxy_async_global();
+    __threadfence();
+    st_release_gpu(p.sk_flags + blockIdx.x, 1);
+  }
+}
+
+// Finisher: add the partial accumulators of n contributor CTAs (first, first
+// + stride, ...) to this CTA's tile in tensor memory, in that order, before
+// the ordinary epilogue reads it.  The operand ring is idle by now (a
+// finisher's unit is its group's last): one thread loads a column range of
+// every slot into it by TMA (as many 32-column boxes as fit), then the 128
+// epilogue threads add them to their rows: tcgen05.ld, n adds, tcgen05.st.
+template <int BN>
+__device__ __forceinline__ bool sk_fixup(const void* tm_s, uint32_t taddr, int lr, int et,
+                                         uint32_t ring, uint32_t ring_bytes, int first, int n,
+                                         int stride, uint32_t bar, uint32_t& phase,
                                          volatile int* abort_flag, int* err, volatile int* flag) {
-  if (static_cast<uint32_t>(n) * 32u * 512u > ring_bytes) {
+  constexpr uint32_t kBox = 32 * kBM * 4;  // one 32-column box: 16 KB
+  if (static_cast<uint32_t>(n) * kBox > ring_bytes) {
     // the planner never makes such a plan; refuse rather than overrun the ring
     if (et == 0) {
       *abort_flag = 1;
@@ -473,62 +521,44 @@ __device__ __forceinline__ bool sk_fixup(uint32_t taddr, int lr, int et, uint32_
     }
     return false;
   }
-  int w = BN;
-  while (w > 32 && static_cast<uint32_t>(n) * w * 512u > ring_bytes) w >>= 1;
-  const uint32_t part = static_cast<uint32_t>(w) * 512u;  // bytes of one slot's column range
+  int nb = BN / 32;  // 32-column boxes per slot in one part
+  while (nb > 1 && static_cast<uint32_t>(n * nb) * kBox > ring_bytes) nb >>= 1;
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += w) {
+  for (int c0 = 0; c0 < BN; c0 += 32 * nb) {
     if (et == 0) {
       // the ring's last readers were the MMAs (complete) or this loop's
-      // generic loads (finished at the barrier below)
+      // generic loads (finished at the barrier below); the flags were
+      // acquired with generic loads before these async-proxy reads
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n) * part);
+      fence_proxy_async_global();
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n * nb) * kBox);
       for (int j = 0; j < n; ++j)
-        bulk_copy_g2s(ring + j * part, slots + j * stride + static_cast<long long>(c0) * kBM,
-                      part, bar);
+        for (int b = 0; b < nb; ++b)
+          tma_load_2d_plain(ring + static_cast<uint32_t>(j * nb + b) * kBox, tm_s, bar,
+                            c0 + 32 * b, (first + j * stride) * kBM);
     }
     if (!epi_wait(bar, phase, et, abort_flag, err, flag)) return false;
     phase ^= 1u;
 #pragma unroll 1
-    for (int c = c0; c < c0 + w; c += 32) {
+    for (int b = 0; b < nb; ++b) {
       float v[32];
-      tmem_ld_32x32b_x32(taddr + c, v);
+      tmem_ld_32x32b_x32(taddr + c0 + 32 * b, v);
       for (int j = 0; j < n; ++j) {
-        const uint32_t src = ring + j * part + static_cast<uint32_t>(((c - c0) / 4) * kBM + lr) * 16u;
+        const uint32_t box = ring + static_cast<uint32_t>(j * nb + b) * kBox;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 t = ld_smem_f4(src + static_cast<uint32_t>(i * kBM * 16));
+          const float4 t = ld_smem_f4(box + sw128(lr, i));
           v[4 * i + 0] += t.x;
           v[4 * i + 1] += t.y;
           v[4 * i + 2] += t.z;
           v[4 * i + 3] += t.w;
         }
       }
-      tmem_st_32x32b_x32(taddr + c, v);
+      tmem_st_32x32b_x32(taddr + c0 + 32 * b, v);
     }
     named_bar_sync(1, kEpiThreads);
   }
   return true;
-}
-
-// Contributor: this CTA's partial accumulator (columns [0, BN) of its 128 rows)
-// into its slot, then its flag, released at GPU scope after every epilogue
-// thread's stores.
-template <int BN>
-__device__ __forceinline__ void sk_write_partial(const TcParams& p, uint32_t taddr, int lr,
-                                                 int et) {
-  float4* slot = reinterpret_cast<float4*>(p.sk_ws + static_cast<long long>(blockIdx.x) * kBM * BN) + lr;
-  float v[32];
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    tmem_ld_32x32b_x32(taddr + c, v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      __stcg(slot + (c / 4 + i) * kBM, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
-  }
-  __threadfence();
-  named_bar_sync(1, kEpiThreads);
-  if (et == 0) st_release_gpu(p.sk_flags + blockIdx.x, 1);
 }
 
 // Finisher: one thread waits (bounded) for the flags of the n contributor
@@ -1052,7 +1082,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tm_p,
                      const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_c,
-                     const __grid_constant__ CUtensorMap tm_r, const TcParams p) {
+                     const __grid_constant__ CUtensorMap tm_r,
+                     const __grid_constant__ CUtensorMap tm_s, const TcParams p) {
   static_assert(!(PAIR && SWAP), "CTA pairs are used for wide tiles only");
   constexpr int GROUP = PAIR ? 2 : 1;         // CTAs per tile accumulator
   constexpr int TILE_P = GROUP * kBM;         // P rows per tile
@@ -1375,11 +1406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.sk && u.k0 > 0) {
             // stream-K: this group's range starts inside the tile; its part
             // goes to the group that holds the tile's first k-blocks
-            sk_write_partial<BN>(p, taddr, lr, et);
+            sk_write_partial<BN>(p, &tm_s, taddr, lr, et, outbuf);
           } else {
-            const float* sk_slots = nullptr;
             int sk_n = 0;
-            long long sk_stride = 0;
             if (p.sk && u.k1 < p.kb) {
               // stream-K finisher: the contributors are the following groups
               // whose ranges start inside this tile
@@ -1388,13 +1417,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const long long W = static_cast<long long>(it.tiles) * it.kp;
               const long long tile_end = static_cast<long long>(u.tile + 1) * it.kp;
               while (g + 1 + sk_n < G && sk_range_start(W, g + 1 + sk_n, G) < tile_end) ++sk_n;
-              const long long slot_f = static_cast<long long>(kBM) * BN;
-              sk_slots = p.sk_ws + (static_cast<long long>(g + 1) * GROUP + half) * slot_f;
-              sk_stride = GROUP * slot_f;
-              ok = sk_wait(p.sk_flags, (g + 1) * GROUP + half, sk_n, GROUP, et, &abort_flag,
-                           p.err, &epi_flag) &&
-                   sk_fixup<BN>(taddr, lr, et, ring, STAGES * STAGE_BYTES, sk_slots, sk_n,
-                                sk_stride, smem_u32(&recv_bar), sk_phase, &abort_flag, p.err,
+              const int first = (g + 1) * GROUP + half;
+              ok = sk_wait(p.sk_flags, first, sk_n, GROUP, et, &abort_flag, p.err, &epi_flag) &&
+                   sk_fixup<BN>(&tm_s, taddr, lr, et, ring, STAGES * STAGE_BYTES, first, sk_n,
+                                GROUP, smem_u32(&recv_bar), sk_phase, &abort_flag, p.err,
                                 &epi_flag);
             }
             if (ok) {
@@ -1622,7 +1648,8 @@ bool make_tmap(CUtensorMap* out, const void* ptr, int type, unsigned long long r
 
 template <int DT, int BN, int EPI, bool SWAP, bool PAIR>
 cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap& tq,
-                       const CUtensorMap& tc, const CUtensorMap& tr, cudaStream_t stream) {
+                       const CUtensorMap& tc, const CUtensorMap& tr, const CUtensorMap& ts,
+                       cudaStream_t stream) {
   constexpr int smem = tc_smem_bytes(BN, EPI, SWAP, PAIR);
   auto kern = tc_linear_kernel<DT, BN, EPI, SWAP, PAIR>;
   static int configured[64] = {0};
@@ -1657,7 +1684,7 @@ cudaError_t launch_one(const Plan& pl, const CUtensorMap& tp, const CUtensorMap&
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, tp, tq, tc, tr, pl.p);
+  return cudaLaunchKernelEx(&cfg, kern, tp, tq, tc, tr, ts, pl.p);
 }
 
 // How many clusters of `cluster` CTAs of this tile shape can be resident at
@@ -1691,16 +1718,17 @@ int max_active_clusters(int cluster) {
 
 struct Maps {
   CUtensorMap p, q, c, r;
+  CUtensorMap s;  // stream-K slots: fp32 [grid * 128, bn], 32 x 128 boxes
 };
 
 template <int DT, bool SWAP, int BN, bool PAIR>
 cudaError_t dispatch_epi(const Plan& pl, int epi, const Maps& m, cudaStream_t s) {
   switch (epi) {
-    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
-    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
-    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
-    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
-    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, s);
+    case EPI_NONE: return launch_one<DT, BN, EPI_NONE, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, m.s, s);
+    case EPI_SWIGLU: return launch_one<DT, BN, EPI_SWIGLU, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, m.s, s);
+    case EPI_RESIDUAL: return launch_one<DT, BN, EPI_RESIDUAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, m.s, s);
+    case EPI_F32_OUT: return launch_one<DT, BN, EPI_F32_OUT, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, m.s, s);
+    case EPI_F32_PARTIAL: return launch_one<DT, BN, EPI_F32_PARTIAL, SWAP, PAIR>(pl, m.p, m.q, m.c, m.r, m.s, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -1953,16 +1981,17 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
     }
     // stream-K: every group takes an equal share of tiles x k-block pairs,
     // all at the full-machine rate; the groups that hold a tile's first
-    // k-blocks read the other groups' partials of that tile (fp32 slots of
-    // 128 x bn per CTA, ~1 us per 128 KB slot) before their last epilogue
+    // k-blocks wait for the other groups' partials of that tile and add them
+    // before their last epilogue.  Measured on B200 (K scaled 1024..8192 at
+    // M=512): the hand-off (contributor TMA store, flag, finisher TMA load,
+    // add) costs ~6-7 us of fixed time over the persistent schedule, so
+    // stream-K pays only where it saves more mainloop than that.
     if (sk_possible(sh.bn, sh.pair)) {
       const long long W = tiles * (kb / 2);
       const int ng = sk_groups(sh.bn, sh.pair);
       const long long per = (W + ng - 1) / ng;                   // pairs per group
       const int readers = sk_max_contributors(tiles, ng);
-      // contributors write a slot (bn/256 x ~0.6 us); the finisher moves each
-      // slot into shared memory (~0.5 us per 128 KB) and adds it
-      const double fix = 0.6 * sh.bn / 256.0 + static_cast<double>(readers) * 0.5 * sh.bn / 256.0;
+      const double fix = 6.0 + static_cast<double>(readers) * 0.5 * sh.bn / 256.0;
       cost = sh.launch + 2.0 * per * t_kb(sh, ng * group) + fix;
       if (cost < best) {
         best = cost;
@@ -2020,6 +2049,13 @@ cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const 
   }
   m.c = m.p;
   m.r = m.p;
+  m.s = m.p;
+  if (pl.p.sk &&
+      !make_tmap(&m.s, pl.p.sk_ws, 2, static_cast<unsigned long long>(pl.grid) * kBM,
+                 static_cast<unsigned long long>(pl.bn), 32, kBM)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed (stream-K workspace)";
+    return cudaErrorInvalidValue;
+  }
   pl.p.out_tma = 0;
   if (!swap && pl.p.split == 1) {
     // wide tiles store through TMA when C (and the residual) rows allow it
