@@ -1991,7 +1991,7 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
       const int ng = sk_groups(sh.bn, sh.pair);
       const long long per = (W + ng - 1) / ng;                   // pairs per group
       const int readers = sk_max_contributors(tiles, ng);
-      const double fix = 6.0 + static_cast<double>(readers) * 0.5 * sh.bn / 256.0;
+      const double fix = 8.0 + static_cast<double>(readers) * 0.5 * sh.bn / 256.0;
       cost = sh.launch + 2.0 * per * t_kb(sh, ng * group) + fix;
       if (cost < best) {
         best = cost;

@@ -60,6 +60,28 @@ def _worker(rank, world, port, q):
         assert_close(out.cpu().float(), from_bits(ref, torch.float16).float(),
                      f"row-parallel rank {rank}", exact_min=EXACT_MIN)
 
+        # the entry point without a caller partial buffer (file-scope device
+        # array): the same kernels and summation order, so the same bits
+        import ctypes
+
+        from orininfer_b200 import _lib
+
+        def row_static(stream=None):
+            o = torch.empty_like(out)
+            s = torch.cuda.current_stream() if stream is None else stream
+            st = _lib.lib.orin_tp_linear_row_static(
+                comm._h, ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(a_dev.data_ptr()),
+                ctypes.c_void_p(w_dev.data_ptr()), M, H, ks, 0, ctypes.c_void_p(r_dev.data_ptr()),
+                ctypes.c_void_p(s.cuda_stream))
+            assert st == _lib.OK, _lib.lib.orin_last_error()
+            comm.wait()
+            ob.device_check()
+            return o
+
+        for _ in range(2):
+            assert torch.equal(row_static().view(torch.int16), out.view(torch.int16)), \
+                "static scratch vs caller scratch (nccl)"
+
         # The same calls reduced over NVLink peer memory, summed in rank order:
         # deterministic, within the bar of the oracle, and for two ranks
         # (p0 + p1 either way) the bits of the NCCL path.
@@ -74,6 +96,9 @@ def _worker(rank, world, port, q):
         out = outs[0]
         for i, o in enumerate(outs[1:]):
             assert torch.equal(o.view(torch.int16), out.view(torch.int16)), f"p2p call {i + 1}"
+        for _ in range(2):
+            assert torch.equal(row_static().view(torch.int16), out.view(torch.int16)), \
+                "static scratch vs caller scratch (p2p)"
         # captured once, replayed: the epoch lives in device memory
         static_out = torch.empty_like(out)
         g = torch.cuda.CUDAGraph()
