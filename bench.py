@@ -541,7 +541,8 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
     lm_head = weight(VOCAB, H)
     w_bytes = 2 * (N_LAYERS * (QKV_N * H + H * H + 2 * IM * H + H * IM) + VOCAB * H)
     out = {"what": "22 layers x (q/k/v, o_proj+residual, gate/up+SwiGLU, down+residual) + "
-                   "LM head (fp32 logits), CUDA graph per M, weights > L2",
+                   "LM head (fp32 logits), CUDA graph per M, weights > L2; each launch on the "
+                   "weight stream also streams the next projection's weights into L2",
            "weight_bytes": w_bytes, "launches_per_step": 4 * N_LAYERS + 1, "by_tokens": {}}
     peaks, _ = load_peaks()
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
@@ -578,21 +579,32 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
         act = torch.empty((m, IM), dtype=torch.float16, device=dev)
         logits = torch.empty((m, VOCAB), dtype=torch.float32, device=dev)
 
-        def ours():
+        # each projection's weights follow the previous one's on the stream; a
+        # launch on the weight stream may stream the next one's into L2
+        # ahead (orin_linear_prefetch)
+        seq = [w for L in layers for w in (L["qkv"], L["o_proj"], L["gate_up"], L["down"])]
+        nxt = {id(w): n for w, n in zip(seq, seq[1:] + [lm_head])}
+
+        def ours(hint=True):
             h.copy_(h0)
             for L in layers:
-                ob.linear_into(qkv, x, L["qkv"])
-                ob.linear_into(h, attn, L["o_proj"], epilogue="residual", residual=h)
-                ob.linear_into(act, x, L["gate_up"], epilogue="swiglu")
-                ob.linear_into(h, act, L["down"], epilogue="residual", residual=h)
+                pf = (lambda w: nxt[id(w)]) if hint else (lambda w: None)
+                ob.linear_into(qkv, x, L["qkv"], prefetch=pf(L["qkv"]))
+                ob.linear_into(h, attn, L["o_proj"], epilogue="residual", residual=h,
+                               prefetch=pf(L["o_proj"]))
+                ob.linear_into(act, x, L["gate_up"], epilogue="swiglu", prefetch=pf(L["gate_up"]))
+                ob.linear_into(h, act, L["down"], epilogue="residual", residual=h,
+                               prefetch=pf(L["down"]))
             ob.linear_into(logits, h, lm_head, epilogue="f32")
 
         ms = graph_ms(ours)
+        ms_plain = graph_ms(lambda: ours(hint=False))
         ob.device_check()
         a_bytes = 2 * m * (N_LAYERS * (H + QKV_N + 3 * H + H + IM + IM + 2 * H) + H) + 4 * m * VOCAB
         gbs = (w_bytes + a_bytes) / (ms / 1e3) / 1e9
         rec = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1),
-               "hbm_frac": round(gbs / hbm, 4)}
+               "hbm_frac": round(gbs / hbm, 4),
+               "ms_per_step_without_l2_hint": round(ms_plain, 4)}
         if with_cublas:
             def ref():
                 hh = h0.clone()
@@ -1075,8 +1087,9 @@ def run_model_decode(args) -> dict:
         tensors[name] = (torch.randn(shape[key], generator=gen, device=dev) * 0.02).half()
     n_sink, window = 4, 1024
     B = int(getattr(args, "batch", 1))
+    fold = bool(getattr(args, "fold_norm", False))
     model = Decoder(tensors, cfg, dev, n_sink=n_sink, window=window, max_tokens=n_sink + window,
-                    batch=B)
+                    batch=B, fold_norm=fold)
     del tensors
     prompts = [torch.randint(0, cfg["vocab_size"], (2048,), generator=gen, device=dev,
                              dtype=torch.int32) for _ in range(B)]
@@ -1148,10 +1161,12 @@ def run_model_decode(args) -> dict:
             # per layer: norm, q/k/v, RoPE + append, attention, combine, o_proj,
             # norm, gate/up, down; then embedding, final norm, LM head (key
             # reset, weight stream, decode), token copy
-            "launches_per_step": L * 9 + 6, "steps": args.model_decode,
+            "launches_per_step": L * (7 if fold else 9) + (5 if fold else 6),
+            "steps": args.model_decode,
             "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
             "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,
-                       "window": window, "prompt": 2048, "batch": B, "graph": True}}
+                       "window": window, "prompt": 2048, "batch": B, "graph": True,
+                       "fold_norm": fold}}
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -1256,6 +1271,8 @@ def main():
                     help="instead of the layer bench: time this many graph-replayed greedy "
                          "decode steps of the whole 22-layer model (prefill of a 2048-token "
                          "prompt first) and print that line")
+    ap.add_argument("--fold-norm", action="store_true",
+                    help="with --model-decode: fold each RMSNorm into the projection after it")
     ap.add_argument("--batch", type=int, default=1,
                     help="with --model-decode: sequences decoded together (per-sequence KV "
                          "pools, one weight stream per step)")

@@ -50,6 +50,10 @@ struct GvParams {
   int n_offset;  // EPI_ARGMAX: vocabulary position of row 0 (a tensor-parallel shard)
   const void* norm;  // NORM: RMSNorm weight [K] applied to every token row of X first
   float eps;
+  // optional: bytes of a later projection's weights this launch streams into
+  // L2 while it waits for the previous kernel (each CTA an equal share)
+  const char* pf;
+  long long pf_bytes;
 };
 
 __device__ __forceinline__ uint4 ld_weights(const void* p) {
@@ -191,22 +195,52 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[h][t][i] = 0.f;
 
-  bool waited = false;
-  __shared__ float s_r[NORM ? kGemvMaxTokens : 1];
-  if constexpr (NORM) {
-    __shared__ float s_ss[kGvWarps][kGemvMaxTokens];
-    // this warp's k-range of every row of the group into L2 while the
-    // previous kernel finishes, then the row statistics
-    if (kb0 < kb1 && lane < kGvRows * H) {
+  // one batch of U k-blocks of this warp's weight rows into registers
+  uint4 w[U][H][2];
+  auto load_w = [&](int kb) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = (kb + u) * kGvBlockK + 8 * q;
+      const bool kin = (kb + u < kb1) && (k < p.K);
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          w[u][h][r] = (kin && wv[h][r]) ? ld_weights(wp[h][r] + (kb + u) * kGvBlockK)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // The weights do not depend on the previous kernel: the first batch goes
+  // into registers and the rest of this warp's k-range into L2 before
+  // griddepcontrol.wait, so the weight stream overlaps the previous kernel.
+  if (kb0 < kb1) load_w(kb0);
+  {
+    const int rest = kb0 + U;
+    if (rest < kb1 && lane < kGvRows * H) {
       const int row = wrow[lane / kGvRows] + lane % kGvRows;
       const int k_end = (kb1 * kGvBlockK < p.K) ? kb1 * kGvBlockK : p.K;
       if (row < p.w_rows)
-        prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + kb0 * kGvBlockK,
-                          static_cast<uint32_t>((k_end - kb0 * kGvBlockK) * 2));
+        prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + rest * kGvBlockK,
+                          static_cast<uint32_t>((k_end - rest * kGvBlockK) * 2));
     }
-    pdl_launch_dependents();
-    pdl_wait();
-    waited = true;
+  }
+  // A later projection's weights, into L2 ahead of its own launch (this CTA's
+  // 256-byte-aligned share, in pieces of at most 64 KB).
+  if (p.pf_bytes > 0 && threadIdx.x == 0) {
+    const long long per = ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 255) & ~255LL;
+    const long long lo = static_cast<long long>(blockIdx.x) * per;
+    const long long hi = lo + per < p.pf_bytes ? lo + per : p.pf_bytes;
+    for (long long a = lo; a < hi; a += 65536) {
+      const long long n = hi - a < 65536 ? hi - a : 65536;
+      prefetch_l2_bytes(p.pf + a, static_cast<uint32_t>(n));
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float s_r[NORM ? kGemvMaxTokens : 1];
+  if constexpr (NORM) {
+    // the row statistics (the token rows come from the previous kernel)
+    __shared__ float s_ss[kGvWarps][kGemvMaxTokens];
     for (int m = 0; m < p.M; ++m) {
       float ss = 0.f;
       for (int c = threadIdx.x; c < p.K / 8; c += kGvThreads) {
@@ -233,32 +267,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   }
   const T* NW = static_cast<const T*>(p.norm);
   for (int kb = kb0; kb < kb1; kb += U) {
-    uint4 w[U][H][2];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int k = (kb + u) * kGvBlockK + 8 * q;
-      const bool kin = (kb + u < kb1) && (k < p.K);
-#pragma unroll
-      for (int h = 0; h < H; ++h)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-          w[u][h][r] = (kin && wv[h][r]) ? ld_weights(wp[h][r] + (kb + u) * kGvBlockK)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-    }
-    if (!waited) {
-      // the rest of this warp's k-range of every row of the group, into L2
-      const int rest = kb + U;
-      if (rest < kb1 && lane < kGvRows * H) {
-        const int row = wrow[lane / kGvRows] + lane % kGvRows;
-        const int k_end = (kb1 * kGvBlockK < p.K) ? kb1 * kGvBlockK : p.K;
-        if (row < p.w_rows)
-          prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + rest * kGvBlockK,
-                            static_cast<uint32_t>((k_end - rest * kGvBlockK) * 2));
-      }
-      pdl_launch_dependents();
-      pdl_wait();
-      waited = true;
-    }
+    if (kb != kb0) load_w(kb);
     uint4 x[U][NT];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -293,13 +302,6 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
                         x[u][t].z, x[u][t].w);
         }
   }
-  if (!waited) {
-    // a warp without k-blocks (K shorter than 8 blocks) still orders its
-    // reads of the residual after the previous kernel
-    pdl_launch_dependents();
-    pdl_wait();
-  }
-
 #pragma unroll
   for (int h = 0; h < H; ++h)
 #pragma unroll
@@ -448,10 +450,12 @@ cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int
 
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t s, int n_offset, const void* norm,
-                        float eps) {
+                        float eps, const void* pf, long long pf_bytes) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
   if (norm && K % 8 != 0) return cudaErrorInvalidValue;
   GvParams p;
+  p.pf = static_cast<const char*>(pf);
+  p.pf_bytes = pf ? pf_bytes : 0;
   p.n_offset = n_offset;
   p.norm = norm;
   p.eps = eps;
