@@ -541,8 +541,7 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
     lm_head = weight(VOCAB, H)
     w_bytes = 2 * (N_LAYERS * (QKV_N * H + H * H + 2 * IM * H + H * IM) + VOCAB * H)
     out = {"what": "22 layers x (q/k/v, o_proj+residual, gate/up+SwiGLU, down+residual) + "
-                   "LM head (fp32 logits), CUDA graph per M, weights > L2; each launch on the "
-                   "weight stream also streams the next projection's weights into L2",
+                   "LM head (fp32 logits), CUDA graph per M, weights > L2",
            "weight_bytes": w_bytes, "launches_per_step": 4 * N_LAYERS + 1, "by_tokens": {}}
     peaks, _ = load_peaks()
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
@@ -579,32 +578,21 @@ def decode_path(dev, reps: int, with_cublas: bool = True) -> dict:
         act = torch.empty((m, IM), dtype=torch.float16, device=dev)
         logits = torch.empty((m, VOCAB), dtype=torch.float32, device=dev)
 
-        # each projection's weights follow the previous one's on the stream; a
-        # launch on the weight stream may stream the next one's into L2
-        # ahead (orin_linear_prefetch)
-        seq = [w for L in layers for w in (L["qkv"], L["o_proj"], L["gate_up"], L["down"])]
-        nxt = {id(w): n for w, n in zip(seq, seq[1:] + [lm_head])}
-
-        def ours(hint=True):
+        def ours():
             h.copy_(h0)
             for L in layers:
-                pf = (lambda w: nxt[id(w)]) if hint else (lambda w: None)
-                ob.linear_into(qkv, x, L["qkv"], prefetch=pf(L["qkv"]))
-                ob.linear_into(h, attn, L["o_proj"], epilogue="residual", residual=h,
-                               prefetch=pf(L["o_proj"]))
-                ob.linear_into(act, x, L["gate_up"], epilogue="swiglu", prefetch=pf(L["gate_up"]))
-                ob.linear_into(h, act, L["down"], epilogue="residual", residual=h,
-                               prefetch=pf(L["down"]))
+                ob.linear_into(qkv, x, L["qkv"])
+                ob.linear_into(h, attn, L["o_proj"], epilogue="residual", residual=h)
+                ob.linear_into(act, x, L["gate_up"], epilogue="swiglu")
+                ob.linear_into(h, act, L["down"], epilogue="residual", residual=h)
             ob.linear_into(logits, h, lm_head, epilogue="f32")
 
         ms = graph_ms(ours)
-        ms_plain = graph_ms(lambda: ours(hint=False))
         ob.device_check()
         a_bytes = 2 * m * (N_LAYERS * (H + QKV_N + 3 * H + H + IM + IM + 2 * H) + H) + 4 * m * VOCAB
         gbs = (w_bytes + a_bytes) / (ms / 1e3) / 1e9
         rec = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1),
-               "hbm_frac": round(gbs / hbm, 4),
-               "ms_per_step_without_l2_hint": round(ms_plain, 4)}
+               "hbm_frac": round(gbs / hbm, 4)}
         if with_cublas:
             def ref():
                 hh = h0.clone()

@@ -142,21 +142,6 @@ orin_status orin_linear_ws(void* C, const void* A, const void* W,
                            const void* residual, void* workspace,
                            size_t workspace_bytes, void* stream);
 
-/*
- * orin_linear plus a hint for a decode step's chain of projections (no
- * counterpart in the reference): when this call runs on the decode weight
- * stream (few token rows), it also streams next_bytes of next_W (typically the
- * weights of the next projection on the stream) into L2 while it waits for the
- * previous kernel, so that HBM keeps streaming weights while each launch's
- * dependent part (token loads, reduction, epilogue) runs.  Results are exactly
- * orin_linear's; other paths ignore the hint.  next_W 16-byte aligned,
- * next_bytes a multiple of 16 (0: no hint).
- */
-orin_status orin_linear_prefetch(void* C, const void* A, const void* W,
-                                 int M, int N, int K, int dtype, int epilogue,
-                                 const void* residual, const void* next_W,
-                                 long long next_bytes, void* stream);
-
 /* Workspace bytes that let orin_linear_ws choose any plan on the current
  * device (one 128 x 256 fp32 slot per SM plus 4 KB of flags: 19 MB on B200). */
 orin_status orin_linear_workspace_bytes(size_t* bytes);

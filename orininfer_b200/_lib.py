@@ -66,7 +66,6 @@ SIGNATURES = {
     "orin_plan_info_ws": (_i, [_i, _i, _i, _i, _i, _i, _sz, ctypes.POINTER(_i)]),
     "orin_linear_ws": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]),
     "orin_linear_workspace_bytes": (_i, [ctypes.POINTER(_sz)]),
-    "orin_linear_prefetch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _ll, _vp]),
     "orin_silu_mul": (_i, [_vp, _vp, _vp, _ll, _i, _vp]),
     "orin_add": (_i, [_vp, _vp, _ll, _i, _vp]),
     "orin_widen_f32": (_i, [_vp, _vp, _ll, _i, _vp]),

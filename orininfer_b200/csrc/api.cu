@@ -107,8 +107,7 @@ int choose_algo(int req, const void* A, const void* W, int M, int K) {
 
 orin_status linear_impl(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epilogue, const void* residual, int algo, void* workspace,
-                        size_t workspace_bytes, void* stream, const void* pf = nullptr,
-                        long long pf_bytes = 0);
+                        size_t workspace_bytes, void* stream);
 
 }  // namespace
 
@@ -134,22 +133,6 @@ orin_status orin_linear_ws(void* C, const void* A, const void* W, int M, int N, 
                      workspace ? workspace_bytes : 0, stream);
 }
 
-orin_status orin_linear_prefetch(void* C, const void* A, const void* W, int M, int N, int K,
-                                 int dtype, int epilogue, const void* residual,
-                                 const void* next_W, long long next_bytes, void* stream) {
-  if (next_bytes < 0 || (next_bytes > 0 && !next_W)) {
-    set_error("orin_linear_prefetch: next_bytes %lld with next_W %p", next_bytes, next_W);
-    return ORIN_ERR_INVALID_ARG;
-  }
-  if (next_bytes > 0 && (!aligned16(next_W) || next_bytes % 16 != 0)) {
-    set_error("orin_linear_prefetch: next_W must be 16-byte aligned and next_bytes a multiple "
-              "of 16");
-    return ORIN_ERR_UNSUPPORTED;
-  }
-  return linear_impl(C, A, W, M, N, K, dtype, epilogue, residual, ORIN_ALGO_AUTO, nullptr, 0,
-                     stream, next_bytes > 0 ? next_W : nullptr, next_bytes);
-}
-
 orin_status orin_linear_workspace_bytes(size_t* bytes) {
   if (!bytes) {
     set_error("orin_linear_workspace_bytes: null output");
@@ -171,8 +154,7 @@ namespace {
 
 orin_status linear_impl(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epilogue, const void* residual, int algo, void* workspace,
-                        size_t workspace_bytes, void* stream, const void* pf,
-                        long long pf_bytes) {
+                        size_t workspace_bytes, void* stream) {
   orin_status st = check_common(dtype, epilogue);
   if (st != ORIN_OK) return st;
   if (!C || !A || !W) {
@@ -209,8 +191,7 @@ orin_status linear_impl(void* C, const void* A, const void* W, int M, int N, int
     return ORIN_OK;
   }
   if (a == 4) {
-    cudaError_t e = launch_gemv(C, A, W, M, N, K, dtype, epilogue, residual, s, 0, nullptr, 0.f,
-                                pf, pf_bytes);
+    cudaError_t e = launch_gemv(C, A, W, M, N, K, dtype, epilogue, residual, s);
     if (e != cudaSuccess) return cuda_fail(e, "orin_linear (gemv)");
     return ORIN_OK;
   }

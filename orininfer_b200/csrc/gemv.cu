@@ -50,10 +50,6 @@ struct GvParams {
   int n_offset;  // EPI_ARGMAX: vocabulary position of row 0 (a tensor-parallel shard)
   const void* norm;  // NORM: RMSNorm weight [K] applied to every token row of X first
   float eps;
-  // optional: bytes of a later projection's weights this launch streams into
-  // L2 while it waits for the previous kernel (each CTA an equal share)
-  const char* pf;
-  long long pf_bytes;
 };
 
 __device__ __forceinline__ uint4 ld_weights(const void* p) {
@@ -222,17 +218,6 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
       if (row < p.w_rows)
         prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + rest * kGvBlockK,
                           static_cast<uint32_t>((k_end - rest * kGvBlockK) * 2));
-    }
-  }
-  // A later projection's weights, into L2 ahead of its own launch (this CTA's
-  // 256-byte-aligned share, in pieces of at most 64 KB).
-  if (p.pf_bytes > 0 && threadIdx.x == 0) {
-    const long long per = ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 255) & ~255LL;
-    const long long lo = static_cast<long long>(blockIdx.x) * per;
-    const long long hi = lo + per < p.pf_bytes ? lo + per : p.pf_bytes;
-    for (long long a = lo; a < hi; a += 65536) {
-      const long long n = hi - a < 65536 ? hi - a : 65536;
-      prefetch_l2_bytes(p.pf + a, static_cast<uint32_t>(n));
     }
   }
   pdl_launch_dependents();
@@ -450,12 +435,10 @@ cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int
 
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t s, int n_offset, const void* norm,
-                        float eps, const void* pf, long long pf_bytes) {
+                        float eps) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
   if (norm && K % 8 != 0) return cudaErrorInvalidValue;
   GvParams p;
-  p.pf = static_cast<const char*>(pf);
-  p.pf_bytes = pf ? pf_bytes : 0;
   p.n_offset = n_offset;
   p.norm = norm;
   p.eps = eps;

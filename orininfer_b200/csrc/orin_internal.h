@@ -81,13 +81,9 @@ cudaError_t launch_tc(const Plan& pl, int dtype, int epi, const void* A, const v
 constexpr int kGemvMaxTokens = 32;
 // norm (optional): RMSNorm weight [K] applied to the rows of A first (eps);
 // epilogues NONE, SWIGLU and ARGMAX only.
-// pf / pf_bytes (optional, both 16-byte multiples): a later projection's
-// weights, streamed into L2 by this launch while it waits for the previous
-// kernel.
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t stream, int n_offset = 0,
-                        const void* norm = nullptr, float eps = 0.f, const void* pf = nullptr,
-                        long long pf_bytes = 0);
+                        const void* norm = nullptr, float eps = 0.f);
 int gemv_grid(int N);
 // LM head + greedy argmax per row: keys[m] = the best 64-bit argmax key of
 // row m over the V vocabulary rows of W (positions v_offset + v), then

@@ -144,16 +144,13 @@ def linear_workspace(device=None) -> torch.Tensor:
 def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue: str = "none",
                 residual: Optional[torch.Tensor] = None, algo: str = "auto",
                 workspace: Optional[torch.Tensor] = None,
-                prefetch: Optional[torch.Tensor] = None,
                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """out = epilogue(x · w^T) written into `out` (see include/orin_b200.h).
 
     x [M, K]; w [N, K] ([2N, K] packed gate/up for "swiglu"); out [M, N]
     (float32 for "f32" / "f32_partial", else x.dtype); residual [M, N].
     With a workspace (linear_workspace()), prefill-sized problems may take the
-    stream-K schedule (orin_linear_ws); algo must then be "auto".  `prefetch`
-    (a later projection's weight tensor) is streamed into L2 by decode-sized
-    calls while they wait for the previous kernel (orin_linear_prefetch).
+    stream-K schedule (orin_linear_ws); algo must then be "auto".
     """
     _need_cuda(out, x, w, residual, workspace)
     dt = _dtype_code(x)
@@ -162,15 +159,6 @@ def linear_into(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *, epilogue
     epi = _EPILOGUES[epilogue]
     M, K = x.shape
     N = out.shape[-1]
-    if prefetch is not None:
-        if workspace is not None or algo != "auto":
-            raise ValueError("prefetch goes with algo='auto' and no workspace")
-        _need_cuda(prefetch)
-        check(_lib.lib.orin_linear_prefetch(_ptr(out), _ptr(x), _ptr(w), M, N, K, dt, epi,
-                                            _ptr(residual), _ptr(prefetch),
-                                            prefetch.numel() * prefetch.element_size(),
-                                            _stream(stream)))
-        return out
     if workspace is not None:
         if algo != "auto":
             raise ValueError("a workspace goes with algo='auto'")

@@ -60,9 +60,7 @@ class DecoderLayer:
         # stream-K workspace of the projections (kernels.linear_workspace),
         # shareable by every layer of a model run on one stream
         self.gemm_ws = gemm_workspace
-        # the weight launched after this layer's last projection (the next
-        # layer's q/k/v, or the LM head): decode steps stream it into L2 ahead
-        self.next_weight: Optional[torch.Tensor] = None
+
         self.fold_norm = bool(fold_norm)
         self.nh = int(cfg["num_attention_heads"])
         self.nkv = int(cfg["num_key_value_heads"])
@@ -122,7 +120,7 @@ class DecoderLayer:
                                    stream=stream)
         else:
             kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
-            self._linear(qkv, xn, w["qkv"], S, stream, nxt=w["o_proj"])
+            kernels.linear_into(qkv, xn, w["qkv"], workspace=self.gemm_ws, stream=stream)
         kernels.qkv_rope_append(q, qkv, k_pool, v_pool, S, start_pos, self.nh, self.nkv,
                                 self.hd, self.theta, self.n_sink, self.window,
                                 q_norm=w.get("q_norm") if self.qk_norm else None,
@@ -152,7 +150,7 @@ class DecoderLayer:
                                    stream=stream)
         else:
             kernels.rmsnorm(xn, x, w["input_layernorm"], B, self.H, self.eps, stream=stream)
-            self._linear(qkv, xn, w["qkv"], B, stream, nxt=w["o_proj"])
+            kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
         kernels.qkv_rope_append_batch(q, qkv, self.k_pools, self.v_pools, 1, start_pos, self.nh,
                                       self.nkv, self.hd, self.theta, self.n_sink, self.window,
                                       q_norm=w.get("q_norm") if self.qk_norm else None,
@@ -168,28 +166,19 @@ class DecoderLayer:
         """o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual."""
         w = self.w
         xn, h = self.xn[:S], self.h[:S]
-        self._linear(x, att, w["o_proj"], S, stream, nxt=w["gate_up"], epilogue="residual",
-                     residual=x)
+        kernels.linear_into(x, att, w["o_proj"], epilogue="residual", residual=x,
+                            workspace=self.gemm_ws, stream=stream)
         if fold:
             kernels.linear_rmsnorm(h, x, w["gate_up"], w["post_attention_layernorm"], self.eps,
                                    epilogue="swiglu", stream=stream)
         else:
             kernels.rmsnorm(xn, x, w["post_attention_layernorm"], S, self.H, self.eps,
                             stream=stream)
-            self._linear(h, xn, w["gate_up"], S, stream, nxt=w["down"], epilogue="swiglu")
-        self._linear(x, h, w["down"], S, stream, nxt=self.next_weight, epilogue="residual",
-                     residual=x)
+            kernels.linear_into(h, xn, w["gate_up"], epilogue="swiglu", workspace=self.gemm_ws,
+                                stream=stream)
+        kernels.linear_into(x, h, w["down"], epilogue="residual", residual=x,
+                            workspace=self.gemm_ws, stream=stream)
         return x
-
-    # decode calls run on the weight stream: they also stream the next
-    # projection's weights into L2; prefill calls may use the stream-K workspace
-    DECODE_TOKENS = 16
-
-    def _linear(self, out, x, w, S, stream, nxt=None, **kw):
-        if S <= self.DECODE_TOKENS and nxt is not None:
-            kernels.linear_into(out, x, w, prefetch=nxt, stream=stream, **kw)
-        else:
-            kernels.linear_into(out, x, w, workspace=self.gemm_ws, stream=stream, **kw)
 
 
 class TPDecoderLayer(DecoderLayer):
@@ -283,9 +272,6 @@ class Decoder:
                          gemm_workspace=self.gemm_ws)
             for i in range(int(cfg["num_hidden_layers"]))
         ]
-        for a, b in zip(self.layers, self.layers[1:]):
-            a.next_weight = b.w["qkv"]
-        self.layers[-1].next_weight = self.lm_head
         self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
         self.xn = torch.empty((self.batch, self.H), dtype=dt, device=device)
         self.keys = torch.empty(self.batch, dtype=torch.int64, device=device)

@@ -180,17 +180,6 @@ def test_batched_attention_and_append_reject_bad_arguments_on_host():
     assert app(batch=0) == _lib.OK
 
 
-def test_linear_prefetch_rejects_bad_hints_on_host():
-    """orin_linear_prefetch checks its hint before any device work: a negative
-    size, a size without a pointer, and an unaligned pointer or size."""
-    L = _lib.lib
-    args = (16, 16, 16, 1, 256, 512, 0, 0, None)
-    assert L.orin_linear_prefetch(*args, 16, -16, None) == _lib.ERR_INVALID_ARG
-    assert L.orin_linear_prefetch(*args, None, 64, None) == _lib.ERR_INVALID_ARG
-    assert L.orin_linear_prefetch(*args, 24, 64, None) == _lib.ERR_UNSUPPORTED
-    assert L.orin_linear_prefetch(*args, 16, 40, None) == _lib.ERR_UNSUPPORTED
-
-
 def test_attention_workspace_plan():
     """Few-token calls split their keys across CTAs; prefill-sized calls don't.
     The split count for TinyLlama decode (32 heads over 4 KV heads, window

@@ -296,20 +296,3 @@ def test_unfused_path_equals_fused_semantics():
     assert (unf == fused).float().mean().item() > 0.99
     assert_close(fused.float().cpu(), unf.float().cpu(), "fused vs unfused swiglu")
 
-
-@pytest.mark.parametrize("M,N,K,epi", [(1, 2048, 2048, "none"), (8, 2560, 2048, "none"),
-                                       (16, 704, 2048, "swiglu"), (4, 2048, 5632, "residual")])
-def test_weight_stream_prefetch_hint_changes_nothing(M, N, K, epi):
-    """orin_linear_prefetch: the L2 hint for a later projection's weights leaves
-    the result bit for bit that of orin_linear."""
-    tdt = torch.float16
-    wr = 2 * N if epi == "swiglu" else N
-    x = seeded((M, K), 41, 1.0, tdt).to(DEV)
-    w = seeded((wr, K), 42, 0.02, tdt).to(DEV)
-    nxt = seeded((3000, 1024), 43, 0.02, tdt).to(DEV)
-    r = seeded((M, N), 44, 1.0, tdt).to(DEV) if epi == "residual" else None
-    a = ob.linear(x, w, epilogue=epi, residual=r)
-    b = torch.empty_like(a)
-    ob.linear_into(b, x, w, epilogue=epi, residual=r, prefetch=nxt)
-    ob.device_check()
-    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
