@@ -436,6 +436,17 @@ orin_status check_attention(const char* fn, int seq_len, int cache_len, int num_
   return ORIN_OK;
 }
 
+// The current device's error word once its set-up has run (a linear call or
+// orin_device_check), else null: a kernel's bounded waits still give up and
+// return, without recording a code.
+int* error_word_if_ready() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || !device_ctx_ready(dev)) return nullptr;
+  cudaError_t e = cudaSuccess;
+  DeviceCtx* ctx = device_ctx(dev, &e);
+  return ctx ? ctx->err : nullptr;
+}
+
 }  // namespace
 
 orin_status orin_attention_workspace_bytes(size_t* bytes, int seq_len, int cache_len,
@@ -476,7 +487,8 @@ orin_status orin_attention(void* out, const void* q, const void* k_pool, const v
   }
   cudaError_t e = launch_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
                                    num_kv_heads, head_dim, scale, n_sink, window_size, dtype,
-                                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                                   1, 0, error_word_if_ready());
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention");
 }
 
@@ -515,7 +527,7 @@ orin_status orin_attention_batch(void* out, const void* q, const void* k_pool, c
   cudaError_t e = launch_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
                                    num_kv_heads, head_dim, scale, n_sink, window_size, dtype,
                                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
-                                   batch, pool_stride);
+                                   batch, pool_stride, error_word_if_ready());
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention_batch");
 }
 

@@ -26,6 +26,9 @@
 // warps on one 16-row group and split each key tile between them, and split
 // the key range across CTAs; partials (running max, sum, unnormalised O)
 // merge in shared memory and, across CTAs, in attn_combine_kernel.
+#include <cstdlib>
+#include <cstring>
+
 #include "orin_common.cuh"
 #include "orin_internal.h"
 
@@ -530,12 +533,40 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
   return pl;
 }
 
+namespace {
+
+// ORIN_ATTN_KERNEL: 0 automatic, 1 "mma" (the mma.sync kernel), 2 "tc" (the
+// tensor-core kernel wherever it applies).
+int attention_kernel_override() {
+  static const int v = [] {
+    const char* e = std::getenv("ORIN_ATTN_KERNEL");
+    if (!e) return 0;
+    if (std::strcmp(e, "mma") == 0) return 1;
+    if (std::strcmp(e, "tc") == 0) return 2;
+    return 0;
+  }();
+  return v;
+}
+
+}  // namespace
+
 cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const void* v_pool,
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
                              void* workspace, size_t workspace_bytes, cudaStream_t s, int batch,
-                             long long pool_stride) {
+                             long long pool_stride, int* err) {
   if (seq_len <= 0 || batch <= 0) return cudaSuccess;
+  if (batch == 1 && attention_tc_supported(seq_len, num_heads, num_kv_heads, head_dim, n_sink,
+                                           window)) {
+    // the tensor-core kernel has no key split: it wants a wave of row blocks
+    const int ov = attention_kernel_override();
+    const int group = num_heads / num_kv_heads;
+    const long long rows = static_cast<long long>(seq_len) * group;
+    const long long ctas = (rows + 127) / 128 * num_kv_heads;
+    if (ov == 2 || (ov == 0 && ctas >= 148))
+      return launch_attention_tc(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
+                                 num_kv_heads, head_dim, scale, n_sink, window, dtype, err, s);
+  }
   // each sequence plans alone, on its share of the workspace
   const AttnPlan pl = plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim,
                                      n_sink, window, workspace ? workspace_bytes / batch : 0);

@@ -1,0 +1,471 @@
+// attention_tc.cu — prefill attention on the 5th-generation tensor cores.
+//
+// The same attention as attention.cu (the reference's sink + sliding-window
+// GQA attention, kernels/attention.cu:27-138, over the ring pools of
+// src/kv_cache.cu:21-41): query token qi of a call of seq_len new tokens and
+// cache_len positions sits at ap = cache_len - seq_len + qi and attends to the
+// positions p <= ap with p < n_sink or p >= ap + 1 - W, each read through its
+// pool slot (after the call's own K/V were scattered), with fp32 scores
+// scale * q.k, an fp32 softmax and one 16-bit rounding of sum_p softmax_p v_p.
+//
+// Kernel (calls of many tokens; decode keeps the split-key mma.sync kernel):
+// one CTA per 128 query rows of one KV head — a row is a (token, query head)
+// pair, the heads of one GQA group stacked so they share every K/V tile — and
+// 6 warps:
+//   warp 0     TMA producer: K and V tiles of 128 pool slots (2-D boxes of
+//              64 columns x 128 slots, 128-byte swizzle, no multicast) into a
+//              two-stage ring;
+//   warp 1     MMA issuer: S = Q K^T (M = 128 rows, N = 128 keys, K = head_dim)
+//              into one of two tensor-memory buffers, then O += P V
+//              (N = head_dim, K = 128 keys) into a tensor-memory accumulator,
+//              V read as an MN-major operand straight from its TMA tile;
+//   warps 2-5  softmax, one thread per row: the row of S from tensor memory,
+//              mask, running max and sum (online softmax), P rounded to 16
+//              bits into a 128-byte-swizzled shared-memory tile (the A
+//              operand of P V), O rescaled in tensor memory; at the end
+//              O / l, rounded and stored.
+// S of the next tile is computed while the softmax works on the current one.
+//
+// Keys are taken in slot order, 128 slots per tile (softmax does not depend on
+// the order of its terms): slot s holds, for a query at ap, the logical
+// position the reference reads there — s itself for a sink slot (attended if
+// s <= ap), and for a window slot the one position p in [ap + 1 - W, ap] with
+// n_sink + (p - n_sink) % W == s (attended if p >= n_sink).  While no query of
+// the CTA has wrapped the ring (ap < n_sink + W), slots equal positions and the
+// tiles past the last query's position are skipped (the causal half).
+// Every wait is bounded (2 s, device error code).
+#include "orin_common.cuh"
+#include "orin_internal.h"
+
+namespace orin {
+
+namespace {
+
+constexpr int kAtThreads = 192;
+constexpr int kAtRows = 128;   // query rows per CTA (MMA M)
+constexpr int kAtKeys = 128;   // key slots per tile (MMA N of S, K of P V)
+constexpr int kAtStages = 2;   // K/V ring
+constexpr uint32_t kAtom = kAtRows * 128;  // one 64-column x 128-row 16-bit box: 16 KB
+
+struct AttnTcParams {
+  void* out;        // [seq_len, num_heads, head_dim] 16-bit
+  const void* q;    // [seq_len, num_heads, head_dim] 16-bit
+  int seq_len, cache_len, num_heads, num_kv_heads, n_sink, window;
+  float scale;
+  int group;  // G = num_heads / num_kv_heads
+  int hpb;    // group heads per row block (min(G, 128))
+  int tpb;    // tokens per row block (128 / hpb)
+  int hsb;    // row blocks per (token block, group) when G > 128
+  int* err;
+};
+
+// Shared memory (after 1024-byte alignment): Q (head_dim / 64 boxes), the ring
+// (per stage: K boxes then V boxes), P (two 64-key boxes).
+template <int HD>
+constexpr uint32_t at_q_bytes() { return (HD / 64) * kAtom; }
+template <int HD>
+constexpr uint32_t at_stage_bytes() { return 2 * (HD / 64) * kAtom; }
+template <int HD>
+constexpr uint32_t at_smem_bytes() {
+  return 1024 + at_q_bytes<HD>() + kAtStages * at_stage_bytes<HD>() + 2 * kAtom;
+}
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t at_sw128(int r, int j) {
+  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// Shared-memory descriptor of an MN-major operand in 128-byte-swizzle boxes:
+// 64 contiguous MN elements per 128-byte row, rows along K; 8-row atoms 1024 B
+// apart along K (stride byte offset), 64-element MN blocks `lbo` bytes apart
+// (leading byte offset).
+__device__ __forceinline__ uint64_t smem_desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// One thread of the 128 softmax threads waits (bounded) on `bar`; the others
+// park on a named barrier.  False, in every thread, on timeout.
+__device__ __forceinline__ bool at_wait(uint32_t bar, uint32_t parity, int et,
+                                        volatile int* abort_flag, int* err) {
+  const bool ok =
+      et != 0 || mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE);
+  return named_bar_and(1, 128, ok);
+}
+
+template <int DT, int HD>
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const AttnTcParams p) {
+  using E = Elem<DT>;
+  constexpr int NB = HD / 64;  // 64-column boxes per row of Q, K, V
+  constexpr uint32_t IDESC_S = instr_desc_f16(DT, kAtRows, kAtKeys);
+  constexpr uint32_t IDESC_O = instr_desc_f16(DT, kAtRows, HD) | (1u << 16);  // B MN-major
+  constexpr uint32_t TMEM_COLS = 512;  // S x 2 (256 columns) + O (head_dim)
+  constexpr uint32_t O_COL = 2 * kAtKeys;
+
+  extern __shared__ uint8_t at_dsmem[];
+  __shared__ __align__(8) uint64_t kv_full[kAtStages];
+  __shared__ __align__(8) uint64_t kv_empty[kAtStages];
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t p_full;
+  __shared__ __align__(8) uint64_t o_done;
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base_s = (smem_u32(at_dsmem) + 1023u) & ~1023u;
+  const uint32_t q_s = base_s;
+  const uint32_t ring = q_s + at_q_bytes<HD>();
+  const uint32_t p_s = ring + kAtStages * at_stage_bytes<HD>();
+
+  const int kvh = blockIdx.y;
+  const int tb = blockIdx.x / p.hsb, hs = blockIdx.x % p.hsb;
+  const int t_lo = tb * p.tpb;
+  const int base = p.cache_len - p.seq_len;
+  int t_hi = t_lo + p.tpb - 1;
+  if (t_hi > p.seq_len - 1) t_hi = p.seq_len - 1;
+  const int slots = p.n_sink + p.window;
+  const int ap_max = base + t_hi;
+  // tiles of 128 slots to visit: all of them once a query may have wrapped
+  // the ring, else the slots up to the last query's position
+  const int n_tiles = (ap_max < slots) ? ap_max / kAtKeys + 1 : (slots + kAtKeys - 1) / kAtKeys;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAtStages; ++s) {
+      mbar_init(smem_u32(&kv_full[s]), 1);
+      mbar_init(smem_u32(&kv_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&s_full[0]), 1);
+    mbar_init(smem_u32(&s_full[1]), 1);
+    mbar_init(smem_u32(&p_full), 128);
+    mbar_init(smem_u32(&o_done), 1);
+    mbar_init(smem_u32(&drain_bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  // q and the pools come from the previous kernels
+  pdl_wait();
+  // Q rows into shared memory (K-major, 128-byte swizzle), every thread
+  const uint16_t* qg = static_cast<const uint16_t*>(p.q);
+  for (int c = threadIdx.x; c < kAtRows * (HD / 8); c += kAtThreads) {
+    const int r = c / (HD / 8), j = c % (HD / 8);  // row, 16-byte chunk of the row
+    const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
+    const int tok = t_lo + tr;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (tr < p.tpb && tok < p.seq_len && hr < p.group)
+      v = *reinterpret_cast<const uint4*>(
+          qg + (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD + 8 * j);
+    const uint32_t a = q_s + (j / 8) * kAtom + at_sw128(r, j % 8);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int n_issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % kAtStages;
+        if (j >= kAtStages &&
+            !mbar_wait_bounded(smem_u32(&kv_empty[st]), ((j / kAtStages) - 1) & 1u, &abort_flag,
+                               p.err, DEVERR_TIMEOUT_PRODUCER))
+          break;
+        const uint32_t kb = ring + st * at_stage_bytes<HD>();
+        const uint32_t fb = smem_u32(&kv_full[st]);
+        mbar_arrive_expect_tx(fb, at_stage_bytes<HD>());
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+          tma_load_2d_plain(kb + c * kAtom, &tm_k, fb, kvh * HD + 64 * c, j * kAtKeys);
+          tma_load_2d_plain(kb + (NB + c) * kAtom, &tm_v, fb, kvh * HD + 64 * c, j * kAtKeys);
+        }
+        ++n_issued;
+      }
+      if (abort_flag) {
+        // let the copies in flight land before the CTA exits
+        const int first = n_issued > kAtStages ? n_issued - kAtStages : 0;
+        for (int j = first; j < n_issued; ++j) {
+          const unsigned long long t0 = global_timer_ns();
+          while (!mbar_try_wait(smem_u32(&kv_full[j % kAtStages]), (j / kAtStages) & 1u))
+            if (global_timer_ns() - t0 > 100000000ull) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint64_t qd0 = smem_desc_kmajor_sw128(q_s);
+      const uint64_t pd0 = smem_desc_kmajor_sw128(p_s);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kAtStages;
+        if (!mbar_wait_bounded(smem_u32(&kv_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
+                               DEVERR_TIMEOUT_MMA))
+          return false;
+        tc_fence_after();
+        const uint32_t kb = ring + st * at_stage_bytes<HD>();
+        const uint64_t kd0 = smem_desc_kmajor_sw128(kb);
+        const uint32_t d = tmem_base + static_cast<uint32_t>((j & 1) * kAtKeys);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk / 4) * kAtom + (kk % 4) * 32) >> 4);
+          tc_mma_f16(d, qd0 + off, kd0 + off, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&s_full[j & 1]));
+        return true;
+      };
+      bool ok = n_tiles > 0 ? issue_s(0) : true;
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        // P of tile j is in shared memory and O rescaled
+        if (!mbar_wait_bounded(smem_u32(&p_full), j & 1u, &abort_flag, p.err,
+                               DEVERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = j % kAtStages;
+        const uint32_t vb = ring + st * at_stage_bytes<HD>() + NB * kAtom;
+        // V: MN-major, head_dim in 64-element blocks one box (16 KB) apart
+        const uint64_t vd0 = smem_desc_mnmajor_sw128(vb, kAtom);
+#pragma unroll
+        for (int kk = 0; kk < kAtKeys / 16; ++kk) {
+          const uint64_t aoff = static_cast<uint64_t>(((kk / 4) * kAtom + (kk % 4) * 32) >> 4);
+          const uint64_t boff = static_cast<uint64_t>((kk * 16 * 128) >> 4);  // 16 keys
+          tc_mma_f16(tmem_base + O_COL, pd0 + aoff, vd0 + boff, IDESC_O,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&o_done));
+        tc_commit(smem_u32(&kv_empty[st]));
+      }
+      if (!ok) {
+        tc_commit(smem_u32(&drain_bar));
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(smem_u32(&drain_bar), 0))
+          if (global_timer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // this thread's row (= tensor-memory lane)
+    const int et = static_cast<int>(threadIdx.x) - 64;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
+    const int tok = t_lo + tr;
+    const bool row_ok = tr < p.tpb && tok < p.seq_len && hr < p.group;
+    const int ap = base + tok;
+    // window slot residue of this row's newest position: (ap - n_sink) % W
+    const int d_ap = (ap >= p.n_sink) ? (ap - p.n_sink) % p.window : 0;
+    float m_run = -INFINITY, l_run = 0.f;
+    // whether the position the reference reads at slot s is attended by this row
+    auto attended = [&](int s) -> bool {
+      if (!row_ok || s >= slots) return false;
+      if (s < p.n_sink) return s <= ap;
+      if (ap < p.n_sink) return false;
+      const int rho = s - p.n_sink;
+      const int dist = (rho <= d_ap) ? d_ap - rho : d_ap - rho + p.window;
+      return ap - dist >= p.n_sink;
+    };
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!at_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1u, et, &abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_t = lane_base + static_cast<uint32_t>((j & 1) * kAtKeys);
+      const int s0 = j * kAtKeys;
+      // pass 1: the row's maximum over this tile
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kAtKeys; c += 32) {
+        float v[32];
+        tmem_ld_32x32b_x32(s_t + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (attended(s0 + c + i)) mx = fmaxf(mx, v[i] * p.scale);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      // a row with nothing attended yet keeps m = -inf and adds nothing
+      const float alpha = (m_new == -INFINITY) ? 1.f : __expf(m_run - m_new);
+      const float m_ref = (m_new == -INFINITY) ? 0.f : m_new;
+      m_run = m_new;
+      // P V of the previous tile has finished: P's buffer is free, O is final
+      if (j > 0 && !at_wait(smem_u32(&o_done), (j - 1) & 1u, et, &abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // pass 2: P = exp(score - m) into shared memory, row sum
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kAtKeys; c += 32) {
+        float v[32];
+        tmem_ld_32x32b_x32(s_t + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e = attended(s0 + c + i) ? __expf(v[i] * p.scale - m_ref) : 0.f;
+          v[i] = e;
+          rs += e;
+        }
+        // 32 keys = four 16-byte chunks of row r in P's box c / 64
+        const uint32_t box = p_s + static_cast<uint32_t>((c / 64) * kAtom);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t a = box + at_sw128(r, ((c % 64) / 8) + i);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                       "r"(E::pack2(v[8 * i + 0], v[8 * i + 1])),
+                       "r"(E::pack2(v[8 * i + 2], v[8 * i + 3])),
+                       "r"(E::pack2(v[8 * i + 4], v[8 * i + 5])),
+                       "r"(E::pack2(v[8 * i + 6], v[8 * i + 7]))
+                       : "memory");
+        }
+      }
+      l_run = l_run * alpha + rs;
+      // tcgen05.ld / st are warp-collective: the warp rescales its 32 rows
+      // together (by 1 where a row's maximum did not move)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float v[32];
+          tmem_ld_32x32b_x32(lane_base + O_COL + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st_32x32b_x32(lane_base + O_COL + c, v);
+        }
+      }
+      fence_proxy_async_smem();  // P, written by threads, is read by the tensor core
+      tc_fence_before();
+      mbar_arrive(smem_u32(&p_full));
+    }
+    if (ok && n_tiles > 0 &&
+        at_wait(smem_u32(&o_done), (n_tiles - 1) & 1u, et, &abort_flag, p.err)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint16_t* dst = static_cast<uint16_t*>(p.out) +
+                      (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float v[32];
+        tmem_ld_32x32b_x32(lane_base + O_COL + c, v);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 u;
+            u.x = E::pack2(v[i + 0] * inv, v[i + 1] * inv);
+            u.y = E::pack2(v[i + 2] * inv, v[i + 3] * inv);
+            u.z = E::pack2(v[i + 4] * inv, v[i + 5] * inv);
+            u.w = E::pack2(v[i + 6] * inv, v[i + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + c + i) = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int DT, int HD>
+cudaError_t launch_at(const AttnTcParams& p, int row_blocks, const void* k_pool,
+                      const void* v_pool, cudaStream_t s) {
+  CUtensorMap tk, tv;
+  // only slots that hold a written position: the rest read as zeros (a slot
+  // no call has written yet may hold any bits, and 0 * NaN would reach O)
+  const long long slots = static_cast<long long>(p.n_sink) + p.window;
+  const unsigned long long rows =
+      static_cast<unsigned long long>(p.cache_len < slots ? p.cache_len : slots);
+  const unsigned long long cols = static_cast<unsigned long long>(p.num_kv_heads) * HD;
+  if (!encode_tmap_2d(&tk, k_pool, DT, rows, cols, 64, kAtKeys) ||
+      !encode_tmap_2d(&tv, v_pool, DT, rows, cols, 64, kAtKeys))
+    return cudaErrorInvalidValue;
+  auto kern = attn_tc_kernel<DT, HD>;
+  constexpr int smem = static_cast<int>(at_smem_bytes<HD>());
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  return launch_pdl_smem(kern, dim3(row_blocks, p.num_kv_heads), dim3(kAtThreads), smem, s, tk,
+                         tv, p);
+}
+
+}  // namespace
+
+bool attention_tc_supported(int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                            int n_sink, int window) {
+  if (head_dim != 64 && head_dim != 128) return false;
+  if (num_kv_heads < 1 || num_heads % num_kv_heads != 0) return false;
+  const int group = num_heads / num_kv_heads;
+  // calls with a full block of rows; a group either divides 128 or is a
+  // multiple of it
+  if (static_cast<long long>(seq_len) * group < kAtRows) return false;
+  if (group <= kAtRows ? (kAtRows % group) != 0 : (group % kAtRows) != 0) return false;
+  if (num_kv_heads > 65535 || window < 1 || n_sink < 0) return false;
+  return true;
+}
+
+cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, const void* v_pool,
+                                int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                                int head_dim, float scale, int n_sink, int window, int dtype,
+                                int* err, cudaStream_t s) {
+  AttnTcParams p;
+  p.out = out;
+  p.q = q;
+  p.seq_len = seq_len;
+  p.cache_len = cache_len;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.n_sink = n_sink;
+  p.window = window;
+  p.scale = scale;
+  p.group = num_heads / num_kv_heads;
+  p.hpb = p.group < kAtRows ? p.group : kAtRows;
+  p.tpb = kAtRows / p.hpb;
+  p.hsb = (p.group + p.hpb - 1) / p.hpb;
+  p.err = err;
+  const long long rb = static_cast<long long>((seq_len + p.tpb - 1) / p.tpb) * p.hsb;
+  if (rb > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const int row_blocks = static_cast<int>(rb);
+  if (dtype == DT_F16)
+    return head_dim == 64 ? launch_at<DT_F16, 64>(p, row_blocks, k_pool, v_pool, s)
+                          : launch_at<DT_F16, 128>(p, row_blocks, k_pool, v_pool, s);
+  return head_dim == 64 ? launch_at<DT_BF16, 64>(p, row_blocks, k_pool, v_pool, s)
+                        : launch_at<DT_BF16, 128>(p, row_blocks, k_pool, v_pool, s);
+}
+
+}  // namespace orin

@@ -430,9 +430,10 @@ __device__ __forceinline__ uint32_t sw128(int r, int j) {
 // every thread.
 __device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, int et,
                                          volatile int* abort_flag, int* err, volatile int* flag) {
-  if (et == 0) *flag = mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE) ? 1 : 0;
-  named_bar_sync(1, kEpiThreads);
-  return *flag != 0;
+  (void)flag;
+  const bool ok =
+      et != 0 || mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE);
+  return named_bar_and(1, kEpiThreads, ok);
 }
 
 // ---------------------------------------------------------------------------
@@ -565,6 +566,8 @@ __device__ __forceinline__ bool sk_fixup(const void* tm_s, uint32_t taddr, int l
 // CTAs first, first + stride, ...; the result reaches all 128 epilogue threads.
 __device__ __forceinline__ bool sk_wait(const int* flags, int first, int n, int stride, int et,
                                         volatile int* abort_flag, int* err, volatile int* flag) {
+  (void)flag;
+  bool ok = true;
   if (et == 0) {
     bool good = true;
     const unsigned long long t0 = global_timer_ns();
@@ -583,11 +586,11 @@ __device__ __forceinline__ bool sk_wait(const int* flags, int first, int n, int 
         __nanosleep(64);
       }
     }
-    *flag = good ? 1 : 0;
+    ok = good;
   }
-  named_bar_sync(1, kEpiThreads);
+  const bool all = named_bar_and(1, kEpiThreads, ok);
   __threadfence();
-  return *flag != 0;
+  return all;
 }
 
 // Store one tile held in tensor memory: for each 128-byte-wide chunk of
@@ -2022,6 +2025,11 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
     }
   }
   fill_tiles(pl, K, best_bn, best_split, best_pair, G, best_sk);
+}
+
+bool encode_tmap_2d(CUtensorMap* out, const void* ptr, int type, unsigned long long rows,
+                    unsigned long long cols, int box_cols, int box_rows) {
+  return make_tmap(out, ptr, type, rows, cols, box_cols, box_rows);
 }
 
 cudaError_t launch_tc(const Plan& pl0, int dtype, int epi, const void* A, const void* W,

@@ -494,6 +494,22 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that ANDs a predicate over the participating threads: every
+// thread returns the same value, with no shared word that a later call could
+// overwrite before a slow thread reads it.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ float silu_f32(float g) {
   // kernels/fused_swiglu.cu:14 — g / (1 + expf(-g)), in fp32.
   return g / (1.0f + expf(-g));

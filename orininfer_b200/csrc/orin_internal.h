@@ -130,7 +130,23 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
                              void* workspace, size_t workspace_bytes, cudaStream_t s,
-                             int batch = 1, long long pool_stride = 0);
+                             int batch = 1, long long pool_stride = 0, int* err = nullptr);
+// The tensor-core prefill kernel (csrc/attention_tc.cu): one sequence, head
+// dim 64 or 128, a GQA group that divides 128 (or a multiple of 128), at
+// least 128 query rows.  launch_attention picks it for calls with at least
+// one wave of 128-row blocks; the ORIN_ATTN_KERNEL tuning override ("mma" or
+// "tc", read once per process) forces one kernel where both apply.
+bool attention_tc_supported(int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                            int n_sink, int window);
+cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, const void* v_pool,
+                                int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                                int head_dim, float scale, int n_sink, int window, int dtype,
+                                int* err, cudaStream_t s);
+// A row-major [rows, cols] 16-bit (type 0 f16, 1 bf16) or fp32 (type 2)
+// matrix as a TMA map with box_cols x box_rows boxes, 128-byte swizzle
+// (box_cols * element size = 128), zero fill (csrc/gemm_tc.cu).
+bool encode_tmap_2d(CUtensorMap* out, const void* ptr, int type, unsigned long long rows,
+                    unsigned long long cols, int box_cols, int box_rows);
 cudaError_t launch_kv_scatter(void* k_pool, void* v_pool, const void* k_src, const void* v_src,
                               int seq_len, int start_pos, int n_sink, int window, int kv_dim,
                               cudaStream_t s);
