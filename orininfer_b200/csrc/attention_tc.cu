@@ -59,8 +59,8 @@ struct AttnTcParams {
   int* err;
 };
 
-// Shared memory (after 1024-byte alignment): Q (head_dim / 64 boxes), the ring
-// (per stage: K boxes then V boxes), P (two 64-key boxes).
+// Shared memory (after 1024-byte alignment): Q (head_dim / 64 boxes), the K
+// ring, the V ring (head_dim / 64 boxes per stage), P (two 64-key boxes).
 template <int HD>
 constexpr uint32_t at_q_bytes() { return (HD / 64) * kAtom; }
 template <int HD>
@@ -98,6 +98,57 @@ __device__ __forceinline__ bool at_wait(uint32_t bar, uint32_t parity, int et,
   return named_bar_and(1, 128, ok);
 }
 
+// 32 lanes x 32 bits, 128 consecutive columns (one row of S per thread) in
+// one load, waited for in the same statement so no use of the registers can
+// be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_ld_32x32b_x128(uint32_t taddr, float* v) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127"
+      "}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+        "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+        "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
+        "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]),
+        "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]),
+        "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
+        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]),
+        "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]),
+        "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]),
+        "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]),
+        "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]),
+        "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]),
+        "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]),
+        "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]),
+        "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int DT, int HD>
 __global__ void __launch_bounds__(kAtThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -108,10 +159,13 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   constexpr uint32_t IDESC_O = instr_desc_f16(DT, kAtRows, HD) | (1u << 16);  // B MN-major
   constexpr uint32_t TMEM_COLS = 512;  // S x 2 (256 columns) + O (head_dim)
   constexpr uint32_t O_COL = 2 * kAtKeys;
+  constexpr uint32_t TILE_BYTES = NB * kAtom;  // one K or one V tile
 
   extern __shared__ uint8_t at_dsmem[];
-  __shared__ __align__(8) uint64_t kv_full[kAtStages];
-  __shared__ __align__(8) uint64_t kv_empty[kAtStages];
+  __shared__ __align__(8) uint64_t k_full[kAtStages];
+  __shared__ __align__(8) uint64_t k_empty[kAtStages];
+  __shared__ __align__(8) uint64_t v_full[kAtStages];
+  __shared__ __align__(8) uint64_t v_empty[kAtStages];
   __shared__ __align__(8) uint64_t s_full[2];
   __shared__ __align__(8) uint64_t p_full;
   __shared__ __align__(8) uint64_t o_done;
@@ -123,8 +177,9 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t base_s = (smem_u32(at_dsmem) + 1023u) & ~1023u;
   const uint32_t q_s = base_s;
-  const uint32_t ring = q_s + at_q_bytes<HD>();
-  const uint32_t p_s = ring + kAtStages * at_stage_bytes<HD>();
+  const uint32_t k_ring = q_s + TILE_BYTES;
+  const uint32_t v_ring = k_ring + kAtStages * TILE_BYTES;
+  const uint32_t p_s = v_ring + kAtStages * TILE_BYTES;
 
   const int kvh = blockIdx.y;
   const int tb = blockIdx.x / p.hsb, hs = blockIdx.x % p.hsb;
@@ -140,8 +195,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAtStages; ++s) {
-      mbar_init(smem_u32(&kv_full[s]), 1);
-      mbar_init(smem_u32(&kv_empty[s]), 1);
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
     }
     mbar_init(smem_u32(&s_full[0]), 1);
     mbar_init(smem_u32(&s_full[1]), 1);
@@ -185,32 +242,43 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // K tile j into stage j % 2 once S of tile j - 2 is done with it, V tile j
+    // once P V of tile j - 2 is
     if (lane == 0) {
-      int n_issued = 0;
+      int n_k = 0, n_v = 0;
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % kAtStages;
-        if (j >= kAtStages &&
-            !mbar_wait_bounded(smem_u32(&kv_empty[st]), ((j / kAtStages) - 1) & 1u, &abort_flag,
-                               p.err, DEVERR_TIMEOUT_PRODUCER))
+        const uint32_t par = ((j / kAtStages) - 1) & 1u;
+        if (j >= kAtStages && !mbar_wait_bounded(smem_u32(&k_empty[st]), par, &abort_flag, p.err,
+                                                 DEVERR_TIMEOUT_PRODUCER))
           break;
-        const uint32_t kb = ring + st * at_stage_bytes<HD>();
-        const uint32_t fb = smem_u32(&kv_full[st]);
-        mbar_arrive_expect_tx(fb, at_stage_bytes<HD>());
+        mbar_arrive_expect_tx(smem_u32(&k_full[st]), TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < NB; ++c) {
-          tma_load_2d_plain(kb + c * kAtom, &tm_k, fb, kvh * HD + 64 * c, j * kAtKeys);
-          tma_load_2d_plain(kb + (NB + c) * kAtom, &tm_v, fb, kvh * HD + 64 * c, j * kAtKeys);
-        }
-        ++n_issued;
+        for (int c = 0; c < NB; ++c)
+          tma_load_2d_plain(k_ring + st * TILE_BYTES + c * kAtom, &tm_k, smem_u32(&k_full[st]),
+                            kvh * HD + 64 * c, j * kAtKeys);
+        ++n_k;
+        if (j >= kAtStages && !mbar_wait_bounded(smem_u32(&v_empty[st]), par, &abort_flag, p.err,
+                                                 DEVERR_TIMEOUT_PRODUCER))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&v_full[st]), TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < NB; ++c)
+          tma_load_2d_plain(v_ring + st * TILE_BYTES + c * kAtom, &tm_v, smem_u32(&v_full[st]),
+                            kvh * HD + 64 * c, j * kAtKeys);
+        ++n_v;
       }
       if (abort_flag) {
         // let the copies in flight land before the CTA exits
-        const int first = n_issued > kAtStages ? n_issued - kAtStages : 0;
-        for (int j = first; j < n_issued; ++j) {
-          const unsigned long long t0 = global_timer_ns();
-          while (!mbar_try_wait(smem_u32(&kv_full[j % kAtStages]), (j / kAtStages) & 1u))
-            if (global_timer_ns() - t0 > 100000000ull) break;
-        }
+        auto drain = [&](uint64_t* full, int n) {
+          for (int j = n > kAtStages ? n - kAtStages : 0; j < n; ++j) {
+            const unsigned long long t0 = global_timer_ns();
+            while (!mbar_try_wait(smem_u32(&full[j % kAtStages]), (j / kAtStages) & 1u))
+              if (global_timer_ns() - t0 > 100000000ull) break;
+          }
+        };
+        drain(k_full, n_k);
+        drain(v_full, n_v);
       }
     }
   } else if (warp == 1) {
@@ -220,12 +288,11 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const uint64_t pd0 = smem_desc_kmajor_sw128(p_s);
       auto issue_s = [&](int j) -> bool {
         const int st = j % kAtStages;
-        if (!mbar_wait_bounded(smem_u32(&kv_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
+        if (!mbar_wait_bounded(smem_u32(&k_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
                                DEVERR_TIMEOUT_MMA))
           return false;
         tc_fence_after();
-        const uint32_t kb = ring + st * at_stage_bytes<HD>();
-        const uint64_t kd0 = smem_desc_kmajor_sw128(kb);
+        const uint64_t kd0 = smem_desc_kmajor_sw128(k_ring + st * TILE_BYTES);
         const uint32_t d = tmem_base + static_cast<uint32_t>((j & 1) * kAtKeys);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -233,25 +300,28 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           tc_mma_f16(d, qd0 + off, kd0 + off, IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&s_full[j & 1]));
+        tc_commit(smem_u32(&k_empty[st]));
         return true;
       };
       bool ok = n_tiles > 0 ? issue_s(0) : true;
       for (int j = 0; ok && j < n_tiles; ++j) {
+        // S of the next tile goes ahead of this tile's softmax
         if (j + 1 < n_tiles && !issue_s(j + 1)) {
           ok = false;
           break;
         }
         // P of tile j is in shared memory and O rescaled
+        const int st = j % kAtStages;
         if (!mbar_wait_bounded(smem_u32(&p_full), j & 1u, &abort_flag, p.err,
+                               DEVERR_TIMEOUT_MMA) ||
+            !mbar_wait_bounded(smem_u32(&v_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
                                DEVERR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int st = j % kAtStages;
-        const uint32_t vb = ring + st * at_stage_bytes<HD>() + NB * kAtom;
         // V: MN-major, head_dim in 64-element blocks one box (16 KB) apart
-        const uint64_t vd0 = smem_desc_mnmajor_sw128(vb, kAtom);
+        const uint64_t vd0 = smem_desc_mnmajor_sw128(v_ring + st * TILE_BYTES, kAtom);
 #pragma unroll
         for (int kk = 0; kk < kAtKeys / 16; ++kk) {
           const uint64_t aoff = static_cast<uint64_t>(((kk / 4) * kAtom + (kk % 4) * 32) >> 4);
@@ -260,7 +330,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
                      (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(smem_u32(&o_done));
-        tc_commit(smem_u32(&kv_empty[st]));
+        tc_commit(smem_u32(&v_empty[st]));
       }
       if (!ok) {
         tc_commit(smem_u32(&drain_bar));
@@ -279,18 +349,36 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     const int tok = t_lo + tr;
     const bool row_ok = tr < p.tpb && tok < p.seq_len && hr < p.group;
     const int ap = base + tok;
-    // window slot residue of this row's newest position: (ap - n_sink) % W
-    const int d_ap = (ap >= p.n_sink) ? (ap - p.n_sink) % p.window : 0;
-    float m_run = -INFINITY, l_run = 0.f;
-    // whether the position the reference reads at slot s is attended by this row
-    auto attended = [&](int s) -> bool {
-      if (!row_ok || s >= slots) return false;
-      if (s < p.n_sink) return s <= ap;
-      if (ap < p.n_sink) return false;
-      const int rho = s - p.n_sink;
-      const int dist = (rho <= d_ap) ? d_ap - rho : d_ap - rho + p.window;
-      return ap - dist >= p.n_sink;
-    };
+    // The row's attended slots as two ranges [0, a_hi) and [b_lo, b_hi): the
+    // sinks, and the window positions [max(n_sink, ap + 1 - W), ap], whose
+    // slots are one run of ring residues (split in two where it wraps).
+    int a_hi = 0, b_lo = 0, b_hi = 0;
+    if (row_ok) {
+      if (ap < p.n_sink) {
+        a_hi = ap + 1;
+      } else {
+        const int w_lo = max(p.n_sink, ap + 1 - p.window);
+        if (ap - w_lo + 1 >= p.window) {
+          a_hi = slots;
+        } else {
+          const int r_lo = (w_lo - p.n_sink) % p.window, r_hi = (ap - p.n_sink) % p.window;
+          if (r_lo == 0) {
+            a_hi = p.n_sink + r_hi + 1;
+          } else if (r_lo <= r_hi) {
+            a_hi = p.n_sink;
+            b_lo = p.n_sink + r_lo;
+            b_hi = p.n_sink + r_hi + 1;
+          } else {
+            a_hi = p.n_sink + r_hi + 1;
+            b_lo = p.n_sink + r_lo;
+            b_hi = slots;
+          }
+        }
+      }
+    }
+    // exp(scale * (s - m)) = 2^(s * c - m * c), c = scale * log2(e)
+    const float c = p.scale * 1.4426950408889634f;
+    float m_run = -INFINITY, l_run = 0.f;  // m in raw score units
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       if (!at_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1u, et, &abort_flag, p.err)) {
@@ -298,22 +386,28 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t s_t = lane_base + static_cast<uint32_t>((j & 1) * kAtKeys);
+      float sv[kAtKeys];
+      tmem_ld_32x32b_x128(lane_base + static_cast<uint32_t>((j & 1) * kAtKeys), sv);
       const int s0 = j * kAtKeys;
-      // pass 1: the row's maximum over this tile
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kAtKeys; c += 32) {
-        float v[32];
-        tmem_ld_32x32b_x32(s_t + c, v);
+      const int a = a_hi - s0, bl = b_lo - s0, bh = b_hi - s0;
+      const bool full = a >= kAtKeys || (bl <= 0 && bh >= kAtKeys);
+      if (!__all_sync(0xffffffffu, full)) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (attended(s0 + c + i)) mx = fmaxf(mx, v[i] * p.scale);
+        for (int i = 0; i < kAtKeys; ++i)
+          if (!(i < a || (i >= bl && i < bh))) sv[i] = -INFINITY;
       }
-      const float m_new = fmaxf(m_run, mx);
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+      for (int i = 8; i < kAtKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+      const float m_tile =
+          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = fmaxf(m_run, m_tile);
       // a row with nothing attended yet keeps m = -inf and adds nothing
-      const float alpha = (m_new == -INFINITY) ? 1.f : __expf(m_run - m_new);
-      const float m_ref = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx((m_run - m_new) * c);
+      const float mc = (m_new == -INFINITY) ? 0.f : m_new * c;
       m_run = m_new;
       // P V of the previous tile has finished: P's buffer is free, O is final
       if (j > 0 && !at_wait(smem_u32(&o_done), (j - 1) & 1u, et, &abort_flag, p.err)) {
@@ -321,42 +415,38 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         break;
       }
       tc_fence_after();
-      // pass 2: P = exp(score - m) into shared memory, row sum
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kAtKeys; c += 32) {
-        float v[32];
-        tmem_ld_32x32b_x32(s_t + c, v);
+      float sum[8];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = attended(s0 + c + i) ? __expf(v[i] * p.scale - m_ref) : 0.f;
-          v[i] = e;
-          rs += e;
-        }
-        // 32 keys = four 16-byte chunks of row r in P's box c / 64
-        const uint32_t box = p_s + static_cast<uint32_t>((c / 64) * kAtom);
+      for (int i = 0; i < 8; ++i) sum[i] = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t a = box + at_sw128(r, ((c % 64) / 8) + i);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                       "r"(E::pack2(v[8 * i + 0], v[8 * i + 1])),
-                       "r"(E::pack2(v[8 * i + 2], v[8 * i + 3])),
-                       "r"(E::pack2(v[8 * i + 4], v[8 * i + 5])),
-                       "r"(E::pack2(v[8 * i + 6], v[8 * i + 7]))
-                       : "memory");
-        }
+      for (int i = 0; i < kAtKeys; ++i) {
+        sv[i] = ex2_approx(fmaf(sv[i], c, -mc));  // masked: 2^-inf = 0
+        sum[i & 7] += sv[i];
       }
-      l_run = l_run * alpha + rs;
+      // P rounded to 16 bits: 16 chunks of 8 keys, row r of two 64-key boxes
+#pragma unroll
+      for (int ch = 0; ch < kAtKeys / 8; ++ch) {
+        const uint32_t addr =
+            p_s + static_cast<uint32_t>((ch / 8) * kAtom) + at_sw128(r, ch % 8);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                     "r"(E::pack2(sv[8 * ch + 0], sv[8 * ch + 1])),
+                     "r"(E::pack2(sv[8 * ch + 2], sv[8 * ch + 3])),
+                     "r"(E::pack2(sv[8 * ch + 4], sv[8 * ch + 5])),
+                     "r"(E::pack2(sv[8 * ch + 6], sv[8 * ch + 7]))
+                     : "memory");
+      }
+      l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3])) +
+              ((sum[4] + sum[5]) + (sum[6] + sum[7]));
       // tcgen05.ld / st are warp-collective: the warp rescales its 32 rows
       // together (by 1 where a row's maximum did not move)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
+        for (int cc = 0; cc < HD; cc += 32) {
           float v[32];
-          tmem_ld_32x32b_x32(lane_base + O_COL + c, v);
+          tmem_ld_32x32b_x32(lane_base + O_COL + cc, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st_32x32b_x32(lane_base + O_COL + c, v);
+          tmem_st_32x32b_x32(lane_base + O_COL + cc, v);
         }
       }
       fence_proxy_async_smem();  // P, written by threads, is read by the tensor core
@@ -370,9 +460,9 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       uint16_t* dst = static_cast<uint16_t*>(p.out) +
                       (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int cc = 0; cc < HD; cc += 32) {
         float v[32];
-        tmem_ld_32x32b_x32(lane_base + O_COL + c, v);
+        tmem_ld_32x32b_x32(lane_base + O_COL + cc, v);
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -381,7 +471,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             u.y = E::pack2(v[i + 2] * inv, v[i + 3] * inv);
             u.z = E::pack2(v[i + 4] * inv, v[i + 5] * inv);
             u.w = E::pack2(v[i + 6] * inv, v[i + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c + i) = u;
+            *reinterpret_cast<uint4*>(dst + cc + i) = u;
           }
         }
       }
