@@ -10,21 +10,24 @@
 //
 // Kernel (calls of many tokens; decode keeps the split-key mma.sync kernel):
 // one CTA per 128 query rows of one KV head — a row is a (token, query head)
-// pair, the heads of one GQA group stacked so they share every K/V tile — and
-// 6 warps:
+// pair, the heads of one GQA group stacked so they share every K/V tile —
+// and 10 warps:
 //   warp 0     TMA producer: K and V tiles of 128 pool slots (2-D boxes of
-//              64 columns x 128 slots, 128-byte swizzle, no multicast) into a
-//              two-stage ring;
+//              64 columns x 128 slots, 128-byte swizzle, no multicast) into
+//              two-stage K and V rings; a K stage is free once S has read it,
+//              a V stage once P V has;
 //   warp 1     MMA issuer: S = Q K^T (M = 128 rows, N = 128 keys, K = head_dim)
 //              into one of two tensor-memory buffers, then O += P V
 //              (N = head_dim, K = 128 keys) into a tensor-memory accumulator,
-//              V read as an MN-major operand straight from its TMA tile;
-//   warps 2-5  softmax, one thread per row: the row of S from tensor memory,
-//              mask, running max and sum (online softmax), P rounded to 16
-//              bits into a 128-byte-swizzled shared-memory tile (the A
-//              operand of P V), O rescaled in tensor memory; at the end
-//              O / l, rounded and stored.
-// S of the next tile is computed while the softmax works on the current one.
+//              V read as an MN-major operand straight from its TMA tile; S of
+//              tile j + 1 is issued before P V of tile j;
+//   warps 2-9  softmax, two threads per row (one per 64-key half): the row's
+//              maximum from tensor memory, masks as two slot ranges per row,
+//              P = 2^(c s - c m) rounded to 16 bits into one of two 128-byte-
+//              swizzled P tiles in shared memory (the A operand of P V), O
+//              rescaled in tensor memory only when a row maximum grows by
+//              more than 2^8; at the end O / l, rounded and stored.
+// CTAs start with the row blocks that have the most key tiles.
 //
 // Keys are taken in slot order, 128 slots per tile (softmax does not depend on
 // the order of its terms): slot s holds, for a query at ap, the logical
@@ -41,11 +44,17 @@ namespace orin {
 
 namespace {
 
-constexpr int kAtThreads = 192;
+constexpr int kAtThreads = 320;  // producer, MMA, 8 softmax warps
 constexpr int kAtRows = 128;   // query rows per CTA (MMA M)
 constexpr int kAtKeys = 128;   // key slots per tile (MMA N of S, K of P V)
 constexpr int kAtStages = 2;   // K/V ring
 constexpr uint32_t kAtom = kAtRows * 128;  // one 64-column x 128-row 16-bit box: 16 KB
+constexpr uint32_t kPBytes = 2 * kAtom;     // one P tile: 128 rows x 128 keys, 16-bit
+// O is rescaled only when a row's maximum grows by more than 2^kLazy in the
+// exponent; until then P is taken against the older, smaller maximum (at
+// most 2^kLazy, exact in 16 bits relative to its size) and O / l is
+// unchanged because l is summed against the same maximum.
+constexpr float kLazy = 8.f;
 
 struct AttnTcParams {
   void* out;        // [seq_len, num_heads, head_dim] 16-bit
@@ -56,18 +65,20 @@ struct AttnTcParams {
   int hpb;    // group heads per row block (min(G, 128))
   int tpb;    // tokens per row block (128 / hpb)
   int hsb;    // row blocks per (token block, group) when G > 128
+  int row_blocks;  // per KV head
   int* err;
 };
 
 // Shared memory (after 1024-byte alignment): Q (head_dim / 64 boxes), the K
-// ring, the V ring (head_dim / 64 boxes per stage), P (two 64-key boxes).
+// ring, the V ring (head_dim / 64 boxes per stage), two P tiles (two 64-key
+// boxes each).
 template <int HD>
 constexpr uint32_t at_q_bytes() { return (HD / 64) * kAtom; }
 template <int HD>
 constexpr uint32_t at_stage_bytes() { return 2 * (HD / 64) * kAtom; }
 template <int HD>
 constexpr uint32_t at_smem_bytes() {
-  return 1024 + at_q_bytes<HD>() + kAtStages * at_stage_bytes<HD>() + 2 * kAtom;
+  return 1024 + at_q_bytes<HD>() + kAtStages * at_stage_bytes<HD>() + 2 * kPBytes;
 }
 
 // Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled box.
@@ -89,31 +100,28 @@ __device__ __forceinline__ uint64_t smem_desc_mnmajor_sw128(uint32_t saddr, uint
   return d;
 }
 
-// One thread of the 128 softmax threads waits (bounded) on `bar`; the others
-// park on a named barrier.  False, in every thread, on timeout.
-__device__ __forceinline__ bool at_wait(uint32_t bar, uint32_t parity, int et,
-                                        volatile int* abort_flag, int* err) {
-  const bool ok =
-      et != 0 || mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE);
-  return named_bar_and(1, 128, ok);
+// Lane 0 of a softmax warp waits (bounded) on `bar` for the warp; false, in
+// every lane, on timeout.  The softmax warps never wait for one another.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int lane,
+                                          volatile int* abort_flag, int* err) {
+  int ok = 1;
+  if (lane == 0)
+    ok = mbar_wait_bounded(bar, parity, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE) ? 1 : 0;
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// 32 lanes x 32 bits, 128 consecutive columns (one row of S per thread) in
-// one load, waited for in the same statement so no use of the registers can
-// be scheduled ahead of the wait.
-__device__ __forceinline__ void tmem_ld_32x32b_x128(uint32_t taddr, float* v) {
-  uint32_t r[128];
+// 32 lanes x 32 bits, 64 consecutive columns, waited for in the same
+// statement.
+__device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, float* v) {
+  uint32_t r[64];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
       "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
       "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
       "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
-      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
-      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
-      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
-      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127"
-      "}, [%128];\n\t"
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63"
+      "}, [%64];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
         "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
@@ -125,22 +133,11 @@ __device__ __forceinline__ void tmem_ld_32x32b_x128(uint32_t taddr, float* v) {
         "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
         "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]),
         "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
-        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]),
-        "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
-        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]),
-        "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]),
-        "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]),
-        "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
-        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]),
-        "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]),
-        "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]),
-        "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
-        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]),
-        "=r"(r[126]), "=r"(r[127])
+        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
       : "r"(taddr)
       : "memory");
 #pragma unroll
-  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -166,12 +163,13 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   __shared__ __align__(8) uint64_t k_empty[kAtStages];
   __shared__ __align__(8) uint64_t v_full[kAtStages];
   __shared__ __align__(8) uint64_t v_empty[kAtStages];
-  __shared__ __align__(8) uint64_t s_full[2];
-  __shared__ __align__(8) uint64_t p_full;
-  __shared__ __align__(8) uint64_t o_done;
+  __shared__ __align__(8) uint64_t s_full[2];   // S of tile j in buffer j % 2
+  __shared__ __align__(8) uint64_t p_full[2];   // P of tile j in buffer j % 2
+  __shared__ __align__(8) uint64_t pv_done[2];  // P V of tile j (and all before)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ float l_half[2][kAtRows];  // the two halves of each row's sum
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -181,8 +179,11 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const uint32_t v_ring = k_ring + kAtStages * TILE_BYTES;
   const uint32_t p_s = v_ring + kAtStages * TILE_BYTES;
 
-  const int kvh = blockIdx.y;
-  const int tb = blockIdx.x / p.hsb, hs = blockIdx.x % p.hsb;
+  // CTAs in launch order take the row blocks with the most key tiles first
+  // (the last tokens), so the short causal blocks fill the last wave
+  const int kvh = static_cast<int>(blockIdx.x % p.num_kv_heads);
+  const int rb = p.row_blocks - 1 - static_cast<int>(blockIdx.x / p.num_kv_heads);
+  const int tb = rb / p.hsb, hs = rb % p.hsb;
   const int t_lo = tb * p.tpb;
   const int base = p.cache_len - p.seq_len;
   int t_hi = t_lo + p.tpb - 1;
@@ -202,8 +203,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
     mbar_init(smem_u32(&s_full[0]), 1);
     mbar_init(smem_u32(&s_full[1]), 1);
-    mbar_init(smem_u32(&p_full), 128);
-    mbar_init(smem_u32(&o_done), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&p_full[b]), 256);
+      mbar_init(smem_u32(&pv_done[b]), 1);
+    }
     mbar_init(smem_u32(&drain_bar), 1);
     abort_flag = 0;
     fence_mbar_init();
@@ -286,6 +289,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     if (lane == 0) {
       const uint64_t qd0 = smem_desc_kmajor_sw128(q_s);
       const uint64_t pd0 = smem_desc_kmajor_sw128(p_s);
+      const uint64_t pd1 = smem_desc_kmajor_sw128(p_s + kPBytes);
       auto issue_s = [&](int j) -> bool {
         const int st = j % kAtStages;
         if (!mbar_wait_bounded(smem_u32(&k_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         // P of tile j is in shared memory and O rescaled
         const int st = j % kAtStages;
-        if (!mbar_wait_bounded(smem_u32(&p_full), j & 1u, &abort_flag, p.err,
+        if (!mbar_wait_bounded(smem_u32(&p_full[j & 1]), (j >> 1) & 1u, &abort_flag, p.err,
                                DEVERR_TIMEOUT_MMA) ||
             !mbar_wait_bounded(smem_u32(&v_full[st]), (j / kAtStages) & 1u, &abort_flag, p.err,
                                DEVERR_TIMEOUT_MMA)) {
@@ -326,10 +330,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         for (int kk = 0; kk < kAtKeys / 16; ++kk) {
           const uint64_t aoff = static_cast<uint64_t>(((kk / 4) * kAtom + (kk % 4) * 32) >> 4);
           const uint64_t boff = static_cast<uint64_t>((kk * 16 * 128) >> 4);  // 16 keys
-          tc_mma_f16(tmem_base + O_COL, pd0 + aoff, vd0 + boff, IDESC_O,
+          tc_mma_f16(tmem_base + O_COL, ((j & 1) ? pd1 : pd0) + aoff, vd0 + boff, IDESC_O,
                      (j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(smem_u32(&o_done));
+        tc_commit(smem_u32(&pv_done[j & 1]));
         tc_commit(smem_u32(&v_empty[st]));
       }
       if (!ok) {
@@ -341,9 +345,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
+    // Two threads per row, in warps w and w + 4 (the same tensor-memory lane
+    // quarter): half h takes keys [64 h, 64 h + 64) of each tile for P and
+    // columns [h HD / 2, (h + 1) HD / 2) of O.  Both read the whole row of S
+    // for its maximum (max is exact in any order, so the two agree bit for
+    // bit and take the same rescaling decisions); the halves of the row sum
+    // meet once, at the end.
+    constexpr int KH = kAtKeys / 2;  // keys per half
+    constexpr int OH = HD / 2;       // O columns per half
     const int quad = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // this thread's row (= tensor-memory lane)
-    const int et = static_cast<int>(threadIdx.x) - 64;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
     const int tok = t_lo + tr;
@@ -376,58 +388,99 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
       }
     }
+    // masks the keys [k0, k0 + n) of v outside the row's ranges; the warp
+    // skips it when every lane attends to all of them
+    auto mask = [&](float* v, int k0, int n) {
+      const int a = a_hi - k0, bl = b_lo - k0, bh = b_hi - k0;
+      const bool full = a >= n || (bl <= 0 && bh >= n);
+      if (!__all_sync(0xffffffffu, full)) {
+#pragma unroll
+        for (int i = 0; i < n; ++i)
+          if (!(i < a || (i >= bl && i < bh))) v[i] = -INFINITY;
+      }
+    };
     // exp(scale * (s - m)) = 2^(s * c - m * c), c = scale * log2(e)
     const float c = p.scale * 1.4426950408889634f;
-    float m_run = -INFINITY, l_run = 0.f;  // m in raw score units
+    // m: the maximum P is taken against (raw score units); l: this half's sum
+    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      if (!at_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1u, et, &abort_flag, p.err)) {
+      const int b = j & 1;
+      if (!warp_wait(smem_u32(&s_full[b]), (j >> 1) & 1u, lane, &abort_flag, p.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[kAtKeys];
-      tmem_ld_32x32b_x128(lane_base + static_cast<uint32_t>((j & 1) * kAtKeys), sv);
+      const uint32_t s_t = lane_base + static_cast<uint32_t>(b * kAtKeys);
       const int s0 = j * kAtKeys;
-      const int a = a_hi - s0, bl = b_lo - s0, bh = b_hi - s0;
-      const bool full = a >= kAtKeys || (bl <= 0 && bh >= kAtKeys);
-      if (!__all_sync(0xffffffffu, full)) {
-#pragma unroll
-        for (int i = 0; i < kAtKeys; ++i)
-          if (!(i < a || (i >= bl && i < bh))) sv[i] = -INFINITY;
-      }
+      float sv[KH];
+      tmem_ld_32x32b_x64(s_t + h * KH, sv);
+      mask(sv, s0 + h * KH, KH);
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = sv[i];
 #pragma unroll
-      for (int i = 8; i < kAtKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+      for (int i = 8; i < KH; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+      // the other half of the row, for the maximum only
+#pragma unroll 1
+      for (int cc = 0; cc < KH; cc += 32) {
+        float t[32];
+        tmem_ld_32x32b_x32(s_t + (1 - h) * KH + cc, t);
+        mask(t, s0 + (1 - h) * KH + cc, 32);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], t[i]);
+      }
       const float m_tile =
           fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m_run, m_tile);
-      // a row with nothing attended yet keeps m = -inf and adds nothing
-      const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx((m_run - m_new) * c);
-      const float mc = (m_new == -INFINITY) ? 0.f : m_new * c;
-      m_run = m_new;
-      // P V of the previous tile has finished: P's buffer is free, O is final
-      if (j > 0 && !at_wait(smem_u32(&o_done), (j - 1) & 1u, et, &abort_flag, p.err)) {
-        ok = false;
-        break;
+      // the warp moves its rows' maxima (and rescales O) only when one of them
+      // grows by more than 2^kLazy; a row with nothing attended yet keeps
+      // m = -inf and adds nothing
+      const bool grow = (m_tile - m_run) * c > kLazy;  // false for -inf - -inf
+      float alpha = 1.f;
+      const bool rescale = __any_sync(0xffffffffu, grow);
+      if (rescale) {
+        const float m_new = fmaxf(m_run, m_tile);
+        alpha = (m_new == -INFINITY) ? 1.f : ex2_approx((m_run - m_new) * c);
+        m_run = m_new;
       }
-      tc_fence_after();
+      if (j > 0 && rescale) {
+        // O holds P V of every earlier tile: wait for the last one
+        if (!warp_wait(smem_u32(&pv_done[b ^ 1]), ((j - 1) >> 1) & 1u, lane, &abort_flag,
+                       p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < OH; cc += 32) {
+          float v[32];
+          tmem_ld_32x32b_x32(lane_base + O_COL + h * OH + cc, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st_32x32b_x32(lane_base + O_COL + h * OH + cc, v);
+        }
+      } else if (j >= 2) {
+        // P buffer b was last read by P V of tile j - 2
+        if (!warp_wait(smem_u32(&pv_done[b]), ((j >> 1) - 1) & 1u, lane, &abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+      }
+      const float mc = (m_run == -INFINITY) ? 0.f : m_run * c;
       float sum[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sum[i] = 0.f;
 #pragma unroll
-      for (int i = 0; i < kAtKeys; ++i) {
+      for (int i = 0; i < KH; ++i) {
         sv[i] = ex2_approx(fmaf(sv[i], c, -mc));  // masked: 2^-inf = 0
         sum[i & 7] += sv[i];
       }
-      // P rounded to 16 bits: 16 chunks of 8 keys, row r of two 64-key boxes
+      // P rounded to 16 bits: this half is box h of P tile b, row r
+      const uint32_t pb = p_s + static_cast<uint32_t>(b) * kPBytes + static_cast<uint32_t>(h) * kAtom;
 #pragma unroll
-      for (int ch = 0; ch < kAtKeys / 8; ++ch) {
-        const uint32_t addr =
-            p_s + static_cast<uint32_t>((ch / 8) * kAtom) + at_sw128(r, ch % 8);
+      for (int ch = 0; ch < KH / 8; ++ch) {
+        const uint32_t addr = pb + at_sw128(r, ch);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
                      "r"(E::pack2(sv[8 * ch + 0], sv[8 * ch + 1])),
                      "r"(E::pack2(sv[8 * ch + 2], sv[8 * ch + 3])),
@@ -437,32 +490,26 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       }
       l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3])) +
               ((sum[4] + sum[5]) + (sum[6] + sum[7]));
-      // tcgen05.ld / st are warp-collective: the warp rescales its 32 rows
-      // together (by 1 where a row's maximum did not move)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-        for (int cc = 0; cc < HD; cc += 32) {
-          float v[32];
-          tmem_ld_32x32b_x32(lane_base + O_COL + cc, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st_32x32b_x32(lane_base + O_COL + cc, v);
-        }
-      }
       fence_proxy_async_smem();  // P, written by threads, is read by the tensor core
       tc_fence_before();
-      mbar_arrive(smem_u32(&p_full));
+      mbar_arrive(smem_u32(&p_full[b]));
     }
-    if (ok && n_tiles > 0 &&
-        at_wait(smem_u32(&o_done), (n_tiles - 1) & 1u, et, &abort_flag, p.err)) {
+    if (ok && n_tiles > 0)
+      ok = warp_wait(smem_u32(&pv_done[(n_tiles - 1) & 1]), ((n_tiles - 1) >> 1) & 1u, lane,
+                     &abort_flag, p.err);
+    // the two halves of the row sum; both warps of the pair get here (every
+    // wait above is bounded) and agree on whether to write
+    l_half[h][r] = l_run;
+    if (named_bar_and(1 + quad, 64, ok) && n_tiles > 0) {
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const float l = l_half[0][r] + l_half[1][r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       uint16_t* dst = static_cast<uint16_t*>(p.out) +
-                      (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD;
+                      (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD + h * OH;
 #pragma unroll 1
-      for (int cc = 0; cc < HD; cc += 32) {
+      for (int cc = 0; cc < OH; cc += 32) {
         float v[32];
-        tmem_ld_32x32b_x32(lane_base + O_COL + cc, v);
+        tmem_ld_32x32b_x32(lane_base + O_COL + h * OH + cc, v);
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -510,7 +557,7 @@ cudaError_t launch_at(const AttnTcParams& p, int row_blocks, const void* k_pool,
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  return launch_pdl_smem(kern, dim3(row_blocks, p.num_kv_heads), dim3(kAtThreads), smem, s, tk,
+  return launch_pdl_smem(kern, dim3(row_blocks * p.num_kv_heads), dim3(kAtThreads), smem, s, tk,
                          tv, p);
 }
 
@@ -549,8 +596,9 @@ cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, co
   p.hsb = (p.group + p.hpb - 1) / p.hpb;
   p.err = err;
   const long long rb = static_cast<long long>((seq_len + p.tpb - 1) / p.tpb) * p.hsb;
-  if (rb > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  if (rb * num_kv_heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int row_blocks = static_cast<int>(rb);
+  p.row_blocks = row_blocks;
   if (dtype == DT_F16)
     return head_dim == 64 ? launch_at<DT_F16, 64>(p, row_blocks, k_pool, v_pool, s)
                           : launch_at<DT_F16, 128>(p, row_blocks, k_pool, v_pool, s);
