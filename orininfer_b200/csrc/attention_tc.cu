@@ -37,6 +37,8 @@
 // the CTA has wrapped the ring (ap < n_sink + W), slots equal positions and the
 // tiles past the last query's position are skipped (the causal half).
 // Every wait is bounded (2 s, device error code).
+#include <type_traits>
+
 #include "orin_common.cuh"
 #include "orin_internal.h"
 
@@ -111,17 +113,23 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int lan
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// 32 lanes x 32 bits, 64 consecutive columns, waited for in the same
-// statement.
-__device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, float* v) {
-  uint32_t r[64];
+// Two 64-column loads (32 lanes x 32 bits) and one wait, in one statement.
+__device__ __forceinline__ void tmem_ld_32x32b_x64x2(uint32_t taddr0, uint32_t taddr1, float* v0,
+                                                     float* v1) {
+  uint32_t r[128];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
       "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
       "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
       "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
       "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63"
-      "}, [%64];\n\t"
+      "}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127"
+      "}, [%129];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
         "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
@@ -133,11 +141,25 @@ __device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, float* v) {
         "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
         "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]),
         "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
-        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr)
+        "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]),
+        "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]),
+        "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]),
+        "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]),
+        "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]),
+        "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]),
+        "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]),
+        "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]),
+        "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr0), "r"(taddr1)
       : "memory");
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 64; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[64 + i]);
+  }
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -204,7 +226,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     mbar_init(smem_u32(&s_full[0]), 1);
     mbar_init(smem_u32(&s_full[1]), 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&p_full[b]), 256);
+      mbar_init(smem_u32(&p_full[b]), 8);  // one arrival per softmax warp
       mbar_init(smem_u32(&pv_done[b]), 1);
     }
     mbar_init(smem_u32(&drain_bar), 1);
@@ -388,15 +410,26 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
       }
     }
-    // masks the keys [k0, k0 + n) of v outside the row's ranges; the warp
-    // skips it when every lane attends to all of them
-    auto mask = [&](float* v, int k0, int n) {
-      const int a = a_hi - k0, bl = b_lo - k0, bh = b_hi - k0;
-      const bool full = a >= n || (bl <= 0 && bh >= n);
-      if (!__all_sync(0xffffffffu, full)) {
+    // a warp with no valid row only keeps the P hand-off in step
+    const bool dead = __all_sync(0xffffffffu, !row_ok);
+    // masks the keys [k0, k0 + N) of v outside the row's ranges (a bit per
+    // key); the warp skips it when every lane attends to all of them
+    auto range_bits = [](int lo, int hi) -> uint64_t {  // bits [lo, hi) of 64
+      lo = max(lo, 0);
+      hi = min(hi, 64);
+      if (hi <= lo) return 0ull;
+      const uint64_t top = hi == 64 ? ~0ull : ((1ull << hi) - 1ull);
+      return top & ~((1ull << lo) - 1ull);
+    };
+    auto mask = [&](float* v, int k0, auto n_tag) {
+      constexpr int N = decltype(n_tag)::value;
+      const uint64_t bits = range_bits(0, a_hi - k0) | range_bits(b_lo - k0, b_hi - k0);
+      const uint64_t all = N == 64 ? ~0ull : ((1ull << N) - 1ull);
+      if (!__all_sync(0xffffffffu, (bits & all) == all)) {
+        const uint32_t lo = static_cast<uint32_t>(bits), hi = static_cast<uint32_t>(bits >> 32);
 #pragma unroll
-        for (int i = 0; i < n; ++i)
-          if (!(i < a || (i >= bl && i < bh))) v[i] = -INFINITY;
+        for (int i = 0; i < N; ++i)
+          if (!(((i < 32 ? lo : hi) >> (i & 31)) & 1u)) v[i] = -INFINITY;
       }
     };
     // exp(scale * (s - m)) = 2^(s * c - m * c), c = scale * log2(e)
@@ -410,26 +443,25 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         ok = false;
         break;
       }
+      if (dead) {
+        // S of tile j exists, so P V of tile j - 2 was issued: this arrival
+        // cannot land in an earlier phase of p_full[b]
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[b]));
+        continue;
+      }
       tc_fence_after();
       const uint32_t s_t = lane_base + static_cast<uint32_t>(b * kAtKeys);
       const int s0 = j * kAtKeys;
-      float sv[KH];
-      tmem_ld_32x32b_x64(s_t + h * KH, sv);
-      mask(sv, s0 + h * KH, KH);
+      // this half of the row, and the other half for the maximum only
+      float sv[KH], so[KH];
+      tmem_ld_32x32b_x64x2(s_t + h * KH, s_t + (1 - h) * KH, sv, so);
+      mask(sv, s0 + h * KH, std::integral_constant<int, KH>());
+      mask(so, s0 + (1 - h) * KH, std::integral_constant<int, KH>());
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(sv[i], so[i]);
 #pragma unroll
-      for (int i = 8; i < KH; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
-      // the other half of the row, for the maximum only
-#pragma unroll 1
-      for (int cc = 0; cc < KH; cc += 32) {
-        float t[32];
-        tmem_ld_32x32b_x32(s_t + (1 - h) * KH + cc, t);
-        mask(t, s0 + (1 - h) * KH + cc, 32);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], t[i]);
-      }
+      for (int i = 8; i < KH; ++i) mx[i & 7] = fmaxf(mx[i & 7], fmaxf(sv[i], so[i]));
       const float m_tile =
           fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
@@ -492,7 +524,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               ((sum[4] + sum[5]) + (sum[6] + sum[7]));
       fence_proxy_async_smem();  // P, written by threads, is read by the tensor core
       tc_fence_before();
-      mbar_arrive(smem_u32(&p_full[b]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[b]));
     }
     if (ok && n_tiles > 0)
       ok = warp_wait(smem_u32(&pv_done[(n_tiles - 1) & 1]), ((n_tiles - 1) >> 1) & 1u, lane,
