@@ -15,8 +15,7 @@
 //   warp 0    TMA producer: 2-D tiled loads, 128-byte swizzle, into a ring of
 //             stage pairs guarded by mbarriers (one full/empty barrier per
 //             pair).  Weight tiles of the first ring pass are issued before
-//             the grid waits on the previous kernel; skinny tiles also
-//             prefetch the rest of their first unit's weight boxes into L2.
+//             the grid waits on the previous kernel.
 //   warp 1    MMA issuer: one thread issues tcgen05.mma kind::f16 (fp16/bf16
 //             in, fp32 accumulate) into a double-buffered tensor-memory
 //             accumulator; tcgen05.commit frees ring slots.
@@ -351,23 +350,46 @@ __device__ __forceinline__ void emit_tile(const TcParams& p, const Src& src, int
     if constexpr (EPI == EPI_SWIGLU) {
       // Packed rows: lanes 0-63 gate, 64-127 up, of output features
       // prow0/2 + (lr % 64).
-      const int n = prow0 / 2 + (lr & 63);
 #pragma unroll 1
       for (int c = 0; c < BN; c += CW) {
         src.get(c, v);
+        // token-major (column j of the 64 gate rows at xch[64 j ..]): a warp's
+        // 32 rows land in 32 consecutive words, one bank each
         if (lr >= 64) {
 #pragma unroll
-          for (int j = 0; j < CW; ++j) xch[(lr - 64) * 32 + j] = E::round(v[j]);
+          for (int j = 0; j < CW; ++j) xch[j * 64 + (lr - 64)] = E::round(v[j]);
         }
         named_bar_sync(1, kEpiThreads);
-        if (lr < 64 && n < p.N) {
+        // the gate rows compute their CW outputs; once every up value has
+        // been read, they go back into the exchange buffer as 16-bit values,
+        // token-major (64 features of a token contiguous), and all 128
+        // threads store them as 16-byte vectors: a feature per thread would
+        // take one 2-byte store per token
+        T* out16 = reinterpret_cast<T*>(xch);
+        float o[CW];
+        if (lr < 64) {
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            const int m = qcol0 + c + j;
-            if (m < p.M) {
-              const float o = silu_fast(E::round(v[j])) * xch[lr * 32 + j];
-              static_cast<T*>(p.C)[m * p.ldc + n] = E::from_f(o);
-            }
+          for (int j = 0; j < CW; ++j) o[j] = silu_fast(E::round(v[j])) * xch[j * 64 + lr];
+        }
+        named_bar_sync(1, kEpiThreads);
+        if (lr < 64) {
+#pragma unroll
+          for (int j = 0; j < CW; ++j) out16[j * 64 + lr] = E::from_f(o[j]);
+        }
+        named_bar_sync(1, kEpiThreads);
+        const int n0 = prow0 / 2;  // first output feature of the tile (a multiple of 64)
+#pragma unroll 1
+        for (int idx = lr; idx < CW * 8; idx += kEpiThreads) {
+          const int j = idx >> 3, q = idx & 7;  // token, 8-feature group
+          const int m = qcol0 + c + j;
+          const int nn = n0 + 8 * q;
+          if (m >= p.M || nn >= p.N) continue;
+          const T* srcv = out16 + j * 64 + 8 * q;
+          T* dst = static_cast<T*>(p.C) + m * p.ldc + nn;
+          if (vec && nn + 8 <= p.N) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(srcv);
+          } else {
+            for (int t = 0; t < 8 && nn + t < p.N; ++t) dst[t] = srcv[t];
           }
         }
         named_bar_sync(1, kEpiThreads);
@@ -1200,17 +1222,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int pend_k[STAGES], pend_row[STAGES];
       uint32_t arm_par[PAIRS];
-      // Skinny tiles: the first unit's weight boxes beyond the ring are
-      // prefetched into L2 before griddepcontrol.wait, so that streaming them
-      // overlaps the previous kernel (weights do not depend on it).
-      int pf_row = -1, pf_k0 = 0, pf_k1 = 0;
-      auto prefetch_weights = [&]() {
-        if constexpr (SWAP) {
-          const int kb_real = (p.K + kBK - 1) / kBK;
-          const int end = pf_k1 < kb_real ? pf_k1 : kb_real;
-          for (int k = pf_k0; k < end; ++k) tma_prefetch_l2_2d(tm_w, k * kBK, pf_row);
-        }
-      };
+      // No L2 prefetch of the weight boxes beyond the ring: one SM's TMA unit
+      // issues prefetches in order with its loads, so the boxes of a whole K
+      // range (28 x 16 KB for gate/up) delay the first token loads by ~3 K
+      // cycles, and the loads of a kernel sharing the SM.  Measured on the
+      // 22-layer decode step: 1.126 -> 1.044 ms at 32 tokens without it.
       int n_issued = 0;
       bool waited = false;
       int stage = 0;
@@ -1224,15 +1240,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords(u.tile, p, tp, tq);
         const int row_w = SWAP ? tp * kBM : tq * BN + half * QR;
         const int row_x = SWAP ? tq * BN : tp * TILE_P + half * kBM;
-        if (pf_row < 0) {
-          pf_row = row_w;
-          pf_k0 = u.k0 + STAGES;
-          pf_k1 = u.k1;
-        }
         for (int k = u.k0; k < u.k1; ++k) {
           if (n_issued >= STAGES) {
             if (!waited) {
-              prefetch_weights();
               pdl_wait();
               for (int i = 0; i < STAGES; ++i)
                 load(ring + i * STAGE_BYTES + off_x, tm_x, full_addr(i), pend_k[i] * kBK,
@@ -1881,10 +1891,11 @@ void plan_tc(Plan& pl, int M, int N, int K, int epi, int algo, int sm_count, siz
       split = G / tiles;
       if (split > 8) split = 8;
       if (split > kb / 2) split = kb / 2 > 0 ? kb / 2 : 1;
-      // every cluster resident in one wave, next to one co-resident kernel
-      // where two skinny CTAs fit on an SM
-      const int share = (tc_skinny_budget(bn) < 114 * 1024) ? 2 : 1;
-      while (split > 1 && cluster_cap(2, bn, 0, split) / share < tiles) --split;
+      // every cluster resident in one wave.  Keeping half of the slots free
+      // for the next kernel's CTAs (where two skinny CTAs fit on an SM) cost
+      // more than the overlap gained: at 32 tokens q/k/v 8.3 -> 6.6 us, o_proj
+      // 8.0 -> 7.0, down 13.3 -> 11.0 without the reservation
+      while (split > 1 && cluster_cap(2, bn, 0, split) < tiles) --split;
     }
     fill_tiles(pl, K, bn, split, 0, G);
     return;

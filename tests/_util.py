@@ -27,6 +27,17 @@ EXACT_MIN = 0.95
 # rounding of acc before the add puts ulp(acc) on outputs that cancel to far
 # below |acc|, which no floor short of |acc| itself excludes.
 ELEM_FLOOR = 1e-2
+# The 1e-2 elementwise bar is fp16's (the path's own dtype).  bf16 keeps 8
+# significand bits to fp16's 11, so one unit is up to 2^-7 of a value: where
+# both sides' roundings of g and u (SwiGLU) and of the output flip by one
+# unit, outputs differ by up to three of them.  bf16 comparisons are held to
+# that, three units.
+ELEM_MAX_BF16 = 3 * 2.0 ** -7
+
+
+def elem_max_for(dt: int) -> float:
+    """Elementwise relative-error bound for 16-bit outputs of dtype code dt."""
+    return MAX_REL if dt == 0 else ELEM_MAX_BF16
 
 TORCH_DT = {0: torch.float16, 1: torch.bfloat16}
 DT_CODE = {torch.float16: 0, torch.bfloat16: 1}

@@ -11,7 +11,7 @@ import torch
 import orininfer_b200 as ob
 from orininfer_b200 import _lib
 from oracle import oracle as orc
-from tests._util import EXACT_MIN, MAX_REL, TORCH_DT, assert_close, bits, from_bits, seeded
+from tests._util import EXACT_MIN, TORCH_DT, assert_close, bits, elem_max_for, from_bits, seeded
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -38,7 +38,7 @@ def run_case(M, N, K, dt, epi, algo="auto", seed=0, check_rows=None):
     # the elementwise relative error is asserted where no residual add cancels
     assert_close(y[rows].float(), ref_t.float(), f"{algo} {epi} dt={dt} M={M} N={N} K={K}",
                  exact_min=None if epi == "f32_partial" else EXACT_MIN,
-                 elem_max=MAX_REL if epi in ("none", "f32", "swiglu") else None)
+                 elem_max=elem_max_for(dt) if epi in ("none", "f32", "swiglu") else None)
     return y
 
 
