@@ -1155,10 +1155,11 @@ def run_model_decode(args) -> dict:
             "prefill_tokens_per_s": round(B * 2048 / (prefill_ms / 1e3), 1),
             "bytes_per_step": w_bytes + kv_bytes, "gbs": round(gbs, 1),
             "hbm_frac": round(gbs / hbm, 4), "peak_hbm_gbs": hbm,
-            # per layer: norm, q/k/v, RoPE + append, attention, combine, o_proj,
-            # norm, gate/up, down; then embedding, final norm, LM head (key
-            # reset, weight stream, decode), token copy
-            "launches_per_step": L * (7 if fold else 9) + (5 if fold else 6),
+            # per layer: norm, q/k/v, RoPE + append, attention (its key splits
+            # merged by the last split CTA), o_proj, norm, gate/up, down; then
+            # embedding, final norm, LM head (key reset, weight stream,
+            # decode), token copy
+            "launches_per_step": L * (6 if fold else 8) + (5 if fold else 6),
             "steps": args.model_decode,
             "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
             "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,

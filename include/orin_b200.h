@@ -307,8 +307,10 @@ orin_status orin_kv_append(void* k_pool, void* v_pool, const void* k_src,
  * head_dim 64 or 128 (else ORIN_ERR_UNSUPPORTED); all pointers 16-byte
  * aligned.  workspace (device, may be NULL) lets few-token calls split the
  * keys across CTAs; orin_attention_workspace_bytes gives the size that
- * unlocks every split, a smaller one splits less.  Calls that share a
- * workspace must be ordered on one stream.
+ * unlocks every split, a smaller one splits less.  Its first 4 KB hold the
+ * arrival counters the split CTAs merge through: they must be zero before
+ * the first call (allocate the workspace zeroed), and every call leaves them
+ * zero.  Calls that share a workspace must be ordered on one stream.
  */
 orin_status orin_attention(void* out, const void* q, const void* k_pool,
                            const void* v_pool, int seq_len, int cache_len,

@@ -21,11 +21,14 @@
 // Keys stream through shared memory in 64-key tiles (cp.async, two stages,
 // rows padded by 16 bytes so the fragment loads are bank-conflict free) in the
 // order of their logical positions: the sink range, then the window range.
+// The split partials of a row block are merged by the last of its split CTAs
+// to arrive (an arrival counter in the workspace's first 4 KB, which every
+// call leaves zero), in split order.
 // S = Q K^T and O += P V run on mma.sync m16n8k16 with an online softmax in
 // registers.  Prefill blocks put 4 warps on 64 rows; decode blocks put the 4
 // warps on one 16-row group and split each key tile between them, and split
 // the key range across CTAs; partials (running max, sum, unnormalised O)
-// merge in shared memory and, across CTAs, in attn_combine_kernel.
+// merge in shared memory and, across CTAs, in the last CTA of the row block.
 #include <cstdlib>
 #include <cstring>
 
@@ -45,6 +48,7 @@ struct AttnParams {
   const void* k_pool;  // [n_sink + W, num_kv_heads, head_dim] 16-bit
   const void* v_pool;
   float* ws;           // split partials (splits > 1): O [splits][rows][HD], then (m, l) pairs
+  int* counters;       // splits > 1: one arrival counter per (grid x, grid y), zero between calls
   int seq_len, cache_len, num_heads, num_kv_heads, n_sink, window;
   float scale;
   int group;   // G = num_heads / num_kv_heads
@@ -403,41 +407,69 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
   }
-}
-
-// out[row] = round16( sum_s f_s O_s / sum_s f_s l_s ), f_s = exp(m_s - max m):
-// one warp per output row.
-template <int DT, int HD>
-__global__ void __launch_bounds__(128)
-    attn_combine_kernel(void* out, const float* ws, int rows_total, int splits) {
-  using E = Elem<DT>;
-  pdl_wait();
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows_total) return;
-  const float* ml = ws + static_cast<size_t>(splits) * rows_total * HD;
-  float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, ml[(static_cast<size_t>(s) * rows_total + row) * 2]);
-  constexpr int DPL = HD / 32;  // dims per lane (2 or 4)
-  float acc[DPL];
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  float l = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const size_t pr = static_cast<size_t>(s) * rows_total + row;
-    const float ms = ml[pr * 2];
-    const float f = ms == -INFINITY ? 0.f : __expf(ms - m);
-    l += f * ml[pr * 2 + 1];
-    const float* os = ws + pr * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] += f * os[i];
+  if (p.splits == 1) return;
+  // The last split CTA of this row block to arrive merges the splits,
+  // out = round16( sum_s f_s O_s / sum_s f_s l_s ), f_s = exp(m_s - max m),
+  // below.  Its partials are fenced before the arrival; the other splits'
+  // are read through L2 after it (threadfence, atomic, threadfence).
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int* cnt = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
+    const int last = atomicAdd(cnt, 1) == p.splits - 1;
+    if (last) *cnt = 0;  // every split has arrived: zero for the next call
+    s_last = last;
   }
-  pdl_launch_dependents();
-  const float inv = l > 0.f ? 1.f / l : 0.f;
-  uint16_t* dst = static_cast<uint16_t*>(out) + static_cast<size_t>(row) * HD + lane * DPL;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // One pass over the splits in order with a running maximum (flash-decoding
+  // style): out = round16(o / l).  Each thread takes 4 dims of a row; the
+  // loads of 8 splits are in flight before their updates.
+  const float* mlb = p.ws + static_cast<size_t>(p.splits) * rows_total * HD;
+  for (int idx = tid; idx < R * (HD / 4); idx += kAttnThreads) {
+    const int r = idx / (HD / 4), d = (idx % (HD / 4)) * 4;
+    const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
+    const int tk = t_lo + tr;
+    if (!(tr < p.tpb && tk < p.seq_len && hr < p.group)) continue;
+    const int orow = static_cast<int>(row_base) + tk * p.num_heads + kvh * p.group + hr;
+    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    auto update = [&](float2 ml, float4 v) {
+      if (ml.x == -INFINITY) return;  // a split with no attended key adds nothing
+      const float m_new = fmaxf(m, ml.x);
+      const float a = m == -INFINITY ? 0.f : __expf(m - m_new);
+      const float f = __expf(ml.x - m_new);
+      l = l * a + f * ml.y;
+      o[0] = o[0] * a + f * v.x;
+      o[1] = o[1] * a + f * v.y;
+      o[2] = o[2] * a + f * v.z;
+      o[3] = o[3] * a + f * v.w;
+      m = m_new;
+    };
+    constexpr int kB = 8;
+    int sp = 0;
+    for (; sp + kB <= p.splits; sp += kB) {
+      float2 mlv[kB];
+      float4 ov[kB];
 #pragma unroll
-  for (int i = 0; i < DPL; i += 2)
-    *reinterpret_cast<uint32_t*>(dst + i) = E::pack2(acc[i] * inv, acc[i + 1] * inv);
+      for (int u = 0; u < kB; ++u) {
+        const size_t pr = static_cast<size_t>(sp + u) * rows_total + orow;
+        mlv[u] = __ldcg(reinterpret_cast<const float2*>(mlb + pr * 2));
+        ov[u] = __ldcg(reinterpret_cast<const float4*>(p.ws + pr * HD + d));
+      }
+#pragma unroll
+      for (int u = 0; u < kB; ++u) update(mlv[u], ov[u]);
+    }
+    for (; sp < p.splits; ++sp) {
+      const size_t pr = static_cast<size_t>(sp) * rows_total + orow;
+      update(__ldcg(reinterpret_cast<const float2*>(mlb + pr * 2)),
+             __ldcg(reinterpret_cast<const float4*>(p.ws + pr * HD + d)));
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + static_cast<size_t>(orow) * HD + d) =
+        make_uint2(E::pack2(o[0] * inv, o[1] * inv), E::pack2(o[2] * inv, o[3] * inv));
+  }
 }
 
 // The call's new K/V rows into their pool slots (src/kv_cache.cu:21-41).  When
@@ -487,12 +519,8 @@ cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t
 
 template <int DT, int HD>
 cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStream_t s) {
-  cudaError_t e = rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
-                          : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
-  if (e != cudaSuccess || p.splits == 1) return e;
-  const int rows_total = p.batch * p.seq_len * p.num_heads;
-  return launch_pdl_smem(attn_combine_kernel<DT, HD>, dim3((rows_total + 3) / 4), dim3(128), 0,
-                         s, p.out, static_cast<const float*>(p.ws), rows_total, p.splits);
+  return rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
+                 : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
 }
 
 }  // namespace
@@ -524,11 +552,17 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
     splits = want < 1 ? 1 : static_cast<int>(want);
     const size_t per_split =
         static_cast<size_t>(seq_len) * num_heads * (head_dim + 2) * sizeof(float);
-    while (splits > 1 && static_cast<size_t>(splits) * per_split > workspace_bytes) --splits;
+    while (splits > 1 &&
+           (workspace_bytes < kAttnCounterBytes ||
+            static_cast<size_t>(splits) * per_split > workspace_bytes - kAttnCounterBytes))
+      --splits;
+    // one arrival counter per CTA row of the grid
+    if (ctas > kAttnCounterBytes / static_cast<long long>(sizeof(int))) splits = 1;
   }
   pl.splits = splits;
-  pl.workspace_bytes = splits > 1 ? static_cast<size_t>(splits) * seq_len * num_heads *
-                                        (head_dim + 2) * sizeof(float)
+  pl.workspace_bytes = splits > 1 ? kAttnCounterBytes + static_cast<size_t>(splits) * seq_len *
+                                                            num_heads * (head_dim + 2) *
+                                                            sizeof(float)
                                   : 0;
   return pl;
 }
@@ -570,9 +604,15 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
       return launch_attention_tc(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
                                  num_kv_heads, head_dim, scale, n_sink, window, dtype, err, s);
   }
-  // each sequence plans alone, on its share of the workspace
-  const AttnPlan pl = plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim,
-                                     n_sink, window, workspace ? workspace_bytes / batch : 0);
+  // each sequence plans alone, on its share of the partials' part of the
+  // workspace (the arrival counters at its start serve the whole call)
+  const size_t share = (workspace && workspace_bytes > kAttnCounterBytes)
+                           ? (workspace_bytes - kAttnCounterBytes) / batch + kAttnCounterBytes
+                           : 0;
+  AttnPlan pl = plan_attention(seq_len, cache_len, num_heads, num_kv_heads, head_dim, n_sink,
+                               window, share);
+  if (pl.row_blocks * num_kv_heads * batch > kAttnCounterBytes / static_cast<long long>(sizeof(int)))
+    pl.splits = 1;
   if (pl.row_blocks > 0x7fffffffLL || static_cast<long long>(num_kv_heads) * batch > 65535 ||
       static_cast<long long>(batch) * seq_len * num_heads > 0x7fffffffLL)
     return cudaErrorInvalidConfiguration;
@@ -581,7 +621,9 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
   p.q = q;
   p.k_pool = k_pool;
   p.v_pool = v_pool;
-  p.ws = static_cast<float*>(workspace);
+  p.counters = static_cast<int*>(workspace);
+  p.ws = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnCounterBytes)
+                   : nullptr;
   p.seq_len = seq_len;
   p.cache_len = cache_len;
   p.num_heads = num_heads;

@@ -119,6 +119,10 @@ struct AttnPlan {
   long long row_blocks;
   size_t workspace_bytes;  // what `splits` needs
 };
+// A split plan's workspace starts with kAttnCounterBytes of arrival counters
+// (one int per CTA row of the grid; zero before the first call, left zero by
+// every call), then the split partials.
+constexpr size_t kAttnCounterBytes = 4096;
 AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
                         int head_dim, int n_sink, int window, size_t workspace_bytes);
 // `batch` sequences of seq_len tokens each, all at the same positions: q/out

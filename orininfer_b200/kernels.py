@@ -311,7 +311,9 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
     sink + sliding-window GQA attention of q [seq_len, num_heads, head_dim]
     over the ring pools [n_sink + window_size, num_kv_heads, head_dim] into
     out.  With split (the default) few-token calls split their keys across
-    CTAs through `workspace` (allocated here when not given)."""
+    CTAs through `workspace` (allocated here when not given; a caller's
+    workspace must start zeroed: its first 4 KB are arrival counters that
+    every call leaves zero)."""
     _need_cuda(out, q, k_pool, v_pool, workspace)
     if len({out.dtype, q.dtype, k_pool.dtype, v_pool.dtype}) != 1:
         raise ValueError("out, q and the pools must share one dtype")
@@ -321,7 +323,7 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
             need = attention_workspace_bytes(seq_len, cache_len, num_heads, num_kv_heads,
                                              head_dim, n_sink, window_size)
             if need:
-                workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+                workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         if workspace is not None:
             ws_bytes = workspace.numel() * workspace.element_size()
     else:
@@ -351,7 +353,7 @@ def attention_batch(out: torch.Tensor, q: torch.Tensor, k_pools: torch.Tensor,
         need = batch * attention_workspace_bytes(seq_len, cache_len, num_heads, num_kv_heads,
                                                  head_dim, n_sink, window_size)
         if need:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(_lib.lib.orin_attention_batch(_ptr(out), _ptr(q), _ptr(k_pools), _ptr(v_pools), batch,
                                         k_pools.stride(0), seq_len, cache_len, num_heads,

@@ -7,7 +7,7 @@ reference makes fifteen:
     orin_rmsnorm(xn, x)                          :53
     orin_linear(qkv, xn, W_qkv)                  :59-61  (q/k/v weights stacked: one GEMM)
     orin_qkv_rope_append(q, qkv, pools)          :64-75  (Qwen3 q/k norm, RoPE, K/V append)
-    orin_attention(att, q, pools)                :79-84  (+ the split-key combine for decode)
+    orin_attention(att, q, pools)                :79-84  (decode splits merged in the kernel)
     orin_linear(x, att, W_o, RESIDUAL, x)        :87-90
     orin_rmsnorm(xn, x)                          :95
     orin_linear(h, xn, W_gate_up, SWIGLU)        :100-104
@@ -263,7 +263,7 @@ class Decoder:
         self.lm_head = tensors["lm_head.weight"].to(device)
         dt = self.embed.dtype
         ws = DecoderLayer.workspace_bytes(cfg, n_sink, window, self.batch)
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=device)
         self.gemm_ws = kernels.linear_workspace(device)
         self.layers = [
             DecoderLayer(layer_for_device(tensors, i, cfg, device), cfg, n_sink=n_sink,
@@ -424,7 +424,7 @@ class TPDecoder(Decoder):
         dt = self.embed.dtype
         local = TPDecoderLayer.local_config(cfg, rank, world)
         ws = DecoderLayer.workspace_bytes(local, n_sink, window)
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=device)
         self.layers = [
             TPDecoderLayer(layer_for_device(tensors, i, cfg, device, rank, world), cfg, comm,
                            n_sink=n_sink, window=window, max_tokens=max_tokens,

@@ -183,12 +183,14 @@ def test_batched_attention_and_append_reject_bad_arguments_on_host():
 def test_attention_workspace_plan():
     """Few-token calls split their keys across CTAs; prefill-sized calls don't.
     The split count for TinyLlama decode (32 heads over 4 KV heads, window
-    1024 + 4 sinks) is one per 64-key tile: 17."""
+    1024 + 4 sinks) is one per 64-key tile: 17.  A split workspace holds 4 KB
+    of arrival counters, then the partials (O, running max and sum per row)."""
     ws = K.attention_workspace_bytes
-    assert ws(1, 2048, 32, 4, 64, 4, 1024) == 17 * 32 * (64 + 2) * 4
+    counters = 4096
+    assert ws(1, 2048, 32, 4, 64, 4, 1024) == counters + 17 * 32 * (64 + 2) * 4
     assert ws(1, 3, 32, 4, 64, 4, 1024) == 0            # one key tile: nothing to split
     assert ws(1028, 1028, 32, 4, 64, 4, 1024) == 0      # 516 CTAs without splitting
-    assert ws(1, 3000, 32, 8, 128, 4, 1024) == 17 * 32 * (128 + 2) * 4
+    assert ws(1, 3000, 32, 8, 128, 4, 1024) == counters + 17 * 32 * (128 + 2) * 4
     assert ws(0, 0, 32, 4, 64, 4, 1024) == 0
 
 

@@ -90,7 +90,7 @@ def test_attention_split_keys_agree(ws):
     need = K.attention_workspace_bytes(S, C, nh, nkv, hd, ns, W)
     assert need > 0
     kw = {"none": dict(split=False),
-          "short": dict(workspace=torch.empty(need // 3, dtype=torch.uint8, device="cuda")),
+          "short": dict(workspace=torch.zeros(need // 3, dtype=torch.uint8, device="cuda")),
           "full": dict()}[ws]
     check(ours(q, kp, vp, S, C, nh, nkv, hd, ns, W, dt, **kw), r, dt, f"split {ws}")
 
@@ -201,7 +201,7 @@ def test_attention_in_a_cuda_graph():
     q, kp, vp = inputs(17, S, nh, nkv, hd, ns, W, dt)
     dq, dk, dv = dev(q, dt), dev(kp, dt), dev(vp, dt)
     out = torch.empty((S, nh, hd), dtype=TORCH_DT[dt], device="cuda")
-    ws = torch.empty(K.attention_workspace_bytes(S, C, nh, nkv, hd, ns, W), dtype=torch.uint8,
+    ws = torch.zeros(K.attention_workspace_bytes(S, C, nh, nkv, hd, ns, W), dtype=torch.uint8,
                      device="cuda")
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
