@@ -21,14 +21,16 @@
 // Keys stream through shared memory in 64-key tiles (cp.async, two stages,
 // rows padded by 16 bytes so the fragment loads are bank-conflict free) in the
 // order of their logical positions: the sink range, then the window range.
-// The split partials of a row block are merged by the last of its split CTAs
-// to arrive (an arrival counter in the workspace's first 4 KB, which every
-// call leaves zero), in split order.
+// The split partials of a decode row block (16 rows) are merged by the last
+// of its split CTAs to arrive (an arrival counter in the workspace's first
+// 4 KB, which every call leaves zero), in split order; those of a prefill row
+// block (64 rows, too many for one CTA's loads in flight) by a combine launch
+// over every SM.
 // S = Q K^T and O += P V run on mma.sync m16n8k16 with an online softmax in
 // registers.  Prefill blocks put 4 warps on 64 rows; decode blocks put the 4
 // warps on one 16-row group and split each key tile between them, and split
 // the key range across CTAs; partials (running max, sum, unnormalised O)
-// merge in shared memory and, across CTAs, in the last CTA of the row block.
+// merge in shared memory and, across CTAs, as above.
 #include <cstdlib>
 #include <cstring>
 
@@ -49,6 +51,7 @@ struct AttnParams {
   const void* v_pool;
   float* ws;           // split partials (splits > 1): O [splits][rows][HD], then (m, l) pairs
   int* counters;       // splits > 1: one arrival counter per (grid x, grid y), zero between calls
+  int merge_here;      // splits > 1: the last split CTA merges (else attn_combine_kernel)
   int seq_len, cache_len, num_heads, num_kv_heads, n_sink, window;
   float scale;
   int group;   // G = num_heads / num_kv_heads
@@ -145,6 +148,50 @@ constexpr int attn_smem_bytes() {
 
 // RW = warps stacked on rows (4: 64 rows, prefill), the other 4 / RW warps
 // split each key tile.
+// out[orow][d, d + 4) = round16(o / l) over the key splits' partials, in
+// split order with a running maximum (flash-decoding style): o = sum_s f_s O_s,
+// l = sum_s f_s l_s, f_s = exp(m_s - max m).  The partials are read through L2
+// (written by other CTAs), 8 splits' loads in flight before their updates.
+template <int DT, int HD>
+__device__ __forceinline__ void merge_splits(void* out, const float* ws, int rows_total,
+                                             int splits, int orow, int d) {
+  using E = Elem<DT>;
+  const float* mlb = ws + static_cast<size_t>(splits) * rows_total * HD;
+  float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int kB = 8;
+  for (int sp = 0; sp < splits; sp += kB) {
+    float2 mlv[kB];
+    float4 ov[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (sp + u < splits) {
+        const size_t pr = static_cast<size_t>(sp + u) * rows_total + orow;
+        mlv[u] = __ldcg(reinterpret_cast<const float2*>(mlb + pr * 2));
+        ov[u] = __ldcg(reinterpret_cast<const float4*>(ws + pr * HD + d));
+      } else {
+        mlv[u] = make_float2(-INFINITY, 0.f);
+        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (mlv[u].x == -INFINITY) continue;  // a split with no attended key adds nothing
+      const float m_new = fmaxf(m, mlv[u].x);
+      const float a = m == -INFINITY ? 0.f : __expf(m - m_new);
+      const float f = __expf(mlv[u].x - m_new);
+      l = l * a + f * mlv[u].y;
+      o[0] = o[0] * a + f * ov[u].x;
+      o[1] = o[1] * a + f * ov[u].y;
+      o[2] = o[2] * a + f * ov[u].z;
+      o[3] = o[3] * a + f * ov[u].w;
+      m = m_new;
+    }
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + static_cast<size_t>(orow) * HD + d) =
+      make_uint2(E::pack2(o[0] * inv, o[1] * inv), E::pack2(o[2] * inv, o[3] * inv));
+}
+
 template <int DT, int HD, int RW>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_kernel(const AttnParams p) {
@@ -407,11 +454,10 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
   }
-  if (p.splits == 1) return;
-  // The last split CTA of this row block to arrive merges the splits,
-  // out = round16( sum_s f_s O_s / sum_s f_s l_s ), f_s = exp(m_s - max m),
-  // below.  Its partials are fenced before the arrival; the other splits'
-  // are read through L2 after it (threadfence, atomic, threadfence).
+  if (p.splits == 1 || !p.merge_here) return;
+  // The last split CTA of this row block to arrive merges the splits.  Its
+  // partials are fenced before the arrival; the other splits' are read
+  // through L2 after it (threadfence, atomic, threadfence).
   __shared__ int s_last;
   __threadfence();
   __syncthreads();
@@ -424,52 +470,27 @@ __global__ void __launch_bounds__(kAttnThreads)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // One pass over the splits in order with a running maximum (flash-decoding
-  // style): out = round16(o / l).  Each thread takes 4 dims of a row; the
-  // loads of 8 splits are in flight before their updates.
-  const float* mlb = p.ws + static_cast<size_t>(p.splits) * rows_total * HD;
   for (int idx = tid; idx < R * (HD / 4); idx += kAttnThreads) {
     const int r = idx / (HD / 4), d = (idx % (HD / 4)) * 4;
     const int tr = r / p.hpb, hr = hs * p.hpb + r % p.hpb;
     const int tk = t_lo + tr;
     if (!(tr < p.tpb && tk < p.seq_len && hr < p.group)) continue;
     const int orow = static_cast<int>(row_base) + tk * p.num_heads + kvh * p.group + hr;
-    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    auto update = [&](float2 ml, float4 v) {
-      if (ml.x == -INFINITY) return;  // a split with no attended key adds nothing
-      const float m_new = fmaxf(m, ml.x);
-      const float a = m == -INFINITY ? 0.f : __expf(m - m_new);
-      const float f = __expf(ml.x - m_new);
-      l = l * a + f * ml.y;
-      o[0] = o[0] * a + f * v.x;
-      o[1] = o[1] * a + f * v.y;
-      o[2] = o[2] * a + f * v.z;
-      o[3] = o[3] * a + f * v.w;
-      m = m_new;
-    };
-    constexpr int kB = 8;
-    int sp = 0;
-    for (; sp + kB <= p.splits; sp += kB) {
-      float2 mlv[kB];
-      float4 ov[kB];
-#pragma unroll
-      for (int u = 0; u < kB; ++u) {
-        const size_t pr = static_cast<size_t>(sp + u) * rows_total + orow;
-        mlv[u] = __ldcg(reinterpret_cast<const float2*>(mlb + pr * 2));
-        ov[u] = __ldcg(reinterpret_cast<const float4*>(p.ws + pr * HD + d));
-      }
-#pragma unroll
-      for (int u = 0; u < kB; ++u) update(mlv[u], ov[u]);
-    }
-    for (; sp < p.splits; ++sp) {
-      const size_t pr = static_cast<size_t>(sp) * rows_total + orow;
-      update(__ldcg(reinterpret_cast<const float2*>(mlb + pr * 2)),
-             __ldcg(reinterpret_cast<const float4*>(p.ws + pr * HD + d)));
-    }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + static_cast<size_t>(orow) * HD + d) =
-        make_uint2(E::pack2(o[0] * inv, o[1] * inv), E::pack2(o[2] * inv, o[3] * inv));
+    merge_splits<DT, HD>(p.out, p.ws, rows_total, p.splits, orow, d);
   }
+}
+
+// The split partials of prefill row blocks merged, one thread per 4 output
+// dims of a row.
+template <int DT, int HD>
+__global__ void __launch_bounds__(128)
+    attn_combine_kernel(void* out, const float* ws, int rows_total, int splits) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const long long idx = static_cast<long long>(blockIdx.x) * 128 + threadIdx.x;
+  if (idx >= static_cast<long long>(rows_total) * (HD / 4)) return;
+  merge_splits<DT, HD>(out, ws, rows_total, splits, static_cast<int>(idx / (HD / 4)),
+                       static_cast<int>(idx % (HD / 4)) * 4);
 }
 
 // The call's new K/V rows into their pool slots (src/kv_cache.cu:21-41).  When
@@ -519,8 +540,14 @@ cudaError_t launch_attn_kernel(const AttnParams& p, int row_blocks, cudaStream_t
 
 template <int DT, int HD>
 cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStream_t s) {
-  return rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
-                 : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
+  cudaError_t e = rw == 1 ? launch_attn_kernel<DT, HD, 1>(p, row_blocks, s)
+                          : launch_attn_kernel<DT, HD, 4>(p, row_blocks, s);
+  if (e != cudaSuccess || p.splits == 1 || p.merge_here) return e;
+  const int rows_total = p.batch * p.seq_len * p.num_heads;
+  const long long items = static_cast<long long>(rows_total) * (HD / 4);
+  return launch_pdl_smem(attn_combine_kernel<DT, HD>, dim3(static_cast<unsigned>((items + 127) / 128)),
+                         dim3(128), 0, s, p.out, static_cast<const float*>(p.ws), rows_total,
+                         p.splits);
 }
 
 }  // namespace
@@ -570,13 +597,16 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
 namespace {
 
 // ORIN_ATTN_KERNEL: 0 automatic, 1 "mma" (the mma.sync kernel), 2 "tc" (the
-// tensor-core kernel wherever it applies).
+// tensor-core kernel wherever it applies), 3 "tc1" / 4 "tc2" (the tensor-core
+// kernel with one / two query tiles per CTA; two needs head dim 64).
 int attention_kernel_override() {
   static const int v = [] {
     const char* e = std::getenv("ORIN_ATTN_KERNEL");
     if (!e) return 0;
     if (std::strcmp(e, "mma") == 0) return 1;
     if (std::strcmp(e, "tc") == 0) return 2;
+    if (std::strcmp(e, "tc1") == 0) return 3;
+    if (std::strcmp(e, "tc2") == 0) return 4;
     return 0;
   }();
   return v;
@@ -600,9 +630,10 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
     const int group = num_heads / num_kv_heads;
     const long long rows = static_cast<long long>(seq_len) * group;
     const long long ctas = (rows + 127) / 128 * num_kv_heads;
-    if (ov == 2 || (ov == 0 && ctas >= 32))
+    if (ov >= 2 || (ov == 0 && ctas >= 32))
       return launch_attention_tc(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
-                                 num_kv_heads, head_dim, scale, n_sink, window, dtype, err, s);
+                                 num_kv_heads, head_dim, scale, n_sink, window, dtype, err, s,
+                                 ov >= 3 ? ov - 2 : 0);
   }
   // each sequence plans alone, on its share of the partials' part of the
   // workspace (the arrival counters at its start serve the whole call)
@@ -636,6 +667,10 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
   p.tpb = pl.tpb;
   p.hsb = pl.hsb;
   p.splits = pl.splits;
+  // decode row blocks merge in the kernel; prefill row blocks in a combine
+  // launch (64 rows x 10 splits on one CTA: 32.3 us against 17.0 for the
+  // 64 x 2048-token call of 32/4 heads of 64)
+  p.merge_here = pl.rw == 1 ? 1 : 0;
   p.batch = batch;
   p.pool_stride = pool_stride;
   const int rb = static_cast<int>(pl.row_blocks);

@@ -29,6 +29,12 @@
 //              more than 2^8; at the end O / l, rounded and stored.
 // CTAs start with the row blocks that have the most key tiles.
 //
+// Head dim 64 has a second form, attn_tc_pp_kernel: two 128-row query tiles
+// per CTA sharing every K/V tile, four softmax warps per tile at one thread
+// per row, the tensor core working on one tile while the other is in softmax.
+// It halves the grid, so the launcher takes it only where every CTA has the
+// same key tiles and halving the CTAs halves the waves.
+//
 // Keys are taken in slot order, 128 slots per tile (softmax does not depend on
 // the order of its terms): slot s holds, for a query at ap, the logical
 // position the reference reads there — s itself for a sink slot (attended if
@@ -166,6 +172,58 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// The row's attended slots as two ranges [0, a_hi) and [b_lo, b_hi): the
+// sinks, and the window positions [max(n_sink, ap + 1 - W), ap], whose slots
+// are one run of ring residues (split in two where it wraps).
+__device__ __forceinline__ void row_ranges(int ap, bool row_ok, int n_sink, int window,
+                                           int& a_hi, int& b_lo, int& b_hi) {
+  const int slots = n_sink + window;
+  a_hi = b_lo = b_hi = 0;
+  if (!row_ok) return;
+  if (ap < n_sink) {
+    a_hi = ap + 1;
+    return;
+  }
+  const int w_lo = max(n_sink, ap + 1 - window);
+  if (ap - w_lo + 1 >= window) {
+    a_hi = slots;
+    return;
+  }
+  const int r_lo = (w_lo - n_sink) % window, r_hi = (ap - n_sink) % window;
+  if (r_lo == 0) {
+    a_hi = n_sink + r_hi + 1;
+  } else if (r_lo <= r_hi) {
+    a_hi = n_sink;
+    b_lo = n_sink + r_lo;
+    b_hi = n_sink + r_hi + 1;
+  } else {
+    a_hi = n_sink + r_hi + 1;
+    b_lo = n_sink + r_lo;
+    b_hi = slots;
+  }
+}
+
+// bits [lo, hi) of 64
+__device__ __forceinline__ uint64_t range_bits64(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 64);
+  if (hi <= lo) return 0ull;
+  const uint64_t top = hi == 64 ? ~0ull : ((1ull << hi) - 1ull);
+  return top & ~((1ull << lo) - 1ull);
+}
+
+// -inf for the 64 keys [k0, k0 + 64) of v outside the ranges; skipped when
+// every lane of the warp attends to all of them
+__device__ __forceinline__ void mask64(float* v, int k0, int a_hi, int b_lo, int b_hi) {
+  const uint64_t bits = range_bits64(0, a_hi - k0) | range_bits64(b_lo - k0, b_hi - k0);
+  if (!__all_sync(0xffffffffu, bits == ~0ull)) {
+    const uint32_t lo = static_cast<uint32_t>(bits), hi = static_cast<uint32_t>(bits >> 32);
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (!(((i < 32 ? lo : hi) >> (i & 31)) & 1u)) v[i] = -INFINITY;
+  }
 }
 
 template <int DT, int HD>
@@ -383,47 +441,15 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     const int tok = t_lo + tr;
     const bool row_ok = tr < p.tpb && tok < p.seq_len && hr < p.group;
     const int ap = base + tok;
-    // The row's attended slots as two ranges [0, a_hi) and [b_lo, b_hi): the
-    // sinks, and the window positions [max(n_sink, ap + 1 - W), ap], whose
-    // slots are one run of ring residues (split in two where it wraps).
-    int a_hi = 0, b_lo = 0, b_hi = 0;
-    if (row_ok) {
-      if (ap < p.n_sink) {
-        a_hi = ap + 1;
-      } else {
-        const int w_lo = max(p.n_sink, ap + 1 - p.window);
-        if (ap - w_lo + 1 >= p.window) {
-          a_hi = slots;
-        } else {
-          const int r_lo = (w_lo - p.n_sink) % p.window, r_hi = (ap - p.n_sink) % p.window;
-          if (r_lo == 0) {
-            a_hi = p.n_sink + r_hi + 1;
-          } else if (r_lo <= r_hi) {
-            a_hi = p.n_sink;
-            b_lo = p.n_sink + r_lo;
-            b_hi = p.n_sink + r_hi + 1;
-          } else {
-            a_hi = p.n_sink + r_hi + 1;
-            b_lo = p.n_sink + r_lo;
-            b_hi = slots;
-          }
-        }
-      }
-    }
+    int a_hi, b_lo, b_hi;
+    row_ranges(ap, row_ok, p.n_sink, p.window, a_hi, b_lo, b_hi);
     // a warp with no valid row only keeps the P hand-off in step
     const bool dead = __all_sync(0xffffffffu, !row_ok);
     // masks the keys [k0, k0 + N) of v outside the row's ranges (a bit per
     // key); the warp skips it when every lane attends to all of them
-    auto range_bits = [](int lo, int hi) -> uint64_t {  // bits [lo, hi) of 64
-      lo = max(lo, 0);
-      hi = min(hi, 64);
-      if (hi <= lo) return 0ull;
-      const uint64_t top = hi == 64 ? ~0ull : ((1ull << hi) - 1ull);
-      return top & ~((1ull << lo) - 1ull);
-    };
     auto mask = [&](float* v, int k0, auto n_tag) {
       constexpr int N = decltype(n_tag)::value;
-      const uint64_t bits = range_bits(0, a_hi - k0) | range_bits(b_lo - k0, b_hi - k0);
+      const uint64_t bits = range_bits64(0, a_hi - k0) | range_bits64(b_lo - k0, b_hi - k0);
       const uint64_t all = N == 64 ? ~0ull : ((1ull << N) - 1ull);
       if (!__all_sync(0xffffffffu, (bits & all) == all)) {
         const uint32_t lo = static_cast<uint32_t>(bits), hi = static_cast<uint32_t>(bits >> 32);
@@ -567,6 +593,380 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Head dim 64: two 128-row query tiles per CTA in ping-pong.  Tiles A and B
+// (row blocks 2c and 2c + 1 of one KV head) share every K/V tile; warps 2-5
+// run tile A's softmax and warps 6-9 tile B's, one thread per row, so the
+// tensor core computes S or P V of one tile while the other is in softmax:
+//   S_A(j), S_B(j); then per tile t: [P_t(j) ready] P V_t(j), S_t(j + 1).
+// Tensor memory: S_A, S_B (128 columns each), O_A, O_B (64 each).  Shared
+// memory: Q_A, Q_B, two-stage K and V rings, P_A, P_B (one per tile: a tile's
+// softmax waits for its P V of tile j - 1 before writing P of tile j).
+// ---------------------------------------------------------------------------
+
+constexpr int kPpThreads = 320;
+
+template <int DT>
+__global__ void __launch_bounds__(kPpThreads, 1)
+    attn_tc_pp_kernel(const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const AttnTcParams p) {
+  using E = Elem<DT>;
+  constexpr int HD = 64;
+  constexpr uint32_t IDESC_S = instr_desc_f16(DT, kAtRows, kAtKeys);
+  constexpr uint32_t IDESC_O = instr_desc_f16(DT, kAtRows, HD) | (1u << 16);  // B MN-major
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t O_COL = 2 * kAtKeys;  // O_t at O_COL + t * HD
+  constexpr uint32_t TILE = kAtom;          // one 64-column x 128-row box
+
+  extern __shared__ uint8_t pp_dsmem[];
+  __shared__ __align__(8) uint64_t k_full[kAtStages];
+  __shared__ __align__(8) uint64_t k_empty[kAtStages];
+  __shared__ __align__(8) uint64_t v_full[kAtStages];
+  __shared__ __align__(8) uint64_t v_empty[kAtStages];
+  __shared__ __align__(8) uint64_t s_full[2];   // per query tile
+  __shared__ __align__(8) uint64_t p_full[2];   // per query tile, one arrival per warp
+  __shared__ __align__(8) uint64_t pv_done[2];  // per query tile
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base_s = (smem_u32(pp_dsmem) + 1023u) & ~1023u;
+  const uint32_t q_s = base_s;                     // Q_A, Q_B
+  const uint32_t k_ring = q_s + 2 * TILE;
+  const uint32_t v_ring = k_ring + kAtStages * TILE;
+  const uint32_t p_s = v_ring + kAtStages * TILE;  // P_A, P_B (two boxes each)
+
+  // CTAs in launch order take the row-block pairs with the most key tiles first
+  const int kvh = static_cast<int>(blockIdx.x % p.num_kv_heads);
+  const int pairs = (p.row_blocks + 1) / 2;
+  const int pair = pairs - 1 - static_cast<int>(blockIdx.x / p.num_kv_heads);
+  const int base = p.cache_len - p.seq_len;
+  const int slots = p.n_sink + p.window;
+  // tile t is row block 2 * pair + t: tokens from tile_lo(t), head slice tile_hs(t)
+  auto tile_lo = [&](int t) { return ((2 * pair + t) / p.hsb) * p.tpb; };
+  auto tile_hs = [&](int t) { return (2 * pair + t) % p.hsb; };
+  auto tile_ok = [&](int t) { return 2 * pair + t < p.row_blocks; };
+  int ap_max = 0;
+  for (int t = 0; t < 2; ++t) {
+    if (tile_ok(t)) {
+      const int t_hi = min(tile_lo(t) + p.tpb - 1, p.seq_len - 1);
+      ap_max = max(ap_max, base + t_hi);
+    }
+  }
+  const int n_tiles = (ap_max < slots) ? ap_max / kAtKeys + 1 : (slots + kAtKeys - 1) / kAtKeys;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAtStages; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&s_full[t]), 1);
+      mbar_init(smem_u32(&p_full[t]), 4);
+      mbar_init(smem_u32(&pv_done[t]), 1);
+    }
+    mbar_init(smem_u32(&drain_bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  pdl_wait();
+  // both tiles' Q rows into shared memory (K-major, 128-byte swizzle)
+  const uint16_t* qg = static_cast<const uint16_t*>(p.q);
+  for (int c = threadIdx.x; c < 2 * kAtRows * (HD / 8); c += kPpThreads) {
+    const int t = c / (kAtRows * (HD / 8));
+    const int cc = c % (kAtRows * (HD / 8));
+    const int r = cc / (HD / 8), j = cc % (HD / 8);
+    const int tr = r / p.hpb, hr = tile_hs(t) * p.hpb + r % p.hpb;
+    const int tok = tile_lo(t) + tr;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (tile_ok(t) && tr < p.tpb && tok < p.seq_len && hr < p.group)
+      v = *reinterpret_cast<const uint4*>(
+          qg + (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD + 8 * j);
+    const uint32_t a = q_s + t * TILE + at_sw128(r, j);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int n_k = 0, n_v = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % kAtStages;
+        const uint32_t par = ((j / kAtStages) - 1) & 1u;
+        if (j >= kAtStages && !mbar_wait_bounded(smem_u32(&k_empty[st]), par, &abort_flag, p.err,
+                                                 DEVERR_TIMEOUT_PRODUCER))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&k_full[st]), TILE);
+        tma_load_2d_plain(k_ring + st * TILE, &tm_k, smem_u32(&k_full[st]), kvh * HD,
+                          j * kAtKeys);
+        ++n_k;
+        if (j >= kAtStages && !mbar_wait_bounded(smem_u32(&v_empty[st]), par, &abort_flag, p.err,
+                                                 DEVERR_TIMEOUT_PRODUCER))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&v_full[st]), TILE);
+        tma_load_2d_plain(v_ring + st * TILE, &tm_v, smem_u32(&v_full[st]), kvh * HD,
+                          j * kAtKeys);
+        ++n_v;
+      }
+      if (abort_flag) {
+        auto drain = [&](uint64_t* full, int n) {
+          for (int j = n > kAtStages ? n - kAtStages : 0; j < n; ++j) {
+            const unsigned long long t0 = global_timer_ns();
+            while (!mbar_try_wait(smem_u32(&full[j % kAtStages]), (j / kAtStages) & 1u))
+              if (global_timer_ns() - t0 > 100000000ull) break;
+          }
+        };
+        drain(k_full, n_k);
+        drain(v_full, n_v);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      auto issue_s = [&](int t, int j) -> bool {
+        const int st = j % kAtStages;
+        if (t == 0 && !mbar_wait_bounded(smem_u32(&k_full[st]), (j / kAtStages) & 1u, &abort_flag,
+                                         p.err, DEVERR_TIMEOUT_MMA))
+          return false;
+        tc_fence_after();
+        const uint64_t qd = smem_desc_kmajor_sw128(q_s + t * TILE);
+        const uint64_t kd = smem_desc_kmajor_sw128(k_ring + st * TILE);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(t * kAtKeys);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>((kk * 32) >> 4);
+          tc_mma_f16(d, qd + off, kd + off, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&s_full[t]));
+        if (t == 1) tc_commit(smem_u32(&k_empty[st]));  // both tiles' S read K(j)
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int st = j % kAtStages;
+        if (!mbar_wait_bounded(smem_u32(&p_full[t]), j & 1u, &abort_flag, p.err,
+                               DEVERR_TIMEOUT_MMA) ||
+            (t == 0 && !mbar_wait_bounded(smem_u32(&v_full[st]), (j / kAtStages) & 1u,
+                                          &abort_flag, p.err, DEVERR_TIMEOUT_MMA)))
+          return false;
+        tc_fence_after();
+        const uint64_t pd = smem_desc_kmajor_sw128(p_s + t * 2 * TILE);
+        const uint64_t vd = smem_desc_mnmajor_sw128(v_ring + st * TILE, TILE);
+#pragma unroll
+        for (int kk = 0; kk < kAtKeys / 16; ++kk) {
+          const uint64_t aoff = static_cast<uint64_t>(((kk / 4) * TILE + (kk % 4) * 32) >> 4);
+          const uint64_t boff = static_cast<uint64_t>((kk * 16 * 128) >> 4);  // 16 keys
+          tc_mma_f16(tmem_base + O_COL + t * HD, pd + aoff, vd + boff, IDESC_O,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&pv_done[t]));
+        if (t == 1) tc_commit(smem_u32(&v_empty[st]));  // both tiles' P V read V(j)
+        return true;
+      };
+      bool ok = n_tiles == 0 || (issue_s(0, 0) && issue_s(1, 0));
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        // per tile: P V of tile j once its P is ready, then its S of tile j + 1
+        // (its S buffer was read before P was written)
+        for (int t = 0; ok && t < 2; ++t) {
+          if (!issue_pv(t, j) || (j + 1 < n_tiles && !issue_s(t, j + 1))) ok = false;
+        }
+      }
+      if (!ok) {
+        tc_commit(smem_u32(&drain_bar));
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(smem_u32(&drain_bar), 0))
+          if (global_timer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 2) >> 2;  // query tile
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // this thread's row (= tensor-memory lane)
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t s_t = lane_base + static_cast<uint32_t>(t * kAtKeys);
+    const uint32_t o_t = lane_base + O_COL + static_cast<uint32_t>(t * HD);
+    const int tr = r / p.hpb, hr = tile_hs(t) * p.hpb + r % p.hpb;
+    const int tok = tile_lo(t) + tr;
+    const bool row_ok = tile_ok(t) && tr < p.tpb && tok < p.seq_len && hr < p.group;
+    const int ap = base + tok;
+    int a_hi, b_lo, b_hi;
+    row_ranges(ap, row_ok, p.n_sink, p.window, a_hi, b_lo, b_hi);
+    const bool dead = __all_sync(0xffffffffu, !row_ok);
+    const float c = p.scale * 1.4426950408889634f;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    const uint32_t pb = p_s + static_cast<uint32_t>(t * 2) * TILE;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!warp_wait(smem_u32(&s_full[t]), j & 1u, lane, &abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      if (dead) {
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
+        continue;
+      }
+      tc_fence_after();
+      // one row is 128 scores, more than the 168 registers a thread has at
+      // 320 threads leave room for: the first half is read for the maximum
+      // and read again for its exponentials (S stays until P is published)
+      const int s0 = j * kAtKeys;
+      float sv[64];
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld_32x32b_x32x2(s_t + half * 64, s_t + half * 64 + 32, sv, sv + 32);
+        mask64(sv, s0 + half * 64, a_hi, b_lo, b_hi);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+      }
+      const float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const bool grow = (m_tile - m_run) * c > kLazy;
+      float alpha = 1.f;
+      const bool rescale = __any_sync(0xffffffffu, grow);
+      if (rescale) {
+        const float m_new = fmaxf(m_run, m_tile);
+        alpha = (m_new == -INFINITY) ? 1.f : ex2_approx((m_run - m_new) * c);
+        m_run = m_new;
+      }
+      // P V of tile j - 1 has finished: P's buffer is free and O is final
+      if (j > 0) {
+        if (!warp_wait(smem_u32(&pv_done[t]), (j - 1) & 1u, lane, &abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (rescale) {
+#pragma unroll 1
+          for (int cc = 0; cc < HD; cc += 32) {
+            float v[32];
+            tmem_ld_32x32b_x32(o_t + cc, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st_32x32b_x32(o_t + cc, v);
+          }
+        }
+      }
+      const float mc = (m_run == -INFINITY) ? 0.f : m_run * c;
+      float sum[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+      // the second half is still in sv; then the first half again
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int half = 1 - pass;
+        if (pass == 1) {
+          tmem_ld_32x32b_x32x2(s_t, s_t + 32, sv, sv + 32);
+          mask64(sv, s0, a_hi, b_lo, b_hi);
+        }
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          sv[i] = ex2_approx(fmaf(sv[i], c, -mc));
+          sum[i & 7] += sv[i];
+        }
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const uint32_t addr = pb + static_cast<uint32_t>(half) * TILE + at_sw128(r, ch);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                       "r"(E::pack2(sv[8 * ch + 0], sv[8 * ch + 1])),
+                       "r"(E::pack2(sv[8 * ch + 2], sv[8 * ch + 3])),
+                       "r"(E::pack2(sv[8 * ch + 4], sv[8 * ch + 5])),
+                       "r"(E::pack2(sv[8 * ch + 6], sv[8 * ch + 7]))
+                       : "memory");
+        }
+      }
+      l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3])) +
+              ((sum[4] + sum[5]) + (sum[6] + sum[7]));
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
+    }
+    if (ok && n_tiles > 0 &&
+        warp_wait(smem_u32(&pv_done[t]), (n_tiles - 1) & 1u, lane, &abort_flag, p.err)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint16_t* dst = static_cast<uint16_t*>(p.out) +
+                      (static_cast<size_t>(tok) * p.num_heads + kvh * p.group + hr) * HD;
+#pragma unroll 1
+      for (int cc = 0; cc < HD; cc += 32) {
+        float v[32];
+        tmem_ld_32x32b_x32(o_t + cc, v);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 u;
+            u.x = E::pack2(v[i + 0] * inv, v[i + 1] * inv);
+            u.y = E::pack2(v[i + 2] * inv, v[i + 3] * inv);
+            u.z = E::pack2(v[i + 4] * inv, v[i + 5] * inv);
+            u.w = E::pack2(v[i + 6] * inv, v[i + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + cc + i) = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// 1024 alignment slack + Q_A, Q_B + K and V rings + P_A, P_B
+constexpr uint32_t kPpSmem = 1024 + (2 + 2 * kAtStages + 4) * kAtom;
+
+template <int DT>
+cudaError_t launch_pp(const AttnTcParams& p, const void* k_pool, const void* v_pool,
+                      cudaStream_t s) {
+  CUtensorMap tk, tv;
+  const long long slots = static_cast<long long>(p.n_sink) + p.window;
+  const unsigned long long rows =
+      static_cast<unsigned long long>(p.cache_len < slots ? p.cache_len : slots);
+  const unsigned long long cols = static_cast<unsigned long long>(p.num_kv_heads) * 64;
+  if (!encode_tmap_2d(&tk, k_pool, DT, rows, cols, 64, kAtKeys) ||
+      !encode_tmap_2d(&tv, v_pool, DT, rows, cols, 64, kAtKeys))
+    return cudaErrorInvalidValue;
+  auto kern = attn_tc_pp_kernel<DT>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  const int pairs = (p.row_blocks + 1) / 2;
+  return launch_pdl_smem(kern, dim3(pairs * p.num_kv_heads), dim3(kPpThreads), kPpSmem, s, tk,
+                         tv, p);
+}
+
 template <int DT, int HD>
 cudaError_t launch_at(const AttnTcParams& p, int row_blocks, const void* k_pool,
                       const void* v_pool, cudaStream_t s) {
@@ -609,10 +1009,41 @@ bool attention_tc_supported(int seq_len, int num_heads, int num_kv_heads, int he
   return true;
 }
 
+namespace {
+
+// Whether two query tiles per CTA beat one.  Both kernels hold one CTA per
+// SM.  A paired step (two tiles' softmax on the same eight warps, the tensor
+// core working on one tile while the other is in softmax) measured 1.74x a
+// single tile's step on B200, so pairing pays only where every CTA has the
+// same key tiles (every row attends the whole ring: no causal tail for the
+// one-tile grid's heaviest-first order to pack) and halving the CTAs halves
+// the waves (1020 x 2048 tokens, 32/4 heads of 64: 256 CTAs in two waves
+// 37.1 us, 128 paired CTAs in one 32.2 us; the causal 1028 x 1028 chunk
+// 22.5 us against 29.0 paired).
+bool pairs_pay(const AttnTcParams& p) {
+  const long long first_ap = static_cast<long long>(p.cache_len) - p.seq_len;
+  if (first_ap < static_cast<long long>(p.n_sink) + p.window - 1) return false;
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int n_sm = (dev >= 0 && dev < 64) ? sms[dev] : 0;
+  if (n_sm == 0) {
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) return false;
+    if (dev >= 0 && dev < 64) sms[dev] = n_sm;
+  }
+  const long long one = static_cast<long long>(p.row_blocks) * p.num_kv_heads;
+  const long long two = static_cast<long long>((p.row_blocks + 1) / 2) * p.num_kv_heads;
+  const long long waves_one = (one + n_sm - 1) / n_sm, waves_two = (two + n_sm - 1) / n_sm;
+  return waves_one >= 2 * waves_two;
+}
+
+}  // namespace
+
 cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, const void* v_pool,
                                 int seq_len, int cache_len, int num_heads, int num_kv_heads,
                                 int head_dim, float scale, int n_sink, int window, int dtype,
-                                int* err, cudaStream_t s) {
+                                int* err, cudaStream_t s, int pairing) {
   AttnTcParams p;
   p.out = out;
   p.q = q;
@@ -632,11 +1063,15 @@ cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, co
   if (rb * num_kv_heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int row_blocks = static_cast<int>(rb);
   p.row_blocks = row_blocks;
-  if (dtype == DT_F16)
-    return head_dim == 64 ? launch_at<DT_F16, 64>(p, row_blocks, k_pool, v_pool, s)
-                          : launch_at<DT_F16, 128>(p, row_blocks, k_pool, v_pool, s);
-  return head_dim == 64 ? launch_at<DT_BF16, 64>(p, row_blocks, k_pool, v_pool, s)
-                        : launch_at<DT_BF16, 128>(p, row_blocks, k_pool, v_pool, s);
+  if (head_dim == 64 && (pairing == 2 || (pairing == 0 && pairs_pay(p)))) {
+    return dtype == DT_F16 ? launch_pp<DT_F16>(p, k_pool, v_pool, s)
+                           : launch_pp<DT_BF16>(p, k_pool, v_pool, s);
+  }
+  if (head_dim == 64)
+    return dtype == DT_F16 ? launch_at<DT_F16, 64>(p, row_blocks, k_pool, v_pool, s)
+                           : launch_at<DT_BF16, 64>(p, row_blocks, k_pool, v_pool, s);
+  return dtype == DT_F16 ? launch_at<DT_F16, 128>(p, row_blocks, k_pool, v_pool, s)
+                         : launch_at<DT_BF16, 128>(p, row_blocks, k_pool, v_pool, s);
 }
 
 }  // namespace orin

@@ -137,15 +137,17 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
                              int batch = 1, long long pool_stride = 0, int* err = nullptr);
 // The tensor-core prefill kernel (csrc/attention_tc.cu): one sequence, head
 // dim 64 or 128, a GQA group that divides 128 (or a multiple of 128), at
-// least 128 query rows.  launch_attention picks it for calls with at least
-// one wave of 128-row blocks; the ORIN_ATTN_KERNEL tuning override ("mma" or
-// "tc", read once per process) forces one kernel where both apply.
+// least 128 query rows.  launch_attention picks it for calls with 32 or more
+// 128-row blocks; the ORIN_ATTN_KERNEL tuning override ("mma", "tc", "tc1"
+// or "tc2", read once per process) forces one kernel where both apply.
+// pairing: 0 lets the launcher choose between one query tile per CTA and two
+// (head dim 64), 1 forces one, 2 forces two where the head dim allows.
 bool attention_tc_supported(int seq_len, int num_heads, int num_kv_heads, int head_dim,
                             int n_sink, int window);
 cudaError_t launch_attention_tc(void* out, const void* q, const void* k_pool, const void* v_pool,
                                 int seq_len, int cache_len, int num_heads, int num_kv_heads,
                                 int head_dim, float scale, int n_sink, int window, int dtype,
-                                int* err, cudaStream_t s);
+                                int* err, cudaStream_t s, int pairing = 0);
 // A row-major [rows, cols] 16-bit (type 0 f16, 1 bf16) or fp32 (type 2)
 // matrix as a TMA map with box_cols x box_rows boxes, 128-byte swizzle
 // (box_cols * element size = 128), zero fill (csrc/gemm_tc.cu).

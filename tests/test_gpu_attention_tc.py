@@ -1,6 +1,8 @@
 """The two attention kernels forced one at a time, against the oracle (B200
 only): the tcgen05 prefill kernel (csrc/attention_tc.cu: S and P.V on the
-tensor cores, accumulators in tensor memory) and the mma.sync kernel
+tensor cores, accumulators in tensor memory) with one query tile per CTA
+("tc1") and, for head dim 64, two paired tiles ("tc2"; head dim 128 runs the
+one-tile form there too), and the mma.sync kernel
 (csrc/attention.cu) on every shape the tcgen05 kernel takes — prefill chunks
 that fill and wrap the ring, small windows wrapped many times, MHA, GQA groups
 of 4, 8, 64 and 128 heads, head dims 64 and 128, rows left over in the last
@@ -37,7 +39,7 @@ CASES = [
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("kernel", ["tc", "mma"])
+@pytest.mark.parametrize("kernel", ["tc1", "tc2", "mma"])
 def test_forced_attention_kernel_matches_oracle(kernel):
     env = dict(os.environ, ORIN_ATTN_KERNEL=kernel, PYTHONPATH=ROOT)
     r = subprocess.run([sys.executable, os.path.abspath(__file__)], env=env, cwd=ROOT,
