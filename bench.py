@@ -998,6 +998,61 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+# prefill attention calls timed by --attention: (new tokens, cached positions
+# after the call, query heads, KV heads, head dim), n_sink 4, W 1024
+ATTN_SHAPES = [(1028, 1028, 32, 4, 64), (1020, 2048, 32, 4, 64), (1028, 1028, 32, 8, 128),
+               (300, 300, 32, 8, 128), (512, 512, 32, 4, 64), (256, 2048, 32, 4, 64),
+               (128, 1028, 32, 4, 64), (64, 2048, 32, 4, 64), (32, 2048, 32, 4, 64)]
+
+
+def run_attention(args):
+    """Prefill attention alone (sink + sliding-window GQA over the ring pools),
+    one call per shape of ATTN_SHAPES, random bf16 inputs: the average of
+    --attention back-to-back calls after --warmup, CUDA events on the
+    launching stream.  The kernel is the launcher's choice unless the
+    ORIN_ATTN_KERNEL tuning override (mma, tc1, tc2) forces one.  Inputs fit
+    in L2 (a few MB): these are kernel times, not HBM-cold ones."""
+    from orininfer_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_sink, window = 4, 1024
+    res = {"kernel": os.environ.get("ORIN_ATTN_KERNEL", "auto"), "dtype": "bf16",
+           "n_sink": n_sink, "window": window, "calls": args.attention, "shapes": {}}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)  # arrival counters start zero
+    for (s_len, c_len, nh, nkv, hd) in ATTN_SHAPES:
+        q = torch.randn((s_len, nh, hd), generator=gen, device=dev).to(torch.bfloat16)
+        kp = torch.randn((n_sink + window, nkv, hd), generator=gen, device=dev).to(torch.bfloat16)
+        vp = torch.randn((n_sink + window, nkv, hd), generator=gen, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+
+        def call():
+            K.attention(out, q, kp, vp, s_len, c_len, nh, nkv, hd, hd ** -0.5, n_sink, window,
+                        workspace=ws)
+
+        for _ in range(args.warmup):
+            call()
+        K.device_check()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.attention):
+            call()
+        b.record()
+        b.synchronize()
+        K.device_check()
+        us = a.elapsed_time(b) / args.attention * 1e3
+        # 4 flops per (query head, attended key, head dim element): S and P V
+        base = c_len - s_len
+        pairs = sum(min(base + i + 1, n_sink + window) for i in range(s_len))
+        res["shapes"][f"{s_len}x{c_len}_h{nh}/{nkv}x{hd}"] = {
+            "us": round(us, 2), "tflops": round(4 * pairs * nh * hd / (us * 1e-6) / 1e12, 1)}
+    return res
+
+
 def run_one_kernel(args):
     """One projection of the layer, eagerly: a bounded case for profilers."""
     dev = torch.device("cuda", 0)
@@ -1274,6 +1329,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="with --model-decode: sequences decoded together (per-sequence KV "
                          "pools, one weight stream per step)")
+    ap.add_argument("--attention", type=int, default=0,
+                    help="instead of the layer bench: time this many back-to-back prefill "
+                         "attention calls per shape (ORIN_ATTN_KERNEL forces a kernel) and "
+                         "print that line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="with --kernel: token rows M of that projection (default: the "
                          "workload's 512; 1..64 is the decode GEMV / skinny path)")
@@ -1290,6 +1349,9 @@ def main():
         return 0
     if args.model_decode > 0:
         print(json.dumps(run_model_decode(args)), flush=True)
+        return 0
+    if args.attention > 0:
+        print(json.dumps(run_attention(args)), flush=True)
         return 0
 
     if args.impl == "reference":

@@ -39,6 +39,10 @@ constexpr int kGvWarps = 8;
 constexpr int kGvThreads = kGvWarps * 32;
 constexpr int kGvRows = 16;    // output features per CTA (MMA M)
 constexpr int kGvBlockK = 32;  // k elements per block: two m16n8k16 MMAs
+// NORM's dynamic shared memory cap (the norm weight, K 16-bit values): with
+// the static arrays (at most 33 KB, the SwiGLU reduction of four token tiles)
+// within the 227 KB a CTA may hold
+constexpr size_t kGvMaxSmem = 192 * 1024;
 
 struct GvParams {
   const void* W;
@@ -220,6 +224,14 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
                           static_cast<uint32_t>((k_end - rest * kGvBlockK) * 2));
     }
   }
+  // NORM: the norm weight does not depend on the previous kernel either; it
+  // is staged in shared memory here, so the main loop's token loads go out
+  // back to back with no global load between them and the normalisation
+  extern __shared__ uint4 s_nw[];  // [K / 8], NORM only
+  if constexpr (NORM) {
+    const T* NWg = static_cast<const T*>(p.norm);
+    for (int c = threadIdx.x; c < p.K / 8; c += kGvThreads) s_nw[c] = ld_weights(NWg + 8 * c);
+  }
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float s_r[NORM ? kGemvMaxTokens : 1];
@@ -250,7 +262,6 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
     }
     __syncthreads();
   }
-  const T* NW = static_cast<const T*>(p.norm);
   for (int kb = kb0; kb < kb1; kb += U) {
     if (kb != kb0) load_w(kb);
     uint4 x[U][NT];
@@ -264,9 +275,13 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
         x[u][t] = (kin && tok < p.M) ? ld_l2_v4(X + static_cast<long long>(tok) * p.K + k)
                                      : make_uint4(0u, 0u, 0u, 0u);
       }
-      if constexpr (NORM) {
-        if (kin) {
-          const uint4 nw = ld_weights(NW + k);
+    }
+    if constexpr (NORM) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = (kb + u) * kGvBlockK + 8 * q;
+        if ((kb + u < kb1) && (k < p.K)) {
+          const uint4 nw = s_nw[k / 8];
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
             const int tok = 8 * t + g;
@@ -360,10 +375,24 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
 
 template <int DT, int EPI, int NT, bool NORM = false>
 cudaError_t gemv_launch(const GvParams& p, cudaStream_t s) {
+  const size_t smem = NORM ? static_cast<size_t>(p.K) * 2 : 0;
+  if (smem > 48 * 1024) {
+    // the cap, once per device: every call's size is at most that
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gemv_kernel<DT, EPI, NT, NORM>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kGvMaxSmem));
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) configured[dev] = 1;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N + kGvRows - 1) / kGvRows);
   cfg.blockDim = dim3(kGvThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -438,6 +467,7 @@ cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int
                         float eps) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
   if (norm && K % 8 != 0) return cudaErrorInvalidValue;
+  if (norm && static_cast<size_t>(K) * 2 > kGvMaxSmem) return cudaErrorInvalidValue;
   GvParams p;
   p.n_offset = n_offset;
   p.norm = norm;

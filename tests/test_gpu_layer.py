@@ -145,7 +145,7 @@ def test_qkv_rope_append(dt, qk_norm, S, start, nh, nkv, hd, ns, W):
 @pytest.mark.parametrize("dt", [0, 1])
 @pytest.mark.parametrize("M", [1, 5, 16, 32])
 @pytest.mark.parametrize("N,Kd,epi", [(2560, 2048, "none"), (5632, 2048, "swiglu"),
-                                      (100, 72, "none")])
+                                      (100, 72, "none"), (512, 4096, "none")])
 def test_linear_rmsnorm_equals_norm_then_linear(dt, M, N, Kd, epi):
     """The norm folded into the weight stream gives what orin_rmsnorm then
     orin_linear give (same per-row sum, same rounding of the normed row), and
