@@ -1112,8 +1112,9 @@ def run_model_decode(args) -> dict:
     the device, 2.07 GB), sink + window KV cache (4 + 1024) per sequence,
     `args.batch` (default 1) 2048-token prompts, each prefilled in the
     reference's chunks of n_sink + W = 1028 and 1020 tokens, then one decode
-    step of all sequences (embedding, 22 x the layer's eight launches + the
-    split-key combine, final norm, LM head + argmax, the tokens fed back on
+    step of all sequences (embedding, 22 x the layer's seven launches with RoPE
+    and the K/V append in the q/k/v epilogue (six with fold_norm), final
+    norm, LM head + argmax, the tokens fed back on
     the device; the batch shares each weight stream) captured in a CUDA graph
     at position 2048 (a full window) and replayed `args.model_decode` times.
     Every replay does a full step's work: the same ring slot is rewritten and
@@ -1214,7 +1215,7 @@ def run_model_decode(args) -> dict:
             # merged by the last split CTA), o_proj, norm, gate/up, down; then
             # embedding, final norm, LM head (key reset, weight stream,
             # decode), token copy
-            "launches_per_step": L * (6 if fold else 8) + (5 if fold else 6),
+            "launches_per_step": L * (6 if fold else 7) + (5 if fold else 6),
             "steps": args.model_decode,
             "dtype": "f16", "data": "synthetic (seeded random-init weights, random prompt)",
             "config": {"workload": "tinyllama_22l_greedy_decode", "n_sink": n_sink,

@@ -272,6 +272,29 @@ orin_status orin_qkv_rope_append_batch(void* q_out, const void* qkv,
                                        float theta, int n_sink, int window_size,
                                        int dtype, void* stream);
 
+/*
+ * The q/k/v projection with RoPE and the K/V append in its epilogue, for
+ * decode-sized calls without per-head q/k norms (Llama-family layers):
+ * replaces orin_linear(qkv, x, w_qkv) followed by
+ * orin_qkv_rope_append_batch(q_out, qkv, NULL, NULL, ...) (src/model.cu:
+ * 59-75) with one launch of the decode weight stream, with the same results
+ * bit for bit: every q/k/v sum is rounded to 16 bits as the projection
+ * stores it, q and k are rotated with the reference's angle, v is copied.
+ * x [batch * seq_len][hidden] (token rows of sequence b after those of
+ * sequence b - 1, all at positions start_pos ..), w_qkv the stacked
+ * [(num_heads + 2 num_kv_heads) * head_dim][hidden] weight, q_out
+ * [batch * seq_len][num_heads][head_dim]; sequence b's K/V go to its pools
+ * at k_pool / v_pool + b * pool_stride.  Needs batch * seq_len <= 32,
+ * hidden % 8 == 0, 16-byte aligned x and w_qkv, and head_dim 64 or 128
+ * (ORIN_ERR_UNSUPPORTED otherwise: use the two calls above).
+ */
+orin_status orin_linear_rope_append(void* q_out, const void* x, const void* w_qkv,
+                                    void* k_pool, void* v_pool, int batch,
+                                    long long pool_stride, int seq_len, int start_pos,
+                                    int hidden, int num_heads, int num_kv_heads,
+                                    int head_dim, float theta, int n_sink,
+                                    int window_size, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Sink + sliding-window GQA attention over the ring KV pool (the callers of */
 /* the linear layers on either side: q/k/v come from the q/k/v projection,   */

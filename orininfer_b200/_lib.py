@@ -82,6 +82,8 @@ SIGNATURES = {
                                   ctypes.c_float, _i, _i, _i, _vp, _sz, _vp]),
     "orin_qkv_rope_append_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i,
                                         _i, ctypes.c_float, ctypes.c_float, _i, _i, _i, _vp]),
+    "orin_linear_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i, _i, _i,
+                                     ctypes.c_float, _i, _i, _i, _vp]),
     "orin_device_check": (_i, [_vp]),
     "orin_tp_unique_id": (_i, [_vp]),
     "orin_tp_init": (_i, [ctypes.POINTER(_vp), _vp, _i, _i, _i, ctypes.c_double]),

@@ -681,6 +681,44 @@ orin_status orin_qkv_rope_append_batch(void* q_out, const void* qkv, const void*
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_qkv_rope_append_batch");
 }
 
+orin_status orin_linear_rope_append(void* q_out, const void* x, const void* w_qkv, void* k_pool,
+                                    void* v_pool, int batch, long long pool_stride, int seq_len,
+                                    int start_pos, int hidden, int num_heads, int num_kv_heads,
+                                    int head_dim, float theta, int n_sink, int window_size,
+                                    int dtype, void* stream) {
+  orin_status st = check_common(dtype, ORIN_EPI_NONE);
+  if (st != ORIN_OK) return st;
+  const long long pool_elems =
+      (static_cast<long long>(n_sink) + window_size) * num_kv_heads * head_dim;
+  if (!q_out || !x || !w_qkv || !k_pool || !v_pool || batch < 1 || seq_len < 1 ||
+      start_pos < 0 || hidden < 1 || num_heads < 1 || num_kv_heads < 1 ||
+      num_heads % num_kv_heads != 0 || n_sink < 0 || window_size < 1 ||
+      (batch > 1 && pool_stride < pool_elems) ||
+      static_cast<long long>(seq_len) > static_cast<long long>(n_sink) + window_size ||
+      static_cast<long long>(start_pos) + seq_len > 0x7fffffffLL) {
+    set_error("orin_linear_rope_append: null pointer or bad size (batch=%d seq_len=%d "
+              "start_pos=%d hidden=%d heads=%d/%d n_sink=%d window=%d pool_stride=%lld)",
+              batch, seq_len, start_pos, hidden, num_heads, num_kv_heads, n_sink, window_size,
+              pool_stride);
+    return ORIN_ERR_INVALID_ARG;
+  }
+  const long long M = static_cast<long long>(batch) * seq_len;
+  if (M > kGemvMaxTokens || hidden % 8 != 0 || !aligned16(x) || !aligned16(w_qkv) ||
+      (head_dim != 64 && head_dim != 128)) {
+    set_error("orin_linear_rope_append: runs on the decode weight stream: needs batch * "
+              "seq_len <= %d, hidden %% 8 == 0, 16-byte aligned x and w_qkv and head_dim 64 or "
+              "128 (M=%lld hidden=%d head_dim=%d); use orin_linear + "
+              "orin_qkv_rope_append_batch otherwise",
+              kGemvMaxTokens, M, hidden, head_dim);
+    return ORIN_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = launch_gemv_rope(q_out, x, w_qkv, static_cast<int>(M), hidden, dtype,
+                                   num_heads, num_kv_heads, head_dim, seq_len, start_pos, theta,
+                                   n_sink, window_size, k_pool, v_pool, pool_stride,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_linear_rope_append");
+}
+
 orin_status orin_device_check(void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(s);

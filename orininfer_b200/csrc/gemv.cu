@@ -54,6 +54,15 @@ struct GvParams {
   int n_offset;  // EPI_ARGMAX: vocabulary position of row 0 (a tensor-parallel shard)
   const void* norm;  // NORM: RMSNorm weight [K] applied to every token row of X first
   float eps;
+  // EPI_ROPE: W is the stacked [q | k | v] weight of num_heads + 2 num_kv_heads
+  // heads; token m is token m % seq_len of sequence m / seq_len, at position
+  // start_pos + m % seq_len; C is q_out [M][num_heads][head_dim], k and v go
+  // to their ring slots in sequence b's pools (pool_stride elements apart)
+  void* k_pool;
+  void* v_pool;
+  long long pool_stride;
+  int head_dim, num_heads, num_kv_heads, seq_len, start_pos, n_sink, window;
+  float theta;
 };
 
 __device__ __forceinline__ uint4 ld_weights(const void* p) {
@@ -161,11 +170,19 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   const int q = lane & 3;
   const int f0 = blockIdx.x * kGvRows;  // first output feature of this CTA
 
-  // first weight row of each row set (packed gate/up: 64-row gate and up groups)
+  // first weight row of each row set (packed gate/up: 64-row gate and up
+  // groups); a lane's two rows are rstride apart: 8, or for EPI_ROPE half a
+  // head, so that each lane holds both dims of its RoPE pairs (the CTA takes
+  // pairs 8j .. 8j + 7 of head f0 / head_dim's rows)
   int wrow[H];
+  int rstride = 8;
   if constexpr (EPI == EPI_SWIGLU) {
     wrow[0] = (f0 / 64) * 128 + (f0 % 64);
     wrow[1] = wrow[0] + 64;
+  } else if constexpr (EPI == EPI_ROPE) {
+    const int cph = p.head_dim / kGvRows;  // CTAs per head
+    wrow[0] = (blockIdx.x / cph) * p.head_dim + 8 * (blockIdx.x % cph);
+    rstride = p.head_dim / 2;
   } else {
     wrow[0] = f0;
   }
@@ -181,7 +198,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   for (int h = 0; h < H; ++h) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int row = wrow[h] + g + 8 * r;
+      const int row = wrow[h] + g + rstride * r;
       wv[h][r] = row < p.w_rows;
       wp[h][r] = W + static_cast<long long>(wv[h][r] ? row : 0) * p.K + 8 * q;
     }
@@ -217,7 +234,8 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   {
     const int rest = kb0 + U;
     if (rest < kb1 && lane < kGvRows * H) {
-      const int row = wrow[lane / kGvRows] + lane % kGvRows;
+      const int lr = lane % kGvRows;  // local row: g = lr % 8 of row set lr / 8
+      const int row = wrow[lane / kGvRows] + (lr & 7) + rstride * (lr >> 3);
       const int k_end = (kb1 * kGvBlockK < p.K) ? kb1 * kGvBlockK : p.K;
       if (row < p.w_rows)
         prefetch_l2_bytes(W + static_cast<long long>(row) * p.K + rest * kGvBlockK,
@@ -309,6 +327,61 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) red[warp][(h * NT + t) * 4 + i][lane] = acc[h][t][i];
   __syncthreads();
+  if constexpr (EPI == EPI_ROPE) {
+    // One warp per (token tile t, token parity jj): lane (g, q) sums dims i
+    // and i + head_dim / 2 of head hb (values t*4 + jj and t*4 + 2 + jj, in
+    // the warp order of the other epilogues) for token 8t + 2q + jj, rounds
+    // each to 16 bits as the projection stores it and rotates the pair as the
+    // RoPE kernel does: one angle per thread.
+    using TT = typename E::T;
+    if (warp >= 2 * NT) return;
+    const int t = warp >> 1, jj = warp & 1;
+    const int m = 8 * t + 2 * q + jj;
+    if (m >= p.M) return;
+    float x0 = red[0][t * 4 + jj][lane], x1 = red[0][t * 4 + 2 + jj][lane];
+#pragma unroll
+    for (int ww = 1; ww < kGvWarps; ++ww) {
+      x0 += red[ww][t * 4 + jj][lane];
+      x1 += red[ww][t * 4 + 2 + jj][lane];
+    }
+    x0 = E::round(x0);
+    x1 = E::round(x1);
+    const int cph = p.head_dim / kGvRows;
+    const int hb = blockIdx.x / cph;
+    const int half = p.head_dim / 2;
+    const int i = 8 * (blockIdx.x % cph) + g;
+    const int b = m / p.seq_len;
+    const int tok = m - b * p.seq_len;
+    const int pos = p.start_pos + tok;
+    if (hb < p.num_heads) {
+      float c, sn;
+      rope_angle(pos, i, p.head_dim, p.theta, c, sn);
+      TT* dst = static_cast<TT*>(p.C) + (static_cast<size_t>(m) * p.num_heads + hb) * p.head_dim;
+      dst[i] = E::from_f(x0 * c - x1 * sn);
+      dst[i + half] = E::from_f(x0 * sn + x1 * c);
+      return;
+    }
+    // a later token of this call that lands in the same ring slot owns it
+    if (pos >= p.n_sink && tok + p.window < p.seq_len) return;
+    const size_t kv_dim = static_cast<size_t>(p.num_kv_heads) * p.head_dim;
+    const size_t ring =
+        static_cast<size_t>(pos < p.n_sink ? pos : p.n_sink + (pos - p.n_sink) % p.window);
+    const size_t off = static_cast<size_t>(b) * p.pool_stride + ring * kv_dim;
+    if (hb < p.num_heads + p.num_kv_heads) {
+      float c, sn;
+      rope_angle(pos, i, p.head_dim, p.theta, c, sn);
+      TT* dst = static_cast<TT*>(p.k_pool) + off +
+                static_cast<size_t>(hb - p.num_heads) * p.head_dim;
+      dst[i] = E::from_f(x0 * c - x1 * sn);
+      dst[i + half] = E::from_f(x0 * sn + x1 * c);
+    } else {
+      TT* dst = static_cast<TT*>(p.v_pool) + off +
+                static_cast<size_t>(hb - p.num_heads - p.num_kv_heads) * p.head_dim;
+      dst[i] = E::from_f(x0);
+      dst[i + half] = E::from_f(x1);
+    }
+    return;
+  }
   if (warp != 0) return;
 
   float s[V];
@@ -419,6 +492,7 @@ cudaError_t gemv_dispatch(const GvParams& p, int epi, cudaStream_t s) {
     case EPI_F32_OUT: return gemv_launch<DT, EPI_F32_OUT, NT>(p, s);
     case EPI_F32_PARTIAL: return gemv_launch<DT, EPI_F32_PARTIAL, NT>(p, s);
     case EPI_ARGMAX: return gemv_launch<DT, EPI_ARGMAX, NT>(p, s);
+    case EPI_ROPE: return gemv_launch<DT, EPI_ROPE, NT>(p, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -462,13 +536,48 @@ cudaError_t launch_argmax_decode(int* token, const unsigned long long* keys, int
   return cudaGetLastError();
 }
 
+cudaError_t launch_gemv_rope(void* q_out, const void* A, const void* W, int M, int K, int dtype,
+                             int num_heads, int num_kv_heads, int head_dim, int seq_len,
+                             int start_pos, float theta, int n_sink, int window, void* k_pool,
+                             void* v_pool, long long pool_stride, cudaStream_t s) {
+  if (M < 1 || M > kGemvMaxTokens || K % 8 != 0 || head_dim % kGvRows != 0 || seq_len < 1 ||
+      M % seq_len != 0)
+    return cudaErrorInvalidValue;
+  GvParams p = {};
+  p.W = W;
+  p.X = A;
+  p.C = q_out;
+  p.M = M;
+  p.N = (num_heads + 2 * num_kv_heads) * head_dim;
+  p.K = K;
+  p.w_rows = p.N;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.pool_stride = pool_stride;
+  p.head_dim = head_dim;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.seq_len = seq_len;
+  p.start_pos = start_pos;
+  p.n_sink = n_sink;
+  p.window = window;
+  p.theta = theta;
+  if (dtype == DT_F16)
+    return (M <= 8)    ? gemv_dispatch<DT_F16, 1>(p, EPI_ROPE, s)
+           : (M <= 16) ? gemv_dispatch<DT_F16, 2>(p, EPI_ROPE, s)
+                       : gemv_dispatch<DT_F16, 4>(p, EPI_ROPE, s);
+  return (M <= 8)    ? gemv_dispatch<DT_BF16, 1>(p, EPI_ROPE, s)
+         : (M <= 16) ? gemv_dispatch<DT_BF16, 2>(p, EPI_ROPE, s)
+                     : gemv_dispatch<DT_BF16, 4>(p, EPI_ROPE, s);
+}
+
 cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int K, int dtype,
                         int epi, const void* R, cudaStream_t s, int n_offset, const void* norm,
                         float eps) {
   if (M < 1 || M > kGemvMaxTokens) return cudaErrorInvalidValue;
   if (norm && K % 8 != 0) return cudaErrorInvalidValue;
   if (norm && static_cast<size_t>(K) * 2 > kGvMaxSmem) return cudaErrorInvalidValue;
-  GvParams p;
+  GvParams p = {};
   p.n_offset = n_offset;
   p.norm = norm;
   p.eps = eps;

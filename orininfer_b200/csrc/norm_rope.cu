@@ -99,14 +99,6 @@ __global__ void __launch_bounds__(256)
   pdl_launch_dependents();
 }
 
-// Rotation angle of pair i at position pos, computed as the reference does.
-__device__ __forceinline__ void rope_angle(int pos, int i, int head_dim, float theta, float& c,
-                                           float& s) {
-  const float angle = pos * powf(theta, -2.0f * i / static_cast<float>(head_dim));
-  c = cosf(angle);
-  s = sinf(angle);
-}
-
 // One thread per (token, head, pair) of q and then k, in place.
 template <int DT>
 __global__ void __launch_bounds__(256)

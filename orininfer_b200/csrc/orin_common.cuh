@@ -20,8 +20,20 @@ enum : int {
   EPI_F32_PARTIAL = 4,
   // internal: the LM head's greedy argmax (orin_lm_head_argmax); C holds one
   // 64-bit key per row, combined with atomicMax
-  EPI_ARGMAX = 5
+  EPI_ARGMAX = 5,
+  // internal: the stacked q/k/v projection followed by RoPE and the K/V
+  // append (orin_linear_rope_append): q to its buffer, k and v to the pools
+  EPI_ROPE = 6
 };
+
+// Rotation angle of RoPE pair i (dims i and i + head_dim / 2) at position
+// pos, computed as the reference does (kernels/rope.cu:24-37).
+__device__ __forceinline__ void rope_angle(int pos, int i, int head_dim, float theta, float& c,
+                                           float& s) {
+  const float angle = pos * powf(theta, -2.0f * i / static_cast<float>(head_dim));
+  c = cosf(angle);
+  s = sinf(angle);
+}
 
 // Device-side error codes written to the per-device error word.
 enum : int {

@@ -85,6 +85,15 @@ cudaError_t launch_gemv(void* C, const void* A, const void* W, int M, int N, int
                         int epi, const void* R, cudaStream_t stream, int n_offset = 0,
                         const void* norm = nullptr, float eps = 0.f);
 int gemv_grid(int N);
+// The stacked q/k/v projection on the weight stream with RoPE and the K/V
+// append in its epilogue (M = batch * seq_len tokens, K % 8 == 0, head_dim a
+// multiple of 16): q_out [M][num_heads][head_dim], k and v into the ring
+// slots of sequence m / seq_len's pools; the same values as launch_gemv then
+// launch_qkv_rope_append without q/k norms.
+cudaError_t launch_gemv_rope(void* q_out, const void* A, const void* W, int M, int K, int dtype,
+                             int num_heads, int num_kv_heads, int head_dim, int seq_len,
+                             int start_pos, float theta, int n_sink, int window, void* k_pool,
+                             void* v_pool, long long pool_stride, cudaStream_t stream);
 // LM head + greedy argmax per row: keys[m] = the best 64-bit argmax key of
 // row m over the V vocabulary rows of W (positions v_offset + v), then
 // token[m] = its position (keys: caller scratch of M words).

@@ -381,6 +381,32 @@ def qkv_rope_append_batch(q_out: torch.Tensor, qkv: torch.Tensor, k_pools: torch
         _stream(stream)))
 
 
+def linear_rope_append(q_out: torch.Tensor, x: torch.Tensor, w_qkv: torch.Tensor,
+                       k_pools: torch.Tensor, v_pools: torch.Tensor, seq_len: int,
+                       start_pos: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                       theta: float, n_sink: int, window_size: int, *,
+                       stream: Optional[torch.cuda.Stream] = None) -> None:
+    """The q/k/v projection of x [batch * seq_len, hidden] with RoPE and the
+    K/V append in the decode weight stream's epilogue
+    (orin_linear_rope_append): the same results as linear_into(qkv, x, w_qkv)
+    then qkv_rope_append_batch(q_out, qkv, k_pools, v_pools, ...) without q/k
+    norms (src/model.cu:59-75).  k_pools / v_pools: [batch, n_sink + window,
+    kv_dim] (or one pool [n_sink + window, kv_dim] for batch 1)."""
+    _need_cuda(q_out, x, w_qkv, k_pools, v_pools)
+    if v_pools.shape != k_pools.shape or k_pools.stride(0) != v_pools.stride(0):
+        raise ValueError("k_pools and v_pools must have one shape and stride")
+    batched = k_pools.dim() == 3
+    batch = k_pools.shape[0] if batched else 1
+    stride = k_pools.stride(0) if batched else 0
+    if x.shape[0] != batch * seq_len:
+        raise ValueError(f"x has {x.shape[0]} rows, expected batch * seq_len = "
+                         f"{batch * seq_len}")
+    check(_lib.lib.orin_linear_rope_append(
+        _ptr(q_out), _ptr(x), _ptr(w_qkv), _ptr(k_pools), _ptr(v_pools), batch, stride, seq_len,
+        start_pos, x.shape[1], num_heads, num_kv_heads, head_dim, float(theta), n_sink,
+        window_size, _dtype_code(x), _stream(stream)))
+
+
 def pack_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor,
                  stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     """Interleave gate_proj and up_proj [IM, K] into the [2*IM, K] layout the

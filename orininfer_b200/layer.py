@@ -14,7 +14,10 @@ reference makes fifteen:
     orin_linear(x, h, W_down, RESIDUAL, x)       :107-110
 
 with the reference's rounding points (the residual and SwiGLU epilogues round
-where its separate add and fused_silu_mul kernels do).  With fold_norm, calls
+where its separate add and fused_silu_mul kernels do).  Decode-sized calls
+(up to 16 tokens) of layers without q/k norms put RoPE and the K/V append in
+the q/k/v weight stream's epilogue (orin_linear_rope_append, the same values
+bit for bit): seven launches.  With fold_norm, calls
 of up to 16 tokens (decode) fold each RMSNorm into the projection after it
 (orin_linear_rmsnorm: the decode weight stream normalises the rows it reads,
 bit for bit the separate kernel's output), six launches; that is faster for
@@ -105,6 +108,13 @@ class DecoderLayer:
 
     # calls of at most this many tokens fold the norms into the weight stream
     FOLD_NORM_TOKENS = 16
+    # calls of at most this many tokens rotate and append q/k/v in the weight
+    # stream's epilogue (no q/k norms: those need whole heads)
+    ROPE_EPILOGUE_TOKENS = 16
+
+    def _rope_in_epilogue(self, tokens: int, fold: bool) -> bool:
+        return (not fold and not self.qk_norm and tokens <= self.ROPE_EPILOGUE_TOKENS
+                and self.hd in (64, 128) and self.H % 8 == 0)
 
     def forward(self, x: torch.Tensor, start_pos: int,
                 stream: Optional[torch.cuda.Stream] = None, seq: int = 0) -> torch.Tensor:
@@ -115,17 +125,23 @@ class DecoderLayer:
         xn, qkv, q, att = self.xn[:S], self.qkv[:S], self.q[:S], self.att[:S]
         k_pool, v_pool = self.k_pools[seq], self.v_pools[seq]
         fold = self.fold_norm and S <= self.FOLD_NORM_TOKENS
-        if fold:
-            kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
-                                   stream=stream)
-        else:
+        if self._rope_in_epilogue(S, fold):
             kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
-            kernels.linear_into(qkv, xn, w["qkv"], workspace=self.gemm_ws, stream=stream)
-        kernels.qkv_rope_append(q, qkv, k_pool, v_pool, S, start_pos, self.nh, self.nkv,
-                                self.hd, self.theta, self.n_sink, self.window,
-                                q_norm=w.get("q_norm") if self.qk_norm else None,
-                                k_norm=w.get("k_norm") if self.qk_norm else None,
-                                eps=self.eps, stream=stream)
+            kernels.linear_rope_append(q, xn, w["qkv"], k_pool, v_pool, S, start_pos, self.nh,
+                                       self.nkv, self.hd, self.theta, self.n_sink, self.window,
+                                       stream=stream)
+        else:
+            if fold:
+                kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
+                                       stream=stream)
+            else:
+                kernels.rmsnorm(xn, x, w["input_layernorm"], S, self.H, self.eps, stream=stream)
+                kernels.linear_into(qkv, xn, w["qkv"], workspace=self.gemm_ws, stream=stream)
+            kernels.qkv_rope_append(q, qkv, k_pool, v_pool, S, start_pos, self.nh, self.nkv,
+                                    self.hd, self.theta, self.n_sink, self.window,
+                                    q_norm=w.get("q_norm") if self.qk_norm else None,
+                                    k_norm=w.get("k_norm") if self.qk_norm else None,
+                                    eps=self.eps, stream=stream)
         kernels.attention(att, q, k_pool, v_pool, S, start_pos + S, self.nh, self.nkv,
                           self.hd, self.scale, self.n_sink, self.window,
                           workspace=self.workspace, stream=stream)
@@ -145,17 +161,24 @@ class DecoderLayer:
         w = self.w
         xn, qkv, q, att = self.xn[:B], self.qkv[:B], self.q[:B], self.att[:B]
         fold = self.fold_norm and B <= self.FOLD_NORM_TOKENS
-        if fold:
-            kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
-                                   stream=stream)
-        else:
+        if self._rope_in_epilogue(B, fold):
             kernels.rmsnorm(xn, x, w["input_layernorm"], B, self.H, self.eps, stream=stream)
-            kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
-        kernels.qkv_rope_append_batch(q, qkv, self.k_pools, self.v_pools, 1, start_pos, self.nh,
-                                      self.nkv, self.hd, self.theta, self.n_sink, self.window,
-                                      q_norm=w.get("q_norm") if self.qk_norm else None,
-                                      k_norm=w.get("k_norm") if self.qk_norm else None,
-                                      eps=self.eps, stream=stream)
+            kernels.linear_rope_append(q, xn, w["qkv"], self.k_pools, self.v_pools, 1, start_pos,
+                                       self.nh, self.nkv, self.hd, self.theta, self.n_sink,
+                                       self.window, stream=stream)
+        else:
+            if fold:
+                kernels.linear_rmsnorm(qkv, x, w["qkv"], w["input_layernorm"], self.eps,
+                                       stream=stream)
+            else:
+                kernels.rmsnorm(xn, x, w["input_layernorm"], B, self.H, self.eps, stream=stream)
+                kernels.linear_into(qkv, xn, w["qkv"], stream=stream)
+            kernels.qkv_rope_append_batch(q, qkv, self.k_pools, self.v_pools, 1, start_pos,
+                                          self.nh, self.nkv, self.hd, self.theta, self.n_sink,
+                                          self.window,
+                                          q_norm=w.get("q_norm") if self.qk_norm else None,
+                                          k_norm=w.get("k_norm") if self.qk_norm else None,
+                                          eps=self.eps, stream=stream)
         kernels.attention_batch(att, q, self.k_pools, self.v_pools, 1, start_pos + 1, self.nh,
                                 self.nkv, self.hd, self.scale, self.n_sink, self.window,
                                 workspace=self.workspace, stream=stream)

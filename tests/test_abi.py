@@ -179,6 +179,22 @@ def test_batched_attention_and_append_reject_bad_arguments_on_host():
     assert app(q_out=0) == _lib.ERR_INVALID_ARG
     assert app(batch=0) == _lib.OK
 
+    def lra(batch=2, stride=pool, S=1, start=7, hidden=2048, hd=64, x=16, nkv=4):
+        return L.orin_linear_rope_append(16, x, 16, 16, 16, batch, stride, S, start, hidden, 32,
+                                         nkv, hd, ctypes.c_float(1e4), 4, 1024, 0, None)
+
+    # every rejection comes before any device work
+    assert lra(stride=pool - 1) == _lib.ERR_INVALID_ARG     # pools would overlap
+    assert lra(batch=0) == _lib.ERR_INVALID_ARG
+    assert lra(S=1029) == _lib.ERR_INVALID_ARG              # more than n_sink + window
+    assert lra(start=-1) == _lib.ERR_INVALID_ARG
+    assert lra(nkv=5) == _lib.ERR_INVALID_ARG
+    assert lra(x=0) == _lib.ERR_INVALID_ARG
+    assert lra(batch=33, stride=pool) == _lib.ERR_UNSUPPORTED  # more than 32 token rows
+    assert lra(hidden=2044) == _lib.ERR_UNSUPPORTED         # hidden % 8
+    assert lra(x=24) == _lib.ERR_UNSUPPORTED                # x not 16-byte aligned
+    assert lra(hd=96, stride=(4 + 1024) * 4 * 96) == _lib.ERR_UNSUPPORTED  # 64 and 128 built
+
 
 def test_attention_workspace_plan():
     """Few-token calls split their keys across CTAs; prefill-sized calls don't.

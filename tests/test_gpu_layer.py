@@ -167,6 +167,45 @@ def test_linear_rmsnorm_equals_norm_then_linear(dt, M, N, Kd, epi):
     close(fused.cpu(), r, dt, f"linear_rmsnorm M={M} N={N} K={Kd} {epi}")
 
 
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("batch,S,start,ns,W", [
+    (1, 1, 2, 4, 1024),      # a sink position
+    (1, 1, 700, 4, 1024),    # inside the window
+    (1, 1, 3000, 4, 1024),   # the ring has wrapped
+    (4, 1, 1500, 4, 1024),   # batched decode: one token of each sequence
+    (16, 1, 1029, 4, 1024),  # batch 16 at the first wrapped slot
+    (1, 5, 1020, 4, 1024),   # a few tokens across the wrap
+    (1, 16, 40, 8, 8),       # tokens of one call sharing ring slots (the later kept)
+    (2, 8, 21, 4, 16),       # two sequences of 8 tokens each
+])
+@pytest.mark.parametrize("shape", [dict(nh=32, nkv=4, hd=64, H=2048),
+                                   dict(nh=8, nkv=2, hd=128, H=512)])
+def test_linear_rope_append_equals_linear_then_rope_append(dt, batch, S, start, ns, W, shape):
+    """RoPE and the K/V append in the q/k/v weight stream's epilogue give bit
+    for bit what the projection then orin_qkv_rope_append give: q and both
+    pools (which start with random contents), for every position kind."""
+    nh, nkv, hd, H = shape["nh"], shape["nkv"], shape["hd"], shape["H"]
+    rng = np.random.default_rng(batch * 1000 + S * 10 + start + hd)
+    M = batch * S
+    rows = (nh + 2 * nkv) * hd
+    x = dev(rand16(rng, (M, H), dt), dt)
+    w = dev(rand16(rng, (rows, H), dt, 0.05), dt)
+    pools = dev(rand16(rng, (2, batch, ns + W, nkv * hd), dt), dt)
+    k1, v1 = pools[0].clone(), pools[1].clone()
+    k2, v2 = pools[0].clone(), pools[1].clone()
+    q1 = torch.empty((M, nh, hd), dtype=TORCH_DT[dt], device="cuda")
+    q2 = torch.empty_like(q1)
+    K.linear_rope_append(q1, x, w, k1, v1, S, start, nh, nkv, hd, 10000.0, ns, W)
+    qkv = torch.empty((M, rows), dtype=TORCH_DT[dt], device="cuda")
+    K.linear_into(qkv, x, w, algo="gemv")
+    K.qkv_rope_append_batch(q2, qkv, k2, v2, S, start, nh, nkv, hd, 10000.0, ns, W)
+    K.device_check()
+    what = f"batch={batch} S={S} start={start} n_sink={ns} W={W} {shape} dt={dt}"
+    assert np.array_equal(bits(q1.cpu()), bits(q2.cpu())), what
+    assert np.array_equal(bits(k1.cpu()), bits(k2.cpu())), what
+    assert np.array_equal(bits(v1.cpu()), bits(v2.cpu())), what
+
+
 @pytest.mark.parametrize("M", [1, 3])
 def test_lm_head_argmax_with_folded_norm(M):
     dt = 1
