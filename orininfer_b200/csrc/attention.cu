@@ -151,14 +151,14 @@ constexpr int attn_smem_bytes() {
 // out[orow][d, d + 4) = round16(o / l) over the key splits' partials, in
 // split order with a running maximum (flash-decoding style): o = sum_s f_s O_s,
 // l = sum_s f_s l_s, f_s = exp(m_s - max m).  The partials are read through L2
-// (written by other CTAs), 8 splits' loads in flight before their updates.
+// (written by other CTAs), 16 splits' loads in flight before their updates.
 template <int DT, int HD>
 __device__ __forceinline__ void merge_splits(void* out, const float* ws, int rows_total,
                                              int splits, int orow, int d) {
   using E = Elem<DT>;
   const float* mlb = ws + static_cast<size_t>(splits) * rows_total * HD;
   float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int kB = 8;
+  constexpr int kB = 16;
   for (int sp = 0; sp < splits; sp += kB) {
     float2 mlv[kB];
     float4 ov[kB];
@@ -552,6 +552,21 @@ cudaError_t attn_dispatch(const AttnParams& p, int rw, int row_blocks, cudaStrea
 
 }  // namespace
 
+namespace {
+
+// ORIN_ATTN_SPLITS: tuning override, the most key splits a decode row block
+// takes (read once per process; 0 or unset: the planner's choice).
+int attention_split_cap() {
+  static const int v = [] {
+    const char* e = std::getenv("ORIN_ATTN_SPLITS");
+    const int n = e ? std::atoi(e) : 0;
+    return n > 0 ? n : 0;
+  }();
+  return v;
+}
+
+}  // namespace
+
 AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
                         int head_dim, int n_sink, int window, size_t workspace_bytes) {
   AttnPlan pl = {};
@@ -576,6 +591,8 @@ AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_he
     long long want = (2 * kSMs + ctas - 1) / ctas;
     if (want > kr.tiles) want = kr.tiles;
     if (want > 256) want = 256;
+    if (pl.rw == 1 && attention_split_cap() > 0 && want > attention_split_cap())
+      want = attention_split_cap();
     splits = want < 1 ? 1 : static_cast<int>(want);
     const size_t per_split =
         static_cast<size_t>(seq_len) * num_heads * (head_dim + 2) * sizeof(float);
