@@ -250,8 +250,6 @@ __global__ void __launch_bounds__(kAttnThreads)
   auto sK = [&](int stage) { return attn_smem + (2 * stage) * attn_stage_elems<HD>(); };
   auto sV = [&](int stage) { return attn_smem + (2 * stage + 1) * attn_stage_elems<HD>(); };
 
-  pdl_wait();  // q and the pools come from the previous kernels
-
   auto tile_start = [&](int t, int& end) {
     if (t < kr.tiles_sink) {
       end = kr.sink_cnt;
@@ -277,7 +275,20 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   };
 
-  if (tile0 < tile1) load_tile(tile0, 0);
+  // q and the new token's K/V row come from the previous kernels.  A
+  // single-token call appends one position, base, the last of the window
+  // range; every other attended position sits in its own ring slot, which no
+  // kernel of this step writes.  So a first tile that ends before base is
+  // loaded before griddepcontrol.wait, overlapping the previous kernel's tail.
+  bool early = false;
+  if (p.seq_len == 1 && tile0 < tile1) {
+    int end;
+    const int start = tile_start(tile0, end);
+    early = min(start + kKeyTile, end) - 1 < base;
+  }
+  if (early) load_tile(tile0, 0);
+  pdl_wait();
+  if (!early && tile0 < tile1) load_tile(tile0, 0);
   cp_async_commit();
 
   // Q fragments of the two rows, straight from global memory.
