@@ -26,6 +26,20 @@ __global__ void __launch_bounds__(kNormThreads)
                    const typename Elem<DT>::T* w, int dim, float eps, int vec) {
   using E = Elem<DT>;
   using T = typename E::T;
+  // The next kernel may be scheduled at once (it waits for this grid's end
+  // before reading the output) and start streaming its weights; the norm
+  // weight does not depend on the previous kernel either, so each thread's
+  // first two vectors of it come in before the wait.
+  pdl_launch_dependents();
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  uint4 w_early[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+  if (vec) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int c = threadIdx.x + k * kNormThreads;
+      if (c < dim / 8) w_early[k] = w4[c];
+    }
+  }
   pdl_wait();
   const size_t row = blockIdx.x;
   const T* xr = x + row * dim;
@@ -56,11 +70,10 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float r = rsqrtf(tot / static_cast<float>(dim) + eps);
-  pdl_launch_dependents();
   if (vec) {
-    for (int c = threadIdx.x; c < dim / 8; c += kNormThreads) {
+    for (int c = threadIdx.x, k = 0; c < dim / 8; c += kNormThreads, ++k) {
       const uint4 u = reinterpret_cast<const uint4*>(xr)[c];
-      const uint4 g = reinterpret_cast<const uint4*>(w)[c];
+      const uint4 g = k == 0 ? w_early[0] : k == 1 ? w_early[1] : w4[c];
       const uint32_t xd[4] = {u.x, u.y, u.z, u.w};
       const uint32_t wd[4] = {g.x, g.y, g.z, g.w};
       uint32_t od[4];
