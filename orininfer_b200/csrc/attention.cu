@@ -275,6 +275,10 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   };
 
+  // The next kernel (o_proj's weight stream) may be scheduled at once: it
+  // waits for this grid's end before reading the output, and streams its
+  // weights meanwhile.
+  pdl_launch_dependents();
   // q and the new token's K/V row come from the previous kernels.  A
   // single-token call appends one position, base, the last of the window
   // range; every other attended position sits in its own ring slot, which no
@@ -405,7 +409,6 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
   cp_async_wait<0>();
   __syncthreads();
-  pdl_launch_dependents();
 
   // Partials of every warp into shared memory (the stages are free now).
 #pragma unroll

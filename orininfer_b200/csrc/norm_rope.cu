@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kNormThreads)
 __global__ void __launch_bounds__(256)
     embedding_kernel(uint16_t* out, const uint16_t* table, const int32_t* ids, int hidden,
                      int vocab, int vec) {
+  pdl_launch_dependents();  // the next kernel waits for this grid's end anyway
   pdl_wait();
   const int t = blockIdx.x;
   const int id = ids[t];
