@@ -30,7 +30,9 @@
 // registers.  Prefill blocks put 4 warps on 64 rows; decode blocks put the 4
 // warps on one 16-row group and split each key tile between them, and split
 // the key range across CTAs; partials (running max, sum, unnormalised O)
-// merge in shared memory and, across CTAs, as above.
+// merge in shared memory and, across CTAs, as above.  Every CTA lets the next
+// kernel launch at once, and a single-token call's splits whose first tile
+// ends before the new token issue their K/V loads before the dependency wait.
 #include <cstdlib>
 #include <cstring>
 

@@ -25,6 +25,11 @@
 // * The 8 warps' partial fragments are summed in shared memory in warp order
 //   (deterministic), and warp 0 applies the epilogue with the rounding points
 //   of the other kernels.
+// * EPI_ROPE (the stacked q/k/v projection at decode): a CTA streams rows
+//   8j + g and 8j + g + head_dim / 2 of one head instead of 16 consecutive
+//   rows, so every lane holds both dims of its RoPE pairs; one warp per
+//   (token tile, token parity) rounds, rotates and writes q to its buffer and
+//   k / v to their ring slots (the separate RoPE/append kernel's values).
 //
 // The reference's decode path is kernels/matmul.cu:25-44 (one CTA per output
 // row, 2-byte loads, shared-memory tree reduction); this replaces it for
