@@ -257,6 +257,26 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
   }
   pdl_launch_dependents();
   pdl_wait();
+  // RESIDUAL: warp 0's residual values (written by the previous kernel) are
+  // fetched now, while the MMAs run, instead of in the epilogue; each lane
+  // reads exactly the elements it later writes, so an in-place call (C == R)
+  // is unaffected.
+  float res[EPI == EPI_RESIDUAL ? NT * 4 : 1];
+  if constexpr (EPI == EPI_RESIDUAL) {
+    if (warp == 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int n = f0 + g + 8 * (i >> 1);
+          const int m = 8 * t + 2 * q + (i & 1);
+          res[t * 4 + i] = (n < p.N && m < p.M)
+                               ? bits_to_f<DT>(ld_l2_u16(static_cast<const T*>(p.R) +
+                                                         static_cast<long long>(m) * p.N + n))
+                               : 0.f;
+        }
+    }
+  }
   __shared__ float s_r[NORM ? kGemvMaxTokens : 1];
   if constexpr (NORM) {
     // the row statistics (the token rows come from the previous kernel)
@@ -437,8 +457,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const GvParams p) {
       if constexpr (EPI == EPI_NONE) {
         static_cast<T*>(p.C)[o] = E::from_f(a);
       } else if constexpr (EPI == EPI_RESIDUAL) {
-        const float r = bits_to_f<DT>(ld_l2_u16(static_cast<const T*>(p.R) + o));
-        static_cast<T*>(p.C)[o] = E::from_f(r + E::round(a));
+        static_cast<T*>(p.C)[o] = E::from_f(res[t * 4 + i] + E::round(a));
       } else if constexpr (EPI == EPI_F32_OUT) {
         static_cast<float*>(p.C)[o] = E::round(a);
       } else if constexpr (EPI == EPI_F32_PARTIAL) {
