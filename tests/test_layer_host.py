@@ -71,3 +71,23 @@ def test_prefill_chunks_follow_the_reference_engine():
     assert prefill_chunks(0, 1028) == []
     with pytest.raises(ValueError):
         prefill_chunks(10, 0)
+
+
+def test_rope_epilogue_taken_for_decode_calls_without_qk_norms():
+    """Decode-sized calls of layers without q/k norms rotate and append q/k/v
+    in the weight stream's epilogue (orin_linear_rope_append); calls with
+    q/k norms (whole heads), longer calls, folded norms and head dims the
+    epilogue is not built for keep the projection + orin_qkv_rope_append."""
+    layer = DecoderLayer(weights(), CFG, n_sink=4, window=16, max_tokens=20)
+    assert layer._rope_in_epilogue(1, False)
+    assert layer._rope_in_epilogue(DecoderLayer.ROPE_EPILOGUE_TOKENS, False)
+    assert not layer._rope_in_epilogue(DecoderLayer.ROPE_EPILOGUE_TOKENS + 1, False)
+    assert not layer._rope_in_epilogue(1, True)          # fold_norm path
+    w = weights()
+    w["q_norm"] = torch.ones(64, dtype=torch.float16)
+    w["k_norm"] = torch.ones(64, dtype=torch.float16)
+    qk = DecoderLayer(w, CFG, n_sink=4, window=16, max_tokens=8, qk_norm=True)
+    assert not qk._rope_in_epilogue(1, False)
+    cfg96 = dict(CFG, head_dim=96)
+    odd = DecoderLayer(weights(cfg96), cfg96, n_sink=4, window=16, max_tokens=8)
+    assert not odd._rope_in_epilogue(1, False)
