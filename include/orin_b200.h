@@ -367,6 +367,24 @@ orin_status orin_attention_batch(void* out, const void* q, const void* k_pool,
                                  void* stream);
 
 /*
+ * orin_attention_batch with flags (batch 1 is a single sequence).
+ * ORIN_ATTN_OWN_SLOTS_ONLY: the caller states that the kernel issued just
+ * before this call on the stream wrote no slot of these pools other than
+ * those of this call's own positions (as orin_linear_rope_append,
+ * orin_qkv_rope_append(_batch) or orin_kv_append of the same tokens do); a
+ * single-token call then loads the other slots' keys and values before that
+ * kernel has finished.  Without the flag every load waits for it.
+ */
+#define ORIN_ATTN_OWN_SLOTS_ONLY 1u
+orin_status orin_attention_batch_ex(void* out, const void* q, const void* k_pool,
+                                    const void* v_pool, int batch,
+                                    long long pool_stride, int seq_len, int cache_len,
+                                    int num_heads, int num_kv_heads, int head_dim,
+                                    float scale, int n_sink, int window_size, int dtype,
+                                    void* workspace, size_t workspace_bytes,
+                                    unsigned flags, void* stream);
+
+/*
  * Synchronise stream and report device-side failures of this library's
  * kernels: every spin-wait inside them gives up after a bounded time and
  * records an error code instead of hanging.  Returns ORIN_ERR_TIMEOUT (and

@@ -80,6 +80,8 @@ SIGNATURES = {
     "orin_attention_workspace_bytes": (_i, [ctypes.POINTER(_sz), _i, _i, _i, _i, _i, _i, _i]),
     "orin_attention_batch": (_i, [_vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i, _i,
                                   ctypes.c_float, _i, _i, _i, _vp, _sz, _vp]),
+    "orin_attention_batch_ex": (_i, [_vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i, _i,
+                                     ctypes.c_float, _i, _i, _i, _vp, _sz, ctypes.c_uint, _vp]),
     "orin_qkv_rope_append_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i,
                                         _i, ctypes.c_float, ctypes.c_float, _i, _i, _i, _vp]),
     "orin_linear_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _ll, _i, _i, _i, _i, _i, _i,

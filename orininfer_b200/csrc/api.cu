@@ -497,6 +497,21 @@ orin_status orin_attention_batch(void* out, const void* q, const void* k_pool, c
                                  int num_heads, int num_kv_heads, int head_dim, float scale,
                                  int n_sink, int window_size, int dtype, void* workspace,
                                  size_t workspace_bytes, void* stream) {
+  return orin_attention_batch_ex(out, q, k_pool, v_pool, batch, pool_stride, seq_len, cache_len,
+                                 num_heads, num_kv_heads, head_dim, scale, n_sink, window_size,
+                                 dtype, workspace, workspace_bytes, 0, stream);
+}
+
+orin_status orin_attention_batch_ex(void* out, const void* q, const void* k_pool,
+                                    const void* v_pool, int batch, long long pool_stride,
+                                    int seq_len, int cache_len, int num_heads, int num_kv_heads,
+                                    int head_dim, float scale, int n_sink, int window_size,
+                                    int dtype, void* workspace, size_t workspace_bytes,
+                                    unsigned flags, void* stream) {
+  if (flags & ~static_cast<unsigned>(ORIN_ATTN_OWN_SLOTS_ONLY)) {
+    set_error("orin_attention_batch_ex: unknown flags 0x%x", flags);
+    return ORIN_ERR_INVALID_ARG;
+  }
   orin_status st = check_common(dtype, ORIN_EPI_NONE);
   if (st != ORIN_OK) return st;
   st = check_attention("orin_attention_batch", seq_len, cache_len, num_heads, num_kv_heads,
@@ -527,7 +542,8 @@ orin_status orin_attention_batch(void* out, const void* q, const void* k_pool, c
   cudaError_t e = launch_attention(out, q, k_pool, v_pool, seq_len, cache_len, num_heads,
                                    num_kv_heads, head_dim, scale, n_sink, window_size, dtype,
                                    workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
-                                   batch, pool_stride, error_word_if_ready());
+                                   batch, pool_stride, error_word_if_ready(),
+                                   (flags & ORIN_ATTN_OWN_SLOTS_ONLY) ? kAttnOwnSlotsOnly : 0);
   return e == cudaSuccess ? ORIN_OK : cuda_fail(e, "orin_attention_batch");
 }
 

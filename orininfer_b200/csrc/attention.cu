@@ -54,6 +54,7 @@ struct AttnParams {
   float* ws;           // split partials (splits > 1): O [splits][rows][HD], then (m, l) pairs
   int* counters;       // splits > 1: one arrival counter per (grid x, grid y), zero between calls
   int merge_here;      // splits > 1: the last split CTA merges (else attn_combine_kernel)
+  int own_slots_only;  // the kernel before this one wrote only the call's own positions' slots
   int seq_len, cache_len, num_heads, num_kv_heads, n_sink, window;
   float scale;
   int group;   // G = num_heads / num_kv_heads
@@ -281,13 +282,15 @@ __global__ void __launch_bounds__(kAttnThreads)
   // waits for this grid's end before reading the output, and streams its
   // weights meanwhile.
   pdl_launch_dependents();
-  // q and the new token's K/V row come from the previous kernels.  A
-  // single-token call appends one position, base, the last of the window
-  // range; every other attended position sits in its own ring slot, which no
-  // kernel of this step writes.  So a first tile that ends before base is
-  // loaded before griddepcontrol.wait, overlapping the previous kernel's tail.
+  // q and the new token's K/V row come from the previous kernels.  When the
+  // caller states that the kernel before this call wrote no pool slot but
+  // those of the call's own positions (own_slots_only: the decoder's RoPE +
+  // append), a single-token call's one new position, base, is the last of
+  // the window range and every other attended position sits in a slot
+  // nothing in flight writes: a first tile that ends before base is loaded
+  // before griddepcontrol.wait, overlapping the previous kernel's tail.
   bool early = false;
-  if (p.seq_len == 1 && tile0 < tile1) {
+  if (p.own_slots_only && p.seq_len == 1 && tile0 < tile1) {
     int end;
     const int start = tile_start(tile0, end);
     early = min(start + kKeyTile, end) - 1 < base;
@@ -651,7 +654,7 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
                              void* workspace, size_t workspace_bytes, cudaStream_t s, int batch,
-                             long long pool_stride, int* err) {
+                             long long pool_stride, int* err, int flags) {
   if (seq_len <= 0 || batch <= 0) return cudaSuccess;
   if (batch == 1 && attention_tc_supported(seq_len, num_heads, num_kv_heads, head_dim, n_sink,
                                            window)) {
@@ -704,6 +707,7 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
   // launch (64 rows x 10 splits on one CTA: 32.3 us against 17.0 for the
   // 64 x 2048-token call of 32/4 heads of 64)
   p.merge_here = pl.rw == 1 ? 1 : 0;
+  p.own_slots_only = (flags & kAttnOwnSlotsOnly) ? 1 : 0;
   p.batch = batch;
   p.pool_stride = pool_stride;
   const int rb = static_cast<int>(pl.row_blocks);

@@ -132,6 +132,9 @@ struct AttnPlan {
 // (one int per CTA row of the grid; zero before the first call, left zero by
 // every call), then the split partials.
 constexpr size_t kAttnCounterBytes = 4096;
+// launch_attention flags: the kernel issued just before on the stream wrote
+// no pool slot other than those of the call's own positions (ORIN_ATTN_OWN_SLOTS_ONLY)
+constexpr int kAttnOwnSlotsOnly = 1;
 AttnPlan plan_attention(int seq_len, int cache_len, int num_heads, int num_kv_heads,
                         int head_dim, int n_sink, int window, size_t workspace_bytes);
 // `batch` sequences of seq_len tokens each, all at the same positions: q/out
@@ -143,7 +146,8 @@ cudaError_t launch_attention(void* out, const void* q, const void* k_pool, const
                              int seq_len, int cache_len, int num_heads, int num_kv_heads,
                              int head_dim, float scale, int n_sink, int window, int dtype,
                              void* workspace, size_t workspace_bytes, cudaStream_t s,
-                             int batch = 1, long long pool_stride = 0, int* err = nullptr);
+                             int batch = 1, long long pool_stride = 0, int* err = nullptr,
+                             int flags = 0);
 // The tensor-core prefill kernel (csrc/attention_tc.cu): one sequence, head
 // dim 64 or 128, a GQA group that divides 128 (or a multiple of 128), at
 // least 128 query rows.  launch_attention picks it for calls with 32 or more

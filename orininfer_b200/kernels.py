@@ -293,6 +293,10 @@ def kv_append(k_pool: torch.Tensor, v_pool: torch.Tensor, k_src: torch.Tensor,
                                   _stream(stream)))
 
 
+# orin_attention_batch_ex flag (include/orin_b200.h ORIN_ATTN_OWN_SLOTS_ONLY)
+ATTN_OWN_SLOTS_ONLY = 1
+
+
 def attention_workspace_bytes(seq_len: int, cache_len: int, num_heads: int, num_kv_heads: int,
                               head_dim: int, n_sink: int, window_size: int) -> int:
     """Device workspace that lets orin_attention split every few-token call."""
@@ -306,6 +310,7 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
               seq_len: int, cache_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
               scale: float, n_sink: int, window_size: int, *,
               workspace: Optional[torch.Tensor] = None, split: bool = True,
+              own_slots_only: bool = False,
               stream: Optional[torch.cuda.Stream] = None) -> None:
     """kernels::attention (include/kernels.h:58-80, kernels/attention.cu:27-175):
     sink + sliding-window GQA attention of q [seq_len, num_heads, head_dim]
@@ -313,7 +318,10 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
     out.  With split (the default) few-token calls split their keys across
     CTAs through `workspace` (allocated here when not given; a caller's
     workspace must start zeroed: its first 4 KB are arrival counters that
-    every call leaves zero)."""
+    every call leaves zero).  own_slots_only: the kernel issued just before
+    on the stream wrote only the slots of this call's own positions
+    (ORIN_ATTN_OWN_SLOTS_ONLY: a single-token call loads the other keys
+    before that kernel ends)."""
     _need_cuda(out, q, k_pool, v_pool, workspace)
     if len({out.dtype, q.dtype, k_pool.dtype, v_pool.dtype}) != 1:
         raise ValueError("out, q and the pools must share one dtype")
@@ -328,6 +336,12 @@ def attention(out: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: 
             ws_bytes = workspace.numel() * workspace.element_size()
     else:
         workspace = None
+    if own_slots_only:
+        check(_lib.lib.orin_attention_batch_ex(
+            _ptr(out), _ptr(q), _ptr(k_pool), _ptr(v_pool), 1, 0, seq_len, cache_len, num_heads,
+            num_kv_heads, head_dim, float(scale), n_sink, window_size, _dtype_code(q),
+            _ptr(workspace), ws_bytes, ATTN_OWN_SLOTS_ONLY, _stream(stream)))
+        return
     check(_lib.lib.orin_attention(_ptr(out), _ptr(q), _ptr(k_pool), _ptr(v_pool), seq_len,
                                   cache_len, num_heads, num_kv_heads, head_dim, float(scale),
                                   n_sink, window_size, _dtype_code(q), _ptr(workspace), ws_bytes,
@@ -338,11 +352,13 @@ def attention_batch(out: torch.Tensor, q: torch.Tensor, k_pools: torch.Tensor,
                     v_pools: torch.Tensor, seq_len: int, cache_len: int, num_heads: int,
                     num_kv_heads: int, head_dim: int, scale: float, n_sink: int,
                     window_size: int, *, workspace: Optional[torch.Tensor] = None,
+                    own_slots_only: bool = False,
                     stream: Optional[torch.cuda.Stream] = None) -> None:
     """attention() over a batch of independent sequences in one launch
     (orin_attention_batch): q/out [batch, seq_len, num_heads, head_dim], pools
     [batch, n_sink + window_size, num_kv_heads, head_dim]; each sequence's
-    result is bit-identical to its own attention() call."""
+    result is bit-identical to its own attention() call.  own_slots_only as
+    for attention()."""
     _need_cuda(out, q, k_pools, v_pools, workspace)
     if len({out.dtype, q.dtype, k_pools.dtype, v_pools.dtype}) != 1:
         raise ValueError("out, q and the pools must share one dtype")
@@ -355,11 +371,12 @@ def attention_batch(out: torch.Tensor, q: torch.Tensor, k_pools: torch.Tensor,
         if need:
             workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
-    check(_lib.lib.orin_attention_batch(_ptr(out), _ptr(q), _ptr(k_pools), _ptr(v_pools), batch,
-                                        k_pools.stride(0), seq_len, cache_len, num_heads,
-                                        num_kv_heads, head_dim, float(scale), n_sink, window_size,
-                                        _dtype_code(q), _ptr(workspace), ws_bytes,
-                                        _stream(stream)))
+    check(_lib.lib.orin_attention_batch_ex(_ptr(out), _ptr(q), _ptr(k_pools), _ptr(v_pools),
+                                           batch, k_pools.stride(0), seq_len, cache_len,
+                                           num_heads, num_kv_heads, head_dim, float(scale),
+                                           n_sink, window_size, _dtype_code(q), _ptr(workspace),
+                                           ws_bytes, ATTN_OWN_SLOTS_ONLY if own_slots_only else 0,
+                                           _stream(stream)))
 
 
 def qkv_rope_append_batch(q_out: torch.Tensor, qkv: torch.Tensor, k_pools: torch.Tensor,

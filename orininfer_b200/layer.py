@@ -142,9 +142,10 @@ class DecoderLayer:
                                     q_norm=w.get("q_norm") if self.qk_norm else None,
                                     k_norm=w.get("k_norm") if self.qk_norm else None,
                                     eps=self.eps, stream=stream)
+        # the kernel before wrote only this call's own slots (RoPE + append)
         kernels.attention(att, q, k_pool, v_pool, S, start_pos + S, self.nh, self.nkv,
                           self.hd, self.scale, self.n_sink, self.window,
-                          workspace=self.workspace, stream=stream)
+                          workspace=self.workspace, own_slots_only=True, stream=stream)
         return self._mlp_tail(x, att, S, fold, stream)
 
     def forward_batch(self, x: torch.Tensor, start_pos: int,
@@ -181,7 +182,7 @@ class DecoderLayer:
                                           eps=self.eps, stream=stream)
         kernels.attention_batch(att, q, self.k_pools, self.v_pools, 1, start_pos + 1, self.nh,
                                 self.nkv, self.hd, self.scale, self.n_sink, self.window,
-                                workspace=self.workspace, stream=stream)
+                                workspace=self.workspace, own_slots_only=True, stream=stream)
         return self._mlp_tail(x, att, B, fold, stream)
 
     def _mlp_tail(self, x: torch.Tensor, att: torch.Tensor, S: int, fold: bool,

@@ -167,6 +167,11 @@ def test_batched_attention_and_append_reject_bad_arguments_on_host():
     assert att(stride=pool + 4) == _lib.ERR_UNSUPPORTED     # stride not 16-byte aligned
     assert att(batch=20000) == _lib.ERR_UNSUPPORTED         # grid y above 65535
     assert att(batch=0) == _lib.OK
+    # the flags form: unknown flags are refused before anything else
+    assert L.orin_attention_batch_ex(16, 16, 16, 16, 2, pool, 1, 10, 32, 4, 64, f, 4, 1024, 0,
+                                     None, 0, 2, None) == _lib.ERR_INVALID_ARG
+    assert L.orin_attention_batch_ex(16, 16, 16, 16, 0, pool, 1, 10, 32, 4, 64, f, 4, 1024, 0,
+                                     None, 0, 1, None) == _lib.OK
 
     def app(batch=2, stride=pool, S=1, start=7, q_out=16):
         return L.orin_qkv_rope_append_batch(q_out, 16, None, None, 16, 16, batch, stride, S,
