@@ -16,6 +16,13 @@
  * call on a device does a one-time set-up (device attributes, the device
  * error word); it must not be inside CUDA stream capture, later calls may be
  * captured into graphs.
+ * Weights read ahead: the projection and RMSNorm entry points are launched
+ * with programmatic dependent launch and start streaming their weights (W,
+ * the norm weight) before the kernel issued just before them on the same
+ * stream has finished, so that kernel must not write those weights; anything
+ * written earlier, or by orin_pack_gate_up, is safe.  Activations, residuals
+ * and pools are read only after it has finished (pools: unless the caller
+ * passes ORIN_ATTN_OWN_SLOTS_ONLY to orin_attention_batch_ex).
  * No C++ exception crosses this boundary: every function returns orin_status,
  * and orin_last_error() gives a thread-local message for the last failure.
  *
@@ -155,7 +162,9 @@ orin_status orin_plan_info_ws(int M, int N, int K, int dtype, int epilogue,
  * Build the packed gate/up weight the SWIGLU epilogue reads:
  * rows [128g, 128g+64) = gate rows [64g, 64g+64), rows [128g+64, 128g+128) =
  * up rows [64g, 64g+64).  w_gate, w_up [IM, K] (include/weight_store.h:17-18);
- * w_packed [2*IM, K].  Requires IM % 64 == 0.  Runs on the device, on stream.
+ * w_packed [2*IM, K].  Requires IM % 64 == 0.  Runs on the device, on stream,
+ * and ends with an ordinary launch, so the next call may use w_packed at once
+ * (see the note on weights read ahead below).
  */
 orin_status orin_pack_gate_up(void* w_packed, const void* w_gate,
                               const void* w_up, int IM, int K, int dtype,

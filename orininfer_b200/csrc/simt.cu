@@ -223,6 +223,10 @@ cudaError_t launch_finish_rows(void* C, const float* S, const void* R, long long
                     static_cast<__nv_bfloat16*>(C), S, static_cast<const __nv_bfloat16*>(R), n);
 }
 
+// Launched without programmatic dependent launch, it starts only once every
+// earlier kernel on the stream has finished and its writes are visible.
+__global__ void stream_order_kernel() {}
+
 cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM, int K, int dtype,
                                 cudaStream_t s) {
   (void)dtype;
@@ -231,9 +235,15 @@ cudaError_t launch_pack_gate_up(void* wp, const void* wg, const void* wu, int IM
                   (reinterpret_cast<uintptr_t>(wu) % 16 == 0);
   const long long total = vec ? 2LL * IM * (K / 8) : 2LL * IM * K;
   if (total <= 0) return cudaSuccess;
-  return launch_pdl(pack_gate_up_kernel, dim3(grid_for(total, 256)), dim3(256), s,
-                    static_cast<uint16_t*>(wp), static_cast<const uint16_t*>(wg),
-                    static_cast<const uint16_t*>(wu), IM, K, vec);
+  cudaError_t e = launch_pdl(pack_gate_up_kernel, dim3(grid_for(total, 256)), dim3(256), s,
+                             static_cast<uint16_t*>(wp), static_cast<const uint16_t*>(wg),
+                             static_cast<const uint16_t*>(wu), IM, K, vec);
+  if (e != cudaSuccess) return e;
+  // the projections read their weights before their dependency wait: an
+  // ordinary launch between the packing and the next call makes the packed
+  // weights visible before that call can start
+  stream_order_kernel<<<1, 32, 0, s>>>();
+  return cudaGetLastError();
 }
 
 }  // namespace orin
