@@ -18,11 +18,14 @@
  * captured into graphs.
  * Weights read ahead: the projection and RMSNorm entry points are launched
  * with programmatic dependent launch and start streaming their weights (W,
- * the norm weight) before the kernel issued just before them on the same
- * stream has finished, so that kernel must not write those weights; anything
- * written earlier, or by orin_pack_gate_up, is safe.  Activations, residuals
- * and pools are read only after it has finished (pools: unless the caller
- * passes ORIN_ATTN_OWN_SLOTS_ONLY to orin_attention_batch_ex).
+ * the norm weight) before the kernels issued before them on the same stream
+ * have finished (this library's kernels let the next one start early, so
+ * more than one can still be running), so no such kernel may write those
+ * weights: write them before a synchronisation point, an ordinary (non-PDL)
+ * launch, or with orin_pack_gate_up (which ends with one).  Activations,
+ * residuals and pools are read only after the previous kernel has finished
+ * (pools: unless the caller passes ORIN_ATTN_OWN_SLOTS_ONLY to
+ * orin_attention_batch_ex).
  * No C++ exception crosses this boundary: every function returns orin_status,
  * and orin_last_error() gives a thread-local message for the last failure.
  *
@@ -377,12 +380,13 @@ orin_status orin_attention_batch(void* out, const void* q, const void* k_pool,
 
 /*
  * orin_attention_batch with flags (batch 1 is a single sequence).
- * ORIN_ATTN_OWN_SLOTS_ONLY: the caller states that the kernel issued just
- * before this call on the stream wrote no slot of these pools other than
- * those of this call's own positions (as orin_linear_rope_append,
- * orin_qkv_rope_append(_batch) or orin_kv_append of the same tokens do); a
- * single-token call then loads the other slots' keys and values before that
- * kernel has finished.  Without the flag every load waits for it.
+ * ORIN_ATTN_OWN_SLOTS_ONLY: the caller states that no kernel that may still
+ * be running when this call starts writes a slot of these pools other than
+ * those of this call's own positions (a decode step whose only pool write is
+ * the new token's orin_linear_rope_append, orin_qkv_rope_append(_batch) or
+ * orin_kv_append); a single-token call then loads the other slots' keys and
+ * values before the previous kernel has finished.  Without the flag every
+ * load waits for it.
  */
 #define ORIN_ATTN_OWN_SLOTS_ONLY 1u
 orin_status orin_attention_batch_ex(void* out, const void* q, const void* k_pool,
