@@ -76,6 +76,13 @@ class DecoderLayer:
         if max_tokens > self.n_sink + self.window:
             raise ValueError("max_tokens exceeds n_sink + window (src/kv_cache.cu:99-103)")
         self.qk_norm = bool(qk_norm)
+        # Set by a caller that orders consecutive calls fully (Decoder: every
+        # step ends with an ordinary launch): a decode call's attention may
+        # then load the pool slots other than the new token's before the
+        # RoPE + append kernel ends (ORIN_ATTN_OWN_SLOTS_ONLY).  Off for calls
+        # made back to back, where kernels launched early can still be
+        # writing the previous call's slot.
+        self.attn_own_slots = False
         if self.qk_norm and ("q_norm" not in self.w or "k_norm" not in self.w):
             raise ValueError("qk_norm needs q_norm and k_norm weights")
         qkv = self.w["qkv"]
@@ -142,10 +149,10 @@ class DecoderLayer:
                                     q_norm=w.get("q_norm") if self.qk_norm else None,
                                     k_norm=w.get("k_norm") if self.qk_norm else None,
                                     eps=self.eps, stream=stream)
-        # the kernel before wrote only this call's own slots (RoPE + append)
         kernels.attention(att, q, k_pool, v_pool, S, start_pos + S, self.nh, self.nkv,
                           self.hd, self.scale, self.n_sink, self.window,
-                          workspace=self.workspace, own_slots_only=True, stream=stream)
+                          workspace=self.workspace, own_slots_only=self.attn_own_slots,
+                          stream=stream)
         return self._mlp_tail(x, att, S, fold, stream)
 
     def forward_batch(self, x: torch.Tensor, start_pos: int,
@@ -182,7 +189,8 @@ class DecoderLayer:
                                           eps=self.eps, stream=stream)
         kernels.attention_batch(att, q, self.k_pools, self.v_pools, 1, start_pos + 1, self.nh,
                                 self.nkv, self.hd, self.scale, self.n_sink, self.window,
-                                workspace=self.workspace, own_slots_only=True, stream=stream)
+                                workspace=self.workspace,
+                                own_slots_only=self.attn_own_slots, stream=stream)
         return self._mlp_tail(x, att, B, fold, stream)
 
     def _mlp_tail(self, x: torch.Tensor, att: torch.Tensor, S: int, fold: bool,
@@ -296,6 +304,11 @@ class Decoder:
                          gemm_workspace=self.gemm_ws)
             for i in range(int(cfg["num_hidden_layers"]))
         ]
+        # every step ends with the argmax decode, an ordinary launch, so the
+        # next step starts after the whole step has finished: within a step
+        # only the new token's RoPE + append writes a layer's pools
+        for layer in self.layers:
+            layer.attn_own_slots = True
         self.x = torch.empty((max_tokens, self.H), dtype=dt, device=device)
         self.xn = torch.empty((self.batch, self.H), dtype=dt, device=device)
         self.keys = torch.empty(self.batch, dtype=torch.int64, device=device)

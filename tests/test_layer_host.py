@@ -79,6 +79,9 @@ def test_rope_epilogue_taken_for_decode_calls_without_qk_norms():
     q/k norms (whole heads), longer calls, folded norms and head dims the
     epilogue is not built for keep the projection + orin_qkv_rope_append."""
     layer = DecoderLayer(weights(), CFG, n_sink=4, window=16, max_tokens=20)
+    # a layer called back to back does not claim ORIN_ATTN_OWN_SLOTS_ONLY
+    # (only Decoder, whose steps end with an ordinary launch, sets it)
+    assert not layer.attn_own_slots
     assert layer._rope_in_epilogue(1, False)
     assert layer._rope_in_epilogue(DecoderLayer.ROPE_EPILOGUE_TOKENS, False)
     assert not layer._rope_in_epilogue(DecoderLayer.ROPE_EPILOGUE_TOKENS + 1, False)
