@@ -215,6 +215,26 @@ def test_attention_workspace_plan():
     assert ws(0, 0, 32, 4, 64, 4, 1024) == 0
 
 
+def test_attention_split_cap_override():
+    """ORIN_ATTN_SPLITS (a tuning override, read once per process) caps the
+    key splits of decode row blocks: the plan's workspace shrinks with it;
+    prefill-sized calls are untouched."""
+    import os
+    import subprocess
+    import sys
+    code = ("from orininfer_b200 import kernels as K; "
+            "print(K.attention_workspace_bytes(1, 2048, 32, 4, 64, 4, 1024), "
+            "K.attention_workspace_bytes(1028, 1028, 32, 4, 64, 4, 1024))")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, ORIN_ATTN_SPLITS="4", PYTHONPATH=root)
+    r = subprocess.run([sys.executable, "-c", code], env=env, cwd=root, capture_output=True,
+                       text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    decode, prefill = (int(v) for v in r.stdout.split())
+    assert decode == 4096 + 4 * 32 * (64 + 2) * 4
+    assert prefill == 0
+
+
 def test_norm_and_rope_reject_bad_arguments_on_host():
     L = _lib.lib
     f = ctypes.c_float
